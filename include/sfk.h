@@ -1,0 +1,217 @@
+/*
+ * sfk.h -- C ABI of the B200 (sm_100a) decode path for StrataFlow.
+ *
+ * This is the drop-in boundary for the per-token MoE decode hot path of
+ * Coaade-Inc/strataflow (reference paths below are relative to that project).
+ * The reference runs the path as ggml graphs built by engine::Engine
+ * (src/model/engine/engine.h:102-308, engine.cpp:2498-3025).  A StrataFlow
+ * build links libsfk.so and calls these entry points from its own C++ host
+ * code: Engine::load -> sfk_engine_create + sfk_weights_put (the HBM tier),
+ * Engine::forward -> sfk_forward, Engine::reset_kv -> sfk_kv_reset.  The
+ * .strata format, the public include/strataflow API and the planner /
+ * predictor contracts are unchanged.
+ *
+ * Conventions
+ *   - Plain C types only; no exceptions cross this boundary.
+ *   - Status codes are the reference's sf_status values
+ *     (include/strataflow/strataflow.h:46-55).
+ *   - Tensor ids and ggml type ids follow GGUF naming (token_embd.weight, ...)
+ *     and ggml.h's ggml_type enum.
+ *   - An engine is used by one host thread at a time (engine.h:101: forward()
+ *     is not thread-safe).  All device work is ordered on the engine's stream.
+ *   - Pointers documented as "device" are CUDA device pointers; "host"
+ *     pointers are ordinary (pageable or pinned) host memory.
+ */
+#ifndef SFK_H
+#define SFK_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define SFK_API __attribute__((visibility("default")))
+#else
+#define SFK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status (== sf_status, strataflow.h:46-55) ------------------------- */
+typedef int32_t sfk_status;
+#define SFK_OK 0
+#define SFK_ERR_INVALID_ARGUMENT 1
+#define SFK_ERR_UNSUPPORTED 3
+#define SFK_ERR_OUT_OF_MEMORY 4
+#define SFK_ERR_RUNTIME 7
+
+/* ggml_type ids (ggml.h) accepted by this library */
+#define SFK_TYPE_F32 0
+#define SFK_TYPE_F16 1
+#define SFK_TYPE_Q8_0 8
+#define SFK_TYPE_Q4_K 12
+#define SFK_TYPE_Q6_K 14
+#define SFK_TYPE_Q8_K 15
+
+/* tensor ids (GGUF names used by engine.cpp:1854-1989,2712,2994) */
+#define SFK_T_TOK_EMBD 0       /* token_embd.weight          [d, V]        */
+#define SFK_T_OUTPUT_NORM 1    /* output_norm.weight         [d]   F32     */
+#define SFK_T_OUTPUT 2         /* output.weight              [d, V]        */
+#define SFK_T_ATTN_NORM 3      /* blk.L.attn_norm.weight     [d]   F32     */
+#define SFK_T_ATTN_Q 4         /* blk.L.attn_q.weight        [d, Hq*hd]    */
+#define SFK_T_ATTN_K 5         /* blk.L.attn_k.weight        [d, Hkv*hd]   */
+#define SFK_T_ATTN_V 6         /* blk.L.attn_v.weight        [d, Hkv*hd]   */
+#define SFK_T_ATTN_OUT 7       /* blk.L.attn_output.weight   [Hq*hd, d]    */
+#define SFK_T_FFN_NORM 8       /* blk.L.ffn_norm.weight      [d]   F32     */
+#define SFK_T_FFN_GATE_INP 9   /* blk.L.ffn_gate_inp.weight  [d, E] F32    */
+#define SFK_T_FFN_GATE_EXPS 10 /* blk.L.ffn_gate_exps.weight [d, F, E]     */
+#define SFK_T_FFN_UP_EXPS 11   /* blk.L.ffn_up_exps.weight   [d, F, E]     */
+#define SFK_T_FFN_DOWN_EXPS 12 /* blk.L.ffn_down_exps.weight [F, d, E]     */
+
+#define SFK_KV_F32 0
+#define SFK_KV_F16 1
+
+/* Model shape and engine options.  The first block mirrors
+ * engine::EngineHParams (engine.h:41-55); types name the quantization of each
+ * weight class; kv_type selects the KV cache element type (the reference keeps
+ * F32 K/V, engine.cpp:1253-1286; F16 pages halve the attention bytes);
+ * max_batch bounds the sequences decoded per step (sfk_forward_batch). */
+typedef struct sfk_hparams {
+    int32_t n_embd, n_head, n_head_kv, n_layer, n_ff, n_expert, n_expert_used, n_vocab, n_ctx;
+    float rms_eps, freq_base;
+    int32_t type_embd, type_attn, type_ffn_gu, type_ffn_down, type_output;
+    int32_t kv_type;
+    int32_t max_batch;
+} sfk_hparams;
+
+typedef struct sfk_engine sfk_engine;
+
+/* Message of the most recent failure on this thread (never NULL). */
+SFK_API const char *sfk_last_error(void);
+SFK_API const char *sfk_status_str(sfk_status s);
+
+/* ---- engine lifecycle: replaces engine::Engine::load (engine.h:153-157,
+ *      engine.cpp:983) for the HBM-resident case --------------------------
+ * Allocates the HBM weight tier (every expert resident: the reference's
+ * expert_slots = 0 "auto" working set, engine.cpp:1389-1394), the paged KV
+ * cache (16-token pages, one page table per sequence) and the step buffers on
+ * CUDA device `device`.  Weights are uninitialised until sfk_weights_put or
+ * sfk_weights_synth. */
+SFK_API sfk_status sfk_engine_create(int device, const sfk_hparams *hp, sfk_engine **out);
+SFK_API void sfk_engine_free(sfk_engine *eng);
+/* The engine's cudaStream_t: every call on this engine is ordered on it, so a
+ * caller can record events or order its own work against the decode steps. */
+SFK_API void *sfk_engine_stream(sfk_engine *eng);
+
+/* Upload one tensor's verbatim GGUF bytes (host) into the HBM tier; the bytes
+ * are what StrataReader::read_bundle / read_trunk_tensor return
+ * (src/tws/strata_file.cpp:368,462) and what a GGUF stores.  Quantized
+ * matrices are re-laid out on the device for coalesced streaming; the byte
+ * count streamed per token is unchanged.  `ne` is the ggml shape. */
+SFK_API sfk_status sfk_weights_put(sfk_engine *eng, int tensor, int layer, int ggml_type, const int64_t ne[3],
+                           const void *host_bytes, size_t n_bytes);
+/* One routed expert bundle gate|up|down as the .strata stores it
+ * (src/tws/strata_format.h:122-130: gate_rel = 0, up_rel = gate_len,
+ * down_rel = gate_len + up_len) -- the SlotPool::acquire load path
+ * (src/tws/weight_store.h:174) with HBM as the tier. */
+SFK_API sfk_status sfk_expert_put(sfk_engine *eng, int layer, int expert, const void *bundle, size_t n_bytes);
+/* Read a tensor back as GGUF bytes (host). */
+SFK_API sfk_status sfk_weights_get(sfk_engine *eng, int tensor, int layer, void *host_out, size_t n_bytes);
+/* Fill every tensor with the seeded synthetic generator on the device (norms
+ * = 1, other tensors N(0, 0.02) as Irwin-Hall(12) then quantized).  Produces
+ * the same bytes as the CPU fixture generator for the same seed. */
+SFK_API sfk_status sfk_weights_synth(sfk_engine *eng, uint64_t seed);
+/* Bytes of a tensor in GGUF layout (0 for an unknown tensor). */
+SFK_API size_t sfk_tensor_bytes(const sfk_engine *eng, int tensor, int layer);
+
+/* ---- decode: replaces Engine::forward / reset_kv (engine.h:241,245) ----- */
+/* Clear every sequence's KV so the next step starts at position 0. */
+SFK_API sfk_status sfk_kv_reset(sfk_engine *eng);
+/* One token of sequence 0 at `pos` (0 <= pos < n_ctx), attending over
+ * positions 0..pos.  logits_host (optional, n_vocab floats) receives the
+ * logits; argmax_out (optional) the greedy token (first max wins,
+ * engine.cpp:3111-3121). */
+SFK_API sfk_status sfk_forward(sfk_engine *eng, int32_t token, int32_t pos, float *logits_host, int32_t *argmax_out);
+/* One step of n_seq <= max_batch independent sequences: sequence s takes
+ * tokens[s] at positions[s].  logits_host: [n_seq][n_vocab] or NULL. */
+SFK_API sfk_status sfk_forward_batch(sfk_engine *eng, int32_t n_seq, const int32_t *tokens, const int32_t *positions,
+                             float *logits_host, int32_t *argmax_out);
+/* Greedy decode of n_steps tokens for the first n_seq sequences, continuing
+ * from the last sfk_forward/_batch step (its argmax is the first input).
+ * The loop runs on the device as one captured CUDA graph per step, with no
+ * host round trip; tokens_out: [n_steps][n_seq] (host). */
+SFK_API sfk_status sfk_decode_greedy(sfk_engine *eng, int32_t n_seq, int32_t n_steps, int32_t *tokens_out);
+
+/* Hidden state after the last step, [n_seq][n_embd] (host). */
+SFK_API sfk_status sfk_hidden_get(sfk_engine *eng, float *host_out, size_t n_floats);
+
+/* Average device time (ms) of each kernel of one decode step, launched
+ * `iters` times back to back on the engine's stream, layer = i % n_layer so
+ * consecutive launches stream different weights.  ms_out[8]: embed, qkv,
+ * attention, o_proj, router, gate_up, down, lm_head.  Needs one prior step
+ * (routing and KV state are reused); afterwards the step state is undefined,
+ * so call sfk_kv_reset before decoding again. */
+SFK_API sfk_status sfk_time_kernels(sfk_engine *eng, int32_t n_seq, int32_t iters, float *ms_out, int32_t n_out);
+
+typedef struct sfk_stats {
+    uint64_t weight_bytes_hbm;   /* resident weight bytes (HBM tier) */
+    uint64_t kv_bytes_hbm;       /* reserved KV cache bytes */
+    uint64_t scratch_bytes_hbm;  /* step buffers */
+    uint64_t steps;              /* decode steps run */
+    uint64_t kernels_per_step;   /* kernel launches per decode step */
+    uint64_t active_bytes_per_token; /* weight bytes one b=1 token streams */
+} sfk_stats;
+SFK_API sfk_status sfk_get_stats(const sfk_engine *eng, sfk_stats *out);
+
+/* ---- operator-level entry points (device pointers, caller's stream) -----
+ * `stream` is a cudaStream_t (NULL = legacy default stream). */
+
+/* Bytes of one row of K columns of `ggml_type` in the device layout. */
+SFK_API int64_t sfk_dev_row_bytes(int ggml_type, int64_t K);
+/* GGUF rows -> device layout and back (nrows rows of K columns). */
+SFK_API sfk_status sfk_repack(int ggml_type, const void *dev_gguf, void *dev_out, int64_t nrows, int64_t K, void *stream);
+SFK_API sfk_status sfk_unpack(int ggml_type, const void *dev_in, void *dev_gguf, int64_t nrows, int64_t K, void *stream);
+
+/* ggml dequantize_row_* (bit-exact) of n elements of GGUF-layout data. */
+SFK_API sfk_status sfk_dequantize(int ggml_type, const void *dev_src, float *dev_dst, int64_t n, void *stream);
+
+/* Quantize b activation rows [b][K] (f32) to Q8_K or Q8_0 blocks in GGUF
+ * block layout (ggml quantize_row_q8_K_ref / quantize_row_q8_0_ref). */
+SFK_API sfk_status sfk_quantize_act(int act_type, const float *dev_x, int32_t b, int64_t K, void *dev_out, void *stream);
+
+/* ggml_mul_mat: y[t][r] = W[r,:] . x[t] for a [rows x K] weight in device
+ * layout, b <= 16 activation rows; activations quantized the ggml way. */
+SFK_API sfk_status sfk_mul_mat(int ggml_type, const void *dev_w, int64_t rows, int64_t K, const float *dev_x, int32_t b,
+                       float *dev_y, void *stream);
+
+/* ggml_mul_mat_id for the routed experts (engine.cpp:1967-1970):
+ * w: stacked [E][rows][K] (device layout), x: [b][K] (one row per token,
+ * broadcast over its k experts) or [b][k][K] when x_per_pair,
+ * ids: [b][k] int32, y: [b][k][rows]. */
+SFK_API sfk_status sfk_mul_mat_id(int ggml_type, const void *dev_w, int32_t n_expert, int64_t rows, int64_t K,
+                          const float *dev_x, int32_t x_per_pair, const int32_t *dev_ids, int32_t b, int32_t k,
+                          float *dev_y, void *stream);
+
+/* The fused routed-expert FFN of build_expert_segment (engine.cpp:1956-1989):
+ * out[t] = res[t] + sum_j w[t][j] * Down_e( silu(Gate_e x[t]) * Up_e x[t] ),
+ * e = ids[t][j].  gate/up: [E][F][d], down: [E][d][F] (device layout);
+ * x, res, out: [b][d]; res may be NULL. */
+SFK_API sfk_status sfk_moe_ffn(int type_gu, int type_down, const void *dev_gate, const void *dev_up, const void *dev_down,
+                       int32_t n_expert, int64_t d, int64_t F, const float *dev_x, const float *dev_res,
+                       const int32_t *dev_ids, const float *dev_w, int32_t b, int32_t k, float *dev_out,
+                       void *stream);
+
+/* GQA decode attention over a paged KV cache (engine.cpp:1751-1761 math):
+ * q [b][Hq][hd] f32; k_pages/v_pages [n_pages][Hkv][16][hd] (f16 or f32 per
+ * kv_type); page_table [b][max_pages]; positions [b]: sequence t attends over
+ * 0..positions[t]; out [b][Hq*hd]. */
+SFK_API sfk_status sfk_attn_decode_paged(const float *dev_q, const void *dev_k_pages, const void *dev_v_pages, int32_t kv_type,
+                                 const int32_t *dev_page_table, int32_t max_pages, const int32_t *dev_positions,
+                                 int32_t b, int32_t n_head, int32_t n_head_kv, int32_t head_dim, float *dev_out,
+                                 void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* SFK_H */

@@ -1,0 +1,1192 @@
+// sfk_api.cu -- host side of the C ABI (include/sfk.h): the HBM weight tier,
+// the paged KV cache, the per-step launch sequence and its CUDA graphs.
+//
+// One decode step (b sequences) is this launch chain on the engine's stream,
+// each kernel launched with programmatic dependent launch so the next GEMV's
+// weights stream while the previous kernel finishes:
+//   embed -> L x [ qkv(norm+quant, RoPE, KV append) -> attention(split-K)
+//               -> o_proj(+residual) -> router(norm, softmax, top-k)
+//               -> gate_up(SwiGLU, requant) -> down(weighted combine + residual) ]
+//   -> lm_head(norm, argmax)
+// which is engine::Engine::forward (src/model/engine/engine.cpp:2498-3025) with
+// every host round trip between its 2L+2 ggml segments removed.  The chain is
+// captured once per (batch, token source) into a CUDA graph and replayed.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/sfk.h"
+#include "sfk_dequant.cuh"
+#include "sfk_device.cuh"
+#include "sfk_kernels.cuh"
+
+using namespace sfk;
+
+namespace {
+
+thread_local std::string g_err = "no error";
+
+sfk_status fail(sfk_status st, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return st;
+}
+
+#define CK(call)                                                                              \
+  do {                                                                                        \
+    cudaError_t e_ = (call);                                                                  \
+    if (e_ != cudaSuccess)                                                                    \
+      return fail(e_ == cudaErrorMemoryAllocation ? SFK_ERR_OUT_OF_MEMORY : SFK_ERR_RUNTIME,  \
+                  "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__); \
+  } while (0)
+
+int act_for(int wtype) { return wtype == T_Q8_0 ? T_Q8_0 : T_Q8_K; }
+bool quant_ok(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
+
+int sm_count_of(int dev) {
+  int n = 0;
+  cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  return n > 0 ? n : 148;
+}
+
+constexpr int XQ_RESIDENT_BUDGET = 48 * 1024;
+constexpr int SMEM_LIMIT = 227 * 1024;
+
+// fill in grid / rows_per_cta / xq_resident and check shared memory
+sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
+  int grid = std::min(sm_count, std::max(1, (p.rows + 15) / 16));
+  int rpc = (p.rows + grid - 1) / grid;
+  rpc = (rpc + p.row_align - 1) / p.row_align * p.row_align;
+  grid = (p.rows + rpc - 1) / rpc;
+  p.rows_per_cta = rpc;
+  p.xq_resident = (int64_t)p.n_vec * qact_bytes(p.K) <= XQ_RESIDENT_BUDGET ? 1 : 0;
+  if (p.pro == PRO_QUANT) p.xq_resident = 1;
+  const int smem = stream_smem_bytes(p, nullptr, nullptr, nullptr);
+  if (smem > SMEM_LIMIT)
+    return fail(SFK_ERR_UNSUPPORTED, "stream kernel needs %d B shared memory (rows %d, K %d, vectors %d)", smem,
+                p.rows, p.K, p.n_vec);
+  *grid_out = grid;
+  return SFK_OK;
+}
+
+// cached scratch for operator-level calls, per device
+struct OpScratch {
+  void* buf = nullptr;
+  size_t bytes = 0;
+  Route* route = nullptr;
+  int* status = nullptr;
+  int* counters = nullptr;  // zeroed, self-resetting
+  size_t n_counters = 0;
+};
+std::mutex g_op_mu;
+std::map<int, OpScratch> g_op;
+
+sfk_status op_scratch(size_t need, size_t n_counters, OpScratch** out) {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> lk(g_op_mu);
+  OpScratch& s = g_op[dev];
+  if (!s.route) {
+    CK(cudaMalloc(&s.route, sizeof(Route)));
+    CK(cudaMalloc(&s.status, sizeof(int)));
+    CK(cudaMemset(s.status, 0, sizeof(int)));
+  }
+  if (s.bytes < need) {
+    if (s.buf) cudaFree(s.buf);
+    s.buf = nullptr;
+    s.bytes = 0;
+    CK(cudaMalloc(&s.buf, need));
+    s.bytes = need;
+  }
+  if (s.n_counters < n_counters) {
+    if (s.counters) cudaFree(s.counters);
+    s.counters = nullptr;
+    CK(cudaMalloc(&s.counters, n_counters * sizeof(int)));
+    CK(cudaMemset(s.counters, 0, n_counters * sizeof(int)));
+    s.n_counters = n_counters;
+  }
+  *out = &s;
+  return SFK_OK;
+}
+
+sfk_status check_status_word(int* dev_status, cudaStream_t st) {
+  int h = 0;
+  CK(cudaMemcpyAsync(&h, dev_status, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  if (h != ERR_NONE) {
+    int z = 0;
+    cudaMemcpy(dev_status, &z, sizeof(int), cudaMemcpyHostToDevice);
+    return fail(SFK_ERR_RUNTIME, "device reported error %d (%s)", h,
+                h == ERR_TIMEOUT ? "bounded wait expired" : h == ERR_BAD_ID ? "id out of range" : "bad position");
+  }
+  return SFK_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// engine
+// ---------------------------------------------------------------------------
+struct LayerW {
+  uint8_t* qkv = nullptr;   // [Hq*hd + 2*Hkv*hd] rows of K = d (device layout)
+  uint8_t* wo = nullptr;    // [d] rows of K = Hq*hd
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  float* router = nullptr;  // [E][d]
+  uint8_t* gate = nullptr;  // [E][F] rows of K = d
+  uint8_t* up = nullptr;
+  uint8_t* down = nullptr;  // [E][d] rows of K = F
+};
+
+struct sfk_engine {
+  int device = 0;
+  sfk_hparams hp{};
+  int hd = 0, nq = 0, nk = 0, nqkv = 0;
+  cudaStream_t stream = nullptr;
+  int sm_count = 148;
+  std::vector<void*> allocs;
+  // weights
+  uint8_t* tok_embd = nullptr;  // GGUF layout
+  float* out_norm = nullptr;
+  uint8_t* output = nullptr;
+  std::vector<LayerW> L;
+  uint64_t weight_bytes = 0, kv_bytes = 0, scratch_bytes = 0;
+  // KV
+  void* k_pool = nullptr;
+  void* v_pool = nullptr;
+  int64_t kv_layer_elems = 0;
+  int* page_table = nullptr;
+  int max_pages = 0;
+  int n_pages = 0;
+  // step buffers
+  float *x = nullptr, *ffn_inp = nullptr, *q = nullptr, *attn_out = nullptr, *h = nullptr, *logits = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr, *router_logits = nullptr;
+  uint8_t *xq_ffn = nullptr, *hq = nullptr;
+  Route* route = nullptr;
+  int *attn_counter = nullptr, *router_counter = nullptr, *grp_counter = nullptr;
+  unsigned long long* argmax_key = nullptr;
+  int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
+  int* status = nullptr;
+  int n_split = 1;
+  // pinned staging
+  int* h_tok = nullptr;
+  int* h_pos = nullptr;
+  int* h_hist = nullptr;
+  unsigned long long* h_keys = nullptr;
+  // graphs: key = b * 2 + greedy
+  std::map<int, cudaGraphExec_t> graphs;
+  uint64_t steps = 0;
+  int kernels_per_step = 0;
+  int last_b = 0;
+  std::vector<int> seq_pos;  // host mirror of the next position per sequence
+
+  template <typename T>
+  sfk_status alloc(T** p, size_t bytes, uint64_t* acct) {
+    void* v = nullptr;
+    cudaError_t e = cudaMalloc(&v, bytes);
+    if (e != cudaSuccess)
+      return fail(SFK_ERR_OUT_OF_MEMORY, "cudaMalloc(%zu) failed: %s", bytes, cudaGetErrorString(e));
+    allocs.push_back(v);
+    *p = reinterpret_cast<T*>(v);
+    if (acct) *acct += bytes;
+    return SFK_OK;
+  }
+};
+
+namespace {
+
+int64_t tensor_rows(const sfk_engine* e, int tid) {
+  const sfk_hparams& hp = e->hp;
+  switch (tid) {
+    case SFK_T_TOK_EMBD: case SFK_T_OUTPUT: return hp.n_vocab;
+    case SFK_T_ATTN_Q: return e->nq;
+    case SFK_T_ATTN_K: case SFK_T_ATTN_V: return e->nk;
+    case SFK_T_ATTN_OUT: return hp.n_embd;
+    case SFK_T_FFN_GATE_INP: return hp.n_expert;
+    case SFK_T_FFN_GATE_EXPS: case SFK_T_FFN_UP_EXPS: return (int64_t)hp.n_expert * hp.n_ff;
+    case SFK_T_FFN_DOWN_EXPS: return (int64_t)hp.n_expert * hp.n_embd;
+    default: return 1;
+  }
+}
+int64_t tensor_cols(const sfk_engine* e, int tid) {
+  const sfk_hparams& hp = e->hp;
+  switch (tid) {
+    case SFK_T_ATTN_OUT: return e->nq;
+    case SFK_T_FFN_DOWN_EXPS: return hp.n_ff;
+    default: return hp.n_embd;
+  }
+}
+int tensor_type(const sfk_engine* e, int tid) {
+  const sfk_hparams& hp = e->hp;
+  switch (tid) {
+    case SFK_T_TOK_EMBD: return hp.type_embd;
+    case SFK_T_OUTPUT: return hp.type_output;
+    case SFK_T_ATTN_Q: case SFK_T_ATTN_K: case SFK_T_ATTN_V: case SFK_T_ATTN_OUT: return hp.type_attn;
+    case SFK_T_FFN_GATE_EXPS: case SFK_T_FFN_UP_EXPS: return hp.type_ffn_gu;
+    case SFK_T_FFN_DOWN_EXPS: return hp.type_ffn_down;
+    default: return T_F32;
+  }
+}
+bool layered(int tid) { return tid >= SFK_T_ATTN_NORM && tid <= SFK_T_FFN_DOWN_EXPS; }
+
+// device destination of a tensor: base pointer (device layout) for matrices,
+// plain pointer for F32 / GGUF-layout tensors
+uint8_t* tensor_dst(sfk_engine* e, int tid, int layer) {
+  const int64_t rs = dev_row_bytes(e->hp.type_attn, e->hp.n_embd);
+  switch (tid) {
+    case SFK_T_TOK_EMBD: return e->tok_embd;
+    case SFK_T_OUTPUT_NORM: return reinterpret_cast<uint8_t*>(e->out_norm);
+    case SFK_T_OUTPUT: return e->output;
+    case SFK_T_ATTN_NORM: return reinterpret_cast<uint8_t*>(e->L[layer].attn_norm);
+    case SFK_T_ATTN_Q: return e->L[layer].qkv;
+    case SFK_T_ATTN_K: return e->L[layer].qkv + (int64_t)e->nq * rs;
+    case SFK_T_ATTN_V: return e->L[layer].qkv + (int64_t)(e->nq + e->nk) * rs;
+    case SFK_T_ATTN_OUT: return e->L[layer].wo;
+    case SFK_T_FFN_NORM: return reinterpret_cast<uint8_t*>(e->L[layer].ffn_norm);
+    case SFK_T_FFN_GATE_INP: return reinterpret_cast<uint8_t*>(e->L[layer].router);
+    case SFK_T_FFN_GATE_EXPS: return e->L[layer].gate;
+    case SFK_T_FFN_UP_EXPS: return e->L[layer].up;
+    case SFK_T_FFN_DOWN_EXPS: return e->L[layer].down;
+    default: return nullptr;
+  }
+}
+// stored in the interleaved device layout (vs verbatim)
+bool relaid(int tid) {
+  return tid == SFK_T_OUTPUT || tid == SFK_T_ATTN_Q || tid == SFK_T_ATTN_K || tid == SFK_T_ATTN_V ||
+         tid == SFK_T_ATTN_OUT || tid == SFK_T_FFN_GATE_EXPS || tid == SFK_T_FFN_UP_EXPS ||
+         tid == SFK_T_FFN_DOWN_EXPS;
+}
+
+uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+// per-tensor seed (same function as the CPU fixture generator)
+uint64_t tensor_seed(uint64_t seed, int tid, int layer) {
+  return splitmix64(seed * 0x100000001B3ull + (uint64_t)(tid + 1) * 0x9E3779B1ull + (uint64_t)(layer + 1) * 0x85EBCA77ull);
+}
+
+// ---- the step launch chain -------------------------------------------------
+enum KernelClass { K_EMBED = 0, K_QKV, K_ATTN, K_OPROJ, K_ROUTER, K_GATEUP, K_DOWN, K_LMHEAD, K_NCLASS };
+
+KvView kv_view(const sfk_engine* e, int l) {
+  const sfk_hparams& hp = e->hp;
+  KvView kv{};
+  kv.page_table = e->page_table;
+  kv.max_pages = e->max_pages;
+  kv.n_head_kv = hp.n_head_kv;
+  kv.head_dim = e->hd;
+  kv.f16 = hp.kv_type == SFK_KV_F16 ? 1 : 0;
+  const size_t kv_elem = kv.f16 ? 2 : 4;
+  kv.k = static_cast<uint8_t*>(e->k_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
+  kv.v = static_cast<uint8_t*>(e->v_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
+  return kv;
+}
+
+// Launch one kernel of the step: class `c` of layer `l` for b sequences.
+sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl) {
+  const sfk_hparams& hp = e->hp;
+  cudaStream_t st = e->stream;
+  const int d = hp.n_embd, F = hp.n_ff, k = hp.n_expert_used;
+  int grid = 0;
+  sfk_status s = SFK_OK;
+  switch (c) {
+    case K_EMBED: {  // ggml_get_rows(token_embd) (engine.cpp:2708-2723)
+      EmbedParams ep{};
+      ep.tok_embd = e->tok_embd;
+      ep.type = hp.type_embd;
+      ep.d = d;
+      ep.V = hp.n_vocab;
+      ep.b = b;
+      ep.tok_in = e->tok_in;
+      ep.argmax_key = e->argmax_key;
+      ep.greedy = greedy ? 1 : 0;
+      ep.tok_hist = e->tok_hist;
+      ep.pos_in = greedy ? nullptr : e->pos_in;
+      ep.pos_state = e->pos_state;
+      ep.pos_cur = e->pos_cur;
+      ep.x = e->x;
+      ep.status = e->status;
+      CK(launch_embed(ep, st, pdl));
+      return SFK_OK;
+    }
+    case K_QKV: {  // attn_norm + Q/K/V + RoPE + KV append (engine.cpp:1878-1897,1646-1656)
+      const LayerW& W = e->L[l];
+      StreamParams p{};
+      p.w0 = W.qkv;
+      p.rowstride = dev_row_bytes(hp.type_attn, d);
+      p.rows = e->nqkv;
+      p.K = d;
+      p.wtype = hp.type_attn;
+      p.nmat = 1;
+      p.act_type = act_for(hp.type_attn);
+      p.row_align = 2;
+      p.b = b; p.k = 1; p.n_pairs = b; p.n_vec = b;
+      p.pro = PRO_QUANT;
+      p.x = e->x;
+      p.norm_w = W.attn_norm;
+      p.eps = hp.rms_eps;
+      p.epi = EPI_QKV;
+      p.y = e->q;
+      p.kv = kv_view(e, l);
+      p.n_head = hp.n_head;
+      p.theta_scale = powf(hp.freq_base, -2.0f / (float)e->hd);
+      p.pos = e->pos_cur;
+      p.status = e->status;
+      if ((s = plan_stream(p, e->sm_count, &grid))) return s;
+      CK(launch_stream(p, grid, st, pdl));
+      return SFK_OK;
+    }
+    case K_ATTN: {  // attention over the paged KV (engine.cpp:1751-1761)
+      AttnParams a{};
+      a.q = e->q;
+      a.kv = kv_view(e, l);
+      a.pos = e->pos_cur;
+      a.b = b;
+      a.n_head = hp.n_head;
+      a.n_split = e->n_split;
+      a.part_o = e->part_o;
+      a.part_ml = e->part_ml;
+      a.counter = e->attn_counter;
+      a.out = e->attn_out;
+      a.status = e->status;
+      CK(launch_attn(a, st, pdl));
+      return SFK_OK;
+    }
+    case K_OPROJ: {  // O projection + residual (engine.cpp:1905-1906)
+      StreamParams p{};
+      p.w0 = e->L[l].wo;
+      p.rowstride = dev_row_bytes(hp.type_attn, e->nq);
+      p.rows = d;
+      p.K = e->nq;
+      p.wtype = hp.type_attn;
+      p.nmat = 1;
+      p.act_type = act_for(hp.type_attn);
+      p.row_align = 1;
+      p.b = b; p.k = 1; p.n_pairs = b; p.n_vec = b;
+      p.pro = PRO_QUANT;
+      p.x = e->attn_out;
+      p.epi = EPI_RESID;
+      p.y = e->ffn_inp;
+      p.res = e->x;
+      p.y_stride = d;
+      p.status = e->status;
+      if ((s = plan_stream(p, e->sm_count, &grid))) return s;
+      CK(launch_stream(p, grid, st, pdl));
+      return SFK_OK;
+    }
+    case K_ROUTER: {  // ffn_norm + router + top-k (engine.cpp:1909-1924)
+      const LayerW& W = e->L[l];
+      RouterParams r{};
+      r.x = e->ffn_inp;
+      r.norm_w = W.ffn_norm;
+      r.w_r = W.router;
+      r.b = b; r.d = d; r.E = hp.n_expert; r.k = k;
+      r.eps = hp.rms_eps;
+      r.act_type = act_for(hp.type_ffn_gu);
+      r.xq = e->xq_ffn;
+      r.route = e->route;
+      r.logits = e->router_logits;
+      r.counter = e->router_counter;
+      r.status = e->status;
+      CK(launch_router(r, st, pdl));
+      return SFK_OK;
+    }
+    case K_GATEUP: {  // routed gate/up + SwiGLU (engine.cpp:1967-1969)
+      const LayerW& W = e->L[l];
+      StreamParams p{};
+      p.w0 = W.gate;
+      p.w1 = W.up;
+      p.rowstride = dev_row_bytes(hp.type_ffn_gu, d);
+      p.expert_stride = (int64_t)F * p.rowstride;
+      p.rows = F;
+      p.K = d;
+      p.wtype = hp.type_ffn_gu;
+      p.nmat = 2;
+      p.act_type = act_for(hp.type_ffn_gu);
+      p.row_align = 1;
+      p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b;
+      p.route = e->route;
+      p.pro = PRO_LOAD;
+      p.qact = e->xq_ffn;
+      p.qact_stride = qact_bytes(d);
+      p.xq_by_pair = 0;
+      p.epi = EPI_GATEUP;
+      p.h = e->h;
+      p.hq = e->hq;
+      p.grp_counter = e->grp_counter;
+      p.h_act_type = act_for(hp.type_ffn_down);
+      p.status = e->status;
+      if ((s = plan_stream(p, e->sm_count, &grid))) return s;
+      CK(launch_stream(p, grid, st, pdl));
+      return SFK_OK;
+    }
+    case K_DOWN: {  // routed down + weighted combine + residual (engine.cpp:1970-1986)
+      StreamParams p{};
+      p.w0 = e->L[l].down;
+      p.rowstride = dev_row_bytes(hp.type_ffn_down, F);
+      p.expert_stride = (int64_t)d * p.rowstride;
+      p.rows = d;
+      p.K = F;
+      p.wtype = hp.type_ffn_down;
+      p.nmat = 1;
+      p.act_type = act_for(hp.type_ffn_down);
+      p.row_align = 1;
+      p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b * k;
+      p.route = e->route;
+      p.pro = PRO_LOAD;
+      p.qact = e->hq;
+      p.qact_stride = qact_bytes(F);
+      p.xq_by_pair = 1;
+      p.epi = EPI_DOWN;
+      p.y = e->x;
+      p.res = e->ffn_inp;
+      p.y_stride = d;
+      p.status = e->status;
+      if ((s = plan_stream(p, e->sm_count, &grid))) return s;
+      CK(launch_stream(p, grid, st, pdl));
+      return SFK_OK;
+    }
+    case K_LMHEAD: {  // output_norm + lm_head + argmax (engine.cpp:2988-3006, ggml_model.cpp:284-292)
+      StreamParams p{};
+      p.w0 = e->output;
+      p.rowstride = dev_row_bytes(hp.type_output, d);
+      p.rows = hp.n_vocab;
+      p.K = d;
+      p.wtype = hp.type_output;
+      p.nmat = 1;
+      p.act_type = act_for(hp.type_output);
+      p.row_align = 1;
+      p.b = b; p.k = 1; p.n_pairs = b; p.n_vec = b;
+      p.pro = PRO_QUANT;
+      p.x = e->x;
+      p.norm_w = e->out_norm;
+      p.eps = hp.rms_eps;
+      p.epi = EPI_LMHEAD;
+      p.y = e->logits;
+      p.y_stride = hp.n_vocab;
+      p.argmax_key = e->argmax_key;
+      p.store_logits = 1;
+      p.status = e->status;
+      if ((s = plan_stream(p, e->sm_count, &grid))) return s;
+      CK(launch_stream(p, grid, st, pdl));
+      return SFK_OK;
+    }
+    default: return fail(SFK_ERR_INVALID_ARGUMENT, "kernel class %d", c);
+  }
+}
+
+sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
+  int nk = 0;
+  sfk_status s = launch_one(e, K_EMBED, 0, b, greedy, true);
+  if (s) return s;
+  ++nk;
+  for (int l = 0; l < e->hp.n_layer; ++l) {
+    for (int c = K_QKV; c <= K_DOWN; ++c) {
+      if ((s = launch_one(e, c, l, b, greedy, true))) return s;
+      ++nk;
+    }
+  }
+  if ((s = launch_one(e, K_LMHEAD, 0, b, greedy, true))) return s;
+  ++nk;
+  e->kernels_per_step = nk;
+  return SFK_OK;
+}
+
+sfk_status get_graph(sfk_engine* e, int b, bool greedy, cudaGraphExec_t* out) {
+  const int key = b * 2 + (greedy ? 1 : 0);
+  auto it = e->graphs.find(key);
+  if (it != e->graphs.end()) {
+    *out = it->second;
+    return SFK_OK;
+  }
+  cudaGraph_t g = nullptr;
+  CK(cudaStreamBeginCapture(e->stream, cudaStreamCaptureModeThreadLocal));
+  sfk_status s = enqueue_step(e, b, greedy);
+  cudaError_t ce = cudaStreamEndCapture(e->stream, &g);
+  if (s != SFK_OK) {
+    if (g) cudaGraphDestroy(g);
+    return s;
+  }
+  if (ce != cudaSuccess) return fail(SFK_ERR_RUNTIME, "graph capture failed: %s", cudaGetErrorString(ce));
+  cudaGraphExec_t ex = nullptr;
+  ce = cudaGraphInstantiate(&ex, g, 0);
+  cudaGraphDestroy(g);
+  if (ce != cudaSuccess) return fail(SFK_ERR_RUNTIME, "graph instantiate failed: %s", cudaGetErrorString(ce));
+  e->graphs[key] = ex;
+  *out = ex;
+  return SFK_OK;
+}
+
+sfk_status validate_hp(const sfk_hparams* hp) {
+  if (!hp) return fail(SFK_ERR_INVALID_ARGUMENT, "null hparams");
+  if (hp->n_embd <= 0 || hp->n_head <= 0 || hp->n_head_kv <= 0 || hp->n_layer <= 0 || hp->n_ff <= 0 ||
+      hp->n_expert <= 0 || hp->n_expert_used <= 0 || hp->n_vocab <= 0 || hp->n_ctx <= 0)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "hparams must be positive");
+  if (hp->n_head % hp->n_head_kv || hp->n_embd % hp->n_head)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "n_head must divide by n_head_kv and n_embd by n_head");
+  const int hd = hp->n_embd / hp->n_head;
+  if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
+    return fail(SFK_ERR_UNSUPPORTED, "head_dim %d not in {32,64,128,256}", hd);
+  if (hp->n_embd % 256 || hp->n_ff % 256)
+    return fail(SFK_ERR_UNSUPPORTED, "n_embd and n_ff must be multiples of 256");
+  if (hp->n_expert_used > hp->n_expert || hp->n_expert_used > 16 || hp->n_expert > 512)
+    return fail(SFK_ERR_UNSUPPORTED, "need n_expert_used <= min(16, n_expert) and n_expert <= 512");
+  if (hp->max_batch < 1 || hp->max_batch > MAXB || hp->max_batch * hp->n_expert_used > MAXP)
+    return fail(SFK_ERR_UNSUPPORTED, "max_batch must be in [1,%d] with max_batch*n_expert_used <= %d", MAXB, MAXP);
+  const int types[] = {hp->type_attn, hp->type_ffn_gu, hp->type_ffn_down, hp->type_output};
+  for (int t : types)
+    if (!quant_ok(t)) return fail(SFK_ERR_UNSUPPORTED, "weight type %d not supported (Q4_K, Q6_K, Q8_0)", t);
+  if (!quant_ok(hp->type_embd) && hp->type_embd != T_F32 && hp->type_embd != T_F16)
+    return fail(SFK_ERR_UNSUPPORTED, "embedding type %d not supported", hp->type_embd);
+  if (hp->kv_type != SFK_KV_F32 && hp->kv_type != SFK_KV_F16)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "kv_type must be SFK_KV_F32 or SFK_KV_F16");
+  return SFK_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+// ---------------------------------------------------------------------------
+extern "C" {
+
+const char* sfk_last_error(void) { return g_err.c_str(); }
+
+const char* sfk_status_str(sfk_status s) {
+  switch (s) {
+    case SFK_OK: return "ok";
+    case SFK_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case SFK_ERR_UNSUPPORTED: return "unsupported";
+    case SFK_ERR_OUT_OF_MEMORY: return "out of memory";
+    case SFK_ERR_RUNTIME: return "runtime error";
+    default: return "unknown status";
+  }
+}
+
+void sfk_engine_free(sfk_engine* e) {
+  if (!e) return;
+  cudaSetDevice(e->device);
+  if (e->stream) cudaStreamSynchronize(e->stream);
+  for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  for (void* p : e->allocs) cudaFree(p);
+  if (e->h_tok) cudaFreeHost(e->h_tok);
+  if (e->h_pos) cudaFreeHost(e->h_pos);
+  if (e->h_hist) cudaFreeHost(e->h_hist);
+  if (e->h_keys) cudaFreeHost(e->h_keys);
+  if (e->stream) cudaStreamDestroy(e->stream);
+  delete e;
+}
+
+void* sfk_engine_stream(sfk_engine* e) { return e ? (void*)e->stream : nullptr; }
+
+sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out) {
+  if (!out) return fail(SFK_ERR_INVALID_ARGUMENT, "null out");
+  *out = nullptr;
+  sfk_status s = validate_hp(hp);
+  if (s) return s;
+  int ndev = 0;
+  CK(cudaGetDeviceCount(&ndev));
+  if (device < 0 || device >= ndev) return fail(SFK_ERR_INVALID_ARGUMENT, "device %d of %d", device, ndev);
+  CK(cudaSetDevice(device));
+  sfk_engine* e = new (std::nothrow) sfk_engine();
+  if (!e) return fail(SFK_ERR_OUT_OF_MEMORY, "host alloc");
+  e->device = device;
+  e->hp = *hp;
+  e->hd = hp->n_embd / hp->n_head;
+  e->nq = hp->n_head * e->hd;
+  e->nk = hp->n_head_kv * e->hd;
+  e->nqkv = e->nq + 2 * e->nk;
+  e->sm_count = sm_count_of(device);
+  e->seq_pos.assign(hp->max_batch, 0);
+#define TRY(x)               \
+  do {                       \
+    sfk_status s_ = (x);     \
+    if (s_) {                \
+      sfk_engine_free(e);    \
+      return s_;             \
+    }                        \
+  } while (0)
+  {
+    cudaError_t ce = cudaStreamCreateWithFlags(&e->stream, cudaStreamNonBlocking);
+    if (ce != cudaSuccess) {
+      sfk_engine_free(e);
+      return fail(SFK_ERR_RUNTIME, "stream create: %s", cudaGetErrorString(ce));
+    }
+  }
+  const int d = hp->n_embd, F = hp->n_ff, E = hp->n_expert, V = hp->n_vocab;
+  const int B = hp->max_batch, k = hp->n_expert_used;
+  // weights (HBM tier)
+  TRY(e->alloc(&e->tok_embd, dev_gguf_row_bytes(hp->type_embd, d) * V, &e->weight_bytes));
+  TRY(e->alloc(&e->out_norm, sizeof(float) * d, &e->weight_bytes));
+  TRY(e->alloc(&e->output, dev_row_bytes(hp->type_output, d) * V, &e->weight_bytes));
+  e->L.resize(hp->n_layer);
+  for (int l = 0; l < hp->n_layer; ++l) {
+    LayerW& W = e->L[l];
+    TRY(e->alloc(&W.qkv, dev_row_bytes(hp->type_attn, d) * e->nqkv, &e->weight_bytes));
+    TRY(e->alloc(&W.wo, dev_row_bytes(hp->type_attn, e->nq) * d, &e->weight_bytes));
+    TRY(e->alloc(&W.attn_norm, sizeof(float) * d, &e->weight_bytes));
+    TRY(e->alloc(&W.ffn_norm, sizeof(float) * d, &e->weight_bytes));
+    TRY(e->alloc(&W.router, sizeof(float) * d * E, &e->weight_bytes));
+    TRY(e->alloc(&W.gate, dev_row_bytes(hp->type_ffn_gu, d) * F * E, &e->weight_bytes));
+    TRY(e->alloc(&W.up, dev_row_bytes(hp->type_ffn_gu, d) * F * E, &e->weight_bytes));
+    TRY(e->alloc(&W.down, dev_row_bytes(hp->type_ffn_down, F) * d * E, &e->weight_bytes));
+  }
+  // paged KV: one pool per layer of B * ceil(n_ctx/16) pages [Hkv][16][hd];
+  // pages are handed to sequences in a seeded permuted order (a fragmented
+  // pool, as a page allocator produces).
+  e->max_pages = (hp->n_ctx + 15) / 16;
+  e->n_pages = B * e->max_pages;
+  e->kv_layer_elems = (int64_t)e->n_pages * hp->n_head_kv * 16 * e->hd;
+  const size_t kv_elem = hp->kv_type == SFK_KV_F16 ? 2 : 4;
+  TRY(e->alloc(&e->k_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
+  TRY(e->alloc(&e->v_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
+  TRY(e->alloc(&e->page_table, sizeof(int) * e->n_pages, &e->kv_bytes));
+  {
+    std::vector<int> perm(e->n_pages);
+    for (int i = 0; i < e->n_pages; ++i) perm[i] = i;
+    uint64_t st = 0x5F3759DFull;
+    for (int i = e->n_pages - 1; i > 0; --i) {
+      st = splitmix64(st);
+      const int j = (int)(st % (uint64_t)(i + 1));
+      std::swap(perm[i], perm[j]);
+    }
+    CK(cudaMemcpy(e->page_table, perm.data(), sizeof(int) * e->n_pages, cudaMemcpyHostToDevice));
+  }
+  // step buffers
+  e->n_split = std::max(1, std::min(64, (2 * e->sm_count) / (hp->n_head_kv * B)));
+  uint64_t* sb = &e->scratch_bytes;
+  TRY(e->alloc(&e->x, sizeof(float) * B * d, sb));
+  TRY(e->alloc(&e->ffn_inp, sizeof(float) * B * d, sb));
+  TRY(e->alloc(&e->q, sizeof(float) * B * e->nq, sb));
+  TRY(e->alloc(&e->attn_out, sizeof(float) * B * e->nq, sb));
+  TRY(e->alloc(&e->h, sizeof(float) * B * k * F, sb));
+  TRY(e->alloc(&e->logits, sizeof(float) * B * V, sb));
+  TRY(e->alloc(&e->part_o, sizeof(float) * B * hp->n_head * e->n_split * e->hd, sb));
+  TRY(e->alloc(&e->part_ml, sizeof(float) * B * hp->n_head * e->n_split * 2, sb));
+  TRY(e->alloc(&e->router_logits, sizeof(float) * B * E, sb));
+  TRY(e->alloc(&e->xq_ffn, qact_bytes(d) * B, sb));
+  TRY(e->alloc(&e->hq, qact_bytes(F) * B * k, sb));
+  TRY(e->alloc(&e->route, sizeof(Route), sb));
+  TRY(e->alloc(&e->attn_counter, sizeof(int) * B * hp->n_head_kv, sb));
+  TRY(e->alloc(&e->router_counter, sizeof(int), sb));
+  TRY(e->alloc(&e->grp_counter, sizeof(int) * (F / 256), sb));
+  TRY(e->alloc(&e->argmax_key, sizeof(unsigned long long) * B, sb));
+  TRY(e->alloc(&e->tok_in, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->pos_in, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->pos_state, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->pos_cur, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->tok_hist, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->status, sizeof(int), sb));
+  {
+    cudaError_t ce = cudaSuccess;
+    ce = cudaMemset(e->attn_counter, 0, sizeof(int) * B * hp->n_head_kv);
+    if (ce == cudaSuccess) ce = cudaMemset(e->router_counter, 0, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemset(e->grp_counter, 0, sizeof(int) * (F / 256));
+    if (ce == cudaSuccess) ce = cudaMemset(e->argmax_key, 0, sizeof(unsigned long long) * B);
+    if (ce == cudaSuccess) ce = cudaMemset(e->pos_state, 0, sizeof(int) * B);
+    if (ce == cudaSuccess) ce = cudaMemset(e->status, 0, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemset(e->k_pool, 0, kv_elem * e->kv_layer_elems * hp->n_layer);
+    if (ce == cudaSuccess) ce = cudaMemset(e->v_pool, 0, kv_elem * e->kv_layer_elems * hp->n_layer);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_tok, sizeof(int) * B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_pos, sizeof(int) * B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_hist, sizeof(int) * B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_keys, sizeof(unsigned long long) * B);
+    if (ce != cudaSuccess) {
+      sfk_engine_free(e);
+      return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
+    }
+  }
+#undef TRY
+  *out = e;
+  return SFK_OK;
+}
+
+size_t sfk_tensor_bytes(const sfk_engine* e, int tid, int layer) {
+  if (!e || tid < 0 || tid > SFK_T_FFN_DOWN_EXPS) return 0;
+  if (layered(tid) ? (layer < 0 || layer >= e->hp.n_layer) : layer != 0) return 0;
+  return (size_t)dev_gguf_row_bytes(tensor_type(e, tid), tensor_cols(e, tid)) * (size_t)tensor_rows(e, tid);
+}
+
+static sfk_status put_gguf_device(sfk_engine* e, int tid, int layer, const uint8_t* dev_gguf) {
+  const int type = tensor_type(e, tid);
+  const int64_t rows = tensor_rows(e, tid), cols = tensor_cols(e, tid);
+  uint8_t* dst = tensor_dst(e, tid, layer);
+  if (relaid(tid)) {
+    CK(launch_repack(type, dev_gguf, dst, rows, (int)cols, e->stream));
+  } else {
+    CK(cudaMemcpyAsync(dst, dev_gguf, sfk_tensor_bytes(e, tid, layer), cudaMemcpyDeviceToDevice, e->stream));
+  }
+  return SFK_OK;
+}
+
+sfk_status sfk_weights_put(sfk_engine* e, int tid, int layer, int ggml_type, const int64_t ne[3], const void* host,
+                           size_t n_bytes) {
+  if (!e || !host) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t want = sfk_tensor_bytes(e, tid, layer);
+  if (want == 0) return fail(SFK_ERR_INVALID_ARGUMENT, "unknown tensor %d layer %d", tid, layer);
+  if (ggml_type != tensor_type(e, tid))
+    return fail(SFK_ERR_INVALID_ARGUMENT, "tensor %d: type %d, engine expects %d", tid, ggml_type, tensor_type(e, tid));
+  if (ne) {
+    const int64_t n_all = ne[0] * std::max<int64_t>(1, ne[1]) * std::max<int64_t>(1, ne[2]);
+    if (ne[0] != tensor_cols(e, tid) || n_all != tensor_cols(e, tid) * tensor_rows(e, tid))
+      return fail(SFK_ERR_INVALID_ARGUMENT, "tensor %d: shape mismatch", tid);
+  }
+  if (n_bytes != want) return fail(SFK_ERR_INVALID_ARGUMENT, "tensor %d: %zu bytes, expected %zu", tid, n_bytes, want);
+  CK(cudaSetDevice(e->device));
+  uint8_t* tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, want, e->stream));
+  CK(cudaMemcpyAsync(tmp, host, want, cudaMemcpyHostToDevice, e->stream));
+  sfk_status s = put_gguf_device(e, tid, layer, tmp);
+  cudaFreeAsync(tmp, e->stream);
+  if (s) return s;
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_expert_put(sfk_engine* e, int layer, int expert, const void* bundle, size_t n_bytes) {
+  if (!e || !bundle) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const sfk_hparams& hp = e->hp;
+  if (layer < 0 || layer >= hp.n_layer || expert < 0 || expert >= hp.n_expert)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "expert (%d,%d) out of range", layer, expert);
+  const size_t gl = dev_gguf_row_bytes(hp.type_ffn_gu, hp.n_embd) * hp.n_ff;
+  const size_t dl = dev_gguf_row_bytes(hp.type_ffn_down, hp.n_ff) * hp.n_embd;
+  if (n_bytes != 2 * gl + dl) return fail(SFK_ERR_INVALID_ARGUMENT, "bundle %zu bytes, expected %zu", n_bytes, 2 * gl + dl);
+  CK(cudaSetDevice(e->device));
+  uint8_t* tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, n_bytes, e->stream));
+  CK(cudaMemcpyAsync(tmp, bundle, n_bytes, cudaMemcpyHostToDevice, e->stream));
+  const LayerW& W = e->L[layer];
+  const int64_t rs_gu = dev_row_bytes(hp.type_ffn_gu, hp.n_embd), rs_dn = dev_row_bytes(hp.type_ffn_down, hp.n_ff);
+  CK(launch_repack(hp.type_ffn_gu, tmp, W.gate + (int64_t)expert * hp.n_ff * rs_gu, hp.n_ff, hp.n_embd, e->stream));
+  CK(launch_repack(hp.type_ffn_gu, tmp + gl, W.up + (int64_t)expert * hp.n_ff * rs_gu, hp.n_ff, hp.n_embd, e->stream));
+  CK(launch_repack(hp.type_ffn_down, tmp + 2 * gl, W.down + (int64_t)expert * hp.n_embd * rs_dn, hp.n_embd, hp.n_ff,
+                   e->stream));
+  cudaFreeAsync(tmp, e->stream);
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_weights_get(sfk_engine* e, int tid, int layer, void* host_out, size_t n_bytes) {
+  if (!e || !host_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t want = sfk_tensor_bytes(e, tid, layer);
+  if (want == 0 || n_bytes != want) return fail(SFK_ERR_INVALID_ARGUMENT, "tensor %d: bad size", tid);
+  CK(cudaSetDevice(e->device));
+  const uint8_t* src = tensor_dst(e, tid, layer);
+  if (relaid(tid)) {
+    uint8_t* tmp = nullptr;
+    CK(cudaMallocAsync(&tmp, want, e->stream));
+    CK(launch_unpack(tensor_type(e, tid), src, tmp, tensor_rows(e, tid), (int)tensor_cols(e, tid), e->stream));
+    CK(cudaMemcpyAsync(host_out, tmp, want, cudaMemcpyDeviceToHost, e->stream));
+    cudaFreeAsync(tmp, e->stream);
+  } else {
+    CK(cudaMemcpyAsync(host_out, src, want, cudaMemcpyDeviceToHost, e->stream));
+  }
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_weights_synth(sfk_engine* e, uint64_t seed) {
+  if (!e) return fail(SFK_ERR_INVALID_ARGUMENT, "null engine");
+  CK(cudaSetDevice(e->device));
+  size_t maxb = 0;
+  for (int tid = 0; tid <= SFK_T_FFN_DOWN_EXPS; ++tid) maxb = std::max(maxb, sfk_tensor_bytes(e, tid, 0));
+  uint8_t* tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, maxb, e->stream));
+  for (int tid = 0; tid <= SFK_T_FFN_DOWN_EXPS; ++tid) {
+    const int nl = layered(tid) ? e->hp.n_layer : 1;
+    for (int l = 0; l < nl; ++l) {
+      const int64_t rows = tensor_rows(e, tid), cols = tensor_cols(e, tid);
+      if (tid == SFK_T_OUTPUT_NORM || tid == SFK_T_ATTN_NORM || tid == SFK_T_FFN_NORM) {
+        CK(launch_fill_f32(reinterpret_cast<float*>(tensor_dst(e, tid, l)), 1.0f, cols, e->stream));
+        continue;
+      }
+      const int type = tensor_type(e, tid);
+      CK(launch_synth(type, tensor_seed(seed, tid, l), 0.02f, tmp, rows, (int)cols, e->stream));
+      sfk_status s = put_gguf_device(e, tid, l, tmp);
+      if (s) {
+        cudaFreeAsync(tmp, e->stream);
+        return s;
+      }
+    }
+  }
+  cudaFreeAsync(tmp, e->stream);
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_kv_reset(sfk_engine* e) {
+  if (!e) return fail(SFK_ERR_INVALID_ARGUMENT, "null engine");
+  CK(cudaSetDevice(e->device));
+  const size_t kv_elem = e->hp.kv_type == SFK_KV_F16 ? 2 : 4;
+  CK(cudaMemsetAsync(e->k_pool, 0, kv_elem * e->kv_layer_elems * e->hp.n_layer, e->stream));
+  CK(cudaMemsetAsync(e->v_pool, 0, kv_elem * e->kv_layer_elems * e->hp.n_layer, e->stream));
+  CK(cudaMemsetAsync(e->pos_state, 0, sizeof(int) * e->hp.max_batch, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  std::fill(e->seq_pos.begin(), e->seq_pos.end(), 0);
+  return SFK_OK;
+}
+
+static sfk_status run_step(sfk_engine* e, int b, bool greedy) {
+  cudaGraphExec_t g = nullptr;
+  sfk_status s = get_graph(e, b, greedy, &g);
+  if (s) return s;
+  CK(cudaGraphLaunch(g, e->stream));
+  e->steps += 1;
+  e->last_b = b;
+  return SFK_OK;
+}
+
+sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens, const int32_t* positions,
+                             float* logits_host, int32_t* argmax_out) {
+  if (!e || !tokens || !positions) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  if (n_seq < 1 || n_seq > e->hp.max_batch) return fail(SFK_ERR_INVALID_ARGUMENT, "n_seq %d", n_seq);
+  for (int t = 0; t < n_seq; ++t) {
+    if (positions[t] < 0 || positions[t] >= e->hp.n_ctx)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "position %d outside [0, n_ctx=%d)", positions[t], e->hp.n_ctx);
+    if (tokens[t] < 0 || tokens[t] >= e->hp.n_vocab)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "token %d outside the vocabulary", tokens[t]);
+  }
+  CK(cudaSetDevice(e->device));
+  memcpy(e->h_tok, tokens, sizeof(int) * n_seq);
+  memcpy(e->h_pos, positions, sizeof(int) * n_seq);
+  CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * n_seq, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->pos_in, e->h_pos, sizeof(int) * n_seq, cudaMemcpyHostToDevice, e->stream));
+  sfk_status s = run_step(e, n_seq, false);
+  if (s) return s;
+  if (logits_host)
+    CK(cudaMemcpyAsync(logits_host, e->logits, sizeof(float) * n_seq * e->hp.n_vocab, cudaMemcpyDeviceToHost,
+                       e->stream));
+  CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * n_seq, cudaMemcpyDeviceToHost, e->stream));
+  s = check_status_word(e->status, e->stream);
+  if (s) return s;
+  for (int t = 0; t < n_seq; ++t) {
+    e->seq_pos[t] = positions[t] + 1;
+    if (argmax_out) argmax_out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(e->h_keys[t] & 0xFFFFFFFFull));
+  }
+  return SFK_OK;
+}
+
+sfk_status sfk_forward(sfk_engine* e, int32_t token, int32_t pos, float* logits_host, int32_t* argmax_out) {
+  return sfk_forward_batch(e, 1, &token, &pos, logits_host, argmax_out);
+}
+
+sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int32_t* tokens_out) {
+  if (!e) return fail(SFK_ERR_INVALID_ARGUMENT, "null engine");
+  if (n_seq < 1 || n_seq > e->hp.max_batch || n_steps < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "n_seq / n_steps");
+  for (int t = 0; t < n_seq; ++t)
+    if (e->seq_pos[t] + n_steps > e->hp.n_ctx)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "sequence %d would exceed n_ctx", t);
+  CK(cudaSetDevice(e->device));
+  for (int i = 0; i < n_steps; ++i) {
+    sfk_status s = run_step(e, n_seq, true);
+    if (s) return s;
+    if (tokens_out) {
+      // token consumed by this step = previous argmax
+      CK(cudaMemcpyAsync(tokens_out + (int64_t)i * n_seq, e->tok_hist, sizeof(int) * n_seq, cudaMemcpyDeviceToHost,
+                         e->stream));
+    }
+  }
+  sfk_status s = check_status_word(e->status, e->stream);
+  if (s) return s;
+  for (int t = 0; t < n_seq; ++t) e->seq_pos[t] += n_steps;
+  return SFK_OK;
+}
+
+sfk_status sfk_hidden_get(sfk_engine* e, float* host_out, size_t n_floats) {
+  if (!e || !host_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t n = (size_t)std::max(1, e->last_b) * e->hp.n_embd;
+  if (n_floats < n) return fail(SFK_ERR_INVALID_ARGUMENT, "need %zu floats", n);
+  CK(cudaSetDevice(e->device));
+  CK(cudaMemcpyAsync(host_out, e->x, n * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_get_stats(const sfk_engine* e, sfk_stats* out) {
+  if (!e || !out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const sfk_hparams& hp = e->hp;
+  out->weight_bytes_hbm = e->weight_bytes;
+  out->kv_bytes_hbm = e->kv_bytes;
+  out->scratch_bytes_hbm = e->scratch_bytes;
+  out->steps = e->steps;
+  out->kernels_per_step = e->kernels_per_step;
+  const uint64_t d = hp.n_embd, F = hp.n_ff;
+  uint64_t per_layer = (uint64_t)dev_gguf_row_bytes(hp.type_attn, d) * e->nqkv +
+                       (uint64_t)dev_gguf_row_bytes(hp.type_attn, e->nq) * d + 4ull * d * hp.n_expert +
+                       (uint64_t)hp.n_expert_used * (2ull * dev_gguf_row_bytes(hp.type_ffn_gu, d) * F +
+                                                     (uint64_t)dev_gguf_row_bytes(hp.type_ffn_down, F) * d);
+  out->active_bytes_per_token = per_layer * hp.n_layer + (uint64_t)dev_gguf_row_bytes(hp.type_output, d) * hp.n_vocab;
+  return SFK_OK;
+}
+
+sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* ms_out, int32_t n_out) {
+  if (!e || !ms_out || n_out < K_NCLASS || iters < 1 || n_seq < 1 || n_seq > e->hp.max_batch)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "time_kernels arguments");
+  if (e->steps == 0) return fail(SFK_ERR_INVALID_ARGUMENT, "run a decode step first");
+  CK(cudaSetDevice(e->device));
+  cudaEvent_t a = nullptr, z = nullptr;
+  CK(cudaEventCreate(&a));
+  CK(cudaEventCreate(&z));
+  sfk_status s = SFK_OK;
+  for (int c = 0; c < K_NCLASS && !s; ++c) {
+    // greedy-mode embed would advance positions; time it in host-token mode
+    CK(cudaEventRecord(a, e->stream));
+    for (int i = 0; i < iters && !s; ++i) s = launch_one(e, c, i % e->hp.n_layer, n_seq, false, false);
+    CK(cudaEventRecord(z, e->stream));
+    CK(cudaEventSynchronize(z));
+    float ms = 0.0f;
+    CK(cudaEventElapsedTime(&ms, a, z));
+    ms_out[c] = ms / iters;
+  }
+  cudaEventDestroy(a);
+  cudaEventDestroy(z);
+  if (s) return s;
+  return check_status_word(e->status, e->stream);
+}
+
+// ---- operator-level -------------------------------------------------------
+int64_t sfk_dev_row_bytes(int t, int64_t K) {
+  if (!quant_ok(t) || K % 256) return 0;
+  return dev_row_bytes(t, (int)K);
+}
+
+sfk_status sfk_repack(int t, const void* src, void* dst, int64_t nrows, int64_t K, void* stream) {
+  if (!quant_ok(t) || K % 256 || !src || !dst) return fail(SFK_ERR_INVALID_ARGUMENT, "repack arguments");
+  CK(launch_repack(t, (const uint8_t*)src, (uint8_t*)dst, nrows, (int)K, (cudaStream_t)stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_unpack(int t, const void* src, void* dst, int64_t nrows, int64_t K, void* stream) {
+  if (!quant_ok(t) || K % 256 || !src || !dst) return fail(SFK_ERR_INVALID_ARGUMENT, "unpack arguments");
+  CK(launch_unpack(t, (const uint8_t*)src, (uint8_t*)dst, nrows, (int)K, (cudaStream_t)stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_dequantize(int t, const void* src, float* dst, int64_t n, void* stream) {
+  if (!src || !dst || n < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "dequantize arguments");
+  const int qk = (t == T_Q8_0) ? 32 : ((t == T_Q4_K || t == T_Q6_K) ? 256 : 1);
+  if (!(quant_ok(t) || t == T_F32 || t == T_F16) || n % qk) return fail(SFK_ERR_INVALID_ARGUMENT, "type / size");
+  if (n == 0) return SFK_OK;
+  CK(launch_dequant(t, (const uint8_t*)src, dst, n, (cudaStream_t)stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_quantize_act(int act_type, const float* x, int32_t b, int64_t K, void* out, void* stream) {
+  if (!x || !out || b < 0 || K % 256 || (act_type != T_Q8_K && act_type != T_Q8_0))
+    return fail(SFK_ERR_INVALID_ARGUMENT, "quantize_act arguments");
+  if (b == 0) return SFK_OK;
+  CK(launch_quant_act_gguf(act_type, x, b, (int)K, (uint8_t*)out, (cudaStream_t)stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_mul_mat(int t, const void* w, int64_t rows, int64_t K, const float* x, int32_t b, float* y,
+                       void* stream) {
+  if (!quant_ok(t) || K % 256 || !w || !x || !y || b < 1 || b > MAXB || rows < 1)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "mul_mat arguments");
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(16, 1, &sc);
+  if (s) return s;
+  StreamParams p{};
+  p.w0 = (const uint8_t*)w;
+  p.rowstride = dev_row_bytes(t, (int)K);
+  p.rows = (int)rows;
+  p.K = (int)K;
+  p.wtype = t;
+  p.nmat = 1;
+  p.act_type = act_for(t);
+  p.row_align = 1;
+  p.b = b; p.k = 1; p.n_pairs = b; p.n_vec = b;
+  p.pro = PRO_QUANT;
+  p.x = x;
+  p.epi = EPI_STORE;
+  p.y = y;
+  p.y_stride = rows;
+  p.status = sc->status;
+  int dev = 0, grid = 0;
+  CK(cudaGetDevice(&dev));
+  s = plan_stream(p, sm_count_of(dev), &grid);
+  if (s) return s;
+  CK(launch_stream(p, grid, (cudaStream_t)stream, false));
+  return check_status_word(sc->status, (cudaStream_t)stream);
+}
+
+sfk_status sfk_mul_mat_id(int t, const void* w, int32_t n_expert, int64_t rows, int64_t K, const float* x,
+                          int32_t x_per_pair, const int32_t* ids, int32_t b, int32_t k, float* y, void* stream) {
+  if (!quant_ok(t) || K % 256 || !w || !x || !ids || !y || b < 1 || b > MAXB || k < 1 || b * k > MAXP ||
+      n_expert < 1 || rows < 1)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "mul_mat_id arguments");
+  const size_t qbytes = (size_t)qact_bytes((int)K) * b * k;
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(qbytes, 1, &sc);
+  if (s) return s;
+  cudaStream_t st = (cudaStream_t)stream;
+  CK(launch_route_build(ids, nullptr, b, k, n_expert, sc->route, sc->status, st));
+  const int nvec = x_per_pair ? b * k : b;
+  CK(launch_quant_act(act_for(t), x, nvec, (int)K, (uint8_t*)sc->buf, st));
+  StreamParams p{};
+  p.w0 = (const uint8_t*)w;
+  p.rowstride = dev_row_bytes(t, (int)K);
+  p.expert_stride = rows * p.rowstride;
+  p.rows = (int)rows;
+  p.K = (int)K;
+  p.wtype = t;
+  p.nmat = 1;
+  p.act_type = act_for(t);
+  p.row_align = 1;
+  p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = nvec;
+  p.route = sc->route;
+  p.pro = PRO_LOAD;
+  p.qact = (const uint8_t*)sc->buf;
+  p.qact_stride = qact_bytes((int)K);
+  p.xq_by_pair = x_per_pair ? 1 : 0;
+  p.epi = EPI_STORE;
+  p.y = y;
+  p.y_stride = rows;
+  p.status = sc->status;
+  int dev = 0, grid = 0;
+  CK(cudaGetDevice(&dev));
+  s = plan_stream(p, sm_count_of(dev), &grid);
+  if (s) return s;
+  CK(launch_stream(p, grid, st, false));
+  return check_status_word(sc->status, st);
+}
+
+sfk_status sfk_moe_ffn(int type_gu, int type_down, const void* gate, const void* up, const void* down,
+                       int32_t n_expert, int64_t d, int64_t F, const float* x, const float* res, const int32_t* ids,
+                       const float* wts, int32_t b, int32_t k, float* out, void* stream) {
+  if (!quant_ok(type_gu) || !quant_ok(type_down) || d % 256 || F % 256 || !gate || !up || !down || !x || !ids ||
+      !wts || !out || b < 1 || b > MAXB || k < 1 || b * k > MAXP || n_expert < 1)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "moe_ffn arguments");
+  const size_t xq_b = (size_t)qact_bytes((int)d) * b;
+  const size_t h_b = sizeof(float) * (size_t)b * k * F;
+  const size_t hq_b = (size_t)qact_bytes((int)F) * b * k;
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(xq_b + h_b + hq_b + 256, (size_t)(F / 256), &sc);
+  if (s) return s;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* xq = (uint8_t*)sc->buf;
+  float* h = (float*)(xq + ((xq_b + 255) & ~(size_t)255));
+  uint8_t* hq = (uint8_t*)h + ((h_b + 255) & ~(size_t)255);
+  if ((size_t)(hq - (uint8_t*)sc->buf) + hq_b > sc->bytes) {
+    s = op_scratch((size_t)(hq - (uint8_t*)sc->buf) + hq_b, (size_t)(F / 256), &sc);
+    if (s) return s;
+    xq = (uint8_t*)sc->buf;
+    h = (float*)(xq + ((xq_b + 255) & ~(size_t)255));
+    hq = (uint8_t*)h + ((h_b + 255) & ~(size_t)255);
+  }
+  CK(launch_route_build(ids, wts, b, k, n_expert, sc->route, sc->status, st));
+  CK(launch_quant_act(act_for(type_gu), x, b, (int)d, xq, st));
+  int dev = 0, grid = 0;
+  CK(cudaGetDevice(&dev));
+  const int sms = sm_count_of(dev);
+  {
+    StreamParams p{};
+    p.w0 = (const uint8_t*)gate;
+    p.w1 = (const uint8_t*)up;
+    p.rowstride = dev_row_bytes(type_gu, (int)d);
+    p.expert_stride = F * p.rowstride;
+    p.rows = (int)F;
+    p.K = (int)d;
+    p.wtype = type_gu;
+    p.nmat = 2;
+    p.act_type = act_for(type_gu);
+    p.row_align = 1;
+    p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b;
+    p.route = sc->route;
+    p.pro = PRO_LOAD;
+    p.qact = xq;
+    p.qact_stride = qact_bytes((int)d);
+    p.epi = EPI_GATEUP;
+    p.h = h;
+    p.hq = hq;
+    p.grp_counter = sc->counters;
+    p.h_act_type = act_for(type_down);
+    p.status = sc->status;
+    s = plan_stream(p, sms, &grid);
+    if (s) return s;
+    CK(launch_stream(p, grid, st, false));
+  }
+  {
+    StreamParams p{};
+    p.w0 = (const uint8_t*)down;
+    p.rowstride = dev_row_bytes(type_down, (int)F);
+    p.expert_stride = d * p.rowstride;
+    p.rows = (int)d;
+    p.K = (int)F;
+    p.wtype = type_down;
+    p.nmat = 1;
+    p.act_type = act_for(type_down);
+    p.row_align = 1;
+    p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b * k;
+    p.route = sc->route;
+    p.pro = PRO_LOAD;
+    p.qact = hq;
+    p.qact_stride = qact_bytes((int)F);
+    p.xq_by_pair = 1;
+    p.epi = EPI_DOWN;
+    p.y = out;
+    p.res = res;
+    p.y_stride = d;
+    p.status = sc->status;
+    s = plan_stream(p, sms, &grid);
+    if (s) return s;
+    CK(launch_stream(p, grid, st, false));
+  }
+  return check_status_word(sc->status, st);
+}
+
+sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp, int32_t kv_type,
+                                 const int32_t* page_table, int32_t max_pages, const int32_t* positions, int32_t b,
+                                 int32_t n_head, int32_t n_head_kv, int32_t head_dim, float* out, void* stream) {
+  if (!q || !kp || !vp || !page_table || !positions || !out || b < 1 || b > MAXB || n_head_kv < 1 ||
+      n_head % n_head_kv || (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) ||
+      (kv_type != SFK_KV_F16 && kv_type != SFK_KV_F32))
+    return fail(SFK_ERR_INVALID_ARGUMENT, "attn_decode_paged arguments");
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  const int sms = sm_count_of(dev);
+  const int n_split = std::max(1, std::min(64, (2 * sms) / (n_head_kv * b)));
+  const size_t po = sizeof(float) * (size_t)b * n_head * n_split * head_dim;
+  const size_t pml = sizeof(float) * (size_t)b * n_head * n_split * 2;
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(po + pml + 256, (size_t)b * n_head_kv, &sc);
+  if (s) return s;
+  AttnParams a{};
+  a.q = q;
+  a.kv.k = const_cast<void*>(kp);
+  a.kv.v = const_cast<void*>(vp);
+  a.kv.page_table = page_table;
+  a.kv.max_pages = max_pages;
+  a.kv.n_head_kv = n_head_kv;
+  a.kv.head_dim = head_dim;
+  a.kv.f16 = kv_type == SFK_KV_F16 ? 1 : 0;
+  a.pos = positions;
+  a.b = b;
+  a.n_head = n_head;
+  a.n_split = n_split;
+  a.part_o = (float*)sc->buf;
+  a.part_ml = (float*)((uint8_t*)sc->buf + ((po + 255) & ~(size_t)255));
+  a.counter = sc->counters;
+  a.out = out;
+  a.status = sc->status;
+  CK(launch_attn(a, (cudaStream_t)stream, false));
+  return check_status_word(sc->status, (cudaStream_t)stream);
+}
+
+}  // extern "C"

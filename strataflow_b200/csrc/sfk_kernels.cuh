@@ -1,0 +1,160 @@
+// sfk_kernels.cuh -- kernel parameter blocks and launch entry points shared by
+// sfk_kernels.cu (device code) and sfk_api.cu (host orchestration).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace sfk {
+
+constexpr int MAXP = 128;  // max (token, expert) pairs per step  (b * k)
+constexpr int MAXB = 16;   // max tokens per step
+constexpr int NW = 8;      // consumer warps per streaming CTA
+constexpr int RING_BYTES = 96 * 1024;
+
+// Routing of one MoE step, written by the router kernel (device memory).
+// Pair p = t * k + j is token t's j-th routed expert.  Slots are the distinct
+// experts in use; each slot lists its pairs in ascending pair order.
+struct Route {
+  int n_slots;
+  int k;
+  int b;
+  int pad;
+  int slot_expert[MAXP];
+  int slot_off[MAXP + 1];
+  int slot_pairs[MAXP];
+  int ids[MAXP];
+  float w[MAXP];
+};
+
+enum Prologue : int {
+  PRO_QUANT = 0,  // x f32 [b][K] (+ optional RMSNorm * w) -> quantize to act type
+  PRO_LOAD = 1,   // copy precomputed qact vectors from global
+};
+enum Epilogue : int {
+  EPI_STORE = 0,    // y[pair][row] = dot            (mul_mat / mul_mat_id)
+  EPI_QKV = 1,      // RoPE, q -> qbuf, k/v -> paged KV cache
+  EPI_RESID = 2,    // y[t][row] = dot + res[t][row]
+  EPI_GATEUP = 3,   // h = silu(gate)*up -> h f32, Q8_K/Q8_0 quant per 256-row group
+  EPI_DOWN = 4,     // y[t][row] = sum_j w_tj * dot_tj + res[t][row]
+  EPI_LMHEAD = 5,   // logits (optional) + per-token argmax (atomicMax)
+};
+
+struct KvView {
+  void* k;               // [n_pages][Hkv][16][hd]  (f16 or f32)
+  void* v;
+  const int* page_table; // [b][max_pages]
+  int max_pages;
+  int n_head_kv;
+  int head_dim;
+  int f16;
+};
+
+struct StreamParams {
+  // weights (device layout)
+  const uint8_t* w0;
+  const uint8_t* w1;       // second matrix (up) when nmat == 2
+  int64_t rowstride;
+  int64_t expert_stride;   // bytes between experts of a stacked tensor
+  int rows;                // rows per matrix
+  int K;
+  int wtype;
+  int nmat;
+  int act_type;            // T_Q8_K or T_Q8_0
+  int row_align;           // CTA row ranges are multiples of this
+  int rows_per_cta;        // ceil(rows / grid), aligned
+  // tokens / routing
+  int b;
+  int k;                   // experts per token (1 for dense)
+  int n_pairs;             // accumulator pairs: b (dense) or b*k (routed)
+  int n_vec;               // activation vectors: b, or b*k when xq_by_pair
+  const Route* route;      // null: dense (one slot, pairs = tokens)
+  // prologue
+  int pro;
+  const float* x;          // PRO_QUANT input [b][K]
+  const float* norm_w;     // RMSNorm weight or null (no norm)
+  float eps;
+  const uint8_t* qact;     // PRO_LOAD source
+  int64_t qact_stride;     // bytes between qact vectors
+  int xq_by_pair;          // PRO_LOAD: vector index = pair (1) or token (0)
+  int xq_resident;         // all groups of all vectors fit in smem
+  // epilogue
+  int epi;
+  float* y;                // EPI_STORE / EPI_RESID / EPI_DOWN output; EPI_QKV q out
+  const float* res;        // residual [b][rows]
+  int64_t y_stride;        // floats between rows of y per vector (== rows)
+  // EPI_QKV
+  KvView kv;
+  int n_head;
+  float theta_scale;       // powf(freq_base, -2/head_dim), computed on the host
+  const int* pos;          // [b] positions
+  // EPI_GATEUP
+  float* h;                // [pairs][rows] f32
+  uint8_t* hq;             // [pairs] qact of h (K = rows)
+  int* grp_counter;        // [rows/256] counters, self-resetting
+  int h_act_type;          // act type of the down projection
+  // EPI_LMHEAD
+  unsigned long long* argmax_key;  // [b]
+  int store_logits;
+  int* status;
+};
+
+struct AttnParams {
+  const float* q;          // [b][Hq][hd]
+  KvView kv;
+  const int* pos;          // [b]; attends over 0..pos
+  int b, n_head, n_split;
+  float* part_o;           // [b][Hq][n_split][hd]
+  float* part_ml;          // [b][Hq][n_split][2]
+  int* counter;            // [b][Hkv], self-resetting
+  float* out;              // [b][Hq*hd]
+  int* status;
+};
+
+struct RouterParams {
+  const float* x;          // [b][d] ffn_inp
+  const float* norm_w;     // ffn_norm weight
+  const float* w_r;        // [E][d] f32 router
+  int b, d, E, k;
+  float eps;
+  int act_type;            // act quant type for gate/up weights
+  uint8_t* xq;             // [b] qact of ffn_norm(x)
+  float* xn;               // [b][d] ffn_norm(x) f32 (optional, may be null)
+  Route* route;
+  float* logits;           // [b][E] scratch
+  int* counter;            // self-resetting
+  int* status;
+};
+
+struct EmbedParams {
+  const uint8_t* tok_embd; // GGUF layout rows [V][d], type `type`
+  int type, d, V, b;
+  const int* tok_in;       // host-supplied tokens [b]
+  unsigned long long* argmax_key;  // [b]; greedy mode reads and resets it
+  int greedy;
+  int* tok_hist;           // [b] token consumed this step (out)
+  const int* pos_in;       // [b] host-supplied positions (or null: use pos_state)
+  int* pos_state;          // [b] persistent position counters (greedy loop)
+  int* pos_cur;            // [b] position of this step (out)
+  float* x;                // [b][d]
+  int* status;
+};
+
+// launch helpers (implemented in sfk_kernels.cu)
+int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp);
+cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
+cudaError_t launch_router(const RouterParams& p, cudaStream_t st, bool pdl);
+cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st, bool pdl);
+cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);
+cudaError_t launch_unpack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);
+cudaError_t launch_dequant(int type, const uint8_t* src, float* dst, int64_t n, cudaStream_t st);
+cudaError_t launch_synth(int type, uint64_t seed, float std_, uint8_t* dst_gguf, int64_t nrows, int K,
+                         cudaStream_t st);
+cudaError_t launch_synth_f32(uint64_t seed, float std_, float* dst, int64_t n, cudaStream_t st);
+cudaError_t launch_quant_act(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
+cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t st);
+cudaError_t launch_route_build(const int* ids, const float* w, int b, int k, int n_expert, Route* r, int* status,
+                               cudaStream_t st);
+cudaError_t launch_quant_act_gguf(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
+
+}  // namespace sfk

@@ -1,0 +1,210 @@
+"""Host-side mirror of StrataFlow's engine::Engine for the B200 decode path.
+
+Reference interface (Coaade-Inc/strataflow, src/model/engine/engine.h):
+  Engine::load(path, expert_slots, kv_window, trunk_pool_layers, backend)  :153
+  Engine::forward(token, pos, std::vector<float>& logits) -> bool          :241
+  Engine::reset_kv()                                                       :245
+  EngineHParams                                                             :41
+
+Here `Engine.load` takes the model shape (the GGUF hparams the reference reads
+at engine.cpp:1077-1087) and fills the HBM tier either from the seeded
+synthetic generator (on the device) or from GGUF tensor bytes; `forward`
+returns the logits (raising on failure where the reference returns false).
+All arithmetic runs in libsfk.so; this module only marshals arguments.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass, asdict
+
+import numpy as np
+
+from . import lib as L
+
+
+@dataclass
+class ModelConfig:
+    """Model shape (EngineHParams) plus the quant type of each weight class."""
+    n_embd: int
+    n_head: int
+    n_head_kv: int
+    n_layer: int
+    n_ff: int
+    n_expert: int
+    n_expert_used: int
+    n_vocab: int
+    n_ctx: int
+    rms_eps: float = 1e-5
+    freq_base: float = 10000.0
+    type_embd: int = L.TYPE_Q8_0
+    type_attn: int = L.TYPE_Q8_0
+    type_ffn_gu: int = L.TYPE_Q8_0
+    type_ffn_down: int = L.TYPE_Q8_0
+    type_output: int = L.TYPE_Q8_0
+    kv_type: int = L.KV_F32
+    max_batch: int = 1
+
+    @property
+    def head_dim(self) -> int:
+        return self.n_embd // self.n_head
+
+    def to_c(self) -> L.Hparams:
+        h = L.Hparams()
+        for name, _ in L.Hparams._fields_:
+            setattr(h, name, getattr(self, name))
+        return h
+
+    def replace(self, **kw) -> "ModelConfig":
+        d = asdict(self)
+        d.update(kw)
+        return ModelConfig(**d)
+
+
+# The BASELINE.json configurations (shapes only; weights are seeded synthetic).
+def tiny_config(**kw) -> ModelConfig:
+    """4 layers, d 256, 8q/4kv heads (hd 32), 8 experts top-2,
+    FFN 512, vocab 4096, Q8_0 weights, RoPE base 1e4, context 80."""
+    c = ModelConfig(n_embd=256, n_head=8, n_head_kv=4, n_layer=4, n_ff=512, n_expert=8, n_expert_used=2,
+                    n_vocab=4096, n_ctx=80, rms_eps=1e-5, freq_base=10000.0)
+    return c.replace(**kw)
+
+
+def mixtral_config(**kw) -> ModelConfig:
+    """Mixtral-8x7B shape -- 32 layers, d 4096, 32q/8kv heads
+    (hd 128), 8 experts top-2, FFN 14336, vocab 32000, RoPE base 1e6; experts
+    Q4_K, attention / embedding / output Q6_K, router F32."""
+    c = ModelConfig(n_embd=4096, n_head=32, n_head_kv=8, n_layer=32, n_ff=14336, n_expert=8, n_expert_used=2,
+                    n_vocab=32000, n_ctx=1024, rms_eps=1e-5, freq_base=1e6, type_embd=L.TYPE_Q6_K,
+                    type_attn=L.TYPE_Q6_K, type_ffn_gu=L.TYPE_Q4_K, type_ffn_down=L.TYPE_Q4_K,
+                    type_output=L.TYPE_Q6_K, kv_type=L.KV_F16)
+    return c.replace(**kw)
+
+
+class Engine:
+    """One model resident in HBM plus its paged KV cache (max_batch sequences)."""
+
+    def __init__(self, cfg: ModelConfig, device: int = 0):
+        self.cfg = cfg
+        self._lib = L.load()
+        self._hp = cfg.to_c()
+        h = C.c_void_p()
+        L.check(self._lib.sfk_engine_create(device, C.byref(self._hp), C.byref(h)))
+        self.h = h
+
+    @classmethod
+    def load(cls, cfg: ModelConfig, seed: int | None = None, tensors=None, device: int = 0) -> "Engine":
+        """Create the engine and fill its HBM tier: from the seeded generator
+        (`seed`) or from an iterable of (tensor_id, layer, ggml_type, ne,
+        bytes) in GGUF layout (`tensors`)."""
+        eng = cls(cfg, device)
+        if seed is not None:
+            L.check(eng._lib.sfk_weights_synth(eng.h, C.c_uint64(seed)))
+        if tensors is not None:
+            for tid, layer, qtype, ne, data in tensors:
+                eng.put(tid, layer, qtype, ne, data)
+        return eng
+
+    def close(self):
+        if getattr(self, "h", None):
+            self._lib.sfk_engine_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def stream(self) -> int:
+        """cudaStream_t (as an int) every call of this engine is ordered on."""
+        return int(self._lib.sfk_engine_stream(self.h) or 0)
+
+    def time_kernels(self, n_seq: int = 1, iters: int = 32) -> dict:
+        """Average device ms of each kernel class of one step (sfk_time_kernels)."""
+        ms = (C.c_float * 8)()
+        L.check(self._lib.sfk_time_kernels(self.h, n_seq, iters, ms, 8))
+        names = ["embed", "qkv", "attention", "o_proj", "router", "gate_up", "down", "lm_head"]
+        return {n: float(v) for n, v in zip(names, ms)}
+
+    # -- weights -----------------------------------------------------------
+    def tensor_bytes(self, tid: int, layer: int = 0) -> int:
+        return int(self._lib.sfk_tensor_bytes(self.h, tid, layer))
+
+    def put(self, tid: int, layer: int, qtype: int, ne, data: np.ndarray) -> None:
+        data = np.ascontiguousarray(data).view(np.uint8)
+        ne_c = (C.c_int64 * 3)(*(list(ne) + [1, 1, 1])[:3])
+        L.check(self._lib.sfk_weights_put(self.h, tid, layer, qtype, ne_c, data.ctypes.data_as(C.c_void_p),
+                                          data.nbytes))
+
+    def put_expert(self, layer: int, expert: int, bundle: np.ndarray) -> None:
+        bundle = np.ascontiguousarray(bundle).view(np.uint8)
+        L.check(self._lib.sfk_expert_put(self.h, layer, expert, bundle.ctypes.data_as(C.c_void_p), bundle.nbytes))
+
+    def get(self, tid: int, layer: int = 0) -> np.ndarray:
+        n = self.tensor_bytes(tid, layer)
+        out = np.empty(n, np.uint8)
+        L.check(self._lib.sfk_weights_get(self.h, tid, layer, out.ctypes.data_as(C.c_void_p), n))
+        return out
+
+    # -- decode --------------------------------------------------------------
+    def reset_kv(self) -> None:
+        L.check(self._lib.sfk_kv_reset(self.h))
+
+    def forward(self, token: int, pos: int, want_logits: bool = True):
+        """Engine::forward: one token at `pos`; returns (argmax, logits)."""
+        logits = np.empty(self.cfg.n_vocab, np.float32) if want_logits else None
+        am = C.c_int32()
+        L.check(self._lib.sfk_forward(self.h, int(token), int(pos),
+                                      logits.ctypes.data_as(C.c_void_p) if want_logits else None, C.byref(am)))
+        return am.value, logits
+
+    def forward_batch(self, tokens, positions, want_logits: bool = True):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        positions = np.ascontiguousarray(positions, np.int32)
+        n = tokens.size
+        logits = np.empty((n, self.cfg.n_vocab), np.float32) if want_logits else None
+        am = np.empty(n, np.int32)
+        L.check(self._lib.sfk_forward_batch(self.h, n, tokens.ctypes.data_as(C.c_void_p),
+                                            positions.ctypes.data_as(C.c_void_p),
+                                            logits.ctypes.data_as(C.c_void_p) if want_logits else None,
+                                            am.ctypes.data_as(C.c_void_p)))
+        return am, logits
+
+    def decode_greedy(self, n_steps: int, n_seq: int = 1, want_tokens: bool = True):
+        """Greedy loop on the device; returns the tokens fed at each step
+        ([n_steps][n_seq]); the first is the argmax of the previous step."""
+        out = np.empty((n_steps, n_seq), np.int32) if want_tokens else None
+        L.check(self._lib.sfk_decode_greedy(self.h, n_seq, n_steps,
+                                            out.ctypes.data_as(C.c_void_p) if want_tokens else None))
+        return out
+
+    def hidden(self, n_seq: int = 1) -> np.ndarray:
+        out = np.empty((n_seq, self.cfg.n_embd), np.float32)
+        L.check(self._lib.sfk_hidden_get(self.h, out.ctypes.data_as(C.c_void_p), out.size))
+        return out
+
+    def stats(self) -> dict:
+        s = L.Stats()
+        L.check(self._lib.sfk_get_stats(self.h, C.byref(s)))
+        return {n: int(getattr(s, n)) for n, _ in L.Stats._fields_}
+
+    def generate(self, prompt, n_gen: int, host_loop: bool = False):
+        """The reference drive pattern (tests/test_engine_oracle.cpp:182-207):
+        prompt tokens one position at a time, then n_gen greedy tokens.
+        Returns (generated tokens, logits of each step when host_loop)."""
+        pos = 0
+        am = None
+        logits_all = []
+        last = None
+        for t in prompt:
+            am, last = self.forward(t, pos, want_logits=host_loop)
+            pos += 1
+        if host_loop:
+            logits_all.append(last)
+            out = []
+            for _ in range(n_gen):
+                out.append(am)
+                am, last = self.forward(am, pos)
+                logits_all.append(last)
+                pos += 1
+            return out, logits_all
+        toks = self.decode_greedy(n_gen, 1)[:, 0].tolist()
+        return toks, None

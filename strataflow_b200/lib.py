@@ -1,0 +1,101 @@
+"""ctypes binding of libsfk.so (include/sfk.h).
+
+The library is required: importing the engine or an op on a machine where the
+shared object is missing raises immediately.  There is no fallback path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import re
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "_lib", "libsfk.so")
+HEADER = os.path.join(os.path.dirname(HERE), "include", "sfk.h")
+
+SFK_OK = 0
+TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = 0, 1, 8, 12, 14, 15
+KV_F32, KV_F16 = 0, 1
+(T_TOK_EMBD, T_OUTPUT_NORM, T_OUTPUT, T_ATTN_NORM, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUT,
+ T_FFN_NORM, T_FFN_GATE_INP, T_FFN_GATE_EXPS, T_FFN_UP_EXPS, T_FFN_DOWN_EXPS) = range(13)
+LAYERED = set(range(T_ATTN_NORM, 13))
+
+
+class SfkError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"sfk status {status}: {msg}")
+        self.status = status
+
+
+class Hparams(C.Structure):
+    _fields_ = [(n, C.c_int32) for n in (
+        "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
+        ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
+            "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_type", "max_batch")]
+
+
+class Stats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in (
+        "weight_bytes_hbm", "kv_bytes_hbm", "scratch_bytes_hbm", "steps", "kernels_per_step",
+        "active_bytes_per_token")]
+
+
+P, I32, I64, U64, SZ, F = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
+_SIGS = {
+    "sfk_last_error": (C.c_char_p, []),
+    "sfk_status_str": (C.c_char_p, [I32]),
+    "sfk_engine_create": (I32, [C.c_int, C.POINTER(Hparams), C.POINTER(P)]),
+    "sfk_engine_free": (None, [P]),
+    "sfk_engine_stream": (P, [P]),
+    "sfk_weights_put": (I32, [P, C.c_int, C.c_int, C.c_int, P, P, SZ]),
+    "sfk_expert_put": (I32, [P, C.c_int, C.c_int, P, SZ]),
+    "sfk_weights_get": (I32, [P, C.c_int, C.c_int, P, SZ]),
+    "sfk_weights_synth": (I32, [P, U64]),
+    "sfk_tensor_bytes": (SZ, [P, C.c_int, C.c_int]),
+    "sfk_kv_reset": (I32, [P]),
+    "sfk_forward": (I32, [P, I32, I32, P, P]),
+    "sfk_forward_batch": (I32, [P, I32, P, P, P, P]),
+    "sfk_decode_greedy": (I32, [P, I32, I32, P]),
+    "sfk_hidden_get": (I32, [P, P, SZ]),
+    "sfk_get_stats": (I32, [P, C.POINTER(Stats)]),
+    "sfk_time_kernels": (I32, [P, I32, I32, P, I32]),
+    "sfk_dev_row_bytes": (I64, [C.c_int, I64]),
+    "sfk_repack": (I32, [C.c_int, P, P, I64, I64, P]),
+    "sfk_unpack": (I32, [C.c_int, P, P, I64, I64, P]),
+    "sfk_dequantize": (I32, [C.c_int, P, P, I64, P]),
+    "sfk_quantize_act": (I32, [C.c_int, P, I32, I64, P, P]),
+    "sfk_mul_mat": (I32, [C.c_int, P, I64, I64, P, I32, P, P]),
+    "sfk_mul_mat_id": (I32, [C.c_int, P, I32, I64, I64, P, I32, P, I32, I32, P, P]),
+    "sfk_moe_ffn": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
+    "sfk_attn_decode_paged": (I32, [P, P, P, I32, P, I32, P, I32, I32, I32, I32, P, P]),
+}
+
+_lib = None
+
+
+def header_functions() -> list[str]:
+    """Function names declared in include/sfk.h."""
+    txt = open(HEADER).read()
+    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
+    return sorted(set(re.findall(r"\b(sfk_[a-z0-9_]+)\s*\(", txt)))
+
+
+def load() -> C.CDLL:
+    """Load libsfk.so; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run `python -m strataflow_b200.build` "
+                              "(the CUDA extension is required; there is no CPU fallback)")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int) -> None:
+    if status != SFK_OK:
+        raise SfkError(status, load().sfk_last_error().decode())

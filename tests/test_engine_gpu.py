@@ -1,0 +1,186 @@
+"""GPU parity of the whole decode step (engine::Engine::forward) against the
+CPU oracle, driven the way the reference's own oracle test drives libllama
+(tests/test_engine_oracle.cpp:145-236: prompt one token per position, then
+greedy tokens): identical greedy sequences, logits within 1e-3 relative L2 and
+1e-2 max-abs (the reference's own engine-vs-libllama
+gate is 1e-3 max-abs for F32, 2e-2 for Q8_0, test_engine_oracle.cpp:136,539).
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+REL_L2, MAX_ABS = 1e-3, 1e-2
+
+
+def _oracle_cfg(cfg, **kw):
+    d = {k: getattr(cfg, k) for k in ("n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used",
+                                      "n_vocab", "n_ctx", "rms_eps", "freq_base", "type_embd", "type_attn",
+                                      "type_ffn_gu", "type_ffn_down", "type_output")}
+    d["kv_f16"] = cfg.kv_type == 1
+    d.update(kw)
+    return O.ModelConfig(**d)
+
+
+def _close(a, b):
+    rel = float(np.linalg.norm(a - b) / np.linalg.norm(b))
+    mx = float(np.abs(a - b).max())
+    return rel < REL_L2 and mx < MAX_ABS, rel, mx
+
+
+def _run_parity(cfg, seed, prompt, n_gen, oracle_model=None):
+    from strataflow_b200 import engine as E
+    eng = E.Engine.load(cfg, seed=seed)
+    om = oracle_model or O.Model(_oracle_cfg(cfg), seed=seed)
+    ref_toks, ref_logits = O.greedy(om, prompt, n_gen, want_logits=True)
+    toks, logits = eng.generate(prompt, n_gen, host_loop=True)
+    worst = (0.0, 0.0)
+    for i, (a, b) in enumerate(zip(logits, ref_logits)):
+        ok, rel, mx = _close(a, b)
+        worst = (max(worst[0], rel), max(worst[1], mx))
+        assert ok, (i, rel, mx)
+    assert toks == ref_toks
+    return eng, om, toks, worst
+
+
+def test_synth_weights_bit_identical_to_oracle(cuda):
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=2, type_ffn_gu=12, type_ffn_down=12, type_attn=14, type_output=14, type_embd=14)
+    eng = E.Engine.load(cfg, seed=3)
+    om = O.Model(_oracle_cfg(cfg), seed=3)
+    for tid, layer in om.tensors():
+        got = eng.get(tid, layer)
+        ref, _, _ = om.tensor(tid, layer)
+        assert np.array_equal(got, ref), (tid, layer)
+
+
+def test_weights_put_get_roundtrip(cuda):
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=1)
+    om = O.Model(_oracle_cfg(cfg), seed=9)
+    tensors = []
+    for tid, l in om.tensors():
+        data, qtype, ne = om.tensor(tid, l)
+        tensors.append((tid, l, qtype, ne, data))
+    eng = E.Engine.load(cfg, tensors=tensors)
+    for tid, l in om.tensors():
+        assert np.array_equal(eng.get(tid, l), om.tensor(tid, l)[0])
+
+
+def test_expert_bundle_put(cuda):
+    """A .strata expert bundle (gate|up|down, strata_format.h:122-130) lands in
+    the stacked tensors at that expert's slice."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=1)
+    eng = E.Engine.load(cfg, seed=1)
+    om = O.Model(_oracle_cfg(cfg), seed=2)
+    g, _, _ = om.tensor(O.T_FFN_GATE_EXPS, 0)
+    u, _, _ = om.tensor(O.T_FFN_UP_EXPS, 0)
+    dn, _, _ = om.tensor(O.T_FFN_DOWN_EXPS, 0)
+    E_ = cfg.n_expert
+    gl, dl = g.size // E_, dn.size // E_
+    e = 5
+    eng.put_expert(0, e, np.concatenate([g[e * gl:(e + 1) * gl], u[e * gl:(e + 1) * gl], dn[e * dl:(e + 1) * dl]]))
+    assert np.array_equal(eng.get(O.T_FFN_GATE_EXPS, 0)[e * gl:(e + 1) * gl], g[e * gl:(e + 1) * gl])
+    assert np.array_equal(eng.get(O.T_FFN_DOWN_EXPS, 0)[e * dl:(e + 1) * dl], dn[e * dl:(e + 1) * dl])
+
+
+def test_tiny_q8_0_greedy_parity(cuda):
+    """16-token prompt (seed 1), 64 greedy tokens, context 80."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config()
+    prompt = np.random.default_rng(1).integers(0, cfg.n_vocab, 16).tolist()
+    eng, om, toks, worst = _run_parity(cfg, 0, prompt, 64)
+    assert len(toks) == 64
+
+
+def test_tiny_kquant_greedy_parity(cuda):
+    """K-quant variant (the reference's make_kquant_moe_gguf shape family):
+    Q4_K experts, Q6_K attention / embedding / output."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(type_ffn_gu=12, type_ffn_down=12, type_attn=14, type_output=14, type_embd=14)
+    prompt = np.random.default_rng(2).integers(0, cfg.n_vocab, 12).tolist()
+    _run_parity(cfg, 7, prompt, 24)
+
+
+def test_tiny_f16_kv_greedy_parity(cuda):
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(kv_type=1)
+    prompt = np.random.default_rng(3).integers(0, cfg.n_vocab, 10).tolist()
+    _run_parity(cfg, 4, prompt, 20)
+
+
+def test_device_greedy_loop_matches_host_loop(cuda):
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config()
+    eng = E.Engine.load(cfg, seed=0)
+    prompt = np.random.default_rng(1).integers(0, cfg.n_vocab, 16).tolist()
+    host, _ = eng.generate(prompt, 32, host_loop=True)
+    eng.reset_kv()
+    dev, _ = eng.generate(prompt, 32, host_loop=False)
+    assert dev == host
+
+
+def test_batched_step_equals_single_sequences(cuda):
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(max_batch=4, n_layer=2)
+    eng = E.Engine.load(cfg, seed=5)
+    rng = np.random.default_rng(6)
+    prompts = [rng.integers(0, cfg.n_vocab, 6).tolist() for _ in range(3)]
+    # batched: 3 sequences stepped together
+    for p in range(6):
+        am_b, lg_b = eng.forward_batch([pr[p] for pr in prompts], [p, p, p])
+    # single: each sequence alone on a fresh engine
+    for s in range(3):
+        e1 = E.Engine.load(cfg, seed=5)
+        for p in range(6):
+            am1, lg1 = e1.forward(prompts[s][p], p)
+        assert am1 == am_b[s]
+        assert np.abs(lg1 - lg_b[s]).max() <= 1e-6 * np.abs(lg1).max()
+    # and the device greedy loop over the batch continues every sequence
+    toks = eng.decode_greedy(5, 3)
+    assert toks.shape == (5, 3) and (toks[0] == am_b).all()
+
+
+def test_mixtral_width_two_layer_parity(cuda):
+    """Mid-size model: every Mixtral-8x7B width (d 4096, 32q/8kv x 128,
+    8 experts top-2, FFN 14336, vocab 32000, RoPE 1e6, Q4_K experts, Q6_K
+    trunk, f16 KV) with 2 layers, 8-token prompt + 8 greedy tokens."""
+    from strataflow_b200 import engine as E
+    cfg = E.mixtral_config(n_layer=2, n_ctx=64)
+    prompt = np.random.default_rng(4).integers(0, cfg.n_vocab, 8).tolist()
+    eng, om, toks, worst = _run_parity(cfg, 4, prompt, 8)
+    # spot-check generator equality at full width too
+    for tid, layer in [(O.T_ATTN_Q, 1), (O.T_FFN_DOWN_EXPS, 0), (O.T_OUTPUT, 0)]:
+        assert np.array_equal(eng.get(tid, layer), om.tensor(tid, layer)[0])
+
+
+def test_forward_rejects_out_of_range_inputs(cuda):
+    from strataflow_b200 import engine as E
+    from strataflow_b200 import lib as L
+    cfg = E.tiny_config(n_layer=1, n_ctx=16)
+    eng = E.Engine.load(cfg, seed=0)
+    with pytest.raises(L.SfkError):
+        eng.forward(cfg.n_vocab, 0)
+    with pytest.raises(L.SfkError):
+        eng.forward(1, cfg.n_ctx)
+    eng.forward(1, 0)
+    with pytest.raises(L.SfkError):
+        eng.decode_greedy(cfg.n_ctx, 1)   # would run past n_ctx
+    am, _ = eng.forward(2, 1)             # the engine still works afterwards
+    assert 0 <= am < cfg.n_vocab
+
+
+def test_kernel_timing_entry_point(cuda):
+    from strataflow_b200 import engine as E
+    import ctypes as C
+    cfg = E.tiny_config(n_layer=2)
+    eng = E.Engine.load(cfg, seed=0)
+    eng.forward(3, 0)
+    ms = (C.c_float * 8)()
+    from strataflow_b200 import lib as L
+    L.check(eng._lib.sfk_time_kernels(eng.h, 1, 4, ms, 8))
+    assert all(v > 0 for v in ms)
+    assert eng.stats()["kernels_per_step"] == 2 + 6 * cfg.n_layer

@@ -1,0 +1,179 @@
+"""CPU tests: the oracle pinned against the golden vectors (gguf-py 0.19.0, a
+numpy restatement of ggml's reference kernels) and checked for the properties
+the reference's ggml arithmetic has.  No GPU."""
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden.npz")
+
+
+@pytest.fixture(scope="module")
+def gold():
+    return np.load(GOLD)
+
+
+def _bits_equal(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    same = (a.view(np.uint32) == b.view(np.uint32)) | (np.isnan(a) & np.isnan(b))
+    return bool(same.all()), int((~same).sum())
+
+
+@pytest.mark.parametrize("name,qtype", [("q4_k", O.Q4_K), ("q6_k", O.Q6_K), ("q8_0", O.Q8_0)])
+def test_dequant_matches_golden_bit_exact(gold, name, qtype):
+    blocks = gold[name + "_blocks"]
+    exp = gold[name + "_deq"]
+    got = O.dequantize(qtype, blocks.reshape(-1), exp.size)
+    ok, n = _bits_equal(got, exp)
+    assert ok, f"{n} mismatching values"
+
+
+def test_q8_0_quantizer_matches_golden(gold):
+    q = O.quantize_q8_0(gold["q8_0_x"])
+    assert np.array_equal(q, gold["q8_0_q"])
+
+
+def test_fp16_conversion_all_halves_roundtrip():
+    L = O.lib()
+    h = np.arange(65536, dtype=np.uint16)
+    back = np.array([L.sfo_fp16_to_fp32(int(i)) for i in h[::7]], np.float32)
+    ref = h[::7].view(np.float16).astype(np.float32)
+    ok, n = _bits_equal(back, ref)
+    assert ok, n
+
+
+def test_fp16_rounding_matches_numpy():
+    rng = np.random.default_rng(5)
+    x = np.concatenate([rng.standard_normal(4000).astype(np.float32) * s for s in (1e-7, 3e-5, 1e-2, 1, 3e4)])
+    x = np.concatenate([x, np.float32([0.0, -0.0, 65504, 65519.99, 65520, 2.98e-8, 2.9802322e-08, 6.1e-5])])
+    L = O.lib()
+    ours = np.array([L.sfo_fp32_to_fp16(float(v)) for v in x], np.uint16)
+    with np.errstate(over="ignore"):
+        ref = x.astype(np.float16).view(np.uint16)
+    assert np.array_equal(ours, ref)
+
+
+def _q8k_unpack(buf, K):
+    nb = K // 256
+    b = buf.reshape(nb, 292)
+    d = b[:, :4].copy().view(np.float32).ravel()
+    qs = b[:, 4:260].copy().view(np.int8).astype(np.int32)
+    bs = b[:, 260:292].copy().view(np.int16).astype(np.int32)
+    return d, qs, bs
+
+
+def test_q8_K_quantizer_properties():
+    rng = np.random.default_rng(7)
+    K = 1024
+    x = rng.standard_normal(K).astype(np.float32)
+    x[256:512] = 0.0  # an all-zero block -> d = 0, codes 0
+    x[600] = -9.0     # the signed max of block 2 is negative
+    x[601] = 9.0      # tie in |x|: the first index wins
+    d, qs, bs = _q8k_unpack(O.quantize_q8_K(x), K)
+    assert d[1] == 0.0 and (qs[1] == 0).all()
+    assert np.allclose(d[2], 1.0 / (-127.0 / -9.0))
+    assert qs[2][600 - 512] == -127 and qs[2][601 - 512] == 127 and d[2] > 0
+    assert (bs == qs.reshape(-1, 16, 16).sum(-1)).all()
+    # reconstruction within half a step
+    rec = (d[:, None] * qs).ravel()
+    assert (np.abs(rec - x) <= np.repeat(np.abs(d), 256) * 0.5 + 1e-6).all()
+
+
+@pytest.mark.parametrize("qtype,tol", [(O.Q4_K, 0.15), (O.Q6_K, 0.035), (O.Q8_0, 0.01)])
+def test_weight_quantizer_roundtrip(qtype, tol):
+    x = O.synth_f32(123, 0, 64 * 512).reshape(64, 512)
+    q = O.quantize_weights(qtype, x)
+    r = O.dequantize(qtype, q, x.size).reshape(x.shape)
+    rel = np.linalg.norm(r - x) / np.linalg.norm(x)
+    assert rel < tol, rel
+
+
+def test_synth_is_deterministic_and_normal_like():
+    a = O.synth_f32(42, 0, 200000)
+    b = O.synth_f32(42, 0, 200000)
+    assert np.array_equal(a, b)
+    c = O.synth_f32(42, 1000, 1000)
+    assert np.array_equal(c, a[1000:2000])
+    assert abs(a.mean()) < 2e-4 and abs(a.std() - 0.02) < 2e-4
+    assert O.tensor_seed(0, 4, 1) != O.tensor_seed(0, 4, 2)
+
+
+@pytest.mark.parametrize("qtype", [O.Q4_K, O.Q6_K, O.Q8_0])
+def test_mul_mat_integer_path_equals_dequantized_dot(qtype):
+    """ggml-exact mul_mat == dot(dequant(W), dequant(quant(x))) up to fp32 rounding."""
+    rng = np.random.default_rng(3)
+    rows, K = 48, 1024
+    w = O.quantize_weights(qtype, (rng.standard_normal((rows, K)) * 0.02).astype(np.float32))
+    x = rng.standard_normal(K).astype(np.float32)
+    y = O.mul_mat(qtype, w, rows, K, x)
+    wd = O.dequantize(qtype, w, rows * K).reshape(rows, K).astype(np.float64)
+    if qtype == O.Q8_0:
+        xd = O.dequantize(O.Q8_0, O.quantize_q8_0(x), K).astype(np.float64)
+    else:
+        xd = O.dequantize(O.Q8_K, O.quantize_q8_K(x), K).astype(np.float64)
+    ref = wd @ xd
+    assert np.abs(y - ref).max() <= 2e-5 * np.abs(ref).max()
+
+
+def test_rope_normal_matches_closed_form():
+    hd, H, pos, base = 32, 3, 17, 10000.0
+    x = np.random.default_rng(1).standard_normal(H * hd).astype(np.float32)
+    y = O.rope_normal(x, H, hd, pos, base)
+    i = np.arange(hd // 2)
+    th = pos * base ** (-2.0 * i / hd)
+    x2 = x.reshape(H, hd // 2, 2).astype(np.float64)
+    ref = np.stack([x2[..., 0] * np.cos(th) - x2[..., 1] * np.sin(th),
+                    x2[..., 0] * np.sin(th) + x2[..., 1] * np.cos(th)], -1).reshape(-1)
+    assert np.abs(y - ref).max() < 1e-5
+
+
+def test_router_topk_ties_and_clamp():
+    d, E, k = 256, 8, 2
+    w = np.zeros((E, d), np.float32)  # all logits equal -> uniform probs, ties
+    ids, wts, probs = O.router(w, np.ones(d, np.float32), k)
+    assert ids.tolist() == [0, 1]      # lower index wins ties
+    assert np.allclose(wts, 0.5)
+    assert np.allclose(probs, 1.0 / E)
+
+
+def test_attention_matches_float64():
+    rng = np.random.default_rng(11)
+    Hq, Hkv, hd, n = 8, 2, 32, 37
+    q = rng.standard_normal(Hq * hd).astype(np.float32)
+    k = rng.standard_normal((n, Hkv, hd)).astype(np.float32)
+    v = rng.standard_normal((n, Hkv, hd)).astype(np.float32)
+    out = O.attn_decode(q, k, v, Hq, Hkv, hd)
+    qh = q.reshape(Hq, hd).astype(np.float64)
+    ref = np.zeros((Hq, hd))
+    for h in range(Hq):
+        s = k[:, h // (Hq // Hkv)].astype(np.float64) @ qh[h] / np.sqrt(hd)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        ref[h] = p @ v[:, h // (Hq // Hkv)]
+    assert np.abs(out.reshape(Hq, hd) - ref).max() < 1e-5
+
+
+def test_tiny_model_greedy_is_deterministic():
+    cfg = O.ModelConfig(n_embd=256, n_head=8, n_head_kv=4, n_layer=4, n_ff=512, n_expert=8, n_expert_used=2,
+                        n_vocab=4096, n_ctx=80)
+    m = O.Model(cfg, seed=0)
+    prompt = np.random.default_rng(1).integers(0, 4096, 16).tolist()
+    a, la = O.greedy(m, prompt, 8, want_logits=True)
+    b, lb = O.greedy(m, prompt, 8, want_logits=True)
+    assert a == b and all(np.array_equal(x, y) for x, y in zip(la, lb))
+    assert len(set(a)) >= 1 and np.isfinite(la[-1]).all()
+
+
+def test_forward_rejects_bad_inputs():
+    cfg = O.ModelConfig(n_embd=256, n_head=8, n_head_kv=4, n_layer=1, n_ff=256, n_expert=4, n_expert_used=2,
+                        n_vocab=64, n_ctx=4)
+    m = O.Model(cfg, seed=0)
+    s = m.new_seq()
+    with pytest.raises(ValueError):
+        s.forward(64, 0)
+    with pytest.raises(ValueError):
+        s.forward(1, 4)
