@@ -143,6 +143,15 @@ SFK_API sfk_status sfk_forward_batch(sfk_engine *eng, int32_t n_seq, const int32
  * host round trip; tokens_out: [n_steps][n_seq] (host). */
 SFK_API sfk_status sfk_decode_greedy(sfk_engine *eng, int32_t n_seq, int32_t n_steps, int32_t *tokens_out);
 
+/* Routing of the last layer of the last step: ids [n_seq][k] and weights
+ * [n_seq][k] (host) -- the router segment's read-back (engine.cpp:2823-2833). */
+SFK_API sfk_status sfk_route_get(sfk_engine *eng, int32_t *ids_out, float *w_out, size_t n);
+
+/* Step buffers of the last layer of the last step, for inspection:
+ * which = 0 attention output [n_seq][Hq*hd], 1 ffn_inp [n_seq][d],
+ * 2 q after RoPE [n_seq][Hq*hd], 3 SwiGLU activation [n_seq*k][n_ff]. */
+SFK_API sfk_status sfk_debug_get(sfk_engine *eng, int32_t which, float *host_out, size_t n_floats);
+
 /* Hidden state after the last step, [n_seq][n_embd] (host). */
 SFK_API sfk_status sfk_hidden_get(sfk_engine *eng, float *host_out, size_t n_floats);
 

@@ -85,6 +85,8 @@ def lib():
             "sfo_tensor_seed": (U64, [U64, I, I]),
             "sfo_set_threads": (None, [I]),
             "sfo_seq_timing": (None, [P, P, P]),
+            "sfo_seq_debug": (P, [P, I, I]),
+            "sfo_expf": (F, [F]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -138,7 +140,11 @@ def synth_f32(seed: int, offset: int, n: int, std: float = 0.02) -> np.ndarray:
     return out
 
 
-def mul_mat(qtype: int, w: np.ndarray, nrows: int, ncols: int, x: np.ndarray, fp32_mode=False) -> np.ndarray:
+def expf(x: float) -> float:
+    return float(lib().sfo_expf(float(x)))
+
+
+def mul_mat(qtype: int, w: np.ndarray, nrows: int, ncols: int, x: np.ndarray, fp32_mode=0) -> np.ndarray:
     w = np.ascontiguousarray(w)
     x = np.ascontiguousarray(x, dtype=np.float32)
     y = np.empty(nrows, np.float32)
@@ -296,6 +302,11 @@ class Seq:
         a, b = C.c_double(), C.c_double()
         lib().sfo_seq_timing(self.h, C.byref(a), C.byref(b))
         return a.value, b.value
+
+    def debug(self, il: int, which: int, n: int) -> np.ndarray:
+        """Layer il intermediates of the last forward (see sfo_seq_debug)."""
+        ptr = lib().sfo_seq_debug(self.h, il, which)
+        return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_float)), shape=(n,)).copy()
 
     def hidden(self, il: int) -> np.ndarray:
         ptr = lib().sfo_seq_hidden(self.h, il)

@@ -441,7 +441,137 @@ void sfo_synth_f32(uint64_t seed, int64_t offset, int64_t n, float std_, float *
     for (int64_t i = 0; i < n; ++i) dst[i] = synth_z(seed, offset + i) * std_;
 }
 
-/* ---- dot products (ggml-cpu vec_dot_*_ref semantics) ---------------------- */
+/* ---- exp -------------------------------------------------------------------
+ * exp(x) for float x by Cody & Waite's argument reduction (x = n ln2 + r with
+ * ln2 split into a 16-bit head and a tail so n*head is exact) and the degree-7
+ * Taylor polynomial of e^r on |r| <= ln2/2 (truncation < 8e-9 relative),
+ * scaled by 2^n through the exponent field.  Every step is one IEEE-rounded
+ * operation, so the CUDA kernels evaluate it to the same bits (they spell each
+ * step with __fmul_rn / __fadd_rn).  Used where ggml calls expf (softmax,
+ * SiLU); ggml's SIMD builds also use their own exp approximations. */
+float sfo_expf(float x) {
+    if (x != x) return x;
+    if (x > 88.72283935546875f) return INFINITY;
+    if (x < -103.97208404541015625f) return 0.0f;
+    const float t = x * 1.44269502162933349609375f;
+    const int n = nearest_int(t);
+    const float fn = (float)n;
+    float r = x - fn * 0.693145751953125f;
+    r = r - fn * 1.428606765330187045037746429443359375e-06f;
+    float p = 1.98412701138295233249664306640625e-04f;
+    p = p * r + 1.38888892251998186111450195312500e-03f;
+    p = p * r + 8.33333376795053482055664062500000e-03f;
+    p = p * r + 4.16666679084300994873046875000000e-02f;
+    p = p * r + 1.66666671633720397949218750000000e-01f;
+    p = p * r + 0.5f;
+    p = p * r + 1.0f;
+    p = p * r + 1.0f;
+    /* p * 2^n, n in [-150, 128]: two exact power-of-two factors */
+    int n1 = n / 2, n2 = n - n / 2;
+    uint32_t b1 = (uint32_t)(n1 + 127) << 23, b2 = (uint32_t)(n2 + 127) << 23;
+    float f1, f2;
+    memcpy(&f1, &b1, 4);
+    memcpy(&f2, &b2, 4);
+    return (p * f1) * f2;
+}
+
+/* ---- dot products ------------------------------------------------------------
+ * Integer parts follow ggml's vec_dot_q4_K_q8_K / vec_dot_q6_K_q8_K /
+ * vec_dot_q8_0_q8_0 exactly (sub-block int8 x int8 sums, 6-bit or int8 scales,
+ * Q8_K bsums for the Q4_K mins).  ggml leaves the fp32 accumulation order of
+ * the block partials to each SIMD backend (generic, AVX2, NEON differ); this
+ * restatement fixes the order the B200 kernels use:
+ *   - a row of K columns is cut into 128-column units (half a 256-block; four
+ *     Q8_0 blocks), each giving one fp32 partial;
+ *   - units are taken 32 at a time (one group); the group's partials are summed
+ *     by the 5-level butterfly p[l] + p[l^16], ^8, ^4, ^2, ^1 (missing units
+ *     count as 0);
+ *   - group sums are added in order to 0.
+ * dot_*_blockorder keep ggml's generic per-block order for comparison. */
+static float unit_q4_K(const blk_q4_K *x, const blk_q8_K *y, int u) {
+    const int b = u >> 1, h = u & 1;
+    int32_t isum = 0, imin = 0;
+    for (int j = 4 * h; j < 4 * h + 4; ++j) {
+        uint8_t sc, m;
+        get_scale_min_k4(j, x[b].scales, &sc, &m);
+        const uint8_t *q = x[b].qs + 32 * (j / 2);
+        const int8_t *a = y[b].qs + 32 * j;
+        int32_t sacc = 0;
+        if ((j & 1) == 0) {
+            for (int l = 0; l < 32; ++l) sacc += (int32_t)(q[l] & 0xF) * a[l];
+        } else {
+            for (int l = 0; l < 32; ++l) sacc += (int32_t)(q[l] >> 4) * a[l];
+        }
+        isum += (int32_t)sc * sacc;
+        imin += (int32_t)m * (y[b].bsums[2 * j] + y[b].bsums[2 * j + 1]);
+    }
+    const float d = sfo_fp16_to_fp32(x[b].d) * y[b].d;
+    const float dmin = sfo_fp16_to_fp32(x[b].dmin) * y[b].d;
+    return d * (float)isum - dmin * (float)imin;
+}
+
+static float unit_q6_K(const blk_q6_K *x, const blk_q8_K *y, int u) {
+    const int b = u >> 1, h = u & 1;
+    const uint8_t *ql = x[b].ql + 64 * h, *qh = x[b].qh + 32 * h;
+    const int8_t *a = y[b].qs + 128 * h;
+    int32_t sacc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int l = 0; l < 32; ++l) {
+        const int q1 = ((ql[l] & 0xF) | (((qh[l] >> 0) & 3) << 4)) - 32;
+        const int q2 = ((ql[l + 32] & 0xF) | (((qh[l] >> 2) & 3) << 4)) - 32;
+        const int q3 = ((ql[l] >> 4) | (((qh[l] >> 4) & 3) << 4)) - 32;
+        const int q4 = ((ql[l + 32] >> 4) | (((qh[l] >> 6) & 3) << 4)) - 32;
+        const int is = l / 16;
+        sacc[is + 0] += q1 * a[l];
+        sacc[is + 2] += q2 * a[l + 32];
+        sacc[is + 4] += q3 * a[l + 64];
+        sacc[is + 6] += q4 * a[l + 96];
+    }
+    int32_t isum = 0;
+    for (int j = 0; j < 8; ++j) isum += (int32_t)x[b].scales[8 * h + j] * sacc[j];
+    return (sfo_fp16_to_fp32(x[b].d) * y[b].d) * (float)isum;
+}
+
+static float unit_q8_0(const blk_q8_0 *x, const blk_q8_0 *y, int u) {
+    float acc = 0.0f;
+    for (int j = 0; j < 4; ++j) {
+        const blk_q8_0 *xb = x + 4 * u + j, *yb = y + 4 * u + j;
+        int32_t sacc = 0;
+        for (int l = 0; l < QK8_0; ++l) sacc += (int32_t)xb->qs[l] * yb->qs[l];
+        acc = acc + (float)sacc * (sfo_fp16_to_fp32(xb->d) * sfo_fp16_to_fp32(yb->d));
+    }
+    return acc;
+}
+
+static float butterfly32(float p[32]) {
+    float q[32];
+    for (int o = 16; o > 0; o >>= 1) {
+        for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ o];
+        memcpy(p, q, sizeof(q));
+    }
+    return p[0];
+}
+
+static float dot_row_units(int type, const void *w, const void *xq, int64_t K) {
+    const int U = (int)(K / 128);
+    float acc = 0.0f;
+    for (int g = 0; g * 32 < U; ++g) {
+        const int ng = U - 32 * g < 32 ? U - 32 * g : 32;
+        float p[32];
+        for (int l = 0; l < 32; ++l) p[l] = 0.0f;
+        for (int l = 0; l < ng; ++l) {
+            const int u = 32 * g + l;
+            switch (type) {
+            case SFO_Q4_K: p[l] = unit_q4_K((const blk_q4_K *)w, (const blk_q8_K *)xq, u); break;
+            case SFO_Q6_K: p[l] = unit_q6_K((const blk_q6_K *)w, (const blk_q8_K *)xq, u); break;
+            case SFO_Q8_0: p[l] = unit_q8_0((const blk_q8_0 *)w, (const blk_q8_0 *)xq, u); break;
+            default: break;
+            }
+        }
+        acc = acc + butterfly32(p);
+    }
+    return acc;
+}
+
 static float dot_q4_K_q8_K(int64_t n, const blk_q4_K *x, const blk_q8_K *y) {
     float sumf = 0.0f;
     for (int64_t i = 0; i < n / QK_K; ++i) {
@@ -521,7 +651,7 @@ int sfo_mul_mat(int type, const void *w, int64_t nrows, int64_t ncols, const flo
         for (int64_t r = 0; r < nrows; ++r) y[r] = dot_f32(ncols, (const float *)w + r * ncols, x);
         return 0;
     }
-    if (fp32_mode) {
+    if (fp32_mode == 1) {
         #pragma omp parallel num_threads(nthreads())
         {
             float *row = (float *)malloc((size_t)ncols * sizeof(float));
@@ -542,9 +672,14 @@ int sfo_mul_mat(int type, const void *w, int64_t nrows, int64_t ncols, const flo
         xq = malloc(sfo_row_bytes(SFO_Q8_K, ncols));
         sfo_quantize_q8_K(x, xq, ncols);
     }
+    const int blockorder = fp32_mode == 2;
     #pragma omp parallel for num_threads(nthreads()) schedule(static)
     for (int64_t r = 0; r < nrows; ++r) {
         const void *wr = (const uint8_t *)w + (size_t)r * rb;
+        if (!blockorder) {
+            y[r] = dot_row_units(type, wr, xq, ncols);
+            continue;
+        }
         switch (type) {
         case SFO_Q4_K: y[r] = dot_q4_K_q8_K(ncols, (const blk_q4_K *)wr, (const blk_q8_K *)xq); break;
         case SFO_Q6_K: y[r] = dot_q6_K_q8_K(ncols, (const blk_q6_K *)wr, (const blk_q8_K *)xq); break;
@@ -607,7 +742,7 @@ void sfo_soft_max(const float *x, float *y, int64_t n, float scale) {
     }
     double sum = 0.0;
     for (int64_t i = 0; i < n; ++i) {
-        const float e = expf(y[i] - max);
+        const float e = sfo_expf(y[i] - max);
         y[i] = e;
         sum += (double)e;
     }
@@ -660,7 +795,7 @@ void sfo_router(const float *w_r, int n_expert, int d, const float *x, int k,
     free(probs);
 }
 
-static inline float silu_f32(float x) { return x / (1.0f + expf(-x)); }
+static inline float silu_f32(float x) { return x / (1.0f + sfo_expf(-x)); }
 
 int sfo_moe_ffn(int type_gu, int type_down, const void *gate, const void *up, const void *down,
                 int n_expert, int d, int F, int b, int k,
@@ -743,6 +878,8 @@ struct sfo_seq {
     float *hidden;            /* [n_layer][d] per-layer outputs of the last forward */
     int32_t *ids;             /* [n_layer][k] */
     double t_layers, t_head;  /* accumulated wall seconds */
+    float *dbg;               /* [n_layer][5][max(d, Hq*hd)] intermediates */
+    size_t dbg_stride;
 };
 
 static double now_s(void) {
@@ -855,7 +992,9 @@ sfo_seq *sfo_seq_create(const sfo_model *m) {
     s->v_cache = (float *)calloc(kv, sizeof(float));
     s->hidden = (float *)calloc((size_t)hp->n_layer * hp->n_embd, sizeof(float));
     s->ids = (int32_t *)calloc((size_t)hp->n_layer * (hp->n_expert_used > 0 ? hp->n_expert_used : 1), sizeof(int32_t));
-    if (!s->k_cache || !s->v_cache || !s->hidden || !s->ids) { sfo_seq_free(s); return NULL; }
+    s->dbg_stride = (size_t)(hp->n_embd > hp->n_head * (int)hd ? hp->n_embd : hp->n_head * (int)hd);
+    s->dbg = (float *)calloc((size_t)hp->n_layer * 5 * s->dbg_stride, sizeof(float));
+    if (!s->k_cache || !s->v_cache || !s->hidden || !s->ids || !s->dbg) { sfo_seq_free(s); return NULL; }
     return s;
 }
 
@@ -865,6 +1004,7 @@ void sfo_seq_free(sfo_seq *s) {
     free(s->v_cache);
     free(s->hidden);
     free(s->ids);
+    free(s->dbg);
     free(s);
 }
 
@@ -878,6 +1018,13 @@ void sfo_seq_reset(sfo_seq *s) {
 
 const float *sfo_seq_hidden(const sfo_seq *s, int il) { return s->hidden + (size_t)il * s->m->hp.n_embd; }
 const int32_t *sfo_seq_ids(const sfo_seq *s, int il) { return s->ids + (size_t)il * s->m->hp.n_expert_used; }
+const float *sfo_seq_debug(const sfo_seq *s, int il, int which) {
+    if (il < 0 || il >= s->m->hp.n_layer || which < 0 || which > 4) return NULL;
+    return s->dbg + ((size_t)il * 5 + (size_t)which) * s->dbg_stride;
+}
+static void dbg_put(sfo_seq *s, int il, int which, const float *v, int n) {
+    memcpy(s->dbg + ((size_t)il * 5 + (size_t)which) * s->dbg_stride, v, sizeof(float) * (size_t)n);
+}
 
 static inline float kv_round(float v, int f16) { return f16 ? sfo_fp16_to_fp32(sfo_fp32_to_fp16(v)) : v; }
 
@@ -924,13 +1071,18 @@ int32_t sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t pos, 
             Kl[(size_t)pos * Hkv * hd + i] = kv_round(kc[i], hp->kv_f16);
             Vl[(size_t)pos * Hkv * hd + i] = kv_round(vc[i], hp->kv_f16);
         }
+        dbg_put(s, il, 4, q, Hq * hd);
         sfo_attn_decode(q, Kl, Vl, pos + 1, Hq, Hkv, hd, att);
+        dbg_put(s, il, 0, att, Hq * hd);
         sfo_mul_mat(wo->type, wo->data, d, Hq * hd, att, tmp, fp32);
         for (int i = 0; i < d; ++i) ffn_inp[i] = tmp[i] + hidden[i];
         sfo_rms_norm(ffn_inp, (const float *)m->t[SFO_T_FFN_NORM][il].data, d, hp->rms_eps, cur);
         int32_t *ids = s->ids + (size_t)il * k;
         float wts[64];
         sfo_router((const float *)m->t[SFO_T_FFN_GATE_INP][il].data, E, d, cur, k, ids, wts, NULL);
+        dbg_put(s, il, 1, ffn_inp, d);
+        dbg_put(s, il, 2, cur, d);
+        dbg_put(s, il, 3, wts, k);
         /* --- expert segment: engine.cpp:1956-1989 --- */
         const sfo_tensor *tg = &m->t[SFO_T_FFN_GATE_EXPS][il], *tu = &m->t[SFO_T_FFN_UP_EXPS][il];
         const sfo_tensor *tdn = &m->t[SFO_T_FFN_DOWN_EXPS][il];

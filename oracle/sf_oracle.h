@@ -66,9 +66,13 @@ int  sfo_quantize_weights(int type, const float *x, void *dst, int64_t nrows, in
 void sfo_synth_f32(uint64_t seed, int64_t offset, int64_t n, float std_, float *dst);
 
 /* ---- ops ---------------------------------------------------------------- */
+/* exp(x) shared bit-for-bit with the CUDA kernels (Cody-Waite + Taylor) */
+float sfo_expf(float x);
 /* y[r] = dot(W[r,:], x) for a quantized or F32 weight matrix [nrows x ncols],
- * activation quantized to the weight's dot type first (ggml-exact mode) or
- * weights dequantized and dotted in f32/double (fp32 mode). */
+ * activation quantized to the weight's dot type first (ggml-exact mode, the
+ * kernels' fp32 accumulation order), weights dequantized and dotted in
+ * f32/double (fp32_mode 1, diagnostic) or ggml's generic per-block fp32
+ * order (fp32_mode 2, for comparison). */
 int  sfo_mul_mat(int type, const void *w, int64_t nrows, int64_t ncols,
                  const float *x, float *y, int fp32_mode);
 void sfo_rms_norm(const float *x, const float *w, int64_t n, float eps, float *y);
@@ -136,6 +140,10 @@ int32_t    sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t po
 /* per-layer hooks for tests: hidden state after layer `il` of the last forward */
 const float *sfo_seq_hidden(const sfo_seq *s, int il);
 const int32_t *sfo_seq_ids(const sfo_seq *s, int il);
+/* intermediates of layer `il` in the last forward: which = 0 attention output
+ * [Hq*hd], 1 ffn_inp [d], 2 ffn-normed expert input [d], 3 routing weights [k],
+ * 4 q after RoPE [Hq*hd]; returns NULL for an unknown buffer */
+const float *sfo_seq_debug(const sfo_seq *s, int il, int which);
 int32_t    sfo_argmax(const float *v, int n);
 /* wall seconds spent in the layer loop and in embedding + head, summed over
  * every sfo_forward of this sequence (for the timed CPU baseline) */

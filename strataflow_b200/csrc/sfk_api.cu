@@ -82,6 +82,10 @@ sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
   return SFK_OK;
 }
 
+// CTAs per (token, kv head) in the attention cluster: 8 (portable) unless a
+// CTA would own more than 2048 positions at the longest context
+int attn_cluster_for(int max_ctx) { return (max_ctx + 7) / 8 > 2048 ? 16 : 8; }
+
 // cached scratch for operator-level calls, per device
 struct OpScratch {
   void* buf = nullptr;
@@ -173,14 +177,16 @@ struct sfk_engine {
   int n_pages = 0;
   // step buffers
   float *x = nullptr, *ffn_inp = nullptr, *q = nullptr, *attn_out = nullptr, *h = nullptr, *logits = nullptr;
-  float *part_o = nullptr, *part_ml = nullptr, *router_logits = nullptr;
+  float *router_logits = nullptr;
+  float* rope = nullptr;  // [n_ctx][hd/2] (cos, sin)
   uint8_t *xq_ffn = nullptr, *hq = nullptr;
   Route* route = nullptr;
-  int *attn_counter = nullptr, *router_counter = nullptr, *grp_counter = nullptr;
+  int *router_counter = nullptr, *grp_counter = nullptr;
   unsigned long long* argmax_key = nullptr;
   int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
   int* status = nullptr;
-  int n_split = 1;
+  int attn_cluster = 8;
+  int attn_max_chunk = 0;
   // pinned staging
   int* h_tok = nullptr;
   int* h_pos = nullptr;
@@ -345,7 +351,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.y = e->q;
       p.kv = kv_view(e, l);
       p.n_head = hp.n_head;
-      p.theta_scale = powf(hp.freq_base, -2.0f / (float)e->hd);
+      p.rope = e->rope;
       p.pos = e->pos_cur;
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
@@ -359,10 +365,8 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       a.pos = e->pos_cur;
       a.b = b;
       a.n_head = hp.n_head;
-      a.n_split = e->n_split;
-      a.part_o = e->part_o;
-      a.part_ml = e->part_ml;
-      a.counter = e->attn_counter;
+      a.cluster = e->attn_cluster;
+      a.max_chunk = e->attn_max_chunk;
       a.out = e->attn_out;
       a.status = e->status;
       CK(launch_attn(a, st, pdl));
@@ -669,7 +673,12 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     CK(cudaMemcpy(e->page_table, perm.data(), sizeof(int) * e->n_pages, cudaMemcpyHostToDevice));
   }
   // step buffers
-  e->n_split = std::max(1, std::min(64, (2 * e->sm_count) / (hp->n_head_kv * B)));
+  e->attn_cluster = attn_cluster_for(e->max_pages * 16);
+  e->attn_max_chunk = (e->max_pages * 16 + e->attn_cluster - 1) / e->attn_cluster;
+  if (attn_smem_bytes(e->hd, hp->n_head / hp->n_head_kv, e->attn_max_chunk) > (size_t)SMEM_LIMIT) {
+    sfk_engine_free(e);
+    return fail(SFK_ERR_UNSUPPORTED, "n_ctx %d too long for the attention kernel's shared memory", hp->n_ctx);
+  }
   uint64_t* sb = &e->scratch_bytes;
   TRY(e->alloc(&e->x, sizeof(float) * B * d, sb));
   TRY(e->alloc(&e->ffn_inp, sizeof(float) * B * d, sb));
@@ -677,13 +686,11 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->attn_out, sizeof(float) * B * e->nq, sb));
   TRY(e->alloc(&e->h, sizeof(float) * B * k * F, sb));
   TRY(e->alloc(&e->logits, sizeof(float) * B * V, sb));
-  TRY(e->alloc(&e->part_o, sizeof(float) * B * hp->n_head * e->n_split * e->hd, sb));
-  TRY(e->alloc(&e->part_ml, sizeof(float) * B * hp->n_head * e->n_split * 2, sb));
+  TRY(e->alloc(&e->rope, sizeof(float) * (size_t)e->max_pages * 16 * e->hd, sb));
   TRY(e->alloc(&e->router_logits, sizeof(float) * B * E, sb));
   TRY(e->alloc(&e->xq_ffn, qact_bytes(d) * B, sb));
   TRY(e->alloc(&e->hq, qact_bytes(F) * B * k, sb));
   TRY(e->alloc(&e->route, sizeof(Route), sb));
-  TRY(e->alloc(&e->attn_counter, sizeof(int) * B * hp->n_head_kv, sb));
   TRY(e->alloc(&e->router_counter, sizeof(int), sb));
   TRY(e->alloc(&e->grp_counter, sizeof(int) * (F / 256), sb));
   TRY(e->alloc(&e->argmax_key, sizeof(unsigned long long) * B, sb));
@@ -695,8 +702,7 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->status, sizeof(int), sb));
   {
     cudaError_t ce = cudaSuccess;
-    ce = cudaMemset(e->attn_counter, 0, sizeof(int) * B * hp->n_head_kv);
-    if (ce == cudaSuccess) ce = cudaMemset(e->router_counter, 0, sizeof(int));
+    ce = cudaMemset(e->router_counter, 0, sizeof(int));
     if (ce == cudaSuccess) ce = cudaMemset(e->grp_counter, 0, sizeof(int) * (F / 256));
     if (ce == cudaSuccess) ce = cudaMemset(e->argmax_key, 0, sizeof(unsigned long long) * B);
     if (ce == cudaSuccess) ce = cudaMemset(e->pos_state, 0, sizeof(int) * B);
@@ -710,6 +716,27 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     if (ce != cudaSuccess) {
       sfk_engine_free(e);
       return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
+    }
+  }
+  {
+    // RoPE cos/sin for every position (ggml rope cache, mode NORMAL,
+    // freq_scale 1, ext_factor 0): theta_0 = pos, theta_{i+1} = theta_i *
+    // powf(base, -2/n_dims), evaluated with the host libm
+    const int half = e->hd / 2, npos = e->max_pages * 16;
+    std::vector<float> tab((size_t)npos * e->hd);
+    const float theta_scale = powf(hp->freq_base, -2.0f / (float)e->hd);
+    for (int pos = 0; pos < npos; ++pos) {
+      float theta = (float)pos;
+      for (int i = 0; i < half; ++i) {
+        tab[((size_t)pos * half + i) * 2 + 0] = cosf(theta);
+        tab[((size_t)pos * half + i) * 2 + 1] = sinf(theta);
+        theta *= theta_scale;
+      }
+    }
+    cudaError_t ce = cudaMemcpy(e->rope, tab.data(), tab.size() * sizeof(float), cudaMemcpyHostToDevice);
+    if (ce != cudaSuccess) {
+      sfk_engine_free(e);
+      return fail(SFK_ERR_RUNTIME, "rope table: %s", cudaGetErrorString(ce));
     }
   }
 #undef TRY
@@ -905,6 +932,36 @@ sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int3
   sfk_status s = check_status_word(e->status, e->stream);
   if (s) return s;
   for (int t = 0; t < n_seq; ++t) e->seq_pos[t] += n_steps;
+  return SFK_OK;
+}
+
+sfk_status sfk_route_get(sfk_engine* e, int32_t* ids_out, float* w_out, size_t n) {
+  if (!e || !ids_out || !w_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t np = (size_t)std::max(1, e->last_b) * e->hp.n_expert_used;
+  if (n < np) return fail(SFK_ERR_INVALID_ARGUMENT, "need %zu entries", np);
+  CK(cudaSetDevice(e->device));
+  CK(cudaMemcpyAsync(ids_out, e->route->ids, np * sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaMemcpyAsync(w_out, e->route->w, np * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+sfk_status sfk_debug_get(sfk_engine* e, int32_t which, float* host_out, size_t n_floats) {
+  if (!e || !host_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const size_t b = (size_t)std::max(1, e->last_b);
+  const float* src = nullptr;
+  size_t n = 0;
+  switch (which) {
+    case 0: src = e->attn_out; n = b * e->nq; break;
+    case 1: src = e->ffn_inp; n = b * e->hp.n_embd; break;
+    case 2: src = e->q; n = b * e->nq; break;
+    case 3: src = e->h; n = b * e->hp.n_expert_used * e->hp.n_ff; break;
+    default: return fail(SFK_ERR_INVALID_ARGUMENT, "unknown buffer %d", which);
+  }
+  if (n_floats < n) return fail(SFK_ERR_INVALID_ARGUMENT, "need %zu floats", n);
+  CK(cudaSetDevice(e->device));
+  CK(cudaMemcpyAsync(host_out, src, n * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
   return SFK_OK;
 }
 
@@ -1158,14 +1215,8 @@ sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp,
       n_head % n_head_kv || (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) ||
       (kv_type != SFK_KV_F16 && kv_type != SFK_KV_F32))
     return fail(SFK_ERR_INVALID_ARGUMENT, "attn_decode_paged arguments");
-  int dev = 0;
-  CK(cudaGetDevice(&dev));
-  const int sms = sm_count_of(dev);
-  const int n_split = std::max(1, std::min(64, (2 * sms) / (n_head_kv * b)));
-  const size_t po = sizeof(float) * (size_t)b * n_head * n_split * head_dim;
-  const size_t pml = sizeof(float) * (size_t)b * n_head * n_split * 2;
   OpScratch* sc = nullptr;
-  sfk_status s = op_scratch(po + pml + 256, (size_t)b * n_head_kv, &sc);
+  sfk_status s = op_scratch(16, 1, &sc);
   if (s) return s;
   AttnParams a{};
   a.q = q;
@@ -1179,10 +1230,10 @@ sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp,
   a.pos = positions;
   a.b = b;
   a.n_head = n_head;
-  a.n_split = n_split;
-  a.part_o = (float*)sc->buf;
-  a.part_ml = (float*)((uint8_t*)sc->buf + ((po + 255) & ~(size_t)255));
-  a.counter = sc->counters;
+  a.cluster = attn_cluster_for(max_pages * 16);
+  a.max_chunk = (max_pages * 16 + a.cluster - 1) / a.cluster;
+  if (attn_smem_bytes(head_dim, n_head / n_head_kv, a.max_chunk) > (size_t)SMEM_LIMIT)
+    return fail(SFK_ERR_UNSUPPORTED, "context of %d pages too long", max_pages);
   a.out = out;
   a.status = sc->status;
   CK(launch_attn(a, (cudaStream_t)stream, false));

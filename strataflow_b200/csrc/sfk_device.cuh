@@ -144,6 +144,32 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 // ggml nearest_int: round half to even; valid for |x| <= 4194303
 __device__ __forceinline__ int nearest_int(float x) { return __float2int_rn(x); }
 
+// exp(x): Cody & Waite argument reduction (x = n ln2 + r, ln2 split into a
+// 16-bit head and a tail) and the degree-7 Taylor polynomial of e^r, scaled by
+// 2^n through two exact power-of-two factors.  Each step is one round-to-
+// nearest operation, so the CPU oracle (sfo_expf, -ffp-contract=off) produces
+// the same bits.  Max error 1.15 ulp against exp in float64.
+__device__ __forceinline__ float sfk_expf(float x) {
+  if (x != x) return x;
+  if (x > 88.72283935546875f) return __int_as_float(0x7f800000);
+  if (x < -103.97208404541015625f) return 0.0f;
+  const float t = __fmul_rn(x, 1.44269502162933349609375f);
+  const int n = __float2int_rn(t);
+  const float fn = (float)n;
+  float r = __fsub_rn(x, __fmul_rn(fn, 0.693145751953125f));
+  r = __fsub_rn(r, __fmul_rn(fn, 1.428606765330187045037746429443359375e-06f));
+  float p = 1.98412701138295233249664306640625e-04f;
+  p = __fadd_rn(__fmul_rn(p, r), 1.38888892251998186111450195312500e-03f);
+  p = __fadd_rn(__fmul_rn(p, r), 8.33333376795053482055664062500000e-03f);
+  p = __fadd_rn(__fmul_rn(p, r), 4.16666679084300994873046875000000e-02f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.66666671633720397949218750000000e-01f);
+  p = __fadd_rn(__fmul_rn(p, r), 0.5f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  p = __fadd_rn(__fmul_rn(p, r), 1.0f);
+  const int n1 = n / 2, n2 = n - n / 2;
+  return __fmul_rn(__fmul_rn(p, __int_as_float((n1 + 127) << 23)), __int_as_float((n2 + 127) << 23));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
@@ -234,9 +260,9 @@ __device__ __forceinline__ float dot_unit_q4k(const WQ4K& w, const XQ8& x, int l
   const int imin = (int)(mn & 0xFF) * b0 + (int)((mn >> 8) & 0xFF) * b1 + (int)((mn >> 16) & 0xFF) * b2 +
                    (int)(mn >> 24) * b3;
   const __half2 dd = *reinterpret_cast<const __half2*>(&w.h0);
-  const float d = __low2float(dd) * x.d;
-  const float dmin = __high2float(dd) * x.d;
-  return d * (float)isum - dmin * (float)imin;
+  const float d = __fmul_rn(__low2float(dd), x.d);
+  const float dmin = __fmul_rn(__high2float(dd), x.d);
+  return __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dmin, (float)imin));
 }
 
 // Q6_K x Q8_K  (ggml vec_dot_q6_K_q8_K): per 16-column sub-block m of the half,
@@ -281,7 +307,7 @@ __device__ __forceinline__ float dot_unit_q6k(const WQ6K& w, const XQ8& x) {
     const int bsum = (int)(int16_t)((bs[m >> 1] >> (16 * (m & 1))) & 0xFFFF);
     isum += scm * (s[m] - 32 * bsum);
   }
-  return (w.d * x.d) * (float)isum;
+  return __fmul_rn(__fmul_rn(w.d, x.d), (float)isum);
 }
 
 // Q8_0 x Q8_0 (ggml vec_dot_q8_0_q8_0): per 32-block, sumi * (d_w * d_x)
@@ -305,7 +331,7 @@ __device__ __forceinline__ float dot_unit_q80(const WQ80& w, const XQ8& x) {
   for (int j = 0; j < 4; ++j) {
     int s = dot4(w.c[2 * j], x.c[2 * j], 0);
     s = dot4(w.c[2 * j + 1], x.c[2 * j + 1], s);
-    acc += (float)s * (wd[j] * xd[j]);
+    acc = __fadd_rn(acc, __fmul_rn((float)s, __fmul_rn(wd[j], xd[j])));
   }
   return acc;
 }

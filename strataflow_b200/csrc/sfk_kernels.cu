@@ -22,6 +22,7 @@
 // round-to-nearest intrinsics (no FMA contraction) so they round exactly as
 // the ggml CPU code does.
 #include <cuda_runtime.h>
+#include <cooperative_groups.h>
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <cstdio>
@@ -213,14 +214,13 @@ __device__ void epi_qkv(const StreamParams& p, const float* acc, int r0, int r1)
     const int pos = p.pos[t];
     float o0 = x0, o1 = x1;
     if (r < nq + nk) {
-      // ggml rope NORMAL: theta_i = pos * theta_scale^i built by repeated
-      // multiplication, rotate (x0, x1) by theta_i
+      // ggml rope NORMAL (engine.cpp:1892-1897): rotate (x0, x1) by theta_i,
+      // theta_i = pos * theta_scale^i; cos/sin come from a host-built table
+      // evaluated exactly like ggml's rope cache
       const int i = (r % hd) >> 1;
-      float theta = (float)pos;
-      for (int j = 0; j < i; ++j) theta = __fmul_rn(theta, p.theta_scale);
-      const float c = cosf(theta), s = sinf(theta);
-      o0 = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, s));
-      o1 = __fadd_rn(__fmul_rn(x0, s), __fmul_rn(x1, c));
+      const float2 cs = reinterpret_cast<const float2*>(p.rope)[(int64_t)pos * (hd >> 1) + i];
+      o0 = __fsub_rn(__fmul_rn(x0, cs.x), __fmul_rn(x1, cs.y));
+      o1 = __fadd_rn(__fmul_rn(x0, cs.y), __fmul_rn(x1, cs.x));
     }
     if (r < nq) {
       p.y[(int64_t)t * nq + r] = o0;
@@ -253,7 +253,7 @@ __device__ void epi_gateup(const StreamParams& p, const float* acc, int r0, int 
     const int row = idx % nr, pr = idx / nr;
     const float g = acc[(row * p.n_pairs + pr) * 2 + 0];
     const float u = acc[(row * p.n_pairs + pr) * 2 + 1];
-    const float sl = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    const float sl = __fdiv_rn(g, __fadd_rn(1.0f, sfk_expf(-g)));
     p.h[(int64_t)pr * p.rows + r0 + row] = __fmul_rn(sl, u);
   }
   __threadfence();
@@ -474,120 +474,166 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
 }
 
 // ---------------------------------------------------------------------------
-// split-K GQA decode attention over the paged KV cache
-// (engine.cpp:1751-1761: kq = K.q, soft_max_ext(scale = 1/sqrt(hd)), kqv = V^T kq)
-// grid (n_split, Hkv, b), 128 threads; warp w serves query heads w, w+4, ...
-// of the kv head's GQA group.  The last split CTA of a (token, kv head)
-// merges the splits: o = sum_s o_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+// GQA decode attention over the paged KV cache, ggml's op order exactly
+// (engine.cpp:1751-1761):
+//   kq_j  = (float) sum_i (double)(k_ji * q_i)          ggml_mul_mat F32
+//   s_j   = kq_j * (1/sqrt(hd)); M = max_j s_j          ggml_soft_max_ext
+//   p_j   = exp(s_j - M); S = sum_j (double) p_j; p'_j = p_j * (float)(1/S)
+//   o_i   = (float) sum_j (double)(v_ji * p'_j)         ggml_mul_mat F32
+// One thread-block cluster per (token, kv head); each CTA of the cluster owns
+// a contiguous slice of positions.  The cross-CTA steps (global max, global
+// sum, the final o reduction) go through distributed shared memory with
+// cluster barriers, so the two-pass softmax is exact without a second kernel.
+// 128 threads; the GQA group's query heads share each K/V load.
 // ---------------------------------------------------------------------------
 constexpr int ATT_THREADS = 128;
+constexpr int ATT_MAXG = 16;  // max query heads per kv head
 
 template <int HD>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
+  namespace cg = cooperative_groups;
   pdl_launch_dependents();
   pdl_wait();
-  __shared__ int last_flag;
-  const int split = blockIdx.x, hk = blockIdx.y, t = blockIdx.z;
+  cg::cluster_group cl = cg::this_cluster();
+  const int C = (int)cl.num_blocks();
+  const int rank = (int)cl.block_rank();
+  const int hk = blockIdx.x / C, t = blockIdx.y;
   const int Hkv = p.kv.n_head_kv;
   const int gqa = p.n_head / Hkv;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int PER = HD / 32;  // dims per lane
-  const int n_kv = p.pos[t] + 1;
-  int chunk = (n_kv + p.n_split - 1) / p.n_split;
-  chunk = (chunk + 15) & ~15;
-  const int start = split * chunk;
-  const int end = min(n_kv, start + chunk);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int PER = HD / 32;  // output dims per lane
+  constexpr int QD = HD / 4;    // dims per lane in the score pass (4 lanes per position)
+
+  // shared layout (attn_smem_bytes): opart [gqa][HD] f64 | qs [gqa][HD] f32 |
+  // lsum [gqa] f64 | wred [4][gqa] f64 | lmax [gqa] f32 | sc [gqa][max_chunk] f32
+  extern __shared__ __align__(16) uint8_t asmem[];
+  double* opart = reinterpret_cast<double*>(asmem);
+  float* qs = reinterpret_cast<float*>(opart + gqa * HD);
+  double* lsum = reinterpret_cast<double*>(qs + gqa * HD);
+  double* wred = lsum + gqa;
+  float* lmax = reinterpret_cast<float*>(wred + 4 * gqa);
+  float* sc = lmax + ((gqa + 3) & ~3);
+  int n_kv = p.pos[t] + 1;
+  if (n_kv < 1 || n_kv > p.kv.max_pages * 16) {  // outside the page table: no access, report
+    if (tid == 0 && rank == 0) atomicExch(p.status, ERR_BAD_POS);
+    n_kv = 0;
+  }
+  const int chunk = (n_kv + C - 1) / C;
+  const int j0 = rank * chunk;
+  const int nloc = max(0, min(n_kv, j0 + chunk) - j0);
   const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
   const int* ptab = p.kv.page_table + t * p.kv.max_pages;
+  const int q0 = hk * gqa;
 
-  for (int hq = hk * gqa + warp; hq < (hk + 1) * gqa; hq += ATT_THREADS / 32) {
-    float q[PER], o[PER];
+  for (int i = tid; i < gqa * HD; i += ATT_THREADS) qs[i] = p.q[((int64_t)t * p.n_head + q0) * HD + i];
+  __syncthreads();
+
+  // ---- pass 1: scores of this CTA's positions; 8 positions per warp step
+  const int n_oct = (nloc + 7) >> 3;
+  for (int item = warp; item < gqa * n_oct; item += ATT_THREADS / 32) {
+    const int h = item % gqa, oct = item / gqa;
+    const int jl = oct * 8 + (lane >> 2);
+    const int c = lane & 3;
+    double acc = 0.0;
+    if (jl < nloc) {
+      const int j = j0 + jl;
+      const int64_t off = (((int64_t)ptab[j >> 4] * Hkv + hk) * 16 + (j & 15)) * HD + c * QD;
+      const float* qh = qs + h * HD + c * QD;
+      if (p.kv.f16) {
+        const __half* kr = reinterpret_cast<const __half*>(p.kv.k) + off;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      q[i] = p.q[((int64_t)t * p.n_head + hq) * HD + lane * PER + i];
-      o[i] = 0.0f;
-    }
-    float m = -INFINITY, l = 0.0f;
-    for (int pos0 = start; pos0 < end; pos0 += 16) {
-      const int page = ptab[pos0 >> 4];
-      const int64_t base = ((int64_t)page * Hkv + hk) * 16 * HD;
-      const int n = min(16, end - pos0);
-      float sc[16];
+        for (int i = 0; i < QD; i += 8) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(kr + i);
+          const __half2* hv = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float d = 0.0f;
-        if (j < n) {
-#pragma unroll
-          for (int i = 0; i < PER; ++i) {
-            const int64_t off = base + (int64_t)j * HD + lane * PER + i;
-            const float kv = p.kv.f16 ? __half2float(reinterpret_cast<const __half*>(p.kv.k)[off])
-                                      : reinterpret_cast<const float*>(p.kv.k)[off];
-            d = fmaf(kv, q[i], d);
+          for (int e = 0; e < 4; ++e) {
+            const float2 kf = __half22float2(hv[e]);
+            acc += (double)__fmul_rn(kf.x, qh[i + 2 * e]);
+            acc += (double)__fmul_rn(kf.y, qh[i + 2 * e + 1]);
           }
         }
-        d = warp_sum(d);
-        sc[j] = j < n ? __fmul_rn(d, scale) : -INFINITY;
-      }
-      float mt = m;
+      } else {
+        const float* kr = reinterpret_cast<const float*>(p.kv.k) + off;
 #pragma unroll
-      for (int j = 0; j < 16; ++j) mt = fmaxf(mt, sc[j]);
-      const float corr = expf(m - mt);  // m == -inf on the first page -> 0
-      l = l * corr;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) o[i] *= corr;
-#pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        if (j < n) {
-          const float pj = expf(sc[j] - mt);
-          l += pj;
-#pragma unroll
-          for (int i = 0; i < PER; ++i) {
-            const int64_t off = base + (int64_t)j * HD + lane * PER + i;
-            const float vv = p.kv.f16 ? __half2float(reinterpret_cast<const __half*>(p.kv.v)[off])
-                                      : reinterpret_cast<const float*>(p.kv.v)[off];
-            o[i] = fmaf(pj, vv, o[i]);
-          }
+        for (int i = 0; i < QD; i += 4) {
+          const float4 kf = *reinterpret_cast<const float4*>(kr + i);
+          acc += (double)__fmul_rn(kf.x, qh[i]);
+          acc += (double)__fmul_rn(kf.y, qh[i + 1]);
+          acc += (double)__fmul_rn(kf.z, qh[i + 2]);
+          acc += (double)__fmul_rn(kf.w, qh[i + 3]);
         }
       }
-      m = mt;
     }
-    const int64_t pidx = ((int64_t)t * p.n_head + hq) * p.n_split + split;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) p.part_o[pidx * HD + lane * PER + i] = o[i];
-    if (lane == 0) {
-      p.part_ml[pidx * 2 + 0] = m;
-      p.part_ml[pidx * 2 + 1] = l;
-    }
-  }
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    const int old = atomicAdd(&p.counter[t * Hkv + hk], 1);
-    last_flag = (old == p.n_split - 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+    if (c == 0 && jl < nloc) sc[h * p.max_chunk + jl] = __fmul_rn((float)acc, scale);
   }
   __syncthreads();
-  if (!last_flag) return;
-  __threadfence();
-  for (int hq = hk * gqa + warp; hq < (hk + 1) * gqa; hq += ATT_THREADS / 32) {
-    const int64_t pb = ((int64_t)t * p.n_head + hq) * p.n_split;
+  // local max per head
+  for (int h = warp; h < gqa; h += ATT_THREADS / 32) {
+    float m = -INFINITY;
+    for (int jl = lane; jl < nloc; jl += 32) m = fmaxf(m, sc[h * p.max_chunk + jl]);
+    m = warp_max(m);
+    if (lane == 0) lmax[h] = m;
+  }
+  cl.sync();
+  // ---- pass 2: global max, exp, local sum
+  for (int h = 0; h < gqa; ++h) {
     float M = -INFINITY;
-    for (int s = 0; s < p.n_split; ++s) M = fmaxf(M, __ldcg(&p.part_ml[(pb + s) * 2]));
-    float L = 0.0f, o[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) o[i] = 0.0f;
-    for (int s = 0; s < p.n_split; ++s) {
-      const float ms = __ldcg(&p.part_ml[(pb + s) * 2]);
-      if (ms == -INFINITY) continue;
-      const float f = expf(ms - M);
-      L += __ldcg(&p.part_ml[(pb + s) * 2 + 1]) * f;
-#pragma unroll
-      for (int i = 0; i < PER; ++i) o[i] = fmaf(__ldcg(&p.part_o[(pb + s) * HD + lane * PER + i]), f, o[i]);
+    for (int r = 0; r < C; ++r) M = fmaxf(M, cl.map_shared_rank(lmax, r)[h]);
+    double s = 0.0;
+    for (int jl = tid; jl < nloc; jl += ATT_THREADS) {
+      const float e = sfk_expf(__fsub_rn(sc[h * p.max_chunk + jl], M));
+      sc[h * p.max_chunk + jl] = e;
+      s += (double)e;
     }
-    const float invL = 1.0f / L;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) p.out[((int64_t)t * p.n_head + hq) * HD + lane * PER + i] = o[i] * invL;
+    s = warp_sum_d(s);
+    if (lane == 0) wred[warp * gqa + h] = s;
   }
-  if (threadIdx.x == 0) atomicExch(&p.counter[t * Hkv + hk], 0);
+  __syncthreads();
+  if (tid < gqa) {
+    double s = 0.0;
+    for (int w = 0; w < ATT_THREADS / 32; ++w) s += wred[w * gqa + tid];
+    lsum[tid] = s;
+  }
+  cl.sync();
+  // ---- pass 3: p' = p * (float)(1/S); o_i = sum_j (double)(v_ji * p'_j)
+  for (int h = warp; h < gqa; h += ATT_THREADS / 32) {
+    double S = 0.0;
+    for (int r = 0; r < C; ++r) S += cl.map_shared_rank(lsum, r)[h];
+    const float inv = (float)(1.0 / S);
+    double o[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) o[i] = 0.0;
+    for (int jl = 0; jl < nloc; ++jl) {
+      const int j = j0 + jl;
+      const float pj = __fmul_rn(sc[h * p.max_chunk + jl], inv);
+      const int64_t off = (((int64_t)ptab[j >> 4] * Hkv + hk) * 16 + (j & 15)) * HD + lane * PER;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        const float vv = p.kv.f16 ? __half2float(reinterpret_cast<const __half*>(p.kv.v)[off + i])
+                                  : reinterpret_cast<const float*>(p.kv.v)[off + i];
+        o[i] += (double)__fmul_rn(vv, pj);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) opart[h * HD + lane * PER + i] = o[i];
+  }
+  cl.sync();
+  // ---- reduce the cluster's partial outputs on rank 0
+  if (rank == 0) {
+    for (int i = tid; i < gqa * HD; i += ATT_THREADS) {
+      double o = 0.0;
+      for (int r = 0; r < C; ++r) o += cl.map_shared_rank(opart, r)[i];
+      p.out[((int64_t)t * p.n_head + q0) * HD + i] = (float)o;
+    }
+  }
+  cl.sync();
+}
+
+size_t attn_smem_bytes(int hd, int gqa, int max_chunk) {
+  return (size_t)gqa * hd * 8 + (size_t)gqa * hd * 4 + (size_t)gqa * 8 + 4 * (size_t)gqa * 8 +
+         (size_t)((gqa + 3) & ~3) * 4 + (size_t)gqa * max_chunk * 4;
 }
 
 // ---------------------------------------------------------------------------
@@ -637,18 +683,19 @@ __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p
     qact_put(p.act_type, xq, d, blk, v, lane);
   }
   // router logits (F32 weights)
+  // ggml F32 mul_mat: float products summed in double
   for (int e = warp; e < p.E; e += RT_THREADS / 32) {
     const float* wr = p.w_r + (int64_t)e * d;
-    float a = 0.0f;
+    double a = 0.0;
     for (int c = lane * 4; c < d; c += 128) {
       const float4 w4 = *reinterpret_cast<const float4*>(wr + c);
-      a = fmaf(w4.x, xn[c], a);
-      a = fmaf(w4.y, xn[c + 1], a);
-      a = fmaf(w4.z, xn[c + 2], a);
-      a = fmaf(w4.w, xn[c + 3], a);
+      a += (double)__fmul_rn(w4.x, xn[c]);
+      a += (double)__fmul_rn(w4.y, xn[c + 1]);
+      a += (double)__fmul_rn(w4.z, xn[c + 2]);
+      a += (double)__fmul_rn(w4.w, xn[c + 3]);
     }
-    a = warp_sum(a);
-    if (lane == 0) probs[e] = a;
+    a = warp_sum_d(a);
+    if (lane == 0) probs[e] = (float)a;
   }
   __syncthreads();
   if (warp == 0) {
@@ -658,7 +705,7 @@ __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p
     mx = warp_max(mx);
     double sum = 0.0;
     for (int e = lane; e < p.E; e += 32) {
-      const float ex = expf(probs[e] - mx);
+      const float ex = sfk_expf(__fsub_rn(probs[e], mx));
       probs[e] = ex;
       sum += (double)ex;
     }
@@ -847,13 +894,40 @@ cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool
   }
 }
 
+template <int HD>
+static cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st, bool pdl) {
+  const size_t smem = attn_smem_bytes(HD, p.n_head / p.kv.n_head_kv, p.max_chunk);
+  cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  if (p.cluster > 8) {
+    e = cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (e != cudaSuccess) return e;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.cluster * p.kv.n_head_kv, p.b, 1);
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = p.cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 2 : 1;
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD>, p);
+}
+
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl) {
-  const dim3 grid(p.n_split, p.kv.n_head_kv, p.b);
+  if (p.n_head % p.kv.n_head_kv || p.n_head / p.kv.n_head_kv > ATT_MAXG || p.cluster < 1 || p.cluster > 16)
+    return cudaErrorInvalidValue;
   switch (p.kv.head_dim) {
-    case 32: return launch_pdl(attn_kernel<32>, grid, dim3(ATT_THREADS), 0, st, pdl, p);
-    case 64: return launch_pdl(attn_kernel<64>, grid, dim3(ATT_THREADS), 0, st, pdl, p);
-    case 128: return launch_pdl(attn_kernel<128>, grid, dim3(ATT_THREADS), 0, st, pdl, p);
-    case 256: return launch_pdl(attn_kernel<256>, grid, dim3(ATT_THREADS), 0, st, pdl, p);
+    case 32: return launch_attn_t<32>(p, st, pdl);
+    case 64: return launch_attn_t<64>(p, st, pdl);
+    case 128: return launch_attn_t<128>(p, st, pdl);
+    case 256: return launch_attn_t<256>(p, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }

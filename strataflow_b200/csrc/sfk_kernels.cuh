@@ -85,7 +85,7 @@ struct StreamParams {
   // EPI_QKV
   KvView kv;
   int n_head;
-  float theta_scale;       // powf(freq_base, -2/head_dim), computed on the host
+  const float* rope;       // [n_ctx][head_dim/2] (cos, sin) pairs, built on the host
   const int* pos;          // [b] positions
   // EPI_GATEUP
   float* h;                // [pairs][rows] f32
@@ -102,10 +102,9 @@ struct AttnParams {
   const float* q;          // [b][Hq][hd]
   KvView kv;
   const int* pos;          // [b]; attends over 0..pos
-  int b, n_head, n_split;
-  float* part_o;           // [b][Hq][n_split][hd]
-  float* part_ml;          // [b][Hq][n_split][2]
-  int* counter;            // [b][Hkv], self-resetting
+  int b, n_head;
+  int cluster;             // CTAs per (token, kv head): one thread-block cluster
+  int max_chunk;           // positions per CTA at the longest context
   float* out;              // [b][Hq*hd]
   int* status;
 };
@@ -143,6 +142,7 @@ struct EmbedParams {
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp);
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
+size_t attn_smem_bytes(int hd, int gqa, int max_chunk);
 cudaError_t launch_router(const RouterParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);

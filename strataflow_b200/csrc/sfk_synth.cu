@@ -205,10 +205,7 @@ __device__ void synth_block_q6k(const float v[8], uint8_t* out, uint8_t* sh, int
     out[128 + j] = (uint8_t)((q1 >> 4) | ((q2 >> 4) << 2) | ((q3 >> 4) << 4) | ((q4 >> 4) << 6));
   }
   if ((lane & 1) == 0) out[192 + (lane >> 1)] = (uint8_t)scq;
-  if (lane == 0) {
-    out[208] = (uint8_t)(dbits & 0xFF);
-    out[209] = (uint8_t)(dbits >> 8);
-  }
+  if (lane == 0) *reinterpret_cast<uint16_t*>(out + 208) = dbits;
   __syncwarp();
 }
 
@@ -222,11 +219,7 @@ __device__ void synth_blocks_q80(const float v[8], uint8_t* out, int lane) {
   const float d = amax / 127.0f;
   const float id = d != 0.0f ? 1.0f / d : 0.0f;
   uint8_t* blk = out + (lane >> 2) * 34;
-  if ((lane & 3) == 0) {
-    const uint16_t h = f16_bits(d);
-    blk[0] = (uint8_t)(h & 0xFF);
-    blk[1] = (uint8_t)(h >> 8);
-  }
+  if ((lane & 3) == 0) *reinterpret_cast<__half*>(blk) = __float2half_rn(d);
 #pragma unroll
   for (int i = 0; i < 8; ++i) blk[2 + (lane & 3) * 8 + i] = (uint8_t)(int8_t)roundf(v[i] * id);
 }

@@ -176,6 +176,25 @@ class Engine:
                                             out.ctypes.data_as(C.c_void_p) if want_tokens else None))
         return out
 
+    def route(self, n_seq: int = 1):
+        """(ids, weights) of the last layer's routing in the last step."""
+        k = self.cfg.n_expert_used
+        ids = np.empty((n_seq, k), np.int32)
+        w = np.empty((n_seq, k), np.float32)
+        L.check(self._lib.sfk_route_get(self.h, ids.ctypes.data_as(C.c_void_p), w.ctypes.data_as(C.c_void_p),
+                                        ids.size))
+        return ids, w
+
+    def debug(self, which: int, n_seq: int = 1) -> np.ndarray:
+        """Step buffers of the last layer (sfk_debug_get): 0 attention output,
+        1 ffn_inp, 2 q after RoPE, 3 SwiGLU activation."""
+        c = self.cfg
+        n = {0: c.n_head * c.head_dim, 1: c.n_embd, 2: c.n_head * c.head_dim,
+             3: c.n_expert_used * c.n_ff}[which] * n_seq
+        out = np.empty(n, np.float32)
+        L.check(self._lib.sfk_debug_get(self.h, which, out.ctypes.data_as(C.c_void_p), n))
+        return out
+
     def hidden(self, n_seq: int = 1) -> np.ndarray:
         out = np.empty((n_seq, self.cfg.n_embd), np.float32)
         L.check(self._lib.sfk_hidden_get(self.h, out.ctypes.data_as(C.c_void_p), out.size))

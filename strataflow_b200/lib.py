@@ -57,6 +57,8 @@ _SIGS = {
     "sfk_forward_batch": (I32, [P, I32, P, P, P, P]),
     "sfk_decode_greedy": (I32, [P, I32, I32, P]),
     "sfk_hidden_get": (I32, [P, P, SZ]),
+    "sfk_route_get": (I32, [P, P, P, SZ]),
+    "sfk_debug_get": (I32, [P, I32, P, SZ]),
     "sfk_get_stats": (I32, [P, C.POINTER(Stats)]),
     "sfk_time_kernels": (I32, [P, I32, I32, P, I32]),
     "sfk_dev_row_bytes": (I64, [C.c_int, I64]),

@@ -119,6 +119,28 @@ def test_mul_mat_integer_path_equals_dequantized_dot(qtype):
     assert np.abs(y - ref).max() <= 2e-5 * np.abs(ref).max()
 
 
+@pytest.mark.parametrize("qtype", [O.Q4_K, O.Q6_K, O.Q8_0])
+def test_kernel_order_and_ggml_block_order_agree(qtype):
+    """The fixed fp32 accumulation order (the kernels') and ggml's generic
+    per-block order differ only by fp32 rounding."""
+    rng = np.random.default_rng(4)
+    rows, K = 64, 14336
+    w = O.quantize_weights(qtype, (rng.standard_normal((rows, K)) * 0.02).astype(np.float32))
+    x = rng.standard_normal(K).astype(np.float32)
+    a = O.mul_mat(qtype, w, rows, K, x)
+    b = O.mul_mat(qtype, w, rows, K, x, fp32_mode=2)
+    assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()
+
+
+def test_own_expf_accuracy():
+    xs = np.concatenate([np.linspace(-87, 88, 20001), np.float32([0, -1e-30, 1e-30])]).astype(np.float32)
+    got = np.array([O.expf(v) for v in xs], np.float64)
+    ref = np.exp(xs.astype(np.float64))
+    ulp = np.abs(got - ref) / np.spacing(ref.astype(np.float32)).astype(np.float64)
+    assert ulp.max() <= 1.5
+    assert O.expf(89.0) == np.inf and O.expf(-105.0) == 0.0 and O.expf(0.0) == 1.0
+
+
 def test_rope_normal_matches_closed_form():
     hd, H, pos, base = 32, 3, 17, 10000.0
     x = np.random.default_rng(1).standard_normal(H * hd).astype(np.float32)
