@@ -211,6 +211,26 @@ SFK_API sfk_status sfk_moe_ffn(int type_gu, int type_down, const void *dev_gate,
                        const int32_t *dev_ids, const float *dev_w, int32_t b, int32_t k, float *dev_out,
                        void *stream);
 
+/* sfk_moe_ffn computed without allocating device memory.  No counterpart in
+ * the reference: it exists for callers that cannot let a library call
+ * cudaMalloc -- an engine whose planner already handed all of HBM to its own
+ * pools, a process whose device memory belongs to another framework's
+ * allocator, or a latency-critical loop where cudaMalloc/cudaFree would
+ * synchronize the device.  Same arguments and result as sfk_moe_ffn.  Its
+ * scratch lives in one fixed array of SFK_NOALLOC_SCRATCH_BYTES compiled into
+ * the library (every GPU that loads the library holds it until exit); a shape
+ * whose scratch does not fit (roughly b*k*F*4 + b*k*F*1.2 + b*d*1.2 bytes) is
+ * rejected with SFK_ERR_INVALID_ARGUMENT before any work is queued.  The first
+ * call on a device looks up the array's device address, so make that first
+ * call before capturing work on that device into a stream graph.  All calls
+ * share the array: calls whose work overlaps on the GPU (other streams, other
+ * threads on the same device) race on it.  The call waits for its stream. */
+#define SFK_NOALLOC_SCRATCH_BYTES (4u << 20)
+SFK_API sfk_status sfk_moe_ffn_noalloc(int type_gu, int type_down, const void *dev_gate, const void *dev_up,
+                                       const void *dev_down, int32_t n_expert, int64_t d, int64_t F,
+                                       const float *dev_x, const float *dev_res, const int32_t *dev_ids,
+                                       const float *dev_w, int32_t b, int32_t k, float *dev_out, void *stream);
+
 /* GQA decode attention over a paged KV cache (engine.cpp:1751-1761 math):
  * q [b][Hq][hd] f32; k_pages/v_pages [n_pages][Hkv][16][hd] (f16 or f32 per
  * kv_type); page_table [b][max_pages]; positions [b]: sequence t attends over

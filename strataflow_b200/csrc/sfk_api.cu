@@ -35,6 +35,14 @@ namespace {
 
 thread_local std::string g_err = "no error";
 
+}  // namespace
+
+namespace sfk {
+void set_last_error(const char* msg) { g_err = msg; }
+}  // namespace sfk
+
+namespace {
+
 sfk_status fail(sfk_status st, const char* fmt, ...) {
   char buf[512];
   va_list ap;

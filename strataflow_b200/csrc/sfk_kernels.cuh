@@ -155,6 +155,8 @@ cudaError_t launch_quant_act(int act_type, const float* x, int b, int K, uint8_t
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t st);
 cudaError_t launch_route_build(const int* ids, const float* w, int b, int k, int n_expert, Route* r, int* status,
                                cudaStream_t st);
+// sets the message sfk_last_error() returns on the calling thread
+void set_last_error(const char* msg);
 cudaError_t launch_quant_act_gguf(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
 
 }  // namespace sfk
