@@ -174,9 +174,10 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
 
     B = args.batch
-    e2e_steps = min(args.steps, 32)
+    PROMPT = args.prompt
+    e2e_steps = 0 if args.no_e2e else min(args.steps, 32)
     n_ctx = PROMPT + args.warmup + args.steps + e2e_steps + 16
-    cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B)
+    cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B, n_layer=args.layers)
     t_load = time.perf_counter()
     eng = E.Engine.load(cfg, seed=SEED, device=local_rank)
     t_load = time.perf_counter() - t_load
@@ -225,17 +226,27 @@ def run_ours(args, rank: int, world: int, local_rank: int):
         t = torch.tensor([e2e_s], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_s = float(t.item())
-    e2e = world * B * e2e_steps / e2e_s
+    e2e = world * B * e2e_steps / e2e_s if e2e_steps else None
 
     # --- dominant kernel: routed gate/up (CUDA events per launch class) -------
     st = eng.stats()
+    if args.no_kernel_times:
+        if rank == 0:
+            print(json.dumps({"value": value, "ms_per_step": ms / args.steps, "steps": args.steps}), flush=True)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        eng.close()
+        return
     kt = eng.time_kernels(B, iters=64)
     peak, peak_kind = _peaks()
     gu_row = 4096 // 256 * 144
     uniq = 2 if B == 1 else None
     if uniq is None:
         uniq = min(8, 2 * B)
-    gu_bytes = uniq * 2 * 14336 * gu_row
+    # routed expert rows of gate and up; the routing prologue (F32 router
+    # weights + the token's hidden state) rides along in the same kernel
+    gu_bytes = uniq * 2 * 14336 * gu_row + (8 * 4096 * 4 + B * 4096 * 4 if kt["router"] == 0.0 else 0)
     gu_ms = kt["gate_up"]
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     kv_bytes_tok = 32 * 2 * 8 * 128 * 2 * (PROMPT + args.warmup + args.steps // 2)
@@ -252,7 +263,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "q4_k/q6_k weights x q8_k int8 dot (dp4a), fp32 accum", "data": "synthetic",
-            "config": {"workload": f"Mixtral-8x7B-shape decode b={B}: 512-token random prompt, then greedy decode",
+            "config": {"workload": f"Mixtral-8x7B-shape decode b={B}: {PROMPT}-token random prompt, then greedy decode",
                        "model": "mixtral-8x7b-shape (32L d4096 32q/8kv E8 top2 F14336 V32000)",
                        "global_batch": B * world, "seq_len": PROMPT, "parallelism": f"replicas x{world}",
                        "kv": "f16 paged (16-token pages, permuted pool)",
@@ -261,7 +272,7 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * B,
                     "d2h_bytes_per_step": 4 * B * cfg.n_vocab + 8 * B + 4},
             "gpu_launches": st["kernels_per_step"] * args.steps,
-            "roofline": {"bound": "hbm", "kernel": "stream_kernel<Q4_K> routed gate/up (mul_mat_id)",
+            "roofline": {"bound": "hbm", "kernel": "stream2_kernel<Q4_K,2>: routing + routed gate/up (mul_mat_id) + SwiGLU",
                          "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_kind": peak_kind, "traffic": None,
                          "bytes_per_launch": gu_bytes, "launch_ms": gu_ms},
@@ -287,6 +298,11 @@ def main():
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline sample")
+    ap.add_argument("--prompt", type=int, default=PROMPT, help="prompt tokens fed before decoding")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end loop")
+    ap.add_argument("--layers", type=int, default=32, help="model depth (32 = the benchmark; fewer for profiling)")
+    ap.add_argument("--no-kernel-times", action="store_true",
+                    help="print only the device-timed decode rate (short profiling runs)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))

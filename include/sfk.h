@@ -233,10 +233,11 @@ SFK_API sfk_status sfk_moe_ffn_noalloc(int type_gu, int type_down, const void *d
 
 /* GQA decode attention over a paged KV cache (engine.cpp:1751-1761 math):
  * q [b][Hq][hd] f32; k_pages/v_pages [n_pages][Hkv][16][hd] (f16 or f32 per
- * kv_type); page_table [b][max_pages]; positions [b]: sequence t attends over
- * 0..positions[t]; out [b][Hq*hd]. */
+ * kv_type); page_table [b][max_pages] of ids in [0, n_pages); positions [b]:
+ * sequence t attends over 0..positions[t]; out [b][Hq*hd].  A page id outside
+ * the pool is never dereferenced: the call returns SFK_ERR_RUNTIME. */
 SFK_API sfk_status sfk_attn_decode_paged(const float *dev_q, const void *dev_k_pages, const void *dev_v_pages, int32_t kv_type,
-                                 const int32_t *dev_page_table, int32_t max_pages, const int32_t *dev_positions,
+                                 int32_t n_pages, const int32_t *dev_page_table, int32_t max_pages, const int32_t *dev_positions,
                                  int32_t b, int32_t n_head, int32_t n_head_kv, int32_t head_dim, float *dev_out,
                                  void *stream);
 

@@ -26,7 +26,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
 # per-file extra flags: the synthetic generator must round exactly as written
 EXTRA = {"sfk_synth.cu": ["-fmad=false"]}
 SOURCES = ["sfk_kernels.cu", "sfk_synth.cu", "sfk_api.cu", "sfk_noalloc.cu"]
-HEADERS = ["sfk_device.cuh", "sfk_act.cuh", "sfk_dequant.cuh", "sfk_kernels.cuh"]
+HEADERS = ["sfk_device.cuh", "sfk_act.cuh", "sfk_dequant.cuh", "sfk_kernels.cuh", "sfk_route.cuh"]
 
 
 def nvcc() -> str:

@@ -142,7 +142,10 @@ sfk_status check_status_word(int* dev_status, cudaStream_t st) {
     int z = 0;
     cudaMemcpy(dev_status, &z, sizeof(int), cudaMemcpyHostToDevice);
     return fail(SFK_ERR_RUNTIME, "device reported error %d (%s)", h,
-                h == ERR_TIMEOUT ? "bounded wait expired" : h == ERR_BAD_ID ? "id out of range" : "bad position");
+                h == ERR_TIMEOUT    ? "bounded wait expired"
+                : h == ERR_BAD_ID   ? "id out of range"
+                : h == ERR_BAD_PAGE ? "page id outside the KV pool"
+                                    : "bad position");
   }
   return SFK_OK;
 }
@@ -193,6 +196,7 @@ struct sfk_engine {
   unsigned long long* argmax_key = nullptr;
   int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
   int* status = nullptr;
+  bool fused_route = false;  // the gate/up kernel routes in its prologue (no router kernel)
   int attn_cluster = 8;
   int attn_max_chunk = 0;
   // pinned staging
@@ -303,6 +307,7 @@ KvView kv_view(const sfk_engine* e, int l) {
   KvView kv{};
   kv.page_table = e->page_table;
   kv.max_pages = e->max_pages;
+  kv.n_pages = e->n_pages;
   kv.n_head_kv = hp.n_head_kv;
   kv.head_dim = e->hd;
   kv.f16 = hp.kv_type == SFK_KV_F16 ? 1 : 0;
@@ -310,6 +315,45 @@ KvView kv_view(const sfk_engine* e, int l) {
   kv.k = static_cast<uint8_t*>(e->k_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
   kv.v = static_cast<uint8_t*>(e->v_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
   return kv;
+}
+
+StreamParams gateup_params(const sfk_engine* e, int l, int b) {
+  const sfk_hparams& hp = e->hp;
+  const int d = hp.n_embd, F = hp.n_ff, k = hp.n_expert_used;
+  const LayerW& W = e->L[l];
+  StreamParams p{};
+  p.w0 = W.gate;
+  p.w1 = W.up;
+  p.rowstride = dev_row_bytes(hp.type_ffn_gu, d);
+  p.expert_stride = (int64_t)F * p.rowstride;
+  p.rows = F;
+  p.K = d;
+  p.wtype = hp.type_ffn_gu;
+  p.nmat = 2;
+  p.act_type = act_for(hp.type_ffn_gu);
+  p.row_align = 1;
+  p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b;
+  p.route = e->route;
+  if (e->fused_route) {
+    p.pro = PRO_ROUTE;  // ffn_norm + quantize + router + top-k in the prologue
+    p.x = e->ffn_inp;
+    p.norm_w = W.ffn_norm;
+    p.eps = hp.rms_eps;
+    p.w_r = W.router;
+    p.n_expert = hp.n_expert;
+  } else {
+    p.pro = PRO_LOAD;
+    p.qact = e->xq_ffn;
+    p.qact_stride = qact_bytes(d);
+  }
+  p.xq_by_pair = 0;
+  p.epi = EPI_GATEUP;
+  p.h = e->h;
+  p.hq = e->hq;
+  p.grp_counter = e->grp_counter;
+  p.h_act_type = act_for(hp.type_ffn_down);
+  p.status = e->status;
+  return p;
 }
 
 // Launch one kernel of the step: class `c` of layer `l` for b sequences.
@@ -361,6 +405,10 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.n_head = hp.n_head;
       p.rope = e->rope;
       p.pos = e->pos_cur;
+      if (l == 0) {  // the embedding kernel has read the argmax keys by now
+        p.clear_keys = e->argmax_key;
+        p.clear_n = b;
+      }
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
       CK(launch_stream(p, grid, st, pdl));
@@ -403,6 +451,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       return SFK_OK;
     }
     case K_ROUTER: {  // ffn_norm + router + top-k (engine.cpp:1909-1924)
+      if (e->fused_route) return SFK_OK;  // done inside the gate/up kernel
       const LayerW& W = e->L[l];
       RouterParams r{};
       r.x = e->ffn_inp;
@@ -419,31 +468,8 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       CK(launch_router(r, st, pdl));
       return SFK_OK;
     }
-    case K_GATEUP: {  // routed gate/up + SwiGLU (engine.cpp:1967-1969)
-      const LayerW& W = e->L[l];
-      StreamParams p{};
-      p.w0 = W.gate;
-      p.w1 = W.up;
-      p.rowstride = dev_row_bytes(hp.type_ffn_gu, d);
-      p.expert_stride = (int64_t)F * p.rowstride;
-      p.rows = F;
-      p.K = d;
-      p.wtype = hp.type_ffn_gu;
-      p.nmat = 2;
-      p.act_type = act_for(hp.type_ffn_gu);
-      p.row_align = 1;
-      p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b;
-      p.route = e->route;
-      p.pro = PRO_LOAD;
-      p.qact = e->xq_ffn;
-      p.qact_stride = qact_bytes(d);
-      p.xq_by_pair = 0;
-      p.epi = EPI_GATEUP;
-      p.h = e->h;
-      p.hq = e->hq;
-      p.grp_counter = e->grp_counter;
-      p.h_act_type = act_for(hp.type_ffn_down);
-      p.status = e->status;
+    case K_GATEUP: {  // (routing +) routed gate/up + SwiGLU (engine.cpp:1909-1924,1967-1969)
+      StreamParams p = gateup_params(e, l, b);
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
       CK(launch_stream(p, grid, st, pdl));
       return SFK_OK;
@@ -510,6 +536,7 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
   ++nk;
   for (int l = 0; l < e->hp.n_layer; ++l) {
     for (int c = K_QKV; c <= K_DOWN; ++c) {
+      if (c == K_ROUTER && e->fused_route) continue;
       if ((s = launch_one(e, c, l, b, greedy, true))) return s;
       ++nk;
     }
@@ -682,8 +709,9 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   }
   // step buffers
   e->attn_cluster = attn_cluster_for(e->max_pages * 16);
-  e->attn_max_chunk = (e->max_pages * 16 + e->attn_cluster - 1) / e->attn_cluster;
-  if (attn_smem_bytes(e->hd, hp->n_head / hp->n_head_kv, e->attn_max_chunk) > (size_t)SMEM_LIMIT) {
+  e->attn_max_chunk = (e->max_pages + e->attn_cluster - 1) / e->attn_cluster * 16;  // whole pages per CTA
+  if (attn_smem_bytes(e->hd, hp->n_head / hp->n_head_kv, hp->kv_type == SFK_KV_F16, e->attn_max_chunk) >
+      (size_t)SMEM_LIMIT) {
     sfk_engine_free(e);
     return fail(SFK_ERR_UNSUPPORTED, "n_ctx %d too long for the attention kernel's shared memory", hp->n_ctx);
   }
@@ -725,6 +753,14 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
       sfk_engine_free(e);
       return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
     }
+  }
+  if (hp->n_expert <= 64) {
+    // fold the router into the gate/up kernel when its warp-tile form fits
+    // (larger expert counts keep the one-CTA router kernel)
+    e->fused_route = true;
+    StreamParams gp = gateup_params(e, 0, B);
+    int grid = 0;
+    if (plan_stream(gp, e->sm_count, &grid) != SFK_OK || stream2_smem_bytes(gp) > SMEM_LIMIT) e->fused_route = false;
   }
   {
     // RoPE cos/sin for every position (ggml rope cache, mode NORMAL,
@@ -1017,7 +1053,7 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
     CK(cudaEventSynchronize(z));
     float ms = 0.0f;
     CK(cudaEventElapsedTime(&ms, a, z));
-    ms_out[c] = ms / iters;
+    ms_out[c] = (c == K_ROUTER && e->fused_route) ? 0.0f : ms / iters;  // routing is inside gate/up
   }
   cudaEventDestroy(a);
   cudaEventDestroy(z);
@@ -1216,10 +1252,11 @@ sfk_status sfk_moe_ffn(int type_gu, int type_down, const void* gate, const void*
   return check_status_word(sc->status, st);
 }
 
-sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp, int32_t kv_type,
+sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp, int32_t kv_type, int32_t n_pages,
                                  const int32_t* page_table, int32_t max_pages, const int32_t* positions, int32_t b,
                                  int32_t n_head, int32_t n_head_kv, int32_t head_dim, float* out, void* stream) {
-  if (!q || !kp || !vp || !page_table || !positions || !out || b < 1 || b > MAXB || n_head_kv < 1 ||
+  if (!q || !kp || !vp || !page_table || !positions || !out || b < 1 || b > MAXB || n_head_kv < 1 || n_pages < 1 ||
+      max_pages < 1 ||
       n_head % n_head_kv || (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) ||
       (kv_type != SFK_KV_F16 && kv_type != SFK_KV_F32))
     return fail(SFK_ERR_INVALID_ARGUMENT, "attn_decode_paged arguments");
@@ -1232,6 +1269,7 @@ sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp,
   a.kv.v = const_cast<void*>(vp);
   a.kv.page_table = page_table;
   a.kv.max_pages = max_pages;
+  a.kv.n_pages = n_pages;
   a.kv.n_head_kv = n_head_kv;
   a.kv.head_dim = head_dim;
   a.kv.f16 = kv_type == SFK_KV_F16 ? 1 : 0;
@@ -1239,8 +1277,8 @@ sfk_status sfk_attn_decode_paged(const float* q, const void* kp, const void* vp,
   a.b = b;
   a.n_head = n_head;
   a.cluster = attn_cluster_for(max_pages * 16);
-  a.max_chunk = (max_pages * 16 + a.cluster - 1) / a.cluster;
-  if (attn_smem_bytes(head_dim, n_head / n_head_kv, a.max_chunk) > (size_t)SMEM_LIMIT)
+  a.max_chunk = (max_pages + a.cluster - 1) / a.cluster * 16;  // whole pages per CTA
+  if (attn_smem_bytes(head_dim, n_head / n_head_kv, a.kv.f16, a.max_chunk) > (size_t)SMEM_LIMIT)
     return fail(SFK_ERR_UNSUPPORTED, "context of %d pages too long", max_pages);
   a.out = out;
   a.status = sc->status;

@@ -121,7 +121,7 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 // error codes written to the device status word
-enum : int { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_BAD_ID = 2, ERR_BAD_POS = 3 };
+enum : int { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_BAD_ID = 2, ERR_BAD_POS = 3, ERR_BAD_PAGE = 4 };
 
 // Bounded mbarrier wait: ~ 2^31 cycles (~1 s at 2 GHz) then records
 // ERR_TIMEOUT in *status and returns false.
@@ -212,6 +212,13 @@ struct XQ8 {
 #pragma unroll
     for (int i = 0; i < 8; ++i) c[i] = lds128(x + ((i * ng) + lane) * 16);
     s = lds128(x + 8 * ng * 16 + lane * 16);
+    d = *reinterpret_cast<const float*>(x + 8 * ng * 16 + ng * 16 + lane * 4);
+  }
+  // same, from a generic address (shared memory or global / L2)
+  __device__ __forceinline__ void load_any(const uint8_t* x, int ng, int lane) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = *reinterpret_cast<const uint4*>(x + ((i * ng) + lane) * 16);
+    s = *reinterpret_cast<const uint4*>(x + 8 * ng * 16 + lane * 16);
     d = *reinterpret_cast<const float*>(x + 8 * ng * 16 + ng * 16 + lane * 4);
   }
 };

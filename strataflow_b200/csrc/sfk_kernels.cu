@@ -31,6 +31,7 @@
 #include "sfk_device.cuh"
 #include "sfk_kernels.cuh"
 #include "sfk_dequant.cuh"
+#include "sfk_route.cuh"
 
 namespace sfk {
 
@@ -68,12 +69,16 @@ __host__ __device__ inline StreamPlan make_plan(const StreamParams& p) {
   return s;
 }
 
+struct Plan2;
+int stream2_smem_bytes(const StreamParams& p);
+
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp) {
   const StreamPlan s = make_plan(p);
   if (n_stages) *n_stages = s.n_stages;
   if (stage_bytes) *stage_bytes = s.stage_bytes;
   if (rows_per_warp) *rows_per_warp = s.rows_per_warp;
-  return s.total;
+  const int v2 = stream2_smem_bytes(p);
+  return v2 <= 227 * 1024 ? v2 : s.total;
 }
 
 // consumer-only named barrier (the producer warp never joins it)
@@ -230,6 +235,10 @@ __device__ void epi_qkv(const StreamParams& p, const float* acc, int r0, int r1)
       const int rr = r - nq - (is_k ? 0 : nk);
       const int h = rr / hd, i0 = rr % hd;
       const int page = p.kv.page_table[t * p.kv.max_pages + pos / 16];
+      if (page < 0 || (p.kv.n_pages > 0 && page >= p.kv.n_pages)) {  // never write outside the pool
+        atomicExch(p.status, ERR_BAD_PAGE);
+        continue;
+      }
       const int64_t off = (((int64_t)page * Hkv + h) * 16 + (pos & 15)) * hd + i0;
       void* base = is_k ? p.kv.k : p.kv.v;
       if (p.kv.f16) {
@@ -328,13 +337,39 @@ __device__ void epi_lmhead(const StreamParams& p, const float* acc, int r0, int 
   }
 }
 
+__device__ void run_epilogue(const StreamParams& p, const float* acc, int r0, int r1, double* red) {
+  switch (p.epi) {
+    case EPI_STORE: {
+      const int nr = r1 - r0;
+      for (int idx = threadIdx.x; idx < nr * p.n_pairs; idx += NW * 32) {
+        const int row = idx % nr, pr = idx / nr;
+        p.y[(int64_t)pr * p.y_stride + r0 + row] = acc[row * p.n_pairs + pr];
+      }
+      break;
+    }
+    case EPI_RESID: {
+      const int nr = r1 - r0;
+      for (int idx = threadIdx.x; idx < nr * p.b; idx += NW * 32) {
+        const int row = idx % nr, t = idx / nr;
+        const float v = acc[row * p.n_pairs + t];
+        p.y[(int64_t)t * p.y_stride + r0 + row] = p.res ? __fadd_rn(v, p.res[(int64_t)t * p.y_stride + r0 + row]) : v;
+      }
+      break;
+    }
+    case EPI_QKV: epi_qkv(p, acc, r0, r1); break;
+    case EPI_GATEUP: epi_gateup(p, acc, r0, r1, reinterpret_cast<int*>(red)); break;
+    case EPI_DOWN: epi_down(p, acc, r0, r1); break;
+    case EPI_LMHEAD: epi_lmhead(p, acc, r0, r1, reinterpret_cast<unsigned long long*>(red)); break;
+    default: break;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // the streaming kernel
 // ---------------------------------------------------------------------------
 template <int WT>
 __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  pdl_launch_dependents();
   const StreamPlan pl = make_plan(p);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem);
   uint64_t* empty = full + pl.n_stages;
@@ -366,14 +401,22 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
   if (warp == NW) {
     // ------------------------------ producer ------------------------------
     if (lane != 0) return;
+    bool waited = false;
     if (p.route) {
       pdl_wait();  // routed experts are known only after the router ran
+      pdl_launch_dependents();
+      waited = true;
       tw.n_slots = p.route->n_slots;
     }
     uint32_t it = 0;
     for (tw.begin(); !tw.done(); tw.next(), ++it) {
       const int s = it % pl.n_stages;
       if (it >= (uint32_t)pl.n_stages) {
+        if (!waited) {  // the ring is full: from here on the consumers pace the copies
+          pdl_wait();
+          pdl_launch_dependents();
+          waited = true;
+        }
         if (!mbar_wait_bounded(&empty[s], ((it / pl.n_stages) - 1) & 1, p.status)) break;
       }
       const int ng = group_units(p.K, tw.g);
@@ -389,12 +432,17 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
           bulk_g2s(dst + (m * pl.rows_tile + r) * gb, base + (int64_t)(rbase + r) * p.rowstride, gb, &full[s]);
       }
     }
-    if (!p.route) pdl_wait();
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
     return;
   }
 
   // ------------------------------ consumers ------------------------------
   pdl_wait();
+  pdl_launch_dependents();
+  if (p.clear_keys && blockIdx.x == 0 && threadIdx.x < p.clear_n) p.clear_keys[threadIdx.x] = 0ull;
   const int nacc = (r1 > r0 ? (r1 - r0) : 0) * p.n_pairs * p.nmat;
   for (int i = threadIdx.x; i < nacc; i += NW * 32) acc[i] = 0.0f;
   if (p.route) tw.n_slots = p.route->n_slots;
@@ -444,33 +492,275 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
     if (lane == 0) mbar_arrive(&empty[s]);
   }
   (void)ng_full;
+  (void)ok;
   consumer_sync();
-  if (!ok || r0 >= r1) return;
+  if (*(volatile int*)p.status == ERR_TIMEOUT || r0 >= r1) return;  // uniform across the consumers
 
-  switch (p.epi) {
-    case EPI_STORE: {
-      const int nr = r1 - r0;
-      for (int idx = threadIdx.x; idx < nr * p.n_pairs; idx += NW * 32) {
-        const int row = idx % nr, pr = idx / nr;
-        p.y[(int64_t)pr * p.y_stride + r0 + row] = acc[row * p.n_pairs + pr];
-      }
-      break;
-    }
-    case EPI_RESID: {
-      const int nr = r1 - r0;
-      for (int idx = threadIdx.x; idx < nr * p.b; idx += NW * 32) {
-        const int row = idx % nr, t = idx / nr;
-        const float v = acc[row * p.n_pairs + t];
-        p.y[(int64_t)t * p.y_stride + r0 + row] = p.res ? __fadd_rn(v, p.res[(int64_t)t * p.y_stride + r0 + row]) : v;
-      }
-      break;
-    }
-    case EPI_QKV: epi_qkv(p, acc, r0, r1); break;
-    case EPI_GATEUP: epi_gateup(p, acc, r0, r1, reinterpret_cast<int*>(red)); break;
-    case EPI_DOWN: epi_down(p, acc, r0, r1); break;
-    case EPI_LMHEAD: epi_lmhead(p, acc, r0, r1, reinterpret_cast<unsigned long long*>(red)); break;
-    default: break;
+  run_epilogue(p, acc, r0, r1, red);
+}
+
+// ---------------------------------------------------------------------------
+// stream2_kernel: warp-owned tiles.  A tile is up to 4 consecutive full rows
+// of each of the nmat matrices (all groups of K), moved by one bulk copy per
+// matrix into a per-warp ring of S2_STAGES stages; tiles go to the consumer
+// warps round-robin, so 8 x S2_STAGES tiles are in flight per SM and each
+// warp's per-tile bookkeeping is spread over up to 8 row dots.  The row sums
+// keep the fixed order of the other kernel (unit partials -> 32-lane
+// butterfly per group -> groups added in order), computed for 8 rows at once
+// with a transposed butterfly (9 shuffles instead of 40).
+// ---------------------------------------------------------------------------
+constexpr int S2_STAGES = 2;
+constexpr int S2_MAXROWS = 4;
+
+struct Plan2 {
+  int tile_rows, tile_bytes, ring_off, xq_off, acc_off, red_off, route_off, xn_off, seg_off, probs_off, total;
+  int xq_smem, xq_vec_bytes;
+};
+
+__host__ __device__ inline Plan2 make_plan2(const StreamParams& p) {
+  Plan2 q;
+  const int64_t rs = p.rowstride;
+  int64_t R = (12 * 1024) / (p.nmat * rs);
+  if (R < 1) R = 1;
+  if (R > S2_MAXROWS) R = S2_MAXROWS;
+  q.tile_rows = (int)R;
+  q.tile_bytes = (int)(R * p.nmat * rs);
+  q.ring_off = 2 * NW * S2_STAGES * 8 < 128 ? 128 : 2 * NW * S2_STAGES * 8;
+  q.xq_off = q.ring_off + NW * S2_STAGES * q.tile_bytes;
+  const int64_t xq_all = (int64_t)p.n_vec * qact_bytes(p.K);
+  q.xq_smem = (p.pro == PRO_QUANT) || (p.pro == PRO_ROUTE) || (xq_all <= 64 * 1024) ? 1 : 0;
+  q.xq_vec_bytes = (int)qact_bytes(p.K);
+  q.acc_off = q.xq_off + (q.xq_smem ? (int)((xq_all + 15) & ~(int64_t)15) : 0);
+  q.red_off = q.acc_off + ((p.rows_per_cta * p.n_pairs * p.nmat * 4 + 15) & ~15);
+  q.route_off = q.red_off + 64 * 8;
+  const bool rt = p.pro == PRO_ROUTE;
+  q.xn_off = q.route_off + (rt ? (int)((sizeof(Route) + 15) & ~15) : 0);
+  q.seg_off = q.xn_off + (rt ? p.K * 4 : 0);
+  q.probs_off = q.seg_off + (rt ? p.n_expert * 4 * 8 : 0);
+  q.total = q.probs_off + (rt ? ((p.n_expert * 4 + 15) & ~15) : 0) + 16;  // + the route-ready mbarrier
+  return q;
+}
+
+struct ConsumerSync {
+  __device__ void operator()() const { consumer_sync(); }
+};
+
+// Sum 8 lane-distributed values over the warp with the 32-lane butterfly
+// (p + p^16, then ^8, ^4, ^2, ^1) applied to each value, exchanging two values
+// per shuffle while lanes still split them.  Value v ends in the lanes with
+// bit 2 = v>>2, bit 3 = (v>>1)&1, bit 4 = v&1.
+__device__ __forceinline__ float reduce8(const float v[8], int lane) {
+  const bool b16 = lane & 16, b8 = lane & 8, b4 = lane & 4;
+  float w[4], x[2];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float A = v[2 * i], B = v[2 * i + 1];
+    const float r = __shfl_xor_sync(0xffffffffu, b16 ? A : B, 16);
+    w[i] = b16 ? __fadd_rn(B, r) : __fadd_rn(A, r);
   }
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float A = w[2 * j], B = w[2 * j + 1];
+    const float r = __shfl_xor_sync(0xffffffffu, b8 ? A : B, 8);
+    x[j] = b8 ? __fadd_rn(B, r) : __fadd_rn(A, r);
+  }
+  float y;
+  {
+    const float r = __shfl_xor_sync(0xffffffffu, b4 ? x[0] : x[1], 4);
+    y = b4 ? __fadd_rn(x[1], r) : __fadd_rn(x[0], r);
+  }
+  y = __fadd_rn(y, __shfl_xor_sync(0xffffffffu, y, 2));
+  y = __fadd_rn(y, __shfl_xor_sync(0xffffffffu, y, 1));
+  return y;
+}
+
+int stream2_smem_bytes(const StreamParams& p) { return make_plan2(p).total; }
+
+template <int WT>
+__device__ __forceinline__ float unit_dot_x(const uint8_t* wg, const XQ8& x, int ng, int lane) {
+  if constexpr (WT == T_Q4_K) {
+    WQ4K w;
+    w.load(wg, ng, lane);
+    return dot_unit_q4k(w, x, lane);
+  } else if constexpr (WT == T_Q6_K) {
+    WQ6K w;
+    w.load(wg, ng, lane);
+    return dot_unit_q6k(w, x);
+  } else {
+    WQ80 w;
+    w.load(wg, ng, lane);
+    return dot_unit_q80(w, x);
+  }
+}
+
+template <int WT, int NMAT>
+__global__ void __launch_bounds__((NW + 1) * 32, 1) stream2_kernel(const StreamParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const Plan2 pl = make_plan2(p);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NW][S2_STAGES]
+  uint64_t* empty = full + NW * S2_STAGES;
+  uint8_t* ring = smem + pl.ring_off;
+  uint8_t* xq_s = smem + pl.xq_off;
+  float* acc = reinterpret_cast<float*>(smem + pl.acc_off);
+  double* red = reinterpret_cast<double*>(smem + pl.red_off);
+  Route* sroute = reinterpret_cast<Route*>(smem + pl.route_off);
+  uint64_t* route_bar = reinterpret_cast<uint64_t*>(smem + pl.total - 16);
+  const bool self_route = p.pro == PRO_ROUTE;
+  const Route* rt = self_route ? sroute : p.route;
+  const bool routed = rt != nullptr;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r0 = blockIdx.x * p.rows_per_cta;
+  const int r1 = min(p.rows, r0 + p.rows_per_cta);
+  const int G = n_groups(p.K);
+  const int R = pl.tile_rows;
+  const int n_rb = r0 < r1 ? (r1 - r0 + R - 1) / R : 0;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NW * S2_STAGES; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(route_bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  if (warp == NW) {
+    // ------------------------------ producer ------------------------------
+    if (lane != 0) return;
+    int n_slots = 1;
+    bool waited = false;
+    if (self_route) {
+      // the consumers route the step first (after their wait on the previous
+      // kernel); the experts are known after that
+      if (!mbar_wait_bounded(route_bar, 0, p.status)) return;
+      pdl_launch_dependents();
+      waited = true;
+      n_slots = rt->n_slots;
+    } else if (routed) {
+      pdl_wait();  // routed experts are known only after the router ran
+      pdl_launch_dependents();
+      waited = true;
+      n_slots = rt->n_slots;
+    }
+    const int n_tiles = n_rb * n_slots;
+    for (int it = 0; it < n_tiles; ++it) {
+      const int w = it % NW, kk = it / NW;
+      const int bi = w * S2_STAGES + kk % S2_STAGES, use = kk / S2_STAGES;
+      if (use > 0 && !waited) {  // the ring is full: from here on the consumers pace the copies
+        pdl_wait();
+        pdl_launch_dependents();
+        waited = true;
+      }
+      if (use > 0 && !mbar_wait_bounded(&empty[bi], (use - 1) & 1, p.status)) break;
+      const int rb = it / n_slots, si = it % n_slots;
+      const int rbase = r0 + rb * R;
+      const int nrows = min(R, r1 - rbase);
+      const uint32_t bytes = (uint32_t)(nrows * p.rowstride);
+      mbar_arrive_expect_tx(&full[bi], bytes * NMAT);
+      const int expert = routed ? rt->slot_expert[si] : 0;
+      const int64_t eoff = (int64_t)expert * p.expert_stride + (int64_t)rbase * p.rowstride;
+      uint8_t* dst = ring + (int64_t)bi * pl.tile_bytes;
+#pragma unroll
+      for (int m = 0; m < NMAT; ++m)
+        bulk_g2s(dst + (int64_t)m * R * p.rowstride, (m == 0 ? p.w0 : p.w1) + eoff, bytes, &full[bi]);
+    }
+    if (!waited) {
+      pdl_wait();
+      pdl_launch_dependents();
+    }
+    return;
+  }
+
+  // ------------------------------ consumers ------------------------------
+  if (self_route) {
+    // the router weights are static: pull this CTA's share toward L2 first
+    const char* wb = reinterpret_cast<const char*>(p.w_r);
+    const int64_t nbytes = (int64_t)p.n_expert * p.K * 4;
+    for (int64_t o = ((int64_t)blockIdx.x * NW * 32 + threadIdx.x) * 128; o < nbytes;
+         o += (int64_t)gridDim.x * NW * 32 * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (p.clear_keys && blockIdx.x == 0 && threadIdx.x < p.clear_n) p.clear_keys[threadIdx.x] = 0ull;
+  if (self_route) {
+    float* xn_s = reinterpret_cast<float*>(smem + pl.xn_off);
+    double* seg_s = reinterpret_cast<double*>(smem + pl.seg_off);
+    float* probs_s = reinterpret_cast<float*>(smem + pl.probs_off);
+    for (int t = 0; t < p.b; ++t)
+      route_one<NW>(p.x + (int64_t)t * p.K, p.norm_w, p.w_r, p.K, p.n_expert, p.k, p.eps, p.act_type,
+                    xq_s + (int64_t)t * pl.xq_vec_bytes, xn_s, seg_s, probs_s, red, &sroute->ids[t * p.k],
+                    &sroute->w[t * p.k], nullptr, ConsumerSync{});
+    if (threadIdx.x == 0) {
+      build_slots(sroute->ids, p.b * p.k, sroute);
+      sroute->k = p.k;
+      sroute->b = p.b;
+      mbar_arrive(route_bar);  // release: the producer may stream the routed experts
+    }
+    consumer_sync();
+    if (blockIdx.x == 0) {  // publish the routing for the down kernel and the host
+      const int* src = reinterpret_cast<const int*>(sroute);
+      int* dst = reinterpret_cast<int*>(const_cast<Route*>(p.route));
+      for (int i = threadIdx.x; i < (int)(sizeof(Route) / 4); i += NW * 32) dst[i] = src[i];
+    }
+  } else if (pl.xq_smem) {
+    if (p.pro == PRO_QUANT)
+      prologue_quant(p, xq_s, pl.xq_vec_bytes, red);
+    else
+      prologue_load(p, xq_s, pl.xq_vec_bytes, -1);
+  }
+  consumer_sync();
+  const int n_slots = routed ? rt->n_slots : 1;
+  const uint8_t* xbase = pl.xq_smem ? xq_s : p.qact;
+  const int64_t xstride = pl.xq_smem ? (int64_t)pl.xq_vec_bytes : p.qact_stride;
+  const int n_tiles = n_rb * n_slots;
+  const int V = R * NMAT;
+  XQ8 xc;
+  int cached_vi = -1;
+  for (int it = warp; it < n_tiles; it += NW) {
+    const int kk = it / NW;
+    const int bi = warp * S2_STAGES + kk % S2_STAGES, use = kk / S2_STAGES;
+    if (!mbar_wait_bounded(&full[bi], use & 1, p.status)) break;
+    const int rb = it / n_slots, si = it % n_slots;
+    const int rbase = r0 + rb * R;
+    const int nrows = min(R, r1 - rbase);
+    const uint8_t* tile = ring + (int64_t)bi * pl.tile_bytes;
+    int pb = 0, pe = p.b;
+    if (routed) { pb = rt->slot_off[si]; pe = rt->slot_off[si + 1]; }
+    for (int pi = pb; pi < pe; ++pi) {
+      const int pair = routed ? rt->slot_pairs[pi] : pi;
+      const int vi = p.xq_by_pair ? pair : (routed ? pair / p.k : pair);
+      float accv = 0.0f;
+      for (int g = 0; g < G; ++g) {
+        const int ng = group_units(p.K, g);
+        if (G > 1 || vi != cached_vi) {
+          if (lane < ng) xc.load_any(xbase + (int64_t)vi * xstride + qact_group_offset(g), ng, lane);
+          cached_vi = (G == 1) ? vi : -1;
+        }
+        const int64_t goff = group_offset(WT, p.K, g);
+        float part[8];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          part[v] = 0.0f;
+          const int r = NMAT == 2 ? (v >> 1) : v, m = NMAT == 2 ? (v & 1) : 0;
+          if (v < V && r < nrows && lane < ng)
+            part[v] = unit_dot_x<WT>(tile + ((int64_t)m * R + r) * p.rowstride + goff, xc, ng, lane);
+        }
+        accv = __fadd_rn(accv, reduce8(part, lane));
+      }
+      if ((lane & 3) == 0) {
+        const int v = ((lane >> 2) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 4) & 1);
+        const int r = NMAT == 2 ? (v >> 1) : v, m = NMAT == 2 ? (v & 1) : 0;
+        if (v < V && r < nrows) acc[((rbase - r0 + r) * p.n_pairs + pair) * NMAT + m] = accv;
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[bi]);
+  }
+  consumer_sync();
+  if (*(volatile int*)p.status == ERR_TIMEOUT || r0 >= r1) return;  // uniform across the consumers
+  run_epilogue(p, acc, r0, r1, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -480,20 +770,54 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
 //   s_j   = kq_j * (1/sqrt(hd)); M = max_j s_j          ggml_soft_max_ext
 //   p_j   = exp(s_j - M); S = sum_j (double) p_j; p'_j = p_j * (float)(1/S)
 //   o_i   = (float) sum_j (double)(v_ji * p'_j)         ggml_mul_mat F32
-// One thread-block cluster per (token, kv head); each CTA of the cluster owns
-// a contiguous slice of positions.  The cross-CTA steps (global max, global
-// sum, the final o reduction) go through distributed shared memory with
-// cluster barriers, so the two-pass softmax is exact without a second kernel.
-// 128 threads; the GQA group's query heads share each K/V load.
+// One thread-block cluster per (token, kv head); CTA r of the cluster owns a
+// contiguous run of whole pages.  A KV page of one head ([16][hd], 4 KB in f16
+// at hd 128) is contiguous in the pool, so each page arrives in shared memory
+// by one bulk copy into a ring of page slots (one ring for K, one for V).
+// Pages that earlier steps wrote are requested before the wait on the previous
+// kernel; only the page holding the current position waits for it.  The
+// cross-CTA steps (global max, global sum, the output reduction) go through
+// distributed shared memory with cluster barriers, so the two-pass softmax is
+// exact in one kernel.  The GQA group's query heads share every K/V page.
 // ---------------------------------------------------------------------------
-constexpr int ATT_THREADS = 128;
-constexpr int ATT_MAXG = 16;  // max query heads per kv head
+constexpr int ATT_NW = 8;
+constexpr int ATT_THREADS = ATT_NW * 32;
+constexpr int ATT_MAXG = 16;       // max query heads per kv head
+constexpr int ATT_MAXC = 16;       // max CTAs per cluster
+constexpr int ATT_RING = 64 * 1024;  // bytes of K + V page slots
 
-template <int HD>
+struct AttnPlan {
+  int ns, slot_bytes;
+  int kring, vring, qs, opart, sc, lsum, wred, gstd, lmax, invs, gst, total;
+};
+
+__host__ __device__ inline int al16(int v) { return (v + 15) & ~15; }
+
+__host__ __device__ inline AttnPlan make_attn_plan(int hd, int gqa, int f16, int max_chunk) {
+  AttnPlan a;
+  a.slot_bytes = 16 * hd * (f16 ? 2 : 4);
+  int ns = ATT_RING / (2 * a.slot_bytes);
+  ns = ns < 2 ? 2 : (ns > 32 ? 32 : ns);
+  a.ns = ns;
+  a.kring = (2 * ns * 8 + 127) & ~127;
+  a.vring = a.kring + ns * a.slot_bytes;
+  a.qs = a.vring + ns * a.slot_bytes;
+  a.opart = a.qs + al16(gqa * hd * 4);
+  a.sc = a.opart + gqa * hd * 8;
+  a.lsum = a.sc + al16(gqa * max_chunk * 4);
+  a.wred = a.lsum + al16(gqa * 8);
+  a.gstd = a.wred + ATT_NW * gqa * 8;
+  a.lmax = a.gstd + ATT_MAXC * gqa * 8;
+  a.invs = a.lmax + al16(gqa * 4);
+  a.gst = a.invs + al16(gqa * 4);
+  a.total = a.gst + al16(ATT_MAXC * gqa * 4);
+  return a;
+}
+
+template <int HD, int F16>
 __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   namespace cg = cooperative_groups;
-  pdl_launch_dependents();
-  pdl_wait();
+  extern __shared__ __align__(128) uint8_t asmem[];
   cg::cluster_group cl = cg::this_cluster();
   const int C = (int)cl.num_blocks();
   const int rank = (int)cl.block_rank();
@@ -501,90 +825,154 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   const int Hkv = p.kv.n_head_kv;
   const int gqa = p.n_head / Hkv;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int PER = HD / 32;  // output dims per lane
-  constexpr int QD = HD / 4;    // dims per lane in the score pass (4 lanes per position)
+  const int mc = p.max_chunk;
+  const AttnPlan pl = make_attn_plan(HD, gqa, F16, mc);
+  uint64_t* kfull = reinterpret_cast<uint64_t*>(asmem);
+  uint64_t* vfull = kfull + pl.ns;
+  uint8_t* kring = asmem + pl.kring;
+  uint8_t* vring = asmem + pl.vring;
+  float* qs = reinterpret_cast<float*>(asmem + pl.qs);
+  double* opart = reinterpret_cast<double*>(asmem + pl.opart);
+  float* sc = reinterpret_cast<float*>(asmem + pl.sc);
+  double* lsum = reinterpret_cast<double*>(asmem + pl.lsum);
+  double* wred = reinterpret_cast<double*>(asmem + pl.wred);
+  double* gstd = reinterpret_cast<double*>(asmem + pl.gstd);
+  float* lmax = reinterpret_cast<float*>(asmem + pl.lmax);
+  float* invs = reinterpret_cast<float*>(asmem + pl.invs);
+  float* gst = reinterpret_cast<float*>(asmem + pl.gst);
 
-  // shared layout (attn_smem_bytes): opart [gqa][HD] f64 | qs [gqa][HD] f32 |
-  // lsum [gqa] f64 | wred [4][gqa] f64 | lmax [gqa] f32 | sc [gqa][max_chunk] f32
-  extern __shared__ __align__(16) uint8_t asmem[];
-  double* opart = reinterpret_cast<double*>(asmem);
-  float* qs = reinterpret_cast<float*>(opart + gqa * HD);
-  double* lsum = reinterpret_cast<double*>(qs + gqa * HD);
-  double* wred = lsum + gqa;
-  float* lmax = reinterpret_cast<float*>(wred + 4 * gqa);
-  float* sc = lmax + ((gqa + 3) & ~3);
+  // Positions and the page table were written before the previous kernel
+  // started (every kernel of the step lets its successor launch only after
+  // its own wait on its predecessor), so they are read before the wait.
   int n_kv = p.pos[t] + 1;
   if (n_kv < 1 || n_kv > p.kv.max_pages * 16) {  // outside the page table: no access, report
     if (tid == 0 && rank == 0) atomicExch(p.status, ERR_BAD_POS);
     n_kv = 0;
   }
-  const int chunk = (n_kv + C - 1) / C;
-  const int j0 = rank * chunk;
-  const int nloc = max(0, min(n_kv, j0 + chunk) - j0);
-  const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
-  const int* ptab = p.kv.page_table + t * p.kv.max_pages;
-  const int q0 = hk * gqa;
+  if ((((n_kv + 15) >> 4) + C - 1) / C * 16 > mc) {  // score buffer too small: no access, report
+    if (tid == 0 && rank == 0) atomicExch(p.status, ERR_BAD_POS);
+    n_kv = 0;
+  }
+  const int np_tot = (n_kv + 15) >> 4;
+  const int ppc = (np_tot + C - 1) / C;
+  const int pb = min(np_tot, rank * ppc);
+  const int np = min(np_tot, pb + ppc) - pb;
+  const int nloc = max(0, min(n_kv, (pb + np) * 16) - pb * 16);
+  const int last_page = (n_kv - 1) >> 4;  // the page this step's K/V row lands in
+  const int* ptab = p.kv.page_table + (int64_t)t * p.kv.max_pages;
+  const int64_t page_stride = (int64_t)Hkv * pl.slot_bytes;
+  const int64_t head_off = (int64_t)hk * pl.slot_bytes;
 
-  for (int i = tid; i < gqa * HD; i += ATT_THREADS) qs[i] = p.q[((int64_t)t * p.n_head + q0) * HD + i];
+  // thread 0: bring page i (local index) of K or V into its ring slot
+  auto issue = [&](int isv, int i) {
+    const int slot = i % pl.ns;
+    uint64_t* bar = (isv ? vfull : kfull) + slot;
+    const int pg = ptab[pb + i];
+    if (pg < 0 || (p.kv.n_pages > 0 && pg >= p.kv.n_pages)) {  // never copy from outside the pool
+      atomicExch(p.status, ERR_BAD_PAGE);
+      mbar_arrive(bar);
+      return;
+    }
+    mbar_arrive_expect_tx(bar, (uint32_t)pl.slot_bytes);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(isv ? p.kv.v : p.kv.k) + pg * page_stride + head_off;
+    bulk_g2s((isv ? vring : kring) + (int64_t)slot * pl.slot_bytes, src, (uint32_t)pl.slot_bytes, bar);
+  };
+
+  if (tid == 0) {
+    for (int i = 0; i < pl.ns; ++i) {
+      mbar_init(&kfull[i], 1);
+      mbar_init(&vfull[i], 1);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int npre = min(np, pl.ns);
+  if (tid == 0) {
+    for (int i = 0; i < npre; ++i)
+      if (pb + i < last_page) issue(0, i);
+    for (int i = 0; i < npre; ++i)
+      if (pb + i < last_page) issue(1, i);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  if (tid == 0) {
+    for (int i = 0; i < npre; ++i)
+      if (pb + i >= last_page) issue(0, i);
+    for (int i = 0; i < npre; ++i)
+      if (pb + i >= last_page) issue(1, i);
+  }
+  const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
+  for (int i = tid; i < gqa * HD; i += ATT_THREADS) qs[i] = p.q[((int64_t)t * p.n_head + hk * gqa) * HD + i];
   __syncthreads();
 
-  // ---- pass 1: scores of this CTA's positions; 8 positions per warp step
-  const int n_oct = (nloc + 7) >> 3;
-  for (int item = warp; item < gqa * n_oct; item += ATT_THREADS / 32) {
-    const int h = item % gqa, oct = item / gqa;
-    const int jl = oct * 8 + (lane >> 2);
-    const int c = lane & 3;
-    double acc = 0.0;
-    if (jl < nloc) {
-      const int j = j0 + jl;
-      const int64_t off = (((int64_t)ptab[j >> 4] * Hkv + hk) * 16 + (j & 15)) * HD + c * QD;
-      const float* qh = qs + h * HD + c * QD;
-      if (p.kv.f16) {
-        const __half* kr = reinterpret_cast<const __half*>(p.kv.k) + off;
-#pragma unroll
-        for (int i = 0; i < QD; i += 8) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(kr + i);
+  // ---- K pages: scores.  LP lanes per position, 8 dims per lane
+  {
+    constexpr int LP = HD / 8;
+    constexpr int PPW = 32 / LP;
+    const int sub = lane / LP, dl = (lane % LP) * 8;
+    for (int i = 0; i < np; ++i) {
+      const int slot = i % pl.ns;
+      mbar_wait_bounded(&kfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
+      const uint8_t* kp = kring + (int64_t)slot * pl.slot_bytes;
+      for (int base = warp * PPW; base < 16; base += ATT_NW * PPW) {
+        const int jj = base + sub;
+        const int jl = i * 16 + jj;
+        float kf[8];
+        if constexpr (F16) {
+          const uint4 raw = lds128(kp + (jj * HD + dl) * 2);
           const __half2* hv = reinterpret_cast<const __half2*>(&raw);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float2 kf = __half22float2(hv[e]);
-            acc += (double)__fmul_rn(kf.x, qh[i + 2 * e]);
-            acc += (double)__fmul_rn(kf.y, qh[i + 2 * e + 1]);
+            const float2 f = __half22float2(hv[e]);
+            kf[2 * e] = f.x;
+            kf[2 * e + 1] = f.y;
           }
+        } else {
+          const uint4 r0 = lds128(kp + (jj * HD + dl) * 4);
+          const uint4 r1 = lds128(kp + (jj * HD + dl) * 4 + 16);
+          kf[0] = __uint_as_float(r0.x); kf[1] = __uint_as_float(r0.y);
+          kf[2] = __uint_as_float(r0.z); kf[3] = __uint_as_float(r0.w);
+          kf[4] = __uint_as_float(r1.x); kf[5] = __uint_as_float(r1.y);
+          kf[6] = __uint_as_float(r1.z); kf[7] = __uint_as_float(r1.w);
         }
-      } else {
-        const float* kr = reinterpret_cast<const float*>(p.kv.k) + off;
+        for (int h = 0; h < gqa; ++h) {
+          const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + dl);
+          const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + dl + 4);
+          double a = (double)__fmul_rn(kf[0], qa.x);
+          a += (double)__fmul_rn(kf[1], qa.y);
+          a += (double)__fmul_rn(kf[2], qa.z);
+          a += (double)__fmul_rn(kf[3], qa.w);
+          a += (double)__fmul_rn(kf[4], qb.x);
+          a += (double)__fmul_rn(kf[5], qb.y);
+          a += (double)__fmul_rn(kf[6], qb.z);
+          a += (double)__fmul_rn(kf[7], qb.w);
 #pragma unroll
-        for (int i = 0; i < QD; i += 4) {
-          const float4 kf = *reinterpret_cast<const float4*>(kr + i);
-          acc += (double)__fmul_rn(kf.x, qh[i]);
-          acc += (double)__fmul_rn(kf.y, qh[i + 1]);
-          acc += (double)__fmul_rn(kf.z, qh[i + 2]);
-          acc += (double)__fmul_rn(kf.w, qh[i + 3]);
+          for (int o = LP / 2; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+          if ((lane % LP) == 0 && jl < nloc) sc[h * mc + jl] = __fmul_rn((float)a, scale);
         }
       }
+      __syncthreads();  // every warp is done with the slot
+      if (tid == 0 && i + pl.ns < np) issue(0, i + pl.ns);
     }
-    acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-    acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-    if (c == 0 && jl < nloc) sc[h * p.max_chunk + jl] = __fmul_rn((float)acc, scale);
   }
-  __syncthreads();
   // local max per head
-  for (int h = warp; h < gqa; h += ATT_THREADS / 32) {
+  for (int h = warp; h < gqa; h += ATT_NW) {
     float m = -INFINITY;
-    for (int jl = lane; jl < nloc; jl += 32) m = fmaxf(m, sc[h * p.max_chunk + jl]);
+    for (int jl = lane; jl < nloc; jl += 32) m = fmaxf(m, sc[h * mc + jl]);
     m = warp_max(m);
     if (lane == 0) lmax[h] = m;
   }
   cl.sync();
-  // ---- pass 2: global max, exp, local sum
+  // ---- global max (one parallel gather of the cluster's maxima), exp, local sum
+  for (int i = tid; i < gqa * C; i += ATT_THREADS) gst[i] = cl.map_shared_rank(lmax, i % C)[i / C];
+  __syncthreads();
   for (int h = 0; h < gqa; ++h) {
     float M = -INFINITY;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, cl.map_shared_rank(lmax, r)[h]);
+    for (int r = 0; r < C; ++r) M = fmaxf(M, gst[h * C + r]);
     double s = 0.0;
     for (int jl = tid; jl < nloc; jl += ATT_THREADS) {
-      const float e = sfk_expf(__fsub_rn(sc[h * p.max_chunk + jl], M));
-      sc[h * p.max_chunk + jl] = e;
+      const float e = sfk_expf(__fsub_rn(sc[h * mc + jl], M));
+      sc[h * mc + jl] = e;
       s += (double)e;
     }
     s = warp_sum_d(s);
@@ -593,157 +981,116 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   __syncthreads();
   if (tid < gqa) {
     double s = 0.0;
-    for (int w = 0; w < ATT_THREADS / 32; ++w) s += wred[w * gqa + tid];
+    for (int w = 0; w < ATT_NW; ++w) s += wred[w * gqa + tid];
     lsum[tid] = s;
   }
   cl.sync();
-  // ---- pass 3: p' = p * (float)(1/S); o_i = sum_j (double)(v_ji * p'_j)
-  for (int h = warp; h < gqa; h += ATT_THREADS / 32) {
+  for (int i = tid; i < gqa * C; i += ATT_THREADS) gstd[i] = cl.map_shared_rank(lsum, i % C)[i / C];
+  __syncthreads();
+  if (tid < gqa) {
     double S = 0.0;
-    for (int r = 0; r < C; ++r) S += cl.map_shared_rank(lsum, r)[h];
-    const float inv = (float)(1.0 / S);
-    double o[PER];
+    for (int r = 0; r < C; ++r) S += gstd[tid * C + r];
+    invs[tid] = (float)(1.0 / S);
+  }
+  __syncthreads();
+
+  // ---- V pages: o_i = sum_j (double)(v_ji * p'_j); each thread owns pairs of
+  // output dims (at most ATT_MAXG * HD / 2 / ATT_THREADS of them)
+  constexpr int NPAIR = (ATT_MAXG * HD / 2 + ATT_THREADS - 1) / ATT_THREADS;
+  const int npairs = gqa * HD / 2;
+  double acc[2 * NPAIR];
 #pragma unroll
-    for (int i = 0; i < PER; ++i) o[i] = 0.0;
-    for (int jl = 0; jl < nloc; ++jl) {
-      const int j = j0 + jl;
-      const float pj = __fmul_rn(sc[h * p.max_chunk + jl], inv);
-      const int64_t off = (((int64_t)ptab[j >> 4] * Hkv + hk) * 16 + (j & 15)) * HD + lane * PER;
+  for (int i = 0; i < 2 * NPAIR; ++i) acc[i] = 0.0;
+  for (int i = 0; i < np; ++i) {
+    const int slot = i % pl.ns;
+    mbar_wait_bounded(&vfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
+    const uint8_t* vp = vring + (int64_t)slot * pl.slot_bytes;
+    const int jn = min(16, nloc - i * 16);
 #pragma unroll
-      for (int i = 0; i < PER; ++i) {
-        const float vv = p.kv.f16 ? __half2float(reinterpret_cast<const __half*>(p.kv.v)[off + i])
-                                  : reinterpret_cast<const float*>(p.kv.v)[off + i];
-        o[i] += (double)__fmul_rn(vv, pj);
+    for (int q2 = 0; q2 < NPAIR; ++q2) {
+      const int pi = tid + q2 * ATT_THREADS;
+      if (pi < npairs) {
+        const int h = (pi * 2) / HD, dd = (pi * 2) % HD;
+        const float inv = invs[h];
+        const float* sh = sc + h * mc + i * 16;
+        for (int jj = 0; jj < jn; ++jj) {
+          const float pj = __fmul_rn(sh[jj], inv);
+          float2 v;
+          if constexpr (F16)
+            v = __half22float2(*reinterpret_cast<const __half2*>(vp + (jj * HD + dd) * 2));
+          else
+            v = *reinterpret_cast<const float2*>(vp + (jj * HD + dd) * 4);
+          acc[2 * q2] += (double)__fmul_rn(v.x, pj);
+          acc[2 * q2 + 1] += (double)__fmul_rn(v.y, pj);
+        }
       }
     }
-#pragma unroll
-    for (int i = 0; i < PER; ++i) opart[h * HD + lane * PER + i] = o[i];
+    __syncthreads();  // every thread is done with the slot
+    if (tid == 0 && i + pl.ns < np) issue(1, i + pl.ns);
   }
-  cl.sync();
-  // ---- reduce the cluster's partial outputs on rank 0
-  if (rank == 0) {
-    for (int i = tid; i < gqa * HD; i += ATT_THREADS) {
-      double o = 0.0;
-      for (int r = 0; r < C; ++r) o += cl.map_shared_rank(opart, r)[i];
-      p.out[((int64_t)t * p.n_head + q0) * HD + i] = (float)o;
+#pragma unroll
+  for (int q2 = 0; q2 < NPAIR; ++q2) {
+    const int pi = tid + q2 * ATT_THREADS;
+    if (pi < npairs) {
+      opart[2 * pi] = acc[2 * q2];
+      opart[2 * pi + 1] = acc[2 * q2 + 1];
     }
   }
   cl.sync();
+  // ---- the cluster's partial outputs: CTA r reduces slice r (remote loads issued together)
+  {
+    const int nout = gqa * HD, per = (nout + C - 1) / C;
+    const int o1 = min(nout, (rank + 1) * per);
+    for (int o = rank * per + tid; o < o1; o += ATT_THREADS) {
+      double v[ATT_MAXC];
+#pragma unroll
+      for (int r = 0; r < ATT_MAXC; ++r) v[r] = r < C ? cl.map_shared_rank(opart, r)[o] : 0.0;
+      double s = 0.0;
+#pragma unroll
+      for (int r = 0; r < ATT_MAXC; ++r)
+        if (r < C) s += v[r];
+      p.out[((int64_t)t * p.n_head + hk * gqa) * HD + o] = (float)s;
+    }
+  }
+  cl.sync();  // no CTA leaves while another still reads its partials
 }
 
-size_t attn_smem_bytes(int hd, int gqa, int max_chunk) {
-  return (size_t)gqa * hd * 8 + (size_t)gqa * hd * 4 + (size_t)gqa * 8 + 4 * (size_t)gqa * 8 +
-         (size_t)((gqa + 3) & ~3) * 4 + (size_t)gqa * max_chunk * 4;
+size_t attn_smem_bytes(int hd, int gqa, int f16, int max_chunk) {
+  return (size_t)make_attn_plan(hd, gqa, f16, max_chunk).total;
 }
 
 // ---------------------------------------------------------------------------
-// router: ffn_norm -> quantized expert input; logits = W_r x (f32);
-// probs = softmax; top-k (descending, lower index on ties);
-// w = probs[ids] / max(sum, 6.103515625e-5)   (engine.cpp:1909-1924)
-// grid b, 256 threads.  The last CTA builds the slot lists.
+// router kernel (used when the routing is not folded into the gate/up kernel):
+// one CTA per token runs route_one; the last CTA builds the slot lists.
 // ---------------------------------------------------------------------------
-constexpr int RT_THREADS = 256;
+constexpr int RT_THREADS = 1024;
 constexpr int RT_MAXE = 512;
 
+struct BlockSync {
+  __device__ void operator()() const { __syncthreads(); }
+};
+
 __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p) {
-  pdl_launch_dependents();
+  const int t = blockIdx.x, tid = threadIdx.x;
+  {
+    // the router weights do not depend on the previous kernel: pull them
+    // toward L2 while it drains
+    const char* wb = reinterpret_cast<const char*>(p.w_r);
+    const int64_t nbytes = (int64_t)p.E * p.d * 4;
+    for (int64_t o = (int64_t)(t * RT_THREADS + tid) * 128; o < nbytes; o += (int64_t)gridDim.x * RT_THREADS * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
+  }
   pdl_wait();
+  pdl_launch_dependents();
   extern __shared__ __align__(16) uint8_t rsm[];
   float* xn = reinterpret_cast<float*>(rsm);  // [d]
   __shared__ double red[RT_THREADS / 32 + 1];
   __shared__ float probs[RT_MAXE];
+  __shared__ double seg[RT_MAXE * 4];
   __shared__ int last_flag;
-  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int d = p.d;
-  const float* x = p.x + (int64_t)t * d;
-  double s = 0.0;
-  for (int c = tid; c < d; c += RT_THREADS) s += (double)__fmul_rn(x[c], x[c]);
-  s = warp_sum_d(s);
-  if (lane == 0) red[warp] = s;
-  __syncthreads();
-  if (tid == 0) {
-    double tot = 0.0;
-    for (int w = 0; w < RT_THREADS / 32; ++w) tot += red[w];
-    red[RT_THREADS / 32] = tot;
-  }
-  __syncthreads();
-  const float mean = (float)(red[RT_THREADS / 32] / (double)d);
-  const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-  for (int c = tid; c < d; c += RT_THREADS) {
-    const float v = __fmul_rn(__fmul_rn(x[c], scale), p.norm_w[c]);
-    xn[c] = v;
-    if (p.xn) p.xn[(int64_t)t * d + c] = v;
-  }
-  __syncthreads();
-  uint8_t* xq = p.xq + (int64_t)t * qact_bytes(d);
-  for (int blk = warp; blk < d / QK_K; blk += RT_THREADS / 32) {
-    float v[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = xn[blk * QK_K + lane * 8 + i];
-    qact_put(p.act_type, xq, d, blk, v, lane);
-  }
-  // router logits (F32 weights)
-  // ggml F32 mul_mat: float products summed in double
-  for (int e = warp; e < p.E; e += RT_THREADS / 32) {
-    const float* wr = p.w_r + (int64_t)e * d;
-    double a = 0.0;
-    for (int c = lane * 4; c < d; c += 128) {
-      const float4 w4 = *reinterpret_cast<const float4*>(wr + c);
-      a += (double)__fmul_rn(w4.x, xn[c]);
-      a += (double)__fmul_rn(w4.y, xn[c + 1]);
-      a += (double)__fmul_rn(w4.z, xn[c + 2]);
-      a += (double)__fmul_rn(w4.w, xn[c + 3]);
-    }
-    a = warp_sum_d(a);
-    if (lane == 0) probs[e] = (float)a;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    // softmax (scale 1): max, e^(x-max), sum in double, * (float)(1/sum)
-    float mx = -INFINITY;
-    for (int e = lane; e < p.E; e += 32) mx = fmaxf(mx, probs[e]);
-    mx = warp_max(mx);
-    double sum = 0.0;
-    for (int e = lane; e < p.E; e += 32) {
-      const float ex = sfk_expf(__fsub_rn(probs[e], mx));
-      probs[e] = ex;
-      sum += (double)ex;
-    }
-    sum = warp_sum_d(sum);
-    const float inv = (float)(1.0 / sum);
-    for (int e = lane; e < p.E; e += 32) probs[e] = __fmul_rn(probs[e], inv);
-    __syncwarp();
-    // top-k by repeated warp argmax (lower index wins ties)
-    int ids[16];
-    float wsel[16];
-    double wsum = 0.0;
-    for (int j = 0; j < p.k; ++j) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int e = lane; e < p.E; e += 32) {
-        bool taken = false;
-        for (int jj = 0; jj < j; ++jj) taken |= (ids[jj] == e);
-        if (!taken && (probs[e] > bv || (probs[e] == bv && e < bi))) { bv = probs[e]; bi = e; }
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      ids[j] = bi;
-      wsel[j] = bv;
-      wsum += (double)bv;
-    }
-    float ws = (float)wsum;
-    if (ws < 6.103515625e-5f) ws = 6.103515625e-5f;
-    if (lane == 0) {
-      for (int j = 0; j < p.k; ++j) {
-        p.route->ids[t * p.k + j] = ids[j];
-        p.route->w[t * p.k + j] = __fdiv_rn(wsel[j], ws);
-      }
-    }
-  }
+  route_one<RT_THREADS / 32>(p.x + (int64_t)t * p.d, p.norm_w, p.w_r, p.d, p.E, p.k, p.eps, p.act_type,
+                             p.xq + (int64_t)t * qact_bytes(p.d), xn, seg, probs, red, &p.route->ids[t * p.k],
+                             &p.route->w[t * p.k], p.xn ? p.xn + (int64_t)t * p.d : nullptr, BlockSync{});
   __threadfence();
   __syncthreads();
   if (tid == 0) {
@@ -753,27 +1100,11 @@ __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p
   __syncthreads();
   if (!last_flag || tid != 0) return;
   __threadfence();
-  // slot lists: distinct experts ascending, each with its pairs ascending
   Route* r = p.route;
   const int np = p.b * p.k;
-  int ns = 0;
   int ids_l[MAXP];
   for (int i = 0; i < np; ++i) ids_l[i] = __ldcg(&r->ids[i]);
-  int prev = -1;
-  r->slot_off[0] = 0;
-  int fill = 0;
-  while (true) {
-    int nxt = 0x7fffffff;
-    for (int i = 0; i < np; ++i)
-      if (ids_l[i] > prev && ids_l[i] < nxt) nxt = ids_l[i];
-    if (nxt == 0x7fffffff) break;
-    r->slot_expert[ns] = nxt;
-    for (int i = 0; i < np; ++i)
-      if (ids_l[i] == nxt) r->slot_pairs[fill++] = i;
-    r->slot_off[++ns] = fill;
-    prev = nxt;
-  }
-  r->n_slots = ns;
+  build_slots(ids_l, np, r);
   r->k = p.k;
   r->b = p.b;
   atomicExch(p.counter, 0);
@@ -784,8 +1115,11 @@ __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p
 // one CTA; greedy mode takes the previous step's argmax and clears it.
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
-  pdl_launch_dependents();
   pdl_wait();
+  pdl_launch_dependents();
+  // every CTA resolves the tokens (read-only); CTA 0 records them.  The
+  // argmax keys are cleared later in the step (layer 0's QKV kernel), after
+  // every CTA here has read them.
   __shared__ int toks[MAXB];
   const int tid = threadIdx.x;
   if (tid < p.b) {
@@ -797,21 +1131,22 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
       tok = p.tok_in[tid];
     }
     if (tok < 0 || tok >= p.V) {
-      atomicExch(p.status, ERR_BAD_ID);
+      if (blockIdx.x == 0) atomicExch(p.status, ERR_BAD_ID);
       tok = 0;
     }
     toks[tid] = tok;
-    int pos = p.pos_in ? p.pos_in[tid] : p.pos_state[tid];
-    p.pos_cur[tid] = pos;
-    if (p.pos_state) p.pos_state[tid] = pos + 1;
-    p.tok_hist[tid] = tok;
+    if (blockIdx.x == 0) {
+      const int pos = p.pos_in ? p.pos_in[tid] : p.pos_state[tid];
+      p.pos_cur[tid] = pos;
+      if (p.pos_state) p.pos_state[tid] = pos + 1;
+      p.tok_hist[tid] = tok;
+    }
   }
   __syncthreads();
-  if (tid < p.b) p.argmax_key[tid] = 0ull;
   const int64_t rb = (int64_t)dev_gguf_row_bytes(p.type, p.d);
-  for (int t = 0; t < p.b; ++t) {
-    const uint8_t* row = p.tok_embd + (int64_t)toks[t] * rb;
-    for (int i = tid; i < p.d; i += blockDim.x) p.x[(int64_t)t * p.d + i] = gguf_dequant_one(p.type, row, i);
+  const int i = blockIdx.x * 256 + tid;
+  if (i < p.d) {
+    for (int t = 0; t < p.b; ++t) p.x[(int64_t)t * p.d + i] = gguf_dequant_one(p.type, p.tok_embd + (int64_t)toks[t] * rb, i);
   }
 }
 
@@ -862,6 +1197,10 @@ cudaError_t launch_route_build(const int* ids, const float* w, int b, int k, int
 // ---------------------------------------------------------------------------
 template <typename Kern, typename Arg>
 static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, const Arg& a) {
+  // every kernel of the step asks for the same L1/shared split (all shared),
+  // so consecutive kernels never wait for an SM to reconfigure its carveout
+  cudaError_t ce = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (ce != cudaSuccess) return ce;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -877,9 +1216,20 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 
 template <int WT>
 static cudaError_t launch_stream_t(const StreamParams& p, int grid, cudaStream_t st, bool pdl) {
+  const Plan2 q = make_plan2(p);
+  if (q.total <= 227 * 1024 && (p.nmat == 1 || p.nmat == 2)) {
+    cudaError_t e;
+    if (p.nmat == 1) {
+      e = cudaFuncSetAttribute(stream2_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, q.total);
+      if (e != cudaSuccess) return e;
+      return launch_pdl(stream2_kernel<WT, 1>, dim3(grid), dim3((NW + 1) * 32), q.total, st, pdl, p);
+    }
+    e = cudaFuncSetAttribute(stream2_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, q.total);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(stream2_kernel<WT, 2>, dim3(grid), dim3((NW + 1) * 32), q.total, st, pdl, p);
+  }
+  if (p.pro == PRO_ROUTE) return cudaErrorInvalidValue;  // only the warp-tile kernel routes in its prologue
   const StreamPlan pl = make_plan(p);
-  static bool attr_set[2] = {false, false};
-  (void)attr_set;
   cudaError_t e = cudaFuncSetAttribute(stream_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, pl.total);
   if (e != cudaSuccess) return e;
   return launch_pdl(stream_kernel<WT>, dim3(grid), dim3((NW + 1) * 32), pl.total, st, pdl, p);
@@ -894,15 +1244,17 @@ cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool
   }
 }
 
-template <int HD>
+template <int HD, int F16>
 static cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st, bool pdl) {
-  const size_t smem = attn_smem_bytes(HD, p.n_head / p.kv.n_head_kv, p.max_chunk);
-  cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const size_t smem = attn_smem_bytes(HD, p.n_head / p.kv.n_head_kv, F16, p.max_chunk);
+  cudaError_t e = cudaFuncSetAttribute(attn_kernel<HD, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   if (p.cluster > 8) {
-    e = cudaFuncSetAttribute(attn_kernel<HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    e = cudaFuncSetAttribute(attn_kernel<HD, F16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     if (e != cudaSuccess) return e;
   }
+  e = cudaFuncSetAttribute(attn_kernel<HD, F16>, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+  if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.cluster * p.kv.n_head_kv, p.b, 1);
   cfg.blockDim = dim3(ATT_THREADS);
@@ -917,17 +1269,18 @@ static cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st, bool pdl)
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
-  return cudaLaunchKernelEx(&cfg, attn_kernel<HD>, p);
+  return cudaLaunchKernelEx(&cfg, attn_kernel<HD, F16>, p);
 }
 
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl) {
-  if (p.n_head % p.kv.n_head_kv || p.n_head / p.kv.n_head_kv > ATT_MAXG || p.cluster < 1 || p.cluster > 16)
+  if (p.n_head % p.kv.n_head_kv || p.n_head / p.kv.n_head_kv > ATT_MAXG || p.cluster < 1 || p.cluster > ATT_MAXC)
     return cudaErrorInvalidValue;
+  const bool h = p.kv.f16 != 0;
   switch (p.kv.head_dim) {
-    case 32: return launch_attn_t<32>(p, st, pdl);
-    case 64: return launch_attn_t<64>(p, st, pdl);
-    case 128: return launch_attn_t<128>(p, st, pdl);
-    case 256: return launch_attn_t<256>(p, st, pdl);
+    case 32: return h ? launch_attn_t<32, 1>(p, st, pdl) : launch_attn_t<32, 0>(p, st, pdl);
+    case 64: return h ? launch_attn_t<64, 1>(p, st, pdl) : launch_attn_t<64, 0>(p, st, pdl);
+    case 128: return h ? launch_attn_t<128, 1>(p, st, pdl) : launch_attn_t<128, 0>(p, st, pdl);
+    case 256: return h ? launch_attn_t<256, 1>(p, st, pdl) : launch_attn_t<256, 0>(p, st, pdl);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -942,7 +1295,7 @@ cudaError_t launch_router(const RouterParams& p, cudaStream_t st, bool pdl) {
 
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st, bool pdl) {
   if (p.b > MAXB) return cudaErrorInvalidValue;
-  return launch_pdl(embed_kernel, dim3(1), dim3(256), 0, st, pdl, p);
+  return launch_pdl(embed_kernel, dim3((p.d + 255) / 256), dim3(256), 0, st, pdl, p);
 }
 
 }  // namespace sfk

@@ -29,6 +29,7 @@ struct Route {
 enum Prologue : int {
   PRO_QUANT = 0,  // x f32 [b][K] (+ optional RMSNorm * w) -> quantize to act type
   PRO_LOAD = 1,   // copy precomputed qact vectors from global
+  PRO_ROUTE = 2,  // gate/up: ffn_norm + quantize + router + top-k in the prologue
 };
 enum Epilogue : int {
   EPI_STORE = 0,    // y[pair][row] = dot            (mul_mat / mul_mat_id)
@@ -44,6 +45,7 @@ struct KvView {
   void* v;
   const int* page_table; // [b][max_pages]
   int max_pages;
+  int n_pages;           // pages in the pool (page ids are checked against it)
   int n_head_kv;
   int head_dim;
   int f16;
@@ -77,6 +79,8 @@ struct StreamParams {
   int64_t qact_stride;     // bytes between qact vectors
   int xq_by_pair;          // PRO_LOAD: vector index = pair (1) or token (0)
   int xq_resident;         // all groups of all vectors fit in smem
+  const float* w_r;        // PRO_ROUTE: F32 router [n_expert][K]; the routing is written to `route`
+  int n_expert;
   // epilogue
   int epi;
   float* y;                // EPI_STORE / EPI_RESID / EPI_DOWN output; EPI_QKV q out
@@ -95,6 +99,8 @@ struct StreamParams {
   // EPI_LMHEAD
   unsigned long long* argmax_key;  // [b]
   int store_logits;
+  unsigned long long* clear_keys;  // zeroed by CTA 0 once the previous kernel finished (or null)
+  int clear_n;
   int* status;
 };
 
@@ -104,7 +110,7 @@ struct AttnParams {
   const int* pos;          // [b]; attends over 0..pos
   int b, n_head;
   int cluster;             // CTAs per (token, kv head): one thread-block cluster
-  int max_chunk;           // positions per CTA at the longest context
+  int max_chunk;           // positions per CTA at the longest context: ceil(max_pages / cluster) * 16
   float* out;              // [b][Hq*hd]
   int* status;
 };
@@ -140,9 +146,10 @@ struct EmbedParams {
 
 // launch helpers (implemented in sfk_kernels.cu)
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp);
+int stream2_smem_bytes(const StreamParams& p);  // the warp-tile kernel's shared memory
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
-size_t attn_smem_bytes(int hd, int gqa, int max_chunk);
+size_t attn_smem_bytes(int hd, int gqa, int f16, int max_chunk);
 cudaError_t launch_router(const RouterParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);

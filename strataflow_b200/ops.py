@@ -90,7 +90,8 @@ def attn_decode_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Ten
     b = q.shape[0]
     kv_type = L.KV_F16 if k_pages.dtype == torch.float16 else L.KV_F32
     out = torch.empty((b, n_head * head_dim), dtype=torch.float32, device=q.device)
-    L.check(L.load().sfk_attn_decode_paged(_ptr(q), _ptr(k_pages), _ptr(v_pages), kv_type, _ptr(page_table),
+    L.check(L.load().sfk_attn_decode_paged(_ptr(q), _ptr(k_pages), _ptr(v_pages), kv_type, k_pages.shape[0],
+                                           _ptr(page_table),
                                            page_table.shape[1], _ptr(positions), b, n_head, n_head_kv, head_dim,
                                            _ptr(out), _stream(q)))
     return out

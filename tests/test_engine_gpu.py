@@ -182,5 +182,18 @@ def test_kernel_timing_entry_point(cuda):
     ms = (C.c_float * 8)()
     from strataflow_b200 import lib as L
     L.check(eng._lib.sfk_time_kernels(eng.h, 1, 4, ms, 8))
-    assert all(v > 0 for v in ms)
+    # up to 64 experts the gate/up kernel routes in its prologue: no router
+    # kernel, and its timing slot reads 0
+    router = 4  # K_ROUTER in the kernel-class order (embed, qkv, attn, o, router, gate/up, down, lm_head)
+    assert ms[router] == 0.0
+    assert all(v > 0 for i, v in enumerate(ms) if i != router)
+    assert eng.stats()["kernels_per_step"] == 2 + 5 * cfg.n_layer
+
+
+def test_many_experts_standalone_router_parity(cuda):
+    """More than 64 experts: routing runs in its own kernel before gate/up."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=2, n_expert=72, n_expert_used=4)
+    prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, 8).tolist()
+    eng, om, toks, worst = _run_parity(cfg, 9, prompt, 12)
     assert eng.stats()["kernels_per_step"] == 2 + 6 * cfg.n_layer

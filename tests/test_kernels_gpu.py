@@ -237,6 +237,37 @@ def test_attn_paged_small_heads(cuda):
         assert np.abs(out[t] - ref).max() <= 1e-6 * np.abs(ref).max()
 
 
+@pytest.mark.parametrize("Hq,Hkv,hd,ctx,f16", [(64, 8, 128, 1024, True),   # GQA group of 8 (the 1T shape)
+                                              (16, 4, 64, 300, False),
+                                              (8, 8, 256, 100, True)])
+def test_attn_paged_other_head_shapes(cuda, Hq, Hkv, hd, ctx, f16):
+    from strataflow_b200 import ops
+    torch = _torch()
+    b = 2
+    q, K, V, (dq, dk, dv, dpt) = _paged_case(b, ctx, Hq, Hkv, hd, f16, seed=hd + ctx)
+    pos = np.array([ctx - 1, ctx // 3], np.int32)
+    out = ops.attn_decode_paged(dq, dk, dv, dpt, torch.from_numpy(pos).cuda(), Hq, Hkv, hd).cpu().numpy()
+    for t in range(b):
+        ref = O.attn_decode(q[t].ravel(), K[t, :pos[t] + 1], V[t, :pos[t] + 1], Hq, Hkv, hd)
+        assert np.abs(out[t] - ref).max() <= 1e-6 * np.abs(ref).max()
+
+
+def test_attn_paged_rejects_page_outside_pool(cuda):
+    """A page id past the pool is checked before any copy and reported."""
+    from strataflow_b200 import lib as L
+    from strataflow_b200 import ops
+    torch = _torch()
+    q, K, V, (dq, dk, dv, dpt) = _paged_case(1, 64, 8, 4, 32, False, seed=5)
+    bad = dpt.clone()
+    bad[0, 1] = dk.shape[0]          # one past the last page
+    pos = torch.tensor([63], dtype=torch.int32, device="cuda")
+    with pytest.raises(L.SfkError):
+        ops.attn_decode_paged(dq, dk, dv, bad, pos, 8, 4, 32)
+    out = ops.attn_decode_paged(dq, dk, dv, dpt, pos, 8, 4, 32).cpu().numpy()   # still usable
+    ref = O.attn_decode(q[0].ravel(), K[0], V[0], 8, 4, 32)
+    assert np.abs(out[0] - ref).max() <= 1e-6 * np.abs(ref).max()
+
+
 def test_mul_mat_id_rejects_bad_expert_id(cuda):
     from strataflow_b200 import ops, lib as L
     torch = _torch()
