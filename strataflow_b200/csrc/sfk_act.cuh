@@ -103,6 +103,82 @@ __device__ __forceinline__ void qact_put_q80(uint8_t* qa, int K, int blk, const 
   if ((lane & 15) == 0) *reinterpret_cast<float*>(gb + 8 * ng * 16 + ng * 16 + ul * 4) = 0.0f;
 }
 
+// Several Q8_K blocks of one warp at once (blocks blk0, blk0 + stride, ...,
+// the first nb of RB): the same arithmetic as qact_put_q8k, with the warp
+// reductions of the blocks interleaved.  The largest |x| (first index on ties)
+// is found through one 64-bit key per lane: |x| bits (monotonic for x >= 0),
+// then 255 - index, then the sign.
+__device__ __forceinline__ unsigned long long shfl_xor_u64(unsigned long long v, int o) {
+  const unsigned lo = __shfl_xor_sync(0xffffffffu, (unsigned)v, o);
+  const unsigned hi = __shfl_xor_sync(0xffffffffu, (unsigned)(v >> 32), o);
+  return ((unsigned long long)hi << 32) | lo;
+}
+template <int RB>
+__device__ __forceinline__ void qact_put_q8k_blocks(uint8_t* qa, int K, int blk0, int stride, int nb,
+                                                    const float (&v)[RB][8], int lane) {
+  unsigned long long key[RB];
+#pragma unroll
+  for (int i = 0; i < RB; ++i) {
+    key[i] = 0ull;
+    if (i < nb) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const unsigned bits = __float_as_uint(v[i][j]);
+        const unsigned long long kj = ((unsigned long long)(bits & 0x7fffffffu) << 32) |
+                                      ((unsigned long long)(255 - (8 * lane + j)) << 1) | (bits >> 31);
+        key[i] = kj > key[i] ? kj : key[i];
+      }
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+    for (int i = 0; i < RB; ++i) {
+      const unsigned long long ok = shfl_xor_u64(key[i], o);
+      key[i] = ok > key[i] ? ok : key[i];
+    }
+  }
+  int q[RB][8], sums[RB];
+  float d[RB];
+#pragma unroll
+  for (int i = 0; i < RB; ++i) {
+    const float ax = __uint_as_float((unsigned)(key[i] >> 32));
+    const float mv = (key[i] & 1ull) ? -ax : ax;
+    d[i] = 0.0f;
+    if (ax == 0.0f) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) q[i][j] = 0;
+    } else {
+      const float iscale = __fdiv_rn(-127.0f, mv);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int t = nearest_int(__fmul_rn(iscale, v[i][j]));
+        q[i][j] = t < 127 ? t : 127;
+      }
+      d[i] = __fdiv_rn(1.0f, iscale);
+    }
+    int s = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) s += q[i][j];
+    sums[i] = s;
+  }
+#pragma unroll
+  for (int i = 0; i < RB; ++i) sums[i] += __shfl_xor_sync(0xffffffffu, sums[i], 1);
+#pragma unroll
+  for (int i = 0; i < RB; ++i) {
+    if (i < nb) {
+      const int blk = blk0 + i * stride;
+      const int u = 2 * blk + (lane >> 4);
+      const int g = u / GROUP_UNITS, ul = u % GROUP_UNITS, ng = group_units(K, g);
+      uint8_t* gb = qa + qact_group_offset(g);
+      const int m = (lane & 15) >> 1;
+      *reinterpret_cast<uint2*>(gb + (m * ng + ul) * 16 + (lane & 1) * 8) = pack8(q[i]);
+      if ((lane & 1) == 0) *reinterpret_cast<int16_t*>(gb + 8 * ng * 16 + ul * 16 + m * 2) = (int16_t)sums[i];
+      if ((lane & 15) == 0) *reinterpret_cast<float*>(gb + 8 * ng * 16 + ng * 16 + ul * 4) = d[i];
+    }
+  }
+}
+
 __device__ __forceinline__ void qact_put(int act_type, uint8_t* qa, int K, int blk, const float v[8], int lane) {
   if (act_type == T_Q8_0)
     qact_put_q80(qa, K, blk, v, lane);

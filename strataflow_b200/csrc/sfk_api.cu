@@ -74,7 +74,25 @@ constexpr int XQ_RESIDENT_BUDGET = 48 * 1024;
 constexpr int SMEM_LIMIT = 227 * 1024;
 
 // fill in grid / rows_per_cta / xq_resident and check shared memory
+// Ring shape of the warp-tile kernel: tile target bytes and stages per warp.
+// 0 keeps the kernel's defaults; SFK_STREAM_TILE_BYTES / SFK_STREAM_STAGES
+// override them (read once, for tuning on new parts).
+struct StreamTuning {
+  int tile = 0, stages = 0;
+};
+const StreamTuning& stream_tuning() {
+  static const StreamTuning t = [] {
+    StreamTuning r;
+    if (const char* v = getenv("SFK_STREAM_TILE_BYTES")) r.tile = atoi(v);
+    if (const char* v = getenv("SFK_STREAM_STAGES")) r.stages = atoi(v);
+    return r;
+  }();
+  return t;
+}
+
 sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
+  if (!p.s2_tile) p.s2_tile = stream_tuning().tile;
+  if (!p.s2_stages) p.s2_stages = stream_tuning().stages;
   int grid = std::min(sm_count, std::max(1, (p.rows + 15) / 16));
   int rpc = (p.rows + grid - 1) / grid;
   rpc = (rpc + p.row_align - 1) / p.row_align * p.row_align;
@@ -302,6 +320,18 @@ uint64_t tensor_seed(uint64_t seed, int tid, int layer) {
 // ---- the step launch chain -------------------------------------------------
 enum KernelClass { K_EMBED = 0, K_QKV, K_ATTN, K_OPROJ, K_ROUTER, K_GATEUP, K_DOWN, K_LMHEAD, K_NCLASS };
 
+// The device status word after a step; on a device error the counters that
+// CTAs hand between launches (routing arrivals, SwiGLU group counters) may be
+// left mid-count, so they are cleared before the engine is used again.
+sfk_status engine_check(sfk_engine* e) {
+  sfk_status s = check_status_word(e->status, e->stream);
+  if (s != SFK_OK) {
+    cudaMemset(e->router_counter, 0, 2 * sizeof(int));
+    cudaMemset(e->grp_counter, 0, sizeof(int) * (e->hp.n_ff / 256));
+  }
+  return s;
+}
+
 KvView kv_view(const sfk_engine* e, int l) {
   const sfk_hparams& hp = e->hp;
   KvView kv{};
@@ -341,6 +371,8 @@ StreamParams gateup_params(const sfk_engine* e, int l, int b) {
     p.eps = hp.rms_eps;
     p.w_r = W.router;
     p.n_expert = hp.n_expert;
+    p.logits = e->router_logits;
+    p.rsync = e->router_counter;
   } else {
     p.pro = PRO_LOAD;
     p.qact = e->xq_ffn;
@@ -727,7 +759,7 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->xq_ffn, qact_bytes(d) * B, sb));
   TRY(e->alloc(&e->hq, qact_bytes(F) * B * k, sb));
   TRY(e->alloc(&e->route, sizeof(Route), sb));
-  TRY(e->alloc(&e->router_counter, sizeof(int), sb));
+  TRY(e->alloc(&e->router_counter, 2 * sizeof(int), sb));
   TRY(e->alloc(&e->grp_counter, sizeof(int) * (F / 256), sb));
   TRY(e->alloc(&e->argmax_key, sizeof(unsigned long long) * B, sb));
   TRY(e->alloc(&e->tok_in, sizeof(int) * B, sb));
@@ -738,7 +770,7 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->status, sizeof(int), sb));
   {
     cudaError_t ce = cudaSuccess;
-    ce = cudaMemset(e->router_counter, 0, sizeof(int));
+    ce = cudaMemset(e->router_counter, 0, 2 * sizeof(int));
     if (ce == cudaSuccess) ce = cudaMemset(e->grp_counter, 0, sizeof(int) * (F / 256));
     if (ce == cudaSuccess) ce = cudaMemset(e->argmax_key, 0, sizeof(unsigned long long) * B);
     if (ce == cudaSuccess) ce = cudaMemset(e->pos_state, 0, sizeof(int) * B);
@@ -944,7 +976,7 @@ sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens
     CK(cudaMemcpyAsync(logits_host, e->logits, sizeof(float) * n_seq * e->hp.n_vocab, cudaMemcpyDeviceToHost,
                        e->stream));
   CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * n_seq, cudaMemcpyDeviceToHost, e->stream));
-  s = check_status_word(e->status, e->stream);
+  s = engine_check(e);
   if (s) return s;
   for (int t = 0; t < n_seq; ++t) {
     e->seq_pos[t] = positions[t] + 1;
@@ -973,7 +1005,7 @@ sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int3
                          e->stream));
     }
   }
-  sfk_status s = check_status_word(e->status, e->stream);
+  sfk_status s = engine_check(e);
   if (s) return s;
   for (int t = 0; t < n_seq; ++t) e->seq_pos[t] += n_steps;
   return SFK_OK;
@@ -1058,7 +1090,7 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
   cudaEventDestroy(a);
   cudaEventDestroy(z);
   if (s) return s;
-  return check_status_word(e->status, e->stream);
+  return engine_check(e);
 }
 
 // ---- operator-level -------------------------------------------------------

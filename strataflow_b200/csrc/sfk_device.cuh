@@ -106,6 +106,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       "l"(src), "r"(bytes), "r"(smem_u32(bar))
       : "memory");
 }
+// Same, with an L2 cache policy (createpolicy): weight streams are read once
+// per step and marked evict-first so they do not push activations, routing
+// weights, KV pages and kernel code out of L2.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar)), "l"(pol)
+      : "memory");
+}
 // Programmatic dependent launch: wait for the previous grid / let the next start.
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_launch_dependents() {
@@ -120,23 +135,34 @@ __device__ __forceinline__ uint4 lds128(const void* p) {
 }
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
+__device__ __forceinline__ int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
 // error codes written to the device status word
 enum : int { ERR_NONE = 0, ERR_TIMEOUT = 1, ERR_BAD_ID = 2, ERR_BAD_POS = 3, ERR_BAD_PAGE = 4 };
 
 // Bounded mbarrier wait: ~ 2^31 cycles (~1 s at 2 GHz) then records
-// ERR_TIMEOUT in *status and returns false.
+// ERR_TIMEOUT in *status and returns false.  The clock and the status word
+// (another warp's timeout ends this wait too) are looked at only every 64th
+// poll: a global load in every poll would add its latency to every wake-up.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (true) {
+  for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (clock64() - t0 > (1ll << 31)) {
-      atomicExch(status, ERR_TIMEOUT);
-      return false;
+    if ((i & 63) == 0) {
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(status, ERR_TIMEOUT);
+        return false;
+      }
+      if (*(volatile int*)status == ERR_TIMEOUT) return false;
     }
-    if (*(volatile int*)status == ERR_TIMEOUT) return false;
   }
 }
+
 
 // ---------------------------------------------------------------------------
 // numerics shared with the CPU oracle

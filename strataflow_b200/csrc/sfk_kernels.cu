@@ -69,7 +69,6 @@ __host__ __device__ inline StreamPlan make_plan(const StreamParams& p) {
   return s;
 }
 
-struct Plan2;
 int stream2_smem_bytes(const StreamParams& p);
 
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp) {
@@ -136,11 +135,76 @@ __device__ __forceinline__ float unit_dot(const uint8_t* wg, const uint8_t* xg, 
 // written to shared memory for every group.  ggml rms_norm: squares summed in
 // double, mean = (float)(sum/n), scale = 1/sqrtf(mean+eps), y = x*scale, then
 // ggml_mul by the weight (engine.cpp:1878-1879).
-__device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_bytes, double* red) {
+struct NoOp {
+  __device__ void operator()() const {}
+};
+
+// `after_loads` runs once the first vector's loads are in flight (a caller
+// queues its weight copies behind them).
+template <typename F = NoOp>
+__device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_bytes, double* red,
+                               F after_loads = F{}) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.K;
+  const int nblk = K / QK_K;
+  constexpr int RB = 4;  // 256-column blocks a warp holds in registers
   for (int t = 0; t < p.n_vec; ++t) {
     const float* x = p.x + (int64_t)t * K;
+    uint8_t* qa = xq + (int64_t)t * xq_vec_bytes;
+    if (nblk <= RB * NW) {
+      // this warp's blocks of x (and of the norm weight), one round trip
+      float xv[RB][8], wv[RB][8];
+#pragma unroll
+      for (int i = 0; i < RB; ++i) {
+        const int blk = warp + i * NW;
+        if (blk < nblk) {
+          const float4* xp = reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8);
+          const float4 x0 = xp[0], x1 = xp[1];
+          xv[i][0] = x0.x; xv[i][1] = x0.y; xv[i][2] = x0.z; xv[i][3] = x0.w;
+          xv[i][4] = x1.x; xv[i][5] = x1.y; xv[i][6] = x1.z; xv[i][7] = x1.w;
+          if (p.norm_w) {
+            const float4* wp = reinterpret_cast<const float4*>(p.norm_w + blk * QK_K + lane * 8);
+            const float4 w0 = wp[0], w1 = wp[1];
+            wv[i][0] = w0.x; wv[i][1] = w0.y; wv[i][2] = w0.z; wv[i][3] = w0.w;
+            wv[i][4] = w1.x; wv[i][5] = w1.y; wv[i][6] = w1.z; wv[i][7] = w1.w;
+          }
+        }
+      }
+      if (t == 0) after_loads();
+      float scale = 1.0f;
+      if (p.norm_w) {
+        double s = 0.0;
+#pragma unroll
+        for (int i = 0; i < RB; ++i)
+          if (warp + i * NW < nblk) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) s += (double)__fmul_rn(xv[i][j], xv[i][j]);
+          }
+        s = warp_sum_d(s);
+        if (lane == 0) red[warp] = s;
+        consumer_sync();
+        double tot = 0.0;
+        for (int w = 0; w < NW; ++w) tot += red[w];  // every thread, same order
+        const float mean = (float)(tot / (double)K);
+        scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
+        consumer_sync();  // red is reused by the next vector
+      }
+      float vn[RB][8];
+#pragma unroll
+      for (int i = 0; i < RB; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) vn[i][j] = p.norm_w ? __fmul_rn(__fmul_rn(xv[i][j], scale), wv[i][j]) : xv[i][j];
+      const int nb = warp < nblk ? (nblk - warp + NW - 1) / NW : 0;
+      if (p.act_type == T_Q8_K) {
+        qact_put_q8k_blocks<RB>(qa, K, warp, NW, nb < RB ? nb : RB, vn, lane);
+      } else {
+#pragma unroll
+        for (int i = 0; i < RB; ++i)
+          if (i < nb) qact_put(p.act_type, qa, K, warp + i * NW, vn[i], lane);
+      }
+      continue;
+    }
+    if (t == 0) after_loads();
     float scale = 1.0f;
     if (p.norm_w) {
       double s = 0.0;
@@ -161,8 +225,7 @@ __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_by
       scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
       consumer_sync();
     }
-    uint8_t* qa = xq + (int64_t)t * xq_vec_bytes;
-    for (int blk = warp; blk < K / QK_K; blk += NW) {
+    for (int blk = warp; blk < nblk; blk += NW) {
       float v[8];
       const float4 a = *reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8);
       const float4 b = *reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8 + 4);
@@ -500,44 +563,62 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
 }
 
 // ---------------------------------------------------------------------------
-// stream2_kernel: warp-owned tiles.  A tile is up to 4 consecutive full rows
-// of each of the nmat matrices (all groups of K), moved by one bulk copy per
-// matrix into a per-warp ring of S2_STAGES stages; tiles go to the consumer
-// warps round-robin, so 8 x S2_STAGES tiles are in flight per SM and each
-// warp's per-tile bookkeeping is spread over up to 8 row dots.  The row sums
-// keep the fixed order of the other kernel (unit partials -> 32-lane
-// butterfly per group -> groups added in order), computed for 8 rows at once
-// with a transposed butterfly (9 shuffles instead of 40).
+// stream2_kernel: warp-owned tiles, each warp its own copy issuer.  A tile is
+// R consecutive full rows (all groups of K) of each of the nmat matrices of
+// one expert; tiles go to the consumer warps round-robin and every warp keeps
+// S of its tiles in flight in its own ring slots, issuing the next tile's bulk
+// copies itself as soon as it is done with a slot.  One thread can keep only
+// about one 1-D bulk copy per quarter microsecond going, so a single producer
+// thread caps the SM at ~1.1 TB/s/148 with 2 KB copies; eight issuing warps
+// stream at HBM speed with 2-8 KB copies.  The row sums keep the fixed order
+// of the other kernel (unit partials -> 32-lane butterfly per group -> groups
+// added in order): the butterflies of a tile's up to 8 (row, matrix, group)
+// values run together (9 shuffles instead of 40), then each (row, matrix)
+// adds its group sums in order.
 // ---------------------------------------------------------------------------
-constexpr int S2_STAGES = 2;
-constexpr int S2_MAXROWS = 4;
+constexpr int S2_MAXSTAGES = 4;
+constexpr int S2_TILE = 16 * 1024;  // default tile target (bytes)
+constexpr int S2_SMEM = 227 * 1024;
 
-struct Plan2 {
-  int tile_rows, tile_bytes, ring_off, xq_off, acc_off, red_off, route_off, xn_off, seg_off, probs_off, total;
-  int xq_smem, xq_vec_bytes;
-};
+__host__ __device__ inline int al16i(int64_t v) { return (int)((v + 15) & ~(int64_t)15); }
 
-__host__ __device__ inline Plan2 make_plan2(const StreamParams& p) {
+inline Plan2 make_plan2(const StreamParams& p) {
   Plan2 q;
   const int64_t rs = p.rowstride;
-  int64_t R = (12 * 1024) / (p.nmat * rs);
-  if (R < 1) R = 1;
-  if (R > S2_MAXROWS) R = S2_MAXROWS;
-  q.tile_rows = (int)R;
-  q.tile_bytes = (int)(R * p.nmat * rs);
-  q.ring_off = 2 * NW * S2_STAGES * 8 < 128 ? 128 : 2 * NW * S2_STAGES * 8;
-  q.xq_off = q.ring_off + NW * S2_STAGES * q.tile_bytes;
+  q.G = n_groups(p.K);
   const int64_t xq_all = (int64_t)p.n_vec * qact_bytes(p.K);
   q.xq_smem = (p.pro == PRO_QUANT) || (p.pro == PRO_ROUTE) || (xq_all <= 64 * 1024) ? 1 : 0;
   q.xq_vec_bytes = (int)qact_bytes(p.K);
-  q.acc_off = q.xq_off + (q.xq_smem ? (int)((xq_all + 15) & ~(int64_t)15) : 0);
-  q.red_off = q.acc_off + ((p.rows_per_cta * p.n_pairs * p.nmat * 4 + 15) & ~15);
-  q.route_off = q.red_off + 64 * 8;
   const bool rt = p.pro == PRO_ROUTE;
-  q.xn_off = q.route_off + (rt ? (int)((sizeof(Route) + 15) & ~15) : 0);
+  const bool routed = rt || p.route != nullptr;  // the routing is kept in shared memory
+  const int xq_b = q.xq_smem ? al16i(xq_all) : 0;
+  const int acc_b = al16i((int64_t)p.rows_per_cta * p.n_pairs * p.nmat * 4);
+  const int route_b = (routed ? al16i(sizeof(Route)) : 0) + (rt ? p.K * 4 + al16i(p.b * p.n_expert * 4) : 0);
+  const int bars = al16i(NW * S2_MAXSTAGES * 8 + 16);  // per-warp full[] | router-weights | prologue
+  const int fixed = bars + xq_b + acc_b + 64 * 8 + route_b;
+  int rmax = 8 / (p.nmat * q.G);
+  if (rmax < 1) rmax = 1;
+  int R = (int)((p.s2_tile > 0 ? p.s2_tile : S2_TILE) / (p.nmat * rs));
+  R = R < 1 ? 1 : (R > rmax ? rmax : R);
+  // keep two tiles per warp in flight: a warp with one slot idles through
+  // every copy's latency
+  while (R > 1 && (S2_SMEM - fixed) / ((int64_t)NW * p.nmat * R * rs) < 2) --R;
+  q.R = R;
+  q.tile_bytes = (int)(p.nmat * R * rs);
+  int S = (int)((S2_SMEM - fixed) / ((int64_t)NW * q.tile_bytes));
+  if (S > S2_MAXSTAGES) S = S2_MAXSTAGES;
+  if (p.s2_stages > 0 && S > p.s2_stages) S = p.s2_stages;
+  if (S < 1) S = 1;
+  q.stages = S;
+  q.ring_off = bars;
+  q.xq_off = q.ring_off + NW * S * q.tile_bytes;
+  q.acc_off = q.xq_off + xq_b;
+  q.red_off = q.acc_off + acc_b;
+  q.route_off = q.red_off + 64 * 8;
+  q.xn_off = q.route_off + (routed ? al16i(sizeof(Route)) : 0);
   q.seg_off = q.xn_off + (rt ? p.K * 4 : 0);
-  q.probs_off = q.seg_off + (rt ? p.n_expert * 4 * 8 : 0);
-  q.total = q.probs_off + (rt ? ((p.n_expert * 4 + 15) & ~15) : 0) + 16;  // + the route-ready mbarrier
+  q.probs_off = q.seg_off;
+  q.total = q.probs_off + (rt ? al16i(p.b * p.n_expert * 4) : 0);
   return q;
 }
 
@@ -574,7 +655,13 @@ __device__ __forceinline__ float reduce8(const float v[8], int lane) {
   return y;
 }
 
-int stream2_smem_bytes(const StreamParams& p) { return make_plan2(p).total; }
+// shared memory of the warp-tile kernel, or more than any SM has when a tile
+// cannot hold all of one row's group sums (nmat * groups > 8)
+int stream2_smem_bytes(const StreamParams& p) {
+  const Plan2 q = make_plan2(p);
+  if ((p.nmat != 1 && p.nmat != 2) || p.nmat * q.G > 8) return 1 << 30;
+  return q.total;
+}
 
 template <int WT>
 __device__ __forceinline__ float unit_dot_x(const uint8_t* wg, const XQ8& x, int ng, int lane) {
@@ -594,109 +681,156 @@ __device__ __forceinline__ float unit_dot_x(const uint8_t* wg, const XQ8& x, int
 }
 
 template <int WT, int NMAT>
-__global__ void __launch_bounds__((NW + 1) * 32, 1) stream2_kernel(const StreamParams p) {
+__global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
-  const Plan2 pl = make_plan2(p);
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);  // [NW][S2_STAGES]
-  uint64_t* empty = full + NW * S2_STAGES;
-  uint8_t* ring = smem + pl.ring_off;
+  const Plan2& pl = p.pl;  // planned on the host: no divisions before the first copy
+  const int S = pl.stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * S;  // this warp's [S]
+  uint64_t* pro_bar = reinterpret_cast<uint64_t*>(smem) + NW * S2_MAXSTAGES;  // prologue copies landed
+  uint8_t* ring_all = smem + pl.ring_off;
+  uint8_t* ring = ring_all + (int64_t)warp * S * pl.tile_bytes;
   uint8_t* xq_s = smem + pl.xq_off;
   float* acc = reinterpret_cast<float*>(smem + pl.acc_off);
   double* red = reinterpret_cast<double*>(smem + pl.red_off);
   Route* sroute = reinterpret_cast<Route*>(smem + pl.route_off);
-  uint64_t* route_bar = reinterpret_cast<uint64_t*>(smem + pl.total - 16);
   const bool self_route = p.pro == PRO_ROUTE;
-  const Route* rt = self_route ? sroute : p.route;
-  const bool routed = rt != nullptr;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool routed = self_route || p.route != nullptr;
+  const Route* rt = sroute;  // the routing, in shared memory once known
   const int r0 = blockIdx.x * p.rows_per_cta;
   const int r1 = min(p.rows, r0 + p.rows_per_cta);
-  const int G = n_groups(p.K);
-  const int R = pl.tile_rows;
+  const int G = pl.G;
+  const int R = pl.R;
+  const int64_t rs = p.rowstride;
   const int n_rb = r0 < r1 ? (r1 - r0 + R - 1) / R : 0;
 
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < NW * S2_STAGES; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
-    }
-    mbar_init(route_bar, 1);
+  if (lane == 0) {
+    for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
+    if (warp == 0) mbar_init(pro_bar, NW);
     fence_mbar_init();
   }
   __syncthreads();
-
-  if (warp == NW) {
-    // ------------------------------ producer ------------------------------
-    if (lane != 0) return;
-    int n_slots = 1;
-    bool waited = false;
-    if (self_route) {
-      // the consumers route the step first (after their wait on the previous
-      // kernel); the experts are known after that
-      if (!mbar_wait_bounded(route_bar, 0, p.status)) return;
-      pdl_launch_dependents();
-      waited = true;
-      n_slots = rt->n_slots;
-    } else if (routed) {
-      pdl_wait();  // routed experts are known only after the router ran
-      pdl_launch_dependents();
-      waited = true;
-      n_slots = rt->n_slots;
-    }
-    const int n_tiles = n_rb * n_slots;
-    for (int it = 0; it < n_tiles; ++it) {
-      const int w = it % NW, kk = it / NW;
-      const int bi = w * S2_STAGES + kk % S2_STAGES, use = kk / S2_STAGES;
-      if (use > 0 && !waited) {  // the ring is full: from here on the consumers pace the copies
-        pdl_wait();
-        pdl_launch_dependents();
-        waited = true;
-      }
-      if (use > 0 && !mbar_wait_bounded(&empty[bi], (use - 1) & 1, p.status)) break;
-      const int rb = it / n_slots, si = it % n_slots;
-      const int rbase = r0 + rb * R;
-      const int nrows = min(R, r1 - rbase);
-      const uint32_t bytes = (uint32_t)(nrows * p.rowstride);
-      mbar_arrive_expect_tx(&full[bi], bytes * NMAT);
-      const int expert = routed ? rt->slot_expert[si] : 0;
-      const int64_t eoff = (int64_t)expert * p.expert_stride + (int64_t)rbase * p.rowstride;
-      uint8_t* dst = ring + (int64_t)bi * pl.tile_bytes;
+  // lane 0: bring tile `it` (row block it / n_slots of slot expert it % n_slots) into ring slot s
+  auto issue = [&](int it, int s, int n_slots) {
+    const int rb = it / n_slots, si = it % n_slots;
+    const int rbase = r0 + rb * R;
+    const uint32_t bytes = (uint32_t)(min(R, r1 - rbase) * rs);
+    mbar_arrive_expect_tx(&full[s], bytes * NMAT);
+    const int expert = routed ? rt->slot_expert[si] : 0;
+    const int64_t eoff = (int64_t)expert * p.expert_stride + (int64_t)rbase * rs;
+    uint8_t* dst = ring + (int64_t)s * pl.tile_bytes;
+    const uint64_t pol = l2_evict_first_policy();
 #pragma unroll
-      for (int m = 0; m < NMAT; ++m)
-        bulk_g2s(dst + (int64_t)m * R * p.rowstride, (m == 0 ? p.w0 : p.w1) + eoff, bytes, &full[bi]);
-    }
-    if (!waited) {
-      pdl_wait();
-      pdl_launch_dependents();
-    }
-    return;
-  }
+    for (int m = 0; m < NMAT; ++m)
+      bulk_g2s_hint(dst + (int64_t)m * R * rs, (m == 0 ? p.w0 : p.w1) + eoff, bytes, &full[s], pol);
+  };
 
-  // ------------------------------ consumers ------------------------------
-  if (self_route) {
-    // the router weights are static: pull this CTA's share toward L2 first
-    const char* wb = reinterpret_cast<const char*>(p.w_r);
-    const int64_t nbytes = (int64_t)p.n_expert * p.K * 4;
-    for (int64_t o = ((int64_t)blockIdx.x * NW * 32 + threadIdx.x) * 128; o < nbytes;
-         o += (int64_t)gridDim.x * NW * 32 * 128)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"(wb + o));
+  // routing: CTA c scores the (token, expert) logits q = c, c + grid, ...;
+  // the router weights are static, so the first row slice is loaded before
+  // the wait on the previous kernel
+  const int nq = self_route ? p.b * p.n_expert : 0;
+  const int rcols = p.K / NW;  // columns of a logit per warp (a multiple of 32)
+  constexpr int WPRE = 4;
+  float4 wpre[WPRE];
+  const bool pre = (int)blockIdx.x < nq && rcols % 128 == 0 && rcols / 128 <= WPRE;
+  if (pre) {
+    const float* wr = p.w_r + (int64_t)(blockIdx.x % p.n_expert) * p.K + warp * rcols + lane * 4;
+#pragma unroll
+    for (int i = 0; i < WPRE; ++i)
+      if (i < rcols / 128) wpre[i] = *reinterpret_cast<const float4*>(wr + i * 128);
   }
   pdl_wait();
   pdl_launch_dependents();
+  // inputs written by the previous kernels: the routing (when another kernel
+  // routed) and precomputed activations, by bulk copies issued from every warp
+  const bool bulk_xq = !self_route && p.pro == PRO_LOAD && pl.xq_smem && (p.qact_stride % 16) == 0 &&
+                       (reinterpret_cast<uintptr_t>(p.qact) % 16) == 0;
+  const bool bulk_pro = bulk_xq || (routed && !self_route);
+  if (bulk_pro && lane == 0) {
+    uint32_t mine = 0;
+    if (routed && !self_route && warp == 0) mine += (uint32_t)sizeof(Route);
+    if (bulk_xq)
+      for (int vi = warp; vi < p.n_vec; vi += NW) mine += (uint32_t)pl.xq_vec_bytes;
+    mbar_arrive_expect_tx(pro_bar, mine);
+    if (routed && !self_route && warp == 0) bulk_g2s(sroute, p.route, (uint32_t)sizeof(Route), pro_bar);
+    if (bulk_xq)
+      for (int vi = warp; vi < p.n_vec; vi += NW)
+        bulk_g2s(xq_s + (int64_t)vi * pl.xq_vec_bytes, p.qact + (int64_t)vi * p.qact_stride,
+                 (uint32_t)pl.xq_vec_bytes, pro_bar);
+  }
   if (p.clear_keys && blockIdx.x == 0 && threadIdx.x < p.clear_n) p.clear_keys[threadIdx.x] = 0ull;
+  int depart_old = -1;
   if (self_route) {
     float* xn_s = reinterpret_cast<float*>(smem + pl.xn_off);
-    double* seg_s = reinterpret_cast<double*>(smem + pl.seg_off);
-    float* probs_s = reinterpret_cast<float*>(smem + pl.probs_off);
-    for (int t = 0; t < p.b; ++t)
-      route_one<NW>(p.x + (int64_t)t * p.K, p.norm_w, p.w_r, p.K, p.n_expert, p.k, p.eps, p.act_type,
-                    xq_s + (int64_t)t * pl.xq_vec_bytes, xn_s, seg_s, probs_s, red, &sroute->ids[t * p.k],
-                    &sroute->w[t * p.k], nullptr, ConsumerSync{});
-    if (threadIdx.x == 0) {
+    float* probs_s = reinterpret_cast<float*>(smem + pl.probs_off);  // [b][E]
+    const int tid = threadIdx.x;
+    for (int t = 0; t < p.b; ++t) {
+      // ffn_norm + quantize token t (every CTA needs its activations)
+      route_norm<NW, 4>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
+                     xn_s, red, nullptr, ConsumerSync{});
+      for (int q = blockIdx.x; q < nq; q += gridDim.x) {
+        if (q / p.n_expert != t) continue;
+        // logit = sum_c (double)(w_r[e][c] * xn[c]): warp w sums its column
+        // slice in four chains, the slices are added in order
+        const float* wr = p.w_r + (int64_t)(q % p.n_expert) * p.K + warp * rcols;
+        const float* xs = xn_s + warp * rcols;
+        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+        if (pre && q == (int)blockIdx.x) {
+#pragma unroll
+          for (int i = 0; i < WPRE; ++i)
+            if (i < rcols / 128) {
+              const float4 x4 = *reinterpret_cast<const float4*>(xs + i * 128 + lane * 4);
+              a0 += (double)__fmul_rn(wpre[i].x, x4.x);
+              a1 += (double)__fmul_rn(wpre[i].y, x4.y);
+              a2 += (double)__fmul_rn(wpre[i].z, x4.z);
+              a3 += (double)__fmul_rn(wpre[i].w, x4.w);
+            }
+        } else {
+          for (int c = lane * 4; c < rcols; c += 128) {
+            const float4 w4 = *reinterpret_cast<const float4*>(wr + c);
+            const float4 x4 = *reinterpret_cast<const float4*>(xs + c);
+            a0 += (double)__fmul_rn(w4.x, x4.x);
+            a1 += (double)__fmul_rn(w4.y, x4.y);
+            a2 += (double)__fmul_rn(w4.z, x4.z);
+            a3 += (double)__fmul_rn(w4.w, x4.w);
+          }
+        }
+        const double a = warp_sum_d((a0 + a1) + (a2 + a3));
+        if (lane == 0) red[warp] = a;
+        consumer_sync();
+        if (tid == 0) {
+          double tot = 0.0;
+          for (int w = 0; w < NW; ++w) tot += red[w];
+          p.logits[q] = (float)tot;
+          __threadfence();
+          atomicAdd(&p.rsync[0], 1);  // release: this logit is visible
+        }
+        consumer_sync();
+      }
+    }
+    // every logit of the step, from every scoring CTA (bounded wait)
+    if (tid == 0) {
+      const long long t0 = clock64();
+      while (ld_acquire(&p.rsync[0]) < nq) {
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(p.status, ERR_TIMEOUT);
+          break;
+        }
+      }
+    }
+    consumer_sync();
+    for (int i = tid; i < nq; i += NW * 32) probs_s[i] = __ldcg(&p.logits[i]);
+    consumer_sync();
+    for (int t = warp; t < p.b; t += NW)
+      route_select(probs_s + t * p.n_expert, p.n_expert, p.k, &sroute->ids[t * p.k], &sroute->w[t * p.k], lane);
+    consumer_sync();
+    if (tid == 0) {
       build_slots(sroute->ids, p.b * p.k, sroute);
       sroute->k = p.k;
       sroute->b = p.b;
-      mbar_arrive(route_bar);  // release: the producer may stream the routed experts
+      // departure count; its result is looked at only when the CTA is done,
+      // so the round trip stays off the critical path
+      depart_old = atomicAdd(&p.rsync[1], 1);
     }
     consumer_sync();
     if (blockIdx.x == 0) {  // publish the routing for the down kernel and the host
@@ -704,61 +838,99 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream2_kernel(const StreamP
       int* dst = reinterpret_cast<int*>(const_cast<Route*>(p.route));
       for (int i = threadIdx.x; i < (int)(sizeof(Route) / 4); i += NW * 32) dst[i] = src[i];
     }
-  } else if (pl.xq_smem) {
-    if (p.pro == PRO_QUANT)
-      prologue_quant(p, xq_s, pl.xq_vec_bytes, red);
-    else
-      prologue_load(p, xq_s, pl.xq_vec_bytes, -1);
+  } else if (bulk_pro) {
+    mbar_wait_bounded(pro_bar, 0, p.status);  // routing and/or activations are in shared memory
+  }
+  const int n_slots = routed ? rt->n_slots : 1;
+  const int n_tiles = n_rb * n_slots;
+  if (routed && lane == 0) {  // the routed experts are known now
+    for (int k = 0; k < S && warp + k * NW < n_tiles; ++k) issue(warp + k * NW, k, n_slots);
+  }
+  // the first ring fill of an unrouted matrix goes out right behind the
+  // activation loads (copied ahead of them, it would delay them by the time
+  // the whole GPU's first fill takes to drain)
+  auto first_fill = [&]() {
+    if (!routed && lane == 0)
+      for (int k = 0; k < S && warp + k * NW < n_tiles; ++k) issue(warp + k * NW, k, 1);
+  };
+  if (!self_route && pl.xq_smem && p.pro == PRO_QUANT) {
+    prologue_quant(p, xq_s, pl.xq_vec_bytes, red, first_fill);
+  } else {
+    first_fill();
+    if (!self_route && pl.xq_smem && !bulk_xq) prologue_load(p, xq_s, pl.xq_vec_bytes, -1);
   }
   consumer_sync();
-  const int n_slots = routed ? rt->n_slots : 1;
   const uint8_t* xbase = pl.xq_smem ? xq_s : p.qact;
   const int64_t xstride = pl.xq_smem ? (int64_t)pl.xq_vec_bytes : p.qact_stride;
-  const int n_tiles = n_rb * n_slots;
-  const int V = R * NMAT;
   XQ8 xc;
-  int cached_vi = -1;
-  for (int it = warp; it < n_tiles; it += NW) {
-    const int kk = it / NW;
-    const int bi = warp * S2_STAGES + kk % S2_STAGES, use = kk / S2_STAGES;
-    if (!mbar_wait_bounded(&full[bi], use & 1, p.status)) break;
+  int cached = -1;  // vi * G + g of the activation group in xc
+  for (int kk = 0, it = warp; it < n_tiles; ++kk, it += NW) {
+    const int s = kk % S;
+    if (!mbar_wait_bounded(&full[s], (kk / S) & 1, p.status)) break;
     const int rb = it / n_slots, si = it % n_slots;
     const int rbase = r0 + rb * R;
     const int nrows = min(R, r1 - rbase);
-    const uint8_t* tile = ring + (int64_t)bi * pl.tile_bytes;
+    const int RM = nrows * NMAT;  // (row, matrix) pairs; values v = rm * G + g
+    const uint8_t* tile = ring + (int64_t)s * pl.tile_bytes;
     int pb = 0, pe = p.b;
     if (routed) { pb = rt->slot_off[si]; pe = rt->slot_off[si + 1]; }
     for (int pi = pb; pi < pe; ++pi) {
       const int pair = routed ? rt->slot_pairs[pi] : pi;
       const int vi = p.xq_by_pair ? pair : (routed ? pair / p.k : pair);
-      float accv = 0.0f;
-      for (int g = 0; g < G; ++g) {
-        const int ng = group_units(p.K, g);
-        if (G > 1 || vi != cached_vi) {
-          if (lane < ng) xc.load_any(xbase + (int64_t)vi * xstride + qact_group_offset(g), ng, lane);
-          cached_vi = (G == 1) ? vi : -1;
-        }
-        const int64_t goff = group_offset(WT, p.K, g);
-        float part[8];
+      float part[8];
 #pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          part[v] = 0.0f;
-          const int r = NMAT == 2 ? (v >> 1) : v, m = NMAT == 2 ? (v & 1) : 0;
-          if (v < V && r < nrows && lane < ng)
-            part[v] = unit_dot_x<WT>(tile + ((int64_t)m * R + r) * p.rowstride + goff, xc, ng, lane);
+      for (int j = 0; j < 8; ++j) part[j] = 0.0f;
+      // one unit dot in the loop body (a small hot loop stays in the
+      // instruction cache); value j = rm * G + g lands in part[j]
+      int j = 0;
+#pragma unroll 1
+      for (int rm = 0; rm < RM; ++rm) {
+        const int r = NMAT == 2 ? (rm >> 1) : rm, m = NMAT == 2 ? (rm & 1) : 0;
+        const uint8_t* wrow = tile + ((int64_t)m * R + r) * rs;
+#pragma unroll 1
+        for (int g = 0; g < G; ++g, ++j) {
+          const int ng = group_units(p.K, g);
+          if (vi * G + g != cached) {
+            if (lane < ng) {
+              const uint8_t* xg = xbase + (int64_t)vi * xstride + qact_group_offset(g);
+              if (pl.xq_smem)
+                xc.load(xg, ng, lane);
+              else
+                xc.load_any(xg, ng, lane);
+            }
+            cached = vi * G + g;
+          }
+          float d = 0.0f;
+          if (lane < ng) d = unit_dot_x<WT>(wrow + group_offset(WT, p.K, g), xc, ng, lane);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) part[q] = (q == j) ? d : part[q];
         }
-        accv = __fadd_rn(accv, reduce8(part, lane));
       }
-      if ((lane & 3) == 0) {
-        const int v = ((lane >> 2) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 4) & 1);
-        const int r = NMAT == 2 ? (v >> 1) : v, m = NMAT == 2 ? (v & 1) : 0;
-        if (v < V && r < nrows) acc[((rbase - r0 + r) * p.n_pairs + pair) * NMAT + m] = accv;
+      const float sum = reduce8(part, lane);
+      // (row, matrix) rm = lane adds its group sums in order; value v sits in
+      // lane ((v >> 2) & 1) << 2 | ((v >> 1) & 1) << 3 | (v & 1) << 4
+      float tot = 0.0f;
+      for (int g = 0; g < G; ++g) {
+        const int v = lane * G + g;
+        const int src = ((v >> 2) & 1) << 2 | ((v >> 1) & 1) << 3 | (v & 1) << 4;
+        const float sg = __shfl_sync(0xffffffffu, sum, src);
+        tot = __fadd_rn(tot, sg);
+      }
+      if (lane < RM) {
+        const int r = NMAT == 2 ? (lane >> 1) : lane, m = NMAT == 2 ? (lane & 1) : 0;
+        acc[((rbase - r0 + r) * p.n_pairs + pair) * NMAT + m] = tot;
       }
     }
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[bi]);
+    const int nxt = it + S * NW;  // this slot's next tile
+    if (lane == 0 && nxt < n_tiles) issue(nxt, s, n_slots);
   }
   consumer_sync();
+  // the last CTA past the routing wait re-arms the counters for the next launch
+  if (depart_old == (int)gridDim.x - 1) {
+    atomicExch(&p.rsync[0], 0);
+    atomicExch(&p.rsync[1], 0);
+  }
   if (*(volatile int*)p.status == ERR_TIMEOUT || r0 >= r1) return;  // uniform across the consumers
   run_epilogue(p, acc, r0, r1, red);
 }
@@ -1216,17 +1388,19 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 
 template <int WT>
 static cudaError_t launch_stream_t(const StreamParams& p, int grid, cudaStream_t st, bool pdl) {
-  const Plan2 q = make_plan2(p);
-  if (q.total <= 227 * 1024 && (p.nmat == 1 || p.nmat == 2)) {
+  const int smem2 = stream2_smem_bytes(p);
+  if (smem2 <= S2_SMEM) {
+    StreamParams q = p;
+    q.pl = make_plan2(p);
     cudaError_t e;
     if (p.nmat == 1) {
-      e = cudaFuncSetAttribute(stream2_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, q.total);
+      e = cudaFuncSetAttribute(stream2_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
       if (e != cudaSuccess) return e;
-      return launch_pdl(stream2_kernel<WT, 1>, dim3(grid), dim3((NW + 1) * 32), q.total, st, pdl, p);
+      return launch_pdl(stream2_kernel<WT, 1>, dim3(grid), dim3(NW * 32), smem2, st, pdl, q);
     }
-    e = cudaFuncSetAttribute(stream2_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, q.total);
+    e = cudaFuncSetAttribute(stream2_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
     if (e != cudaSuccess) return e;
-    return launch_pdl(stream2_kernel<WT, 2>, dim3(grid), dim3((NW + 1) * 32), q.total, st, pdl, p);
+    return launch_pdl(stream2_kernel<WT, 2>, dim3(grid), dim3(NW * 32), smem2, st, pdl, q);
   }
   if (p.pro == PRO_ROUTE) return cudaErrorInvalidValue;  // only the warp-tile kernel routes in its prologue
   const StreamPlan pl = make_plan(p);

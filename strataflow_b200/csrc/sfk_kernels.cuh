@@ -24,7 +24,9 @@ struct Route {
   int slot_pairs[MAXP];
   int ids[MAXP];
   float w[MAXP];
+  int pad2[3];  // size a multiple of 16 bytes: one bulk copy moves it
 };
+static_assert(sizeof(Route) % 16 == 0, "Route is moved by 1-D bulk copies");
 
 enum Prologue : int {
   PRO_QUANT = 0,  // x f32 [b][K] (+ optional RMSNorm * w) -> quantize to act type
@@ -49,6 +51,14 @@ struct KvView {
   int n_head_kv;
   int head_dim;
   int f16;
+};
+
+// Shared-memory plan of the warp-tile streaming kernel (computed on the host
+// at launch; the kernel reads it from its parameters)
+struct Plan2 {
+  int stages, R, G, tile_bytes;
+  int ring_off, xq_off, acc_off, red_off, route_off, xn_off, seg_off, probs_off, total;
+  int xq_smem, xq_vec_bytes;
 };
 
 struct StreamParams {
@@ -81,6 +91,8 @@ struct StreamParams {
   int xq_resident;         // all groups of all vectors fit in smem
   const float* w_r;        // PRO_ROUTE: F32 router [n_expert][K]; the routing is written to `route`
   int n_expert;
+  float* logits;           // PRO_ROUTE: [b][n_expert] router logits, exchanged between the CTAs
+  int* rsync;              // PRO_ROUTE: [2] arrival / departure counters, zero between launches
   // epilogue
   int epi;
   float* y;                // EPI_STORE / EPI_RESID / EPI_DOWN output; EPI_QKV q out
@@ -102,6 +114,10 @@ struct StreamParams {
   unsigned long long* clear_keys;  // zeroed by CTA 0 once the previous kernel finished (or null)
   int clear_n;
   int* status;
+  // warp-tile kernel ring: tile target bytes and stages per warp (0: defaults)
+  int s2_tile;
+  int s2_stages;
+  Plan2 pl;  // filled by the launcher
 };
 
 struct AttnParams {
