@@ -742,6 +742,26 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   // step buffers
   e->attn_cluster = attn_cluster_for(e->max_pages * 16);
   e->attn_max_chunk = (e->max_pages + e->attn_cluster - 1) / e->attn_cluster * 16;  // whole pages per CTA
+  {
+    // 16-CTA clusters (twice the SMs per kv head) when every (sequence, kv
+    // head) cluster of a step fits on the GPU at once; SFK_ATTN_CLUSTER
+    // forces 8 or 16
+    int want = 0;
+    if (const char* v = getenv("SFK_ATTN_CLUSTER")) want = atoi(v);
+    if (want == 0 && B * hp->n_head_kv <= 8 && e->max_pages >= 32) want = 16;
+    if (want == 16 && e->attn_cluster != 16) {
+      const int mc16 = (e->max_pages + 15) / 16 * 16;
+      if (attn_active_clusters(e->hd, hp->kv_type == SFK_KV_F16, hp->n_head / hp->n_head_kv, 16, mc16) >=
+          B * hp->n_head_kv) {
+        e->attn_cluster = 16;
+        e->attn_max_chunk = mc16;
+      }
+    }
+    if (want == 8 && e->attn_cluster == 16 && e->max_pages * 16 <= 8 * 2048) {
+      e->attn_cluster = 8;
+      e->attn_max_chunk = (e->max_pages + 7) / 8 * 16;
+    }
+  }
   if (attn_smem_bytes(e->hd, hp->n_head / hp->n_head_kv, hp->kv_type == SFK_KV_F16, e->attn_max_chunk) >
       (size_t)SMEM_LIMIT) {
     sfk_engine_free(e);

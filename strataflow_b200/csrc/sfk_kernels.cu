@@ -26,6 +26,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 
 #include "sfk_act.cuh"
 #include "sfk_device.cuh"
@@ -81,7 +82,8 @@ int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, in
 }
 
 // consumer-only named barrier (the producer warp never joins it)
-__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"r"(NW * 32) : "memory"); }
+template <int NWS>
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"r"(NWS * 32) : "memory"); }
 
 // Tile walk shared by producer and consumers.  Row-outer when the whole
 // activation is resident in shared memory, group-outer otherwise (then the
@@ -141,22 +143,22 @@ struct NoOp {
 
 // `after_loads` runs once the first vector's loads are in flight (a caller
 // queues its weight copies behind them).
-template <typename F = NoOp>
+template <int NWS, typename F = NoOp>
 __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_bytes, double* red,
                                F after_loads = F{}) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.K;
   const int nblk = K / QK_K;
-  constexpr int RB = 4;  // 256-column blocks a warp holds in registers
+  constexpr int RB = 32 / NWS;  // 256-column blocks a warp holds in registers (K <= 8192 on this path)
   for (int t = 0; t < p.n_vec; ++t) {
     const float* x = p.x + (int64_t)t * K;
     uint8_t* qa = xq + (int64_t)t * xq_vec_bytes;
-    if (nblk <= RB * NW) {
+    if (nblk <= RB * NWS) {
       // this warp's blocks of x (and of the norm weight), one round trip
       float xv[RB][8], wv[RB][8];
 #pragma unroll
       for (int i = 0; i < RB; ++i) {
-        const int blk = warp + i * NW;
+        const int blk = warp + i * NWS;
         if (blk < nblk) {
           const float4* xp = reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8);
           const float4 x0 = xp[0], x1 = xp[1];
@@ -176,31 +178,31 @@ __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_by
         double s = 0.0;
 #pragma unroll
         for (int i = 0; i < RB; ++i)
-          if (warp + i * NW < nblk) {
+          if (warp + i * NWS < nblk) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) s += (double)__fmul_rn(xv[i][j], xv[i][j]);
           }
         s = warp_sum_d(s);
         if (lane == 0) red[warp] = s;
-        consumer_sync();
+        consumer_sync<NWS>();
         double tot = 0.0;
-        for (int w = 0; w < NW; ++w) tot += red[w];  // every thread, same order
+        for (int w = 0; w < NWS; ++w) tot += red[w];  // every thread, same order
         const float mean = (float)(tot / (double)K);
         scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-        consumer_sync();  // red is reused by the next vector
+        consumer_sync<NWS>();  // red is reused by the next vector
       }
       float vn[RB][8];
 #pragma unroll
       for (int i = 0; i < RB; ++i)
 #pragma unroll
         for (int j = 0; j < 8; ++j) vn[i][j] = p.norm_w ? __fmul_rn(__fmul_rn(xv[i][j], scale), wv[i][j]) : xv[i][j];
-      const int nb = warp < nblk ? (nblk - warp + NW - 1) / NW : 0;
+      const int nb = warp < nblk ? (nblk - warp + NWS - 1) / NWS : 0;
       if (p.act_type == T_Q8_K) {
-        qact_put_q8k_blocks<RB>(qa, K, warp, NW, nb < RB ? nb : RB, vn, lane);
+        qact_put_q8k_blocks<RB>(qa, K, warp, NWS, nb < RB ? nb : RB, vn, lane);
       } else {
 #pragma unroll
         for (int i = 0; i < RB; ++i)
-          if (i < nb) qact_put(p.act_type, qa, K, warp + i * NW, vn[i], lane);
+          if (i < nb) qact_put(p.act_type, qa, K, warp + i * NWS, vn[i], lane);
       }
       continue;
     }
@@ -208,24 +210,24 @@ __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_by
     float scale = 1.0f;
     if (p.norm_w) {
       double s = 0.0;
-      for (int c = tid; c < K; c += NW * 32) {
+      for (int c = tid; c < K; c += NWS * 32) {
         const float v = x[c];
         s += (double)__fmul_rn(v, v);
       }
       s = warp_sum_d(s);
       if (lane == 0) red[warp] = s;
-      consumer_sync();
+      consumer_sync<NWS>();
       if (tid == 0) {
         double tot = 0.0;
-        for (int w = 0; w < NW; ++w) tot += red[w];
-        red[NW] = tot;
+        for (int w = 0; w < NWS; ++w) tot += red[w];
+        red[NWS] = tot;
       }
-      consumer_sync();
-      const float mean = (float)(red[NW] / (double)K);
+      consumer_sync<NWS>();
+      const float mean = (float)(red[NWS] / (double)K);
       scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-      consumer_sync();
+      consumer_sync<NWS>();
     }
-    for (int blk = warp; blk < nblk; blk += NW) {
+    for (int blk = warp; blk < nblk; blk += NWS) {
       float v[8];
       const float4 a = *reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8);
       const float4 b = *reinterpret_cast<const float4*>(x + blk * QK_K + lane * 8 + 4);
@@ -243,6 +245,7 @@ __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_by
 }
 
 // Copy qact vectors (all groups, or group g only) from global to shared.
+template <int NWS>
 __device__ void prologue_load(const StreamParams& p, uint8_t* xq, int xq_vec_bytes, int g_only) {
   const int tid = threadIdx.x;
   for (int vi = 0; vi < p.n_vec; ++vi) {
@@ -257,7 +260,7 @@ __device__ void prologue_load(const StreamParams& p, uint8_t* xq, int xq_vec_byt
       src += qact_group_offset(g_only);
       nbytes = (qact_group_bytes(group_units(p.K, g_only)) + 15) & ~15;
     }
-    for (int64_t o = tid * 16; o < nbytes; o += NW * 32 * 16)
+    for (int64_t o = tid * 16; o < nbytes; o += NWS * 32 * 16)
       *reinterpret_cast<uint4*>(dst + o) = __ldcg(reinterpret_cast<const uint4*>(src + o));
   }
 }
@@ -270,11 +273,12 @@ __device__ __forceinline__ unsigned int ordered_f32(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+template <int NWS>
 __device__ void epi_qkv(const StreamParams& p, const float* acc, int r0, int r1) {
   const int hd = p.kv.head_dim, Hkv = p.kv.n_head_kv;
   const int nq = p.n_head * hd, nk = Hkv * hd;
   const int npair_rows = (r1 - r0) / 2;
-  for (int idx = threadIdx.x; idx < npair_rows * p.b; idx += NW * 32) {
+  for (int idx = threadIdx.x; idx < npair_rows * p.b; idx += NWS * 32) {
     const int t = idx / npair_rows;
     const int r = r0 + 2 * (idx % npair_rows);
     const float x0 = acc[((r - r0) * p.n_pairs + t)];
@@ -317,11 +321,12 @@ __device__ void epi_qkv(const StreamParams& p, const float* acc, int r0, int r1)
   }
 }
 
+template <int NWS>
 __device__ void epi_gateup(const StreamParams& p, const float* acc, int r0, int r1, int* flags) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nr = r1 - r0;
   // h = silu(gate) * up  (ggml_swiglu_split(gate, up), engine.cpp:1969)
-  for (int idx = tid; idx < nr * p.n_pairs; idx += NW * 32) {
+  for (int idx = tid; idx < nr * p.n_pairs; idx += NWS * 32) {
     const int row = idx % nr, pr = idx / nr;
     const float g = acc[(row * p.n_pairs + pr) * 2 + 0];
     const float u = acc[(row * p.n_pairs + pr) * 2 + 1];
@@ -329,7 +334,7 @@ __device__ void epi_gateup(const StreamParams& p, const float* acc, int r0, int 
     p.h[(int64_t)pr * p.rows + r0 + row] = __fmul_rn(sl, u);
   }
   __threadfence();
-  consumer_sync();
+  consumer_sync<NWS>();
   // 256-row groups completed by this CTA's rows get requantized (Q8_K / Q8_0)
   // by whichever CTA adds the last rows to the group's counter.
   const int q0 = r0 / QK_K, q1 = (r1 - 1) / QK_K;
@@ -340,11 +345,11 @@ __device__ void epi_gateup(const StreamParams& p, const float* acc, int r0, int 
       flags[q - q0] = (old + (hi - lo) == QK_K) ? 1 : 0;
     }
   }
-  consumer_sync();
+  consumer_sync<NWS>();
   for (int q = q0; q <= q1; ++q) {
     if (!flags[q - q0]) continue;
     __threadfence();
-    for (int pr = warp; pr < p.n_pairs; pr += NW) {
+    for (int pr = warp; pr < p.n_pairs; pr += NWS) {
       const float* hp = p.h + (int64_t)pr * p.rows + q * QK_K + lane * 8;
       const float4 a = __ldcg(reinterpret_cast<const float4*>(hp));
       const float4 b = __ldcg(reinterpret_cast<const float4*>(hp + 4));
@@ -355,10 +360,11 @@ __device__ void epi_gateup(const StreamParams& p, const float* acc, int r0, int 
   }
 }
 
+template <int NWS>
 __device__ void epi_down(const StreamParams& p, const float* acc, int r0, int r1) {
   const int nr = r1 - r0;
   const int k = p.k;
-  for (int idx = threadIdx.x; idx < nr * p.b; idx += NW * 32) {
+  for (int idx = threadIdx.x; idx < nr * p.b; idx += NWS * 32) {
     const int row = idx % nr, t = idx / nr;
     // experts * weights, then moe_out = e0 + e1 + ..., then + ffn_inp
     // (engine.cpp:1973-1986)
@@ -369,13 +375,14 @@ __device__ void epi_down(const StreamParams& p, const float* acc, int r0, int r1
   }
 }
 
+template <int NWS>
 __device__ void epi_lmhead(const StreamParams& p, const float* acc, int r0, int r1, unsigned long long* red) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nr = r1 - r0;
   for (int t = 0; t < p.b; ++t) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int row = tid; row < nr; row += NW * 32) {
+    for (int row = tid; row < nr; row += NWS * 32) {
       const float v = acc[row * p.n_pairs + t];
       if (p.store_logits) p.y[(int64_t)t * p.y_stride + r0 + row] = v;
       if (v > best) { best = v; bi = r0 + row; }
@@ -390,21 +397,22 @@ __device__ void epi_lmhead(const StreamParams& p, const float* acc, int r0, int 
       red[warp] = bi == 0x7fffffff ? 0ull
                                    : (((unsigned long long)ordered_f32(best) << 32) |
                                       (unsigned long long)(0xFFFFFFFFu - (unsigned)bi));
-    consumer_sync();
+    consumer_sync<NWS>();
     if (tid == 0) {
       unsigned long long m = 0;
-      for (int w = 0; w < NW; ++w) m = red[w] > m ? red[w] : m;
+      for (int w = 0; w < NWS; ++w) m = red[w] > m ? red[w] : m;
       if (m) atomicMax(&p.argmax_key[t], m);
     }
-    consumer_sync();
+    consumer_sync<NWS>();
   }
 }
 
+template <int NWS>
 __device__ void run_epilogue(const StreamParams& p, const float* acc, int r0, int r1, double* red) {
   switch (p.epi) {
     case EPI_STORE: {
       const int nr = r1 - r0;
-      for (int idx = threadIdx.x; idx < nr * p.n_pairs; idx += NW * 32) {
+      for (int idx = threadIdx.x; idx < nr * p.n_pairs; idx += NWS * 32) {
         const int row = idx % nr, pr = idx / nr;
         p.y[(int64_t)pr * p.y_stride + r0 + row] = acc[row * p.n_pairs + pr];
       }
@@ -412,17 +420,17 @@ __device__ void run_epilogue(const StreamParams& p, const float* acc, int r0, in
     }
     case EPI_RESID: {
       const int nr = r1 - r0;
-      for (int idx = threadIdx.x; idx < nr * p.b; idx += NW * 32) {
+      for (int idx = threadIdx.x; idx < nr * p.b; idx += NWS * 32) {
         const int row = idx % nr, t = idx / nr;
         const float v = acc[row * p.n_pairs + t];
         p.y[(int64_t)t * p.y_stride + r0 + row] = p.res ? __fadd_rn(v, p.res[(int64_t)t * p.y_stride + r0 + row]) : v;
       }
       break;
     }
-    case EPI_QKV: epi_qkv(p, acc, r0, r1); break;
-    case EPI_GATEUP: epi_gateup(p, acc, r0, r1, reinterpret_cast<int*>(red)); break;
-    case EPI_DOWN: epi_down(p, acc, r0, r1); break;
-    case EPI_LMHEAD: epi_lmhead(p, acc, r0, r1, reinterpret_cast<unsigned long long*>(red)); break;
+    case EPI_QKV: epi_qkv<NWS>(p, acc, r0, r1); break;
+    case EPI_GATEUP: epi_gateup<NWS>(p, acc, r0, r1, reinterpret_cast<int*>(red)); break;
+    case EPI_DOWN: epi_down<NWS>(p, acc, r0, r1); break;
+    case EPI_LMHEAD: epi_lmhead<NWS>(p, acc, r0, r1, reinterpret_cast<unsigned long long*>(red)); break;
     default: break;
   }
 }
@@ -511,20 +519,20 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
   if (p.route) tw.n_slots = p.route->n_slots;
   if (p.xq_resident) {
     if (p.pro == PRO_QUANT)
-      prologue_quant(p, xq, pl.xq_vec_bytes, red);
+      prologue_quant<NW>(p, xq, pl.xq_vec_bytes, red);
     else
-      prologue_load(p, xq, pl.xq_vec_bytes, -1);
+      prologue_load<NW>(p, xq, pl.xq_vec_bytes, -1);
   }
-  consumer_sync();
+  consumer_sync<NW>();
 
   uint32_t it = 0;
   int cur_g = -1;
   bool ok = true;
   for (tw.begin(); !tw.done(); tw.next(), ++it) {
     if (!p.xq_resident && tw.g != cur_g) {
-      consumer_sync();
-      prologue_load(p, xq, pl.xq_vec_bytes, tw.g);
-      consumer_sync();
+      consumer_sync<NW>();
+      prologue_load<NW>(p, xq, pl.xq_vec_bytes, tw.g);
+      consumer_sync<NW>();
       cur_g = tw.g;
     }
     const int s = it % pl.n_stages;
@@ -556,10 +564,10 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
   }
   (void)ng_full;
   (void)ok;
-  consumer_sync();
+  consumer_sync<NW>();
   if (*(volatile int*)p.status == ERR_TIMEOUT || r0 >= r1) return;  // uniform across the consumers
 
-  run_epilogue(p, acc, r0, r1, red);
+  run_epilogue<NW>(p, acc, r0, r1, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -582,8 +590,9 @@ constexpr int S2_SMEM = 227 * 1024;
 
 __host__ __device__ inline int al16i(int64_t v) { return (int)((v + 15) & ~(int64_t)15); }
 
-inline Plan2 make_plan2(const StreamParams& p) {
+inline Plan2 make_plan2(const StreamParams& p, int NWS) {
   Plan2 q;
+  q.nws = NWS;
   const int64_t rs = p.rowstride;
   q.G = n_groups(p.K);
   const int64_t xq_all = (int64_t)p.n_vec * qact_bytes(p.K);
@@ -594,7 +603,7 @@ inline Plan2 make_plan2(const StreamParams& p) {
   const int xq_b = q.xq_smem ? al16i(xq_all) : 0;
   const int acc_b = al16i((int64_t)p.rows_per_cta * p.n_pairs * p.nmat * 4);
   const int route_b = (routed ? al16i(sizeof(Route)) : 0) + (rt ? p.K * 4 + al16i(p.b * p.n_expert * 4) : 0);
-  const int bars = al16i(NW * S2_MAXSTAGES * 8 + 16);  // per-warp full[] | router-weights | prologue
+  const int bars = al16i(NWS * S2_MAXSTAGES * 8 + 16);  // per-warp full[] | router-weights | prologue
   const int fixed = bars + xq_b + acc_b + 64 * 8 + route_b;
   int rmax = 8 / (p.nmat * q.G);
   if (rmax < 1) rmax = 1;
@@ -602,16 +611,16 @@ inline Plan2 make_plan2(const StreamParams& p) {
   R = R < 1 ? 1 : (R > rmax ? rmax : R);
   // keep two tiles per warp in flight: a warp with one slot idles through
   // every copy's latency
-  while (R > 1 && (S2_SMEM - fixed) / ((int64_t)NW * p.nmat * R * rs) < 2) --R;
+  while (R > 1 && (S2_SMEM - fixed) / ((int64_t)NWS * p.nmat * R * rs) < 2) --R;
   q.R = R;
   q.tile_bytes = (int)(p.nmat * R * rs);
-  int S = (int)((S2_SMEM - fixed) / ((int64_t)NW * q.tile_bytes));
+  int S = (int)((S2_SMEM - fixed) / ((int64_t)NWS * q.tile_bytes));
   if (S > S2_MAXSTAGES) S = S2_MAXSTAGES;
   if (p.s2_stages > 0 && S > p.s2_stages) S = p.s2_stages;
   if (S < 1) S = 1;
   q.stages = S;
   q.ring_off = bars;
-  q.xq_off = q.ring_off + NW * S * q.tile_bytes;
+  q.xq_off = q.ring_off + NWS * S * q.tile_bytes;
   q.acc_off = q.xq_off + xq_b;
   q.red_off = q.acc_off + acc_b;
   q.route_off = q.red_off + 64 * 8;
@@ -622,8 +631,9 @@ inline Plan2 make_plan2(const StreamParams& p) {
   return q;
 }
 
+template <int NWS>
 struct ConsumerSync {
-  __device__ void operator()() const { consumer_sync(); }
+  __device__ void operator()() const { consumer_sync<NWS>(); }
 };
 
 // Sum 8 lane-distributed values over the warp with the 32-lane butterfly
@@ -657,10 +667,38 @@ __device__ __forceinline__ float reduce8(const float v[8], int lane) {
 
 // shared memory of the warp-tile kernel, or more than any SM has when a tile
 // cannot hold all of one row's group sums (nmat * groups > 8)
+// Warp count and plan of the warp-tile kernel: 16 consumer warps when each
+// keeps two tiles in flight, else 8 (SFK_STREAM_WARPS forces 8 or 16);
+// nws = 0 when a tile cannot hold all of one row's group sums or the rings
+// do not fit.
+static int stream_warps_forced() {
+  static const int v = [] {
+    const char* e = getenv("SFK_STREAM_WARPS");
+    return e ? atoi(e) : 0;
+  }();
+  return v;
+}
+Plan2 choose_plan2(const StreamParams& p) {
+  Plan2 none{};
+  none.nws = 0;
+  if (p.nmat != 1 && p.nmat != 2) return none;
+  const int forced = stream_warps_forced();
+  Plan2 best = none;
+  for (int nws : {16, 8}) {
+    if (forced && forced != nws) continue;
+    const Plan2 q = make_plan2(p, nws);
+    if (p.nmat * q.G > 8 || q.total > S2_SMEM) continue;
+    if (q.stages >= 2 || forced) return q;
+    if (best.nws == 0) best = q;
+  }
+  return best;
+}
+
+// shared memory of the warp-tile kernel, or more than any SM has when it
+// cannot run the launch
 int stream2_smem_bytes(const StreamParams& p) {
-  const Plan2 q = make_plan2(p);
-  if ((p.nmat != 1 && p.nmat != 2) || p.nmat * q.G > 8) return 1 << 30;
-  return q.total;
+  const Plan2 q = choose_plan2(p);
+  return q.nws ? q.total : 1 << 30;
 }
 
 template <int WT>
@@ -680,14 +718,14 @@ __device__ __forceinline__ float unit_dot_x(const uint8_t* wg, const XQ8& x, int
   }
 }
 
-template <int WT, int NMAT>
-__global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams p) {
+template <int WT, int NMAT, int NWS>
+__global__ void __launch_bounds__(NWS * 32, 1) stream2_kernel(const StreamParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const Plan2& pl = p.pl;  // planned on the host: no divisions before the first copy
   const int S = pl.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem) + warp * S;  // this warp's [S]
-  uint64_t* pro_bar = reinterpret_cast<uint64_t*>(smem) + NW * S2_MAXSTAGES;  // prologue copies landed
+  uint64_t* pro_bar = reinterpret_cast<uint64_t*>(smem) + NWS * S2_MAXSTAGES;  // prologue copies landed
   uint8_t* ring_all = smem + pl.ring_off;
   uint8_t* ring = ring_all + (int64_t)warp * S * pl.tile_bytes;
   uint8_t* xq_s = smem + pl.xq_off;
@@ -706,7 +744,7 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
 
   if (lane == 0) {
     for (int i = 0; i < S; ++i) mbar_init(&full[i], 1);
-    if (warp == 0) mbar_init(pro_bar, NW);
+    if (warp == 0) mbar_init(pro_bar, NWS);
     fence_mbar_init();
   }
   __syncthreads();
@@ -729,12 +767,15 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
   // the router weights are static, so the first row slice is loaded before
   // the wait on the previous kernel
   const int nq = self_route ? p.b * p.n_expert : 0;
-  const int rcols = p.K / NW;  // columns of a logit per warp (a multiple of 32)
+  // columns of a logit per warp: a multiple of 4 (16-byte loads), the last
+  // warp's range clipped at K
+  const int rcols = ((p.K + NWS - 1) / NWS + 3) & ~3;
+  const int rc0 = min(p.K, warp * rcols), rc1 = min(p.K, rc0 + rcols);
   constexpr int WPRE = 4;
   float4 wpre[WPRE];
-  const bool pre = (int)blockIdx.x < nq && rcols % 128 == 0 && rcols / 128 <= WPRE;
+  const bool pre = (int)blockIdx.x < nq && rcols % 128 == 0 && rcols / 128 <= WPRE && rc1 - rc0 == rcols;
   if (pre) {
-    const float* wr = p.w_r + (int64_t)(blockIdx.x % p.n_expert) * p.K + warp * rcols + lane * 4;
+    const float* wr = p.w_r + (int64_t)(blockIdx.x % p.n_expert) * p.K + rc0 + lane * 4;
 #pragma unroll
     for (int i = 0; i < WPRE; ++i)
       if (i < rcols / 128) wpre[i] = *reinterpret_cast<const float4*>(wr + i * 128);
@@ -750,11 +791,11 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
     uint32_t mine = 0;
     if (routed && !self_route && warp == 0) mine += (uint32_t)sizeof(Route);
     if (bulk_xq)
-      for (int vi = warp; vi < p.n_vec; vi += NW) mine += (uint32_t)pl.xq_vec_bytes;
+      for (int vi = warp; vi < p.n_vec; vi += NWS) mine += (uint32_t)pl.xq_vec_bytes;
     mbar_arrive_expect_tx(pro_bar, mine);
     if (routed && !self_route && warp == 0) bulk_g2s(sroute, p.route, (uint32_t)sizeof(Route), pro_bar);
     if (bulk_xq)
-      for (int vi = warp; vi < p.n_vec; vi += NW)
+      for (int vi = warp; vi < p.n_vec; vi += NWS)
         bulk_g2s(xq_s + (int64_t)vi * pl.xq_vec_bytes, p.qact + (int64_t)vi * p.qact_stride,
                  (uint32_t)pl.xq_vec_bytes, pro_bar);
   }
@@ -766,14 +807,14 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
     const int tid = threadIdx.x;
     for (int t = 0; t < p.b; ++t) {
       // ffn_norm + quantize token t (every CTA needs its activations)
-      route_norm<NW, 4>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
-                     xn_s, red, nullptr, ConsumerSync{});
+      route_norm<NWS, 32 / NWS>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
+                     xn_s, red, nullptr, ConsumerSync<NWS>{});
       for (int q = blockIdx.x; q < nq; q += gridDim.x) {
         if (q / p.n_expert != t) continue;
         // logit = sum_c (double)(w_r[e][c] * xn[c]): warp w sums its column
         // slice in four chains, the slices are added in order
-        const float* wr = p.w_r + (int64_t)(q % p.n_expert) * p.K + warp * rcols;
-        const float* xs = xn_s + warp * rcols;
+        const float* wr = p.w_r + (int64_t)(q % p.n_expert) * p.K + rc0;
+        const float* xs = xn_s + rc0;
         double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
         if (pre && q == (int)blockIdx.x) {
 #pragma unroll
@@ -786,7 +827,7 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
               a3 += (double)__fmul_rn(wpre[i].w, x4.w);
             }
         } else {
-          for (int c = lane * 4; c < rcols; c += 128) {
+          for (int c = lane * 4; c < rc1 - rc0; c += 128) {
             const float4 w4 = *reinterpret_cast<const float4*>(wr + c);
             const float4 x4 = *reinterpret_cast<const float4*>(xs + c);
             a0 += (double)__fmul_rn(w4.x, x4.x);
@@ -797,15 +838,15 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
         }
         const double a = warp_sum_d((a0 + a1) + (a2 + a3));
         if (lane == 0) red[warp] = a;
-        consumer_sync();
+        consumer_sync<NWS>();
         if (tid == 0) {
           double tot = 0.0;
-          for (int w = 0; w < NW; ++w) tot += red[w];
+          for (int w = 0; w < NWS; ++w) tot += red[w];
           p.logits[q] = (float)tot;
           __threadfence();
           atomicAdd(&p.rsync[0], 1);  // release: this logit is visible
         }
-        consumer_sync();
+        consumer_sync<NWS>();
       }
     }
     // every logit of the step, from every scoring CTA (bounded wait)
@@ -818,12 +859,12 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
         }
       }
     }
-    consumer_sync();
-    for (int i = tid; i < nq; i += NW * 32) probs_s[i] = __ldcg(&p.logits[i]);
-    consumer_sync();
-    for (int t = warp; t < p.b; t += NW)
+    consumer_sync<NWS>();
+    for (int i = tid; i < nq; i += NWS * 32) probs_s[i] = __ldcg(&p.logits[i]);
+    consumer_sync<NWS>();
+    for (int t = warp; t < p.b; t += NWS)
       route_select(probs_s + t * p.n_expert, p.n_expert, p.k, &sroute->ids[t * p.k], &sroute->w[t * p.k], lane);
-    consumer_sync();
+    consumer_sync<NWS>();
     if (tid == 0) {
       build_slots(sroute->ids, p.b * p.k, sroute);
       sroute->k = p.k;
@@ -832,11 +873,11 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
       // so the round trip stays off the critical path
       depart_old = atomicAdd(&p.rsync[1], 1);
     }
-    consumer_sync();
+    consumer_sync<NWS>();
     if (blockIdx.x == 0) {  // publish the routing for the down kernel and the host
       const int* src = reinterpret_cast<const int*>(sroute);
       int* dst = reinterpret_cast<int*>(const_cast<Route*>(p.route));
-      for (int i = threadIdx.x; i < (int)(sizeof(Route) / 4); i += NW * 32) dst[i] = src[i];
+      for (int i = threadIdx.x; i < (int)(sizeof(Route) / 4); i += NWS * 32) dst[i] = src[i];
     }
   } else if (bulk_pro) {
     mbar_wait_bounded(pro_bar, 0, p.status);  // routing and/or activations are in shared memory
@@ -844,27 +885,27 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
   const int n_slots = routed ? rt->n_slots : 1;
   const int n_tiles = n_rb * n_slots;
   if (routed && lane == 0) {  // the routed experts are known now
-    for (int k = 0; k < S && warp + k * NW < n_tiles; ++k) issue(warp + k * NW, k, n_slots);
+    for (int k = 0; k < S && warp + k * NWS < n_tiles; ++k) issue(warp + k * NWS, k, n_slots);
   }
   // the first ring fill of an unrouted matrix goes out right behind the
   // activation loads (copied ahead of them, it would delay them by the time
   // the whole GPU's first fill takes to drain)
   auto first_fill = [&]() {
     if (!routed && lane == 0)
-      for (int k = 0; k < S && warp + k * NW < n_tiles; ++k) issue(warp + k * NW, k, 1);
+      for (int k = 0; k < S && warp + k * NWS < n_tiles; ++k) issue(warp + k * NWS, k, 1);
   };
   if (!self_route && pl.xq_smem && p.pro == PRO_QUANT) {
-    prologue_quant(p, xq_s, pl.xq_vec_bytes, red, first_fill);
+    prologue_quant<NWS>(p, xq_s, pl.xq_vec_bytes, red, first_fill);
   } else {
     first_fill();
-    if (!self_route && pl.xq_smem && !bulk_xq) prologue_load(p, xq_s, pl.xq_vec_bytes, -1);
+    if (!self_route && pl.xq_smem && !bulk_xq) prologue_load<NWS>(p, xq_s, pl.xq_vec_bytes, -1);
   }
-  consumer_sync();
+  consumer_sync<NWS>();
   const uint8_t* xbase = pl.xq_smem ? xq_s : p.qact;
   const int64_t xstride = pl.xq_smem ? (int64_t)pl.xq_vec_bytes : p.qact_stride;
   XQ8 xc;
   int cached = -1;  // vi * G + g of the activation group in xc
-  for (int kk = 0, it = warp; it < n_tiles; ++kk, it += NW) {
+  for (int kk = 0, it = warp; it < n_tiles; ++kk, it += NWS) {
     const int s = kk % S;
     if (!mbar_wait_bounded(&full[s], (kk / S) & 1, p.status)) break;
     const int rb = it / n_slots, si = it % n_slots;
@@ -922,17 +963,17 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
       }
     }
     __syncwarp();
-    const int nxt = it + S * NW;  // this slot's next tile
+    const int nxt = it + S * NWS;  // this slot's next tile
     if (lane == 0 && nxt < n_tiles) issue(nxt, s, n_slots);
   }
-  consumer_sync();
+  consumer_sync<NWS>();
   // the last CTA past the routing wait re-arms the counters for the next launch
   if (depart_old == (int)gridDim.x - 1) {
     atomicExch(&p.rsync[0], 0);
     atomicExch(&p.rsync[1], 0);
   }
   if (*(volatile int*)p.status == ERR_TIMEOUT || r0 >= r1) return;  // uniform across the consumers
-  run_epilogue(p, acc, r0, r1, red);
+  run_epilogue<NWS>(p, acc, r0, r1, red);
 }
 
 // ---------------------------------------------------------------------------
@@ -948,9 +989,10 @@ __global__ void __launch_bounds__(NW * 32, 1) stream2_kernel(const StreamParams 
 // by one bulk copy into a ring of page slots (one ring for K, one for V).
 // Pages that earlier steps wrote are requested before the wait on the previous
 // kernel; only the page holding the current position waits for it.  The
-// cross-CTA steps (global max, global sum, the output reduction) go through
-// distributed shared memory with cluster barriers, so the two-pass softmax is
-// exact in one kernel.  The GQA group's query heads share every K/V page.
+// cross-CTA steps (global max, global sum, the output reduction) are pushes
+// into the other CTAs' shared memory, each closed by one mbarrier arrival per
+// CTA pair, so the two-pass softmax is exact in one kernel without cluster-wide
+// barriers.  The GQA group's query heads share every K/V page.
 // ---------------------------------------------------------------------------
 constexpr int ATT_NW = 8;
 constexpr int ATT_THREADS = ATT_NW * 32;
@@ -960,7 +1002,7 @@ constexpr int ATT_RING = 64 * 1024;  // bytes of K + V page slots
 
 struct AttnPlan {
   int ns, slot_bytes;
-  int kring, vring, qs, opart, sc, lsum, wred, gstd, lmax, invs, gst, total;
+  int kring, vring, qs, sc, lsum, gstd, lmax, invs, gst, ored, total;
 };
 
 __host__ __device__ inline int al16(int v) { return (v + 15) & ~15; }
@@ -971,18 +1013,17 @@ __host__ __device__ inline AttnPlan make_attn_plan(int hd, int gqa, int f16, int
   int ns = ATT_RING / (2 * a.slot_bytes);
   ns = ns < 2 ? 2 : (ns > 32 ? 32 : ns);
   a.ns = ns;
-  a.kring = (2 * ns * 8 + 127) & ~127;
+  a.kring = ((2 * ns + 3) * 8 + 127) & ~127;  // kfull[ns] | vfull[ns] | xbar[3]
   a.vring = a.kring + ns * a.slot_bytes;
   a.qs = a.vring + ns * a.slot_bytes;
-  a.opart = a.qs + al16(gqa * hd * 4);
-  a.sc = a.opart + gqa * hd * 8;
+  a.sc = a.qs + al16(gqa * hd * 4);
   a.lsum = a.sc + al16(gqa * max_chunk * 4);
-  a.wred = a.lsum + al16(gqa * 8);
-  a.gstd = a.wred + ATT_NW * gqa * 8;
+  a.gstd = a.lsum + al16(gqa * 8);
   a.lmax = a.gstd + ATT_MAXC * gqa * 8;
   a.invs = a.lmax + al16(gqa * 4);
   a.gst = a.invs + al16(gqa * 4);
-  a.total = a.gst + al16(ATT_MAXC * gqa * 4);
+  a.ored = a.gst + al16(ATT_MAXC * gqa * 4);
+  a.total = a.ored + (gqa * hd + ATT_MAXC) * 8;  // [C][ceil(gqa*hd/C)] partial outputs received
   return a;
 }
 
@@ -1004,14 +1045,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   uint8_t* kring = asmem + pl.kring;
   uint8_t* vring = asmem + pl.vring;
   float* qs = reinterpret_cast<float*>(asmem + pl.qs);
-  double* opart = reinterpret_cast<double*>(asmem + pl.opart);
   float* sc = reinterpret_cast<float*>(asmem + pl.sc);
   double* lsum = reinterpret_cast<double*>(asmem + pl.lsum);
-  double* wred = reinterpret_cast<double*>(asmem + pl.wred);
   double* gstd = reinterpret_cast<double*>(asmem + pl.gstd);
   float* lmax = reinterpret_cast<float*>(asmem + pl.lmax);
   float* invs = reinterpret_cast<float*>(asmem + pl.invs);
   float* gst = reinterpret_cast<float*>(asmem + pl.gst);
+  double* ored = reinterpret_cast<double*>(asmem + pl.ored);
+  uint64_t* xbar = vfull + pl.ns;  // [3]: maxima, sums, partial outputs received from the cluster
+  const int nout = gqa * HD, per = (nout + C - 1) / C;
 
   // Positions and the page table were written before the previous kernel
   // started (every kernel of the step lets its successor launch only after
@@ -1055,22 +1097,26 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
       mbar_init(&kfull[i], 1);
       mbar_init(&vfull[i], 1);
     }
+    for (int i = 0; i < 3; ++i) mbar_init(&xbar[i], C);  // one arrival per cluster CTA
     fence_mbar_init();
   }
   __syncthreads();
+  cluster_arrive();  // barriers initialised; waited on before the first remote push
+  // page copies are issued by every warp's lane 0 (one thread keeps only
+  // about one bulk copy per quarter microsecond going)
   const int npre = min(np, pl.ns);
-  if (tid == 0) {
-    for (int i = 0; i < npre; ++i)
+  if (lane == 0) {
+    for (int i = warp; i < npre; i += ATT_NW)
       if (pb + i < last_page) issue(0, i);
-    for (int i = 0; i < npre; ++i)
+    for (int i = warp; i < npre; i += ATT_NW)
       if (pb + i < last_page) issue(1, i);
   }
   pdl_wait();
   pdl_launch_dependents();
-  if (tid == 0) {
-    for (int i = 0; i < npre; ++i)
+  if (lane == 0) {
+    for (int i = warp; i < npre; i += ATT_NW)
       if (pb + i >= last_page) issue(0, i);
-    for (int i = 0; i < npre; ++i)
+    for (int i = warp; i < npre; i += ATT_NW)
       if (pb + i >= last_page) issue(1, i);
   }
   const float scale = __fdiv_rn(1.0f, sqrtf((float)HD));
@@ -1107,26 +1153,54 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
           kf[4] = __uint_as_float(r1.x); kf[5] = __uint_as_float(r1.y);
           kf[6] = __uint_as_float(r1.z); kf[7] = __uint_as_float(r1.w);
         }
-        for (int h = 0; h < gqa; ++h) {
-          const float4 qa = *reinterpret_cast<const float4*>(qs + h * HD + dl);
-          const float4 qb = *reinterpret_cast<const float4*>(qs + h * HD + dl + 4);
-          double a = (double)__fmul_rn(kf[0], qa.x);
-          a += (double)__fmul_rn(kf[1], qa.y);
-          a += (double)__fmul_rn(kf[2], qa.z);
-          a += (double)__fmul_rn(kf[3], qa.w);
-          a += (double)__fmul_rn(kf[4], qb.x);
-          a += (double)__fmul_rn(kf[5], qb.y);
-          a += (double)__fmul_rn(kf[6], qb.z);
-          a += (double)__fmul_rn(kf[7], qb.w);
+        // four heads at a time, two accumulation chains each (the double
+        // sums are order-free at this length), so the chains overlap
+        for (int h0 = 0; h0 < gqa; h0 += 4) {
+          double r[4];
 #pragma unroll
-          for (int o = LP / 2; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
-          if ((lane % LP) == 0 && jl < nloc) sc[h * mc + jl] = __fmul_rn((float)a, scale);
+          for (int hh = 0; hh < 4; ++hh) {
+            r[hh] = 0.0;
+            if (h0 + hh < gqa) {
+              const float4 qa = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl);
+              const float4 qb = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl + 4);
+              double a0 = (double)__fmul_rn(kf[0], qa.x), a1 = (double)__fmul_rn(kf[1], qa.y);
+              a0 += (double)__fmul_rn(kf[2], qa.z);
+              a1 += (double)__fmul_rn(kf[3], qa.w);
+              a0 += (double)__fmul_rn(kf[4], qb.x);
+              a1 += (double)__fmul_rn(kf[5], qb.y);
+              a0 += (double)__fmul_rn(kf[6], qb.z);
+              a1 += (double)__fmul_rn(kf[7], qb.w);
+              r[hh] = a0 + a1;
+            }
+          }
+#pragma unroll
+          for (int o = LP / 2; o > 0; o >>= 1)
+#pragma unroll
+            for (int hh = 0; hh < 4; ++hh) r[hh] += __shfl_xor_sync(0xffffffffu, r[hh], o);
+          if ((lane % LP) == 0 && jl < nloc) {
+#pragma unroll
+            for (int hh = 0; hh < 4; ++hh)
+              if (h0 + hh < gqa) sc[(h0 + hh) * mc + jl] = __fmul_rn((float)r[hh], scale);
+          }
         }
       }
-      __syncthreads();  // every warp is done with the slot
-      if (tid == 0 && i + pl.ns < np) issue(0, i + pl.ns);
+      if (i + pl.ns < np) {  // the slot is refilled: every warp must be done with it
+        __syncthreads();
+        if (lane == 0 && warp == i % ATT_NW) issue(0, i + pl.ns);
+      }
     }
   }
+  __syncthreads();  // all scores are in
+  // Exchanges between the cluster's CTAs are pushes: every CTA stores its
+  // values into each CTA's receive slots (distributed shared memory), then
+  // arrives once on each CTA's exchange barrier; a CTA waits on its own
+  // barrier for all C arrivals.  One hop, no cluster-wide barrier.
+  auto push_done = [&](int x) {
+    fence_cluster();  // this thread's remote stores, before the arrivals below
+    __syncthreads();
+    if (tid < C) mbar_arrive_remote(dsmem_addr(&xbar[x], tid));
+    mbar_wait_cluster_bounded(&xbar[x], 0, p.status);
+  };
   // local max per head
   for (int h = warp; h < gqa; h += ATT_NW) {
     float m = -INFINITY;
@@ -1134,31 +1208,32 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
     m = warp_max(m);
     if (lane == 0) lmax[h] = m;
   }
-  cl.sync();
-  // ---- global max (one parallel gather of the cluster's maxima), exp, local sum
-  for (int i = tid; i < gqa * C; i += ATT_THREADS) gst[i] = cl.map_shared_rank(lmax, i % C)[i / C];
   __syncthreads();
-  for (int h = 0; h < gqa; ++h) {
-    float M = -INFINITY;
-    for (int r = 0; r < C; ++r) M = fmaxf(M, gst[h * C + r]);
+  cluster_wait();  // every CTA of the cluster has initialised its barriers
+  if (tid < gqa * C) {
+    const int h = tid / C, r = tid % C;
+    dsmem_st_f32(dsmem_addr(&gst[h * C + rank], r), lmax[h]);
+  }
+  push_done(0);
+  // ---- global max, exp, local sum: warp h owns head h
+  for (int h = warp; h < gqa; h += ATT_NW) {
+    float M = lane < C ? gst[h * C + lane] : -INFINITY;
+    M = warp_max(M);
     double s = 0.0;
-    for (int jl = tid; jl < nloc; jl += ATT_THREADS) {
+    for (int jl = lane; jl < nloc; jl += 32) {
       const float e = sfk_expf(__fsub_rn(sc[h * mc + jl], M));
       sc[h * mc + jl] = e;
       s += (double)e;
     }
     s = warp_sum_d(s);
-    if (lane == 0) wred[warp * gqa + h] = s;
+    if (lane == 0) lsum[h] = s;
   }
   __syncthreads();
-  if (tid < gqa) {
-    double s = 0.0;
-    for (int w = 0; w < ATT_NW; ++w) s += wred[w * gqa + tid];
-    lsum[tid] = s;
+  if (tid < gqa * C) {
+    const int h = tid / C, r = tid % C;
+    dsmem_st_f64(dsmem_addr(&gstd[h * C + rank], r), lsum[h]);
   }
-  cl.sync();
-  for (int i = tid; i < gqa * C; i += ATT_THREADS) gstd[i] = cl.map_shared_rank(lsum, i % C)[i / C];
-  __syncthreads();
+  push_done(1);
   if (tid < gqa) {
     double S = 0.0;
     for (int r = 0; r < C; ++r) S += gstd[tid * C + r];
@@ -1170,9 +1245,9 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   // output dims (at most ATT_MAXG * HD / 2 / ATT_THREADS of them)
   constexpr int NPAIR = (ATT_MAXG * HD / 2 + ATT_THREADS - 1) / ATT_THREADS;
   const int npairs = gqa * HD / 2;
-  double acc[2 * NPAIR];
+  double acc[2 * NPAIR][2];  // two chains per output dim (order-free double sums)
 #pragma unroll
-  for (int i = 0; i < 2 * NPAIR; ++i) acc[i] = 0.0;
+  for (int i = 0; i < 2 * NPAIR; ++i) acc[i][0] = acc[i][1] = 0.0;
   for (int i = 0; i < np; ++i) {
     const int slot = i % pl.ns;
     mbar_wait_bounded(&vfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
@@ -1185,46 +1260,51 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
         const int h = (pi * 2) / HD, dd = (pi * 2) % HD;
         const float inv = invs[h];
         const float* sh = sc + h * mc + i * 16;
-        for (int jj = 0; jj < jn; ++jj) {
+        auto step = [&](int jj, int c) {
           const float pj = __fmul_rn(sh[jj], inv);
           float2 v;
           if constexpr (F16)
             v = __half22float2(*reinterpret_cast<const __half2*>(vp + (jj * HD + dd) * 2));
           else
             v = *reinterpret_cast<const float2*>(vp + (jj * HD + dd) * 4);
-          acc[2 * q2] += (double)__fmul_rn(v.x, pj);
-          acc[2 * q2 + 1] += (double)__fmul_rn(v.y, pj);
+          acc[2 * q2][c] += (double)__fmul_rn(v.x, pj);
+          acc[2 * q2 + 1][c] += (double)__fmul_rn(v.y, pj);
+        };
+        if (jn == 16) {
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) step(jj, jj & 1);
+        } else {
+          for (int jj = 0; jj < jn; ++jj) step(jj, jj & 1);
         }
       }
     }
-    __syncthreads();  // every thread is done with the slot
-    if (tid == 0 && i + pl.ns < np) issue(1, i + pl.ns);
+    if (i + pl.ns < np) {  // the slot is refilled: every thread must be done with it
+      __syncthreads();
+      if (lane == 0 && warp == i % ATT_NW) issue(1, i + pl.ns);
+    }
   }
+  // ---- partial outputs: output o belongs to CTA o / per, which adds the C
+  // partials in rank order
 #pragma unroll
   for (int q2 = 0; q2 < NPAIR; ++q2) {
     const int pi = tid + q2 * ATT_THREADS;
     if (pi < npairs) {
-      opart[2 * pi] = acc[2 * q2];
-      opart[2 * pi + 1] = acc[2 * q2 + 1];
+#pragma unroll
+      for (int d2 = 0; d2 < 2; ++d2) {
+        const int o = 2 * pi + d2, r = o / per;
+        dsmem_st_f64(dsmem_addr(&ored[rank * per + (o - r * per)], r), acc[2 * q2 + d2][0] + acc[2 * q2 + d2][1]);
+      }
     }
   }
-  cl.sync();
-  // ---- the cluster's partial outputs: CTA r reduces slice r (remote loads issued together)
+  push_done(2);
   {
-    const int nout = gqa * HD, per = (nout + C - 1) / C;
-    const int o1 = min(nout, (rank + 1) * per);
-    for (int o = rank * per + tid; o < o1; o += ATT_THREADS) {
-      double v[ATT_MAXC];
-#pragma unroll
-      for (int r = 0; r < ATT_MAXC; ++r) v[r] = r < C ? cl.map_shared_rank(opart, r)[o] : 0.0;
-      double s = 0.0;
-#pragma unroll
-      for (int r = 0; r < ATT_MAXC; ++r)
-        if (r < C) s += v[r];
-      p.out[((int64_t)t * p.n_head + hk * gqa) * HD + o] = (float)s;
+    const int o0 = rank * per, o1 = min(nout, o0 + per);
+    for (int o = o0 + tid; o < o1; o += ATT_THREADS) {
+      double sum = 0.0;
+      for (int r = 0; r < C; ++r) sum += ored[r * per + (o - o0)];
+      p.out[((int64_t)t * p.n_head + hk * gqa) * HD + o] = (float)sum;
     }
   }
-  cl.sync();  // no CTA leaves while another still reads its partials
 }
 
 size_t attn_smem_bytes(int hd, int gqa, int f16, int max_chunk) {
@@ -1388,19 +1468,26 @@ static cudaError_t launch_pdl(Kern k, dim3 grid, dim3 block, size_t smem, cudaSt
 
 template <int WT>
 static cudaError_t launch_stream_t(const StreamParams& p, int grid, cudaStream_t st, bool pdl) {
-  const int smem2 = stream2_smem_bytes(p);
-  if (smem2 <= S2_SMEM) {
+  const Plan2 pl2 = choose_plan2(p);
+  if (pl2.nws) {
     StreamParams q = p;
-    q.pl = make_plan2(p);
+    q.pl = pl2;
+    const int smem2 = pl2.total;
+    const dim3 block(pl2.nws * 32);
     cudaError_t e;
+#define SFK_LAUNCH2(NM, NWV)                                                                                      \
+  do {                                                                                                         \
+    e = cudaFuncSetAttribute(stream2_kernel<WT, NM, NWV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2); \
+    if (e != cudaSuccess) return e;                                                                            \
+    return launch_pdl(stream2_kernel<WT, NM, NWV>, dim3(grid), block, smem2, st, pdl, q);                      \
+  } while (0)
     if (p.nmat == 1) {
-      e = cudaFuncSetAttribute(stream2_kernel<WT, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
-      if (e != cudaSuccess) return e;
-      return launch_pdl(stream2_kernel<WT, 1>, dim3(grid), dim3(NW * 32), smem2, st, pdl, q);
+      if (pl2.nws == 16) SFK_LAUNCH2(1, 16);
+      SFK_LAUNCH2(1, 8);
     }
-    e = cudaFuncSetAttribute(stream2_kernel<WT, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2);
-    if (e != cudaSuccess) return e;
-    return launch_pdl(stream2_kernel<WT, 2>, dim3(grid), dim3(NW * 32), smem2, st, pdl, q);
+    if (pl2.nws == 16) SFK_LAUNCH2(2, 16);
+    SFK_LAUNCH2(2, 8);
+#undef SFK_LAUNCH2
   }
   if (p.pro == PRO_ROUTE) return cudaErrorInvalidValue;  // only the warp-tile kernel routes in its prologue
   const StreamPlan pl = make_plan(p);
@@ -1444,6 +1531,43 @@ static cudaError_t launch_attn_t(const AttnParams& p, cudaStream_t st, bool pdl)
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, attn_kernel<HD, F16>, p);
+}
+
+template <int HD, int F16>
+static int attn_active_clusters_t(int gqa, int cluster, int max_chunk) {
+  const size_t smem = attn_smem_bytes(HD, gqa, F16, max_chunk);
+  if (cudaFuncSetAttribute(attn_kernel<HD, F16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return 0;
+  if (cluster > 8 &&
+      cudaFuncSetAttribute(attn_kernel<HD, F16>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess)
+    return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(cluster, 1, 1);
+  cfg.blockDim = dim3(ATT_THREADS);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = cluster;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, attn_kernel<HD, F16>, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return n;
+}
+
+int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_chunk) {
+  switch (head_dim) {
+    case 32: return f16 ? attn_active_clusters_t<32, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<32, 0>(gqa, cluster, max_chunk);
+    case 64: return f16 ? attn_active_clusters_t<64, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<64, 0>(gqa, cluster, max_chunk);
+    case 128: return f16 ? attn_active_clusters_t<128, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<128, 0>(gqa, cluster, max_chunk);
+    case 256: return f16 ? attn_active_clusters_t<256, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<256, 0>(gqa, cluster, max_chunk);
+    default: return 0;
+  }
 }
 
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl) {

@@ -8,7 +8,7 @@ namespace sfk {
 
 constexpr int MAXP = 128;  // max (token, expert) pairs per step  (b * k)
 constexpr int MAXB = 16;   // max tokens per step
-constexpr int NW = 8;      // consumer warps per streaming CTA
+constexpr int NW = 8;      // consumer warps of the producer/consumer streaming kernel
 constexpr int RING_BYTES = 96 * 1024;
 
 // Routing of one MoE step, written by the router kernel (device memory).
@@ -56,6 +56,7 @@ struct KvView {
 // Shared-memory plan of the warp-tile streaming kernel (computed on the host
 // at launch; the kernel reads it from its parameters)
 struct Plan2 {
+  int nws;  // consumer warps (the block is nws * 32 threads)
   int stages, R, G, tile_bytes;
   int ring_off, xq_off, acc_off, red_off, route_off, xn_off, seg_off, probs_off, total;
   int xq_smem, xq_vec_bytes;
@@ -165,6 +166,9 @@ int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, in
 int stream2_smem_bytes(const StreamParams& p);  // the warp-tile kernel's shared memory
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
+// clusters of `cluster` attention CTAs that fit on the device at once (0 if
+// that cluster size cannot be launched)
+int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_chunk);
 size_t attn_smem_bytes(int hd, int gqa, int f16, int max_chunk);
 cudaError_t launch_router(const RouterParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_embed(const EmbedParams& p, cudaStream_t st, bool pdl);
