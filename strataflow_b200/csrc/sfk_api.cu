@@ -78,13 +78,14 @@ constexpr int SMEM_LIMIT = 227 * 1024;
 // 0 keeps the kernel's defaults; SFK_STREAM_TILE_BYTES / SFK_STREAM_STAGES
 // override them (read once, for tuning on new parts).
 struct StreamTuning {
-  int tile = 0, stages = 0;
+  int tile = 0, stages = 0, occ = 0;
 };
 const StreamTuning& stream_tuning() {
   static const StreamTuning t = [] {
     StreamTuning r;
     if (const char* v = getenv("SFK_STREAM_TILE_BYTES")) r.tile = atoi(v);
     if (const char* v = getenv("SFK_STREAM_STAGES")) r.stages = atoi(v);
+    if (const char* v = getenv("SFK_STREAM_OCC")) r.occ = atoi(v);
     return r;
   }();
   return t;
@@ -93,6 +94,24 @@ const StreamTuning& stream_tuning() {
 sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
   if (!p.s2_tile) p.s2_tile = stream_tuning().tile;
   if (!p.s2_stages) p.s2_stages = stream_tuning().stages;
+  if (stream_tuning().occ == 2 && p.s2_occ == 0) {
+    // two CTAs per SM: the next kernel's CTAs start beside this kernel's last ones
+    StreamParams q = p;
+    q.s2_occ = 2;
+    int g2 = std::min(2 * sm_count, std::max(1, (q.rows + 7) / 8));
+    int r2 = (q.rows + g2 - 1) / g2;
+    r2 = (r2 + q.row_align - 1) / q.row_align * q.row_align;
+    g2 = (q.rows + r2 - 1) / r2;
+    q.rows_per_cta = r2;
+    q.xq_resident = (int64_t)q.n_vec * qact_bytes(q.K) <= XQ_RESIDENT_BUDGET ? 1 : 0;
+    if (q.pro == PRO_QUANT) q.xq_resident = 1;
+    if (stream2_occupancy(q) == 2) {
+      p = q;
+      *grid_out = g2;
+      return SFK_OK;
+    }
+  }
+  p.s2_occ = 0;
   int grid = std::min(sm_count, std::max(1, (p.rows + 15) / 16));
   int rpc = (p.rows + grid - 1) / grid;
   rpc = (rpc + p.row_align - 1) / p.row_align * p.row_align;

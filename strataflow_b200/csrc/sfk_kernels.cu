@@ -143,17 +143,16 @@ struct NoOp {
 
 // `after_loads` runs once the first vector's loads are in flight (a caller
 // queues its weight copies behind them).
-template <int NWS, typename F = NoOp>
+template <int NWS, int RB = 32 / NWS, typename F = NoOp>
 __device__ void prologue_quant(const StreamParams& p, uint8_t* xq, int xq_vec_bytes, double* red,
                                F after_loads = F{}) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K = p.K;
   const int nblk = K / QK_K;
-  constexpr int RB = 32 / NWS;  // 256-column blocks a warp holds in registers (K <= 8192 on this path)
   for (int t = 0; t < p.n_vec; ++t) {
     const float* x = p.x + (int64_t)t * K;
     uint8_t* qa = xq + (int64_t)t * xq_vec_bytes;
-    if (nblk <= RB * NWS) {
+    if (nblk <= RB * NWS) {  // RB 256-column blocks per warp held in registers
       // this warp's blocks of x (and of the norm weight), one round trip
       float xv[RB][8], wv[RB][8];
 #pragma unroll
@@ -590,9 +589,11 @@ constexpr int S2_SMEM = 227 * 1024;
 
 __host__ __device__ inline int al16i(int64_t v) { return (int)((v + 15) & ~(int64_t)15); }
 
-inline Plan2 make_plan2(const StreamParams& p, int NWS) {
+inline Plan2 make_plan2(const StreamParams& p, int NWS, int occ) {
   Plan2 q;
   q.nws = NWS;
+  q.occ = occ;
+  const int S2_BUDGET = occ == 2 ? 113 * 1024 : S2_SMEM;
   const int64_t rs = p.rowstride;
   q.G = n_groups(p.K);
   const int64_t xq_all = (int64_t)p.n_vec * qact_bytes(p.K);
@@ -611,10 +612,10 @@ inline Plan2 make_plan2(const StreamParams& p, int NWS) {
   R = R < 1 ? 1 : (R > rmax ? rmax : R);
   // keep two tiles per warp in flight: a warp with one slot idles through
   // every copy's latency
-  while (R > 1 && (S2_SMEM - fixed) / ((int64_t)NWS * p.nmat * R * rs) < 2) --R;
+  while (R > 1 && (S2_BUDGET - fixed) / ((int64_t)NWS * p.nmat * R * rs) < 2) --R;
   q.R = R;
   q.tile_bytes = (int)(p.nmat * R * rs);
-  int S = (int)((S2_SMEM - fixed) / ((int64_t)NWS * q.tile_bytes));
+  int S = (int)((S2_BUDGET - fixed) / ((int64_t)NWS * q.tile_bytes));
   if (S > S2_MAXSTAGES) S = S2_MAXSTAGES;
   if (p.s2_stages > 0 && S > p.s2_stages) S = p.s2_stages;
   if (S < 1) S = 1;
@@ -667,8 +668,8 @@ __device__ __forceinline__ float reduce8(const float v[8], int lane) {
 
 // shared memory of the warp-tile kernel, or more than any SM has when a tile
 // cannot hold all of one row's group sums (nmat * groups > 8)
-// Warp count and plan of the warp-tile kernel: 16 consumer warps when each
-// keeps two tiles in flight, else 8 (SFK_STREAM_WARPS forces 8 or 16);
+// Warp count and plan of the warp-tile kernel: 16 consumer warps when their
+// rings fit, else 8 (SFK_STREAM_WARPS forces 8 or 16);
 // nws = 0 when a tile cannot hold all of one row's group sums or the rings
 // do not fit.
 static int stream_warps_forced() {
@@ -682,16 +683,27 @@ Plan2 choose_plan2(const StreamParams& p) {
   Plan2 none{};
   none.nws = 0;
   if (p.nmat != 1 && p.nmat != 2) return none;
+  if (p.s2_occ == 2) {  // two 8-warp CTAs per SM
+    const Plan2 q = make_plan2(p, 8, 2);
+    if (p.nmat * q.G <= 8 && q.total <= 113 * 1024) return q;
+    return none;
+  }
+  // 16 warps whenever their rings fit, even with one slot each: sixteen
+  // warps with one tile in flight beat eight with two (measured on the
+  // Mixtral down projection, 8 KB rows)
   const int forced = stream_warps_forced();
-  Plan2 best = none;
   for (int nws : {16, 8}) {
     if (forced && forced != nws) continue;
-    const Plan2 q = make_plan2(p, nws);
+    const Plan2 q = make_plan2(p, nws, 1);
     if (p.nmat * q.G > 8 || q.total > S2_SMEM) continue;
-    if (q.stages >= 2 || forced) return q;
-    if (best.nws == 0) best = q;
+    return q;
   }
-  return best;
+  return none;
+}
+
+int stream2_occupancy(const StreamParams& p) {
+  const Plan2 q = choose_plan2(p);
+  return q.nws ? q.occ : 0;
 }
 
 // shared memory of the warp-tile kernel, or more than any SM has when it
@@ -718,8 +730,9 @@ __device__ __forceinline__ float unit_dot_x(const uint8_t* wg, const XQ8& x, int
   }
 }
 
-template <int WT, int NMAT, int NWS>
-__global__ void __launch_bounds__(NWS * 32, 1) stream2_kernel(const StreamParams p) {
+template <int WT, int NMAT, int NWS, int MINB>
+__global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamParams p) {
+  constexpr int RBV = MINB >= 2 ? 2 : 32 / NWS;  // register blocks of the activation prologues
   extern __shared__ __align__(128) uint8_t smem[];
   const Plan2& pl = p.pl;  // planned on the host: no divisions before the first copy
   const int S = pl.stages;
@@ -807,7 +820,7 @@ __global__ void __launch_bounds__(NWS * 32, 1) stream2_kernel(const StreamParams
     const int tid = threadIdx.x;
     for (int t = 0; t < p.b; ++t) {
       // ffn_norm + quantize token t (every CTA needs its activations)
-      route_norm<NWS, 32 / NWS>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
+      route_norm<NWS, RBV>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
                      xn_s, red, nullptr, ConsumerSync<NWS>{});
       for (int q = blockIdx.x; q < nq; q += gridDim.x) {
         if (q / p.n_expert != t) continue;
@@ -895,7 +908,7 @@ __global__ void __launch_bounds__(NWS * 32, 1) stream2_kernel(const StreamParams
       for (int k = 0; k < S && warp + k * NWS < n_tiles; ++k) issue(warp + k * NWS, k, 1);
   };
   if (!self_route && pl.xq_smem && p.pro == PRO_QUANT) {
-    prologue_quant<NWS>(p, xq_s, pl.xq_vec_bytes, red, first_fill);
+    prologue_quant<NWS, RBV>(p, xq_s, pl.xq_vec_bytes, red, first_fill);
   } else {
     first_fill();
     if (!self_route && pl.xq_smem && !bulk_xq) prologue_load<NWS>(p, xq_s, pl.xq_vec_bytes, -1);
@@ -1475,18 +1488,21 @@ static cudaError_t launch_stream_t(const StreamParams& p, int grid, cudaStream_t
     const int smem2 = pl2.total;
     const dim3 block(pl2.nws * 32);
     cudaError_t e;
-#define SFK_LAUNCH2(NM, NWV)                                                                                      \
+#define SFK_LAUNCH2(NM, NWV, MB)                                                                              \
   do {                                                                                                         \
-    e = cudaFuncSetAttribute(stream2_kernel<WT, NM, NWV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem2); \
+    e = cudaFuncSetAttribute(stream2_kernel<WT, NM, NWV, MB>, cudaFuncAttributeMaxDynamicSharedMemorySize,     \
+                             smem2);                                                                           \
     if (e != cudaSuccess) return e;                                                                            \
-    return launch_pdl(stream2_kernel<WT, NM, NWV>, dim3(grid), block, smem2, st, pdl, q);                      \
+    return launch_pdl(stream2_kernel<WT, NM, NWV, MB>, dim3(grid), block, smem2, st, pdl, q);                  \
   } while (0)
     if (p.nmat == 1) {
-      if (pl2.nws == 16) SFK_LAUNCH2(1, 16);
-      SFK_LAUNCH2(1, 8);
+      if (pl2.occ == 2) SFK_LAUNCH2(1, 8, 2);
+      if (pl2.nws == 16) SFK_LAUNCH2(1, 16, 1);
+      SFK_LAUNCH2(1, 8, 1);
     }
-    if (pl2.nws == 16) SFK_LAUNCH2(2, 16);
-    SFK_LAUNCH2(2, 8);
+    if (pl2.occ == 2) SFK_LAUNCH2(2, 8, 2);
+    if (pl2.nws == 16) SFK_LAUNCH2(2, 16, 1);
+    SFK_LAUNCH2(2, 8, 1);
 #undef SFK_LAUNCH2
   }
   if (p.pro == PRO_ROUTE) return cudaErrorInvalidValue;  // only the warp-tile kernel routes in its prologue

@@ -57,6 +57,7 @@ struct KvView {
 // at launch; the kernel reads it from its parameters)
 struct Plan2 {
   int nws;  // consumer warps (the block is nws * 32 threads)
+  int occ;  // CTAs per SM the plan is sized for (1, or 2 so the next kernel's CTAs can start beside this one's)
   int stages, R, G, tile_bytes;
   int ring_off, xq_off, acc_off, red_off, route_off, xn_off, seg_off, probs_off, total;
   int xq_smem, xq_vec_bytes;
@@ -118,6 +119,7 @@ struct StreamParams {
   // warp-tile kernel ring: tile target bytes and stages per warp (0: defaults)
   int s2_tile;
   int s2_stages;
+  int s2_occ;  // 2: size the kernel for two CTAs per SM (half the shared memory and registers)
   Plan2 pl;  // filled by the launcher
 };
 
@@ -164,6 +166,7 @@ struct EmbedParams {
 // launch helpers (implemented in sfk_kernels.cu)
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp);
 int stream2_smem_bytes(const StreamParams& p);  // the warp-tile kernel's shared memory
+int stream2_occupancy(const StreamParams& p);   // CTAs per SM its plan allows (0: the kernel cannot run it)
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
 // clusters of `cluster` attention CTAs that fit on the device at once (0 if
