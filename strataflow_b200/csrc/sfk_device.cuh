@@ -307,19 +307,28 @@ __device__ __forceinline__ uint4 shr4_and(const uint4 a, int s, uint32_t m) {
   return make_uint4((a.x >> s) & m, (a.y >> s) & m, (a.z >> s) & m, (a.w >> s) & m);
 }
 
+// unsigned weight bytes x signed activation bytes
+__device__ __forceinline__ int dot4u(const uint4 w, const uint4 x, int acc) {
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w.x), "r"(x.x));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w.y), "r"(x.y));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w.z), "r"(x.z));
+  asm("dp4a.u32.s32 %0, %1, %2, %0;" : "+r"(acc) : "r"(w.w), "r"(x.w));
+  return acc;
+}
 __device__ __forceinline__ float dot_unit_q4k(const WQ4K& w, const XQ8& x, int lane) {
   // unit parity: half h of the 256-block
   const int h = lane & 1;
-  // chunks: i=0,1 -> qs chunk c=2h bytes [0..31]; i=2,3 -> chunk 2h+1
-  int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-  s0 = dot4(and4(w.c[0], 0x0F0F0F0Fu), x.c[0], s0);
-  s0 = dot4(and4(w.c[1], 0x0F0F0F0Fu), x.c[1], s0);
-  s1 = dot4(shr4_and(w.c[0], 4, 0x0F0F0F0Fu), x.c[2], s1);
-  s1 = dot4(shr4_and(w.c[1], 4, 0x0F0F0F0Fu), x.c[3], s1);
-  s2 = dot4(and4(w.c[2], 0x0F0F0F0Fu), x.c[4], s2);
-  s2 = dot4(and4(w.c[3], 0x0F0F0F0Fu), x.c[5], s2);
-  s3 = dot4(shr4_and(w.c[2], 4, 0x0F0F0F0Fu), x.c[6], s3);
-  s3 = dot4(shr4_and(w.c[3], 4, 0x0F0F0F0Fu), x.c[7], s3);
+  // chunks: i=0,1 -> qs chunk c=2h bytes [0..31]; i=2,3 -> chunk 2h+1.  High
+  // nibbles stay in place (16 x the code) and the sum is shifted back: it is
+  // a multiple of 16, so the shift is exact.
+  int s0 = dot4u(and4(w.c[0], 0x0F0F0F0Fu), x.c[0], 0);
+  s0 = dot4u(and4(w.c[1], 0x0F0F0F0Fu), x.c[1], s0);
+  int s1 = dot4u(and4(w.c[0], 0xF0F0F0F0u), x.c[2], 0);
+  s1 = dot4u(and4(w.c[1], 0xF0F0F0F0u), x.c[3], s1) >> 4;
+  int s2 = dot4u(and4(w.c[2], 0x0F0F0F0Fu), x.c[4], 0);
+  s2 = dot4u(and4(w.c[3], 0x0F0F0F0Fu), x.c[5], s2);
+  int s3 = dot4u(and4(w.c[2], 0xF0F0F0F0u), x.c[6], 0);
+  s3 = dot4u(and4(w.c[3], 0xF0F0F0F0u), x.c[7], s3) >> 4;
   // 6-bit scales / mins of sub-blocks 4h..4h+3 (ggml get_scale_min_k4)
   uint32_t sc, mn;
   if (h == 0) {
@@ -331,13 +340,12 @@ __device__ __forceinline__ float dot_unit_q4k(const WQ4K& w, const XQ8& x, int l
   }
   const int isum = (int)(sc & 0xFF) * s0 + (int)((sc >> 8) & 0xFF) * s1 + (int)((sc >> 16) & 0xFF) * s2 +
                    (int)(sc >> 24) * s3;
-  // bsum32_j = bsum16_2j + bsum16_2j+1
-  const int b0 = (int)(int16_t)(x.s.x & 0xFFFF) + (int)(int16_t)(x.s.x >> 16);
-  const int b1 = (int)(int16_t)(x.s.y & 0xFFFF) + (int)(int16_t)(x.s.y >> 16);
-  const int b2 = (int)(int16_t)(x.s.z & 0xFFFF) + (int)(int16_t)(x.s.z >> 16);
-  const int b3 = (int)(int16_t)(x.s.w & 0xFFFF) + (int)(int16_t)(x.s.w >> 16);
-  const int imin = (int)(mn & 0xFF) * b0 + (int)((mn >> 8) & 0xFF) * b1 + (int)((mn >> 16) & 0xFF) * b2 +
-                   (int)(mn >> 24) * b3;
+  // imin = sum_j m_j * (bsum16_2j + bsum16_2j+1): one 2-way dot per
+  // sub-block with m_j in both low bytes
+  int imin = __dp2a_lo((int)x.s.x, (int)__byte_perm(mn, 0, 0x0000), 0);
+  imin = __dp2a_lo((int)x.s.y, (int)__byte_perm(mn, 0, 0x1111), imin);
+  imin = __dp2a_lo((int)x.s.z, (int)__byte_perm(mn, 0, 0x2222), imin);
+  imin = __dp2a_lo((int)x.s.w, (int)__byte_perm(mn, 0, 0x3333), imin);
   const __half2 dd = *reinterpret_cast<const __half2*>(&w.h0);
   const float d = __fmul_rn(__low2float(dd), x.d);
   const float dmin = __fmul_rn(__high2float(dd), x.d);
@@ -378,14 +386,19 @@ __device__ __forceinline__ float dot_unit_q6k(const WQ6K& w, const XQ8& x) {
                    ((B.z >> 4) & m4) | ((H.z >> 2) & m2), ((B.w >> 4) & m4) | ((H.w >> 2) & m2));
     s[6 + q] = dot4(v, x.c[6 + q], 0);
   }
-  const uint32_t bs[4] = {x.s.x, x.s.y, x.s.z, x.s.w};
+  // isum = sum_m sc_m * (s_m - 32 * bsum_m); the bsum part is four 2-way
+  // dots of (bsum_2j, bsum_2j+1) with (sc_2j, sc_2j+1)
   int isum = 0;
 #pragma unroll
   for (int m = 0; m < 8; ++m) {
     const int scm = (int)(int8_t)((m < 4 ? w.sc.x : w.sc.y) >> (8 * (m & 3)));
-    const int bsum = (int)(int16_t)((bs[m >> 1] >> (16 * (m & 1))) & 0xFFFF);
-    isum += scm * (s[m] - 32 * bsum);
+    isum += scm * s[m];
   }
+  int sb = __dp2a_lo((int)x.s.x, (int)w.sc.x, 0);
+  sb = __dp2a_hi((int)x.s.y, (int)w.sc.x, sb);
+  sb = __dp2a_lo((int)x.s.z, (int)w.sc.y, sb);
+  sb = __dp2a_hi((int)x.s.w, (int)w.sc.y, sb);
+  isum -= 32 * sb;
   return __fmul_rn(__fmul_rn(w.d, x.d), (float)isum);
 }
 
