@@ -610,9 +610,11 @@ inline Plan2 make_plan2(const StreamParams& p, int NWS, int occ) {
   if (rmax < 1) rmax = 1;
   int R = (int)((p.s2_tile > 0 ? p.s2_tile : S2_TILE) / (p.nmat * rs));
   R = R < 1 ? 1 : (R > rmax ? rmax : R);
-  // keep two tiles per warp in flight: a warp with one slot idles through
-  // every copy's latency
-  while (R > 1 && (S2_BUDGET - fixed) / ((int64_t)NWS * p.nmat * R * rs) < 2) --R;
+  // bigger tiles over deeper rings: with 16 warps each holding one tile,
+  // the per-tile work (butterfly, bookkeeping, copy issue) amortises over
+  // more rows (measured: gate/up 43 -> 39 us, QKV 12.5 -> 11.2 us)
+  const int min_stages = p.s2_stages >= 2 ? 2 : 1;
+  while (R > 1 && (S2_BUDGET - fixed) / ((int64_t)NWS * p.nmat * R * rs) < min_stages) --R;
   q.R = R;
   q.tile_bytes = (int)(p.nmat * R * rs);
   int S = (int)((S2_BUDGET - fixed) / ((int64_t)NWS * q.tile_bytes));
@@ -784,9 +786,22 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
   // warp's range clipped at K
   const int rcols = ((p.K + NWS - 1) / NWS + 3) & ~3;
   const int rc0 = min(p.K, warp * rcols), rc1 = min(p.K, rc0 + rcols);
+  // When the whole router fits in the ring (idle until the experts are
+  // known), every CTA copies it in before the wait and scores all logits
+  // itself: no exchange between CTAs.
+  const bool wr_local = self_route && (int64_t)p.n_expert * p.K * 4 <= (int64_t)NWS * S * pl.tile_bytes;
+  float* wr_s = reinterpret_cast<float*>(smem + pl.ring_off);
+  if (wr_local && lane == 0) {
+    uint32_t mine = 0;
+    for (int e = warp; e < p.n_expert; e += NWS) mine += (uint32_t)(p.K * 4);
+    mbar_arrive_expect_tx(pro_bar, mine);
+    for (int e = warp; e < p.n_expert; e += NWS)
+      bulk_g2s(wr_s + (int64_t)e * p.K, p.w_r + (int64_t)e * p.K, (uint32_t)(p.K * 4), pro_bar);
+  }
   constexpr int WPRE = 4;
   float4 wpre[WPRE];
-  const bool pre = (int)blockIdx.x < nq && rcols % 128 == 0 && rcols / 128 <= WPRE && rc1 - rc0 == rcols;
+  const bool pre = !wr_local && (int)blockIdx.x < nq && rcols % 128 == 0 && rcols / 128 <= WPRE &&
+                   rc1 - rc0 == rcols;
   if (pre) {
     const float* wr = p.w_r + (int64_t)(blockIdx.x % p.n_expert) * p.K + rc0 + lane * 4;
 #pragma unroll
@@ -814,7 +829,63 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
   }
   if (p.clear_keys && blockIdx.x == 0 && threadIdx.x < p.clear_n) p.clear_keys[threadIdx.x] = 0ull;
   int depart_old = -1;
-  if (self_route) {
+  if (self_route && wr_local) {
+    float* xn_s = reinterpret_cast<float*>(smem + pl.xn_off);
+    float* probs_s = reinterpret_cast<float*>(smem + pl.probs_off);  // [b][E]
+    for (int t = 0; t < p.b; ++t) {
+      route_norm<NWS, RBV>(p.x + (int64_t)t * p.K, p.norm_w, p.K, p.eps, p.act_type, xq_s + (int64_t)t * pl.xq_vec_bytes,
+                           xn_s, red, nullptr, ConsumerSync<NWS>{});
+      if (t == 0) mbar_wait_bounded(pro_bar, 0, p.status);  // the router rows are in
+      // logit e = sum_c (double)(w_r[e][c] * xn[c]); with at least two
+      // warps per expert each takes half the columns (four chains each), the
+      // halves added in order
+      const int wpe = (p.n_expert * 2 <= NWS && p.n_expert * 2 <= 64) ? 2 : 1;
+      const int span = p.K / wpe;
+      for (int item = warp; item < p.n_expert * wpe; item += NWS) {
+        const int e = item / wpe, part = item % wpe;
+        const float* wr = wr_s + (int64_t)e * p.K + part * span;
+        const float* xs = xn_s + part * span;
+        double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
+        for (int c = lane * 4; c < span; c += 128) {
+          const float4 w4 = *reinterpret_cast<const float4*>(wr + c);
+          const float4 x4 = *reinterpret_cast<const float4*>(xs + c);
+          a0 += (double)__fmul_rn(w4.x, x4.x);
+          a1 += (double)__fmul_rn(w4.y, x4.y);
+          a2 += (double)__fmul_rn(w4.z, x4.z);
+          a3 += (double)__fmul_rn(w4.w, x4.w);
+        }
+        const double a = warp_sum_d((a0 + a1) + (a2 + a3));
+        if (wpe == 1) {
+          if (lane == 0) probs_s[t * p.n_expert + e] = (float)a;
+        } else if (lane == 0) {
+          red[item] = a;
+        }
+      }
+      consumer_sync<NWS>();
+      if (wpe == 2)
+        for (int e = threadIdx.x; e < p.n_expert; e += NWS * 32)
+          probs_s[t * p.n_expert + e] = (float)(red[2 * e] + red[2 * e + 1]);
+      consumer_sync<NWS>();  // xn and red are rewritten by the next token
+    }
+    for (int t = warp; t < p.b; t += NWS)
+      route_select(probs_s + t * p.n_expert, p.n_expert, p.k, &sroute->ids[t * p.k], &sroute->w[t * p.k], lane);
+    consumer_sync<NWS>();
+    if (p.b * p.k <= 32 && p.n_expert <= 64) {
+      if (warp == 0) build_slots_warp(sroute->ids, p.b * p.k, sroute, lane);
+    } else if (threadIdx.x == 0) {
+      build_slots(sroute->ids, p.b * p.k, sroute);
+    }
+    if (threadIdx.x == 0) {
+      sroute->k = p.k;
+      sroute->b = p.b;
+    }
+    consumer_sync<NWS>();
+    if (blockIdx.x == 0) {  // publish the routing for the down kernel and the host
+      const int* src = reinterpret_cast<const int*>(sroute);
+      int* dst = reinterpret_cast<int*>(const_cast<Route*>(p.route));
+      for (int i = threadIdx.x; i < (int)(sizeof(Route) / 4); i += NWS * 32) dst[i] = src[i];
+    }
+  } else if (self_route) {
     float* xn_s = reinterpret_cast<float*>(smem + pl.xn_off);
     float* probs_s = reinterpret_cast<float*>(smem + pl.probs_off);  // [b][E]
     const int tid = threadIdx.x;
@@ -866,6 +937,7 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
     if (tid == 0) {
       const long long t0 = clock64();
       while (ld_acquire(&p.rsync[0]) < nq) {
+        __nanosleep(64);
         if (clock64() - t0 > (1ll << 31)) {
           atomicExch(p.status, ERR_TIMEOUT);
           break;
@@ -934,6 +1006,29 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
       float part[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) part[j] = 0.0f;
+      if (G == 1 && RM == 4) {
+        // the common tile (4 row-matrices of one 32-unit group): four
+        // independent unit dots in one basic block, so their dp4a chains
+        // interleave
+        const int ng = group_units(p.K, 0);
+        if (vi != cached) {
+          if (lane < ng) {
+            const uint8_t* xg = xbase + (int64_t)vi * xstride;
+            if (pl.xq_smem)
+              xc.load(xg, ng, lane);
+            else
+              xc.load_any(xg, ng, lane);
+          }
+          cached = vi;
+        }
+        if (lane < ng) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = NMAT == 2 ? (q >> 1) : q, m = NMAT == 2 ? (q & 1) : 0;
+            part[q] = unit_dot_x<WT>(tile + ((int64_t)m * R + r) * rs, xc, ng, lane);
+          }
+        }
+      } else {
       // one unit dot in the loop body (a small hot loop stays in the
       // instruction cache); value j = rm * G + g lands in part[j]
       int j = 0;
@@ -959,6 +1054,7 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
 #pragma unroll
           for (int q = 0; q < 8; ++q) part[q] = (q == j) ? d : part[q];
         }
+      }
       }
       const float sum = reduce8(part, lane);
       // (row, matrix) rm = lane adds its group sums in order; value v sits in
@@ -1071,6 +1167,13 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   // Positions and the page table were written before the previous kernel
   // started (every kernel of the step lets its successor launch only after
   // its own wait on its predecessor), so they are read before the wait.
+  // this sequence's page ids (up to 256), loaded alongside the position so
+  // the page copies do not wait for two dependent round trips
+  __shared__ int ptab_s[256];
+  {
+    const int* prow = p.kv.page_table + (int64_t)t * p.kv.max_pages;
+    if (tid < min(p.kv.max_pages, 256)) ptab_s[tid] = prow[tid];
+  }
   int n_kv = p.pos[t] + 1;
   if (n_kv < 1 || n_kv > p.kv.max_pages * 16) {  // outside the page table: no access, report
     if (tid == 0 && rank == 0) atomicExch(p.status, ERR_BAD_POS);
@@ -1094,7 +1197,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   auto issue = [&](int isv, int i) {
     const int slot = i % pl.ns;
     uint64_t* bar = (isv ? vfull : kfull) + slot;
-    const int pg = ptab[pb + i];
+    const int pg = pb + i < 256 ? ptab_s[pb + i] : ptab[pb + i];
     if (pg < 0 || (p.kv.n_pages > 0 && pg >= p.kv.n_pages)) {  // never copy from outside the pool
       atomicExch(p.status, ERR_BAD_PAGE);
       mbar_arrive(bar);
@@ -1110,7 +1213,12 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
       mbar_init(&kfull[i], 1);
       mbar_init(&vfull[i], 1);
     }
-    for (int i = 0; i < 3; ++i) mbar_init(&xbar[i], C);  // one arrival per cluster CTA
+    // exchange barriers: one local arrival that expects every byte the
+    // cluster will push (maxima, sums, this CTA's slice of the outputs)
+    for (int i = 0; i < 3; ++i) mbar_init(&xbar[i], 1);
+    mbar_arrive_expect_tx(&xbar[0], (uint32_t)(gqa * C * 4));
+    mbar_arrive_expect_tx(&xbar[1], (uint32_t)(gqa * C * 8));
+    mbar_arrive_expect_tx(&xbar[2], (uint32_t)(max(0, min(nout, rank * per + per) - rank * per) * C * 8));
     fence_mbar_init();
   }
   __syncthreads();
@@ -1205,15 +1313,11 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   }
   __syncthreads();  // all scores are in
   // Exchanges between the cluster's CTAs are pushes: every CTA stores its
-  // values into each CTA's receive slots (distributed shared memory), then
-  // arrives once on each CTA's exchange barrier; a CTA waits on its own
-  // barrier for all C arrivals.  One hop, no cluster-wide barrier.
-  auto push_done = [&](int x) {
-    fence_cluster();  // this thread's remote stores, before the arrivals below
-    __syncthreads();
-    if (tid < C) mbar_arrive_remote(dsmem_addr(&xbar[x], tid));
-    mbar_wait_cluster_bounded(&xbar[x], 0, p.status);
-  };
+  // values into each CTA's receive slots with asynchronous DSMEM stores that
+  // count their bytes on the receiver's exchange barrier; a CTA waits on its
+  // own barrier until every byte it expects has landed.  One hop, no fence,
+  // no cluster-wide barrier.
+  auto push_done = [&](int x) { mbar_wait_cluster_bounded(&xbar[x], 0, p.status); };
   // local max per head
   for (int h = warp; h < gqa; h += ATT_NW) {
     float m = -INFINITY;
@@ -1225,7 +1329,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   cluster_wait();  // every CTA of the cluster has initialised its barriers
   if (tid < gqa * C) {
     const int h = tid / C, r = tid % C;
-    dsmem_st_f32(dsmem_addr(&gst[h * C + rank], r), lmax[h]);
+    dsmem_st_async_f32(dsmem_addr(&gst[h * C + rank], r), lmax[h], dsmem_addr(&xbar[0], r));
   }
   push_done(0);
   // ---- global max, exp, local sum: warp h owns head h
@@ -1244,7 +1348,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   __syncthreads();
   if (tid < gqa * C) {
     const int h = tid / C, r = tid % C;
-    dsmem_st_f64(dsmem_addr(&gstd[h * C + rank], r), lsum[h]);
+    dsmem_st_async_f64(dsmem_addr(&gstd[h * C + rank], r), lsum[h], dsmem_addr(&xbar[1], r));
   }
   push_done(1);
   if (tid < gqa) {
@@ -1305,7 +1409,8 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
 #pragma unroll
       for (int d2 = 0; d2 < 2; ++d2) {
         const int o = 2 * pi + d2, r = o / per;
-        dsmem_st_f64(dsmem_addr(&ored[rank * per + (o - r * per)], r), acc[2 * q2 + d2][0] + acc[2 * q2 + d2][1]);
+        dsmem_st_async_f64(dsmem_addr(&ored[rank * per + (o - r * per)], r), acc[2 * q2 + d2][0] + acc[2 * q2 + d2][1],
+                           dsmem_addr(&xbar[2], r));
       }
     }
   }

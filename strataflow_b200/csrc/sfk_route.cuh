@@ -252,6 +252,42 @@ __device__ void route_one(const float* x, const float* norm_w, const float* w_r,
   sync();
 }
 
+// The same slot lists built by one warp when np <= 32 and every id < 64:
+// lane i holds pair i; the slot of an expert is the number of distinct
+// smaller experts in use, a pair's place in its slot the number of earlier
+// pairs of the same expert.
+__device__ inline void build_slots_warp(const int* ids, int np, Route* r, int lane) {
+  const int id = lane < np ? ids[lane] : -1;
+  const unsigned act = __ballot_sync(0xffffffffu, lane < np);
+  unsigned lo = 0, hi = 0;
+  if (id >= 0 && id < 32) lo = 1u << id;
+  if (id >= 32) hi = 1u << (id - 32);
+  lo = __reduce_or_sync(0xffffffffu, lo);
+  hi = __reduce_or_sync(0xffffffffu, hi);
+  const int n_lo = __popc(lo), ns = n_lo + __popc(hi);
+  // expert b in use (bit b) sits in slot popc(bits below b)
+  if (lo & (1u << lane)) r->slot_expert[__popc(lo & ((1u << lane) - 1u))] = lane;
+  if (hi & (1u << lane)) r->slot_expert[n_lo + __popc(hi & ((1u << lane) - 1u))] = 32 + lane;
+  // pairs of each expert, and the pairs of all smaller experts before them
+  const unsigned same = __match_any_sync(0xffffffffu, id) & act;
+  const int slot = id < 0 ? 0 : (id < 32 ? __popc(lo & ((1u << id) - 1u)) : n_lo + __popc(hi & ((1u << (id - 32)) - 1u)));
+  int before = 0;  // pairs whose expert is smaller than mine
+  for (int j = 0; j < np; ++j) {
+    const int oj = __shfl_sync(0xffffffffu, id, j);
+    before += (oj < id) ? 1 : 0;
+  }
+  const int place = __popc(same & ((1u << lane) - 1u));
+  if (lane < np) r->slot_pairs[before + place] = lane;
+  // slot_off[s] = pairs of the s smallest experts: the first pair of slot s
+  // knows it, and the total closes the list
+  if (lane < np && place == 0) r->slot_off[slot] = before;
+  if (lane == 0) {
+    r->slot_off[ns] = np;
+    r->n_slots = ns;
+  }
+  __syncwarp();
+}
+
 // Slot lists from the pairs' expert ids: distinct experts ascending, each with
 // its pairs ascending.  One thread.
 __device__ inline void build_slots(const int* ids, int np, Route* r) {
