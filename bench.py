@@ -297,6 +297,112 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 GU_TRAFFIC_BYTES = 136.04e6
 
 
+def run_ep(args, rank: int, world: int, local_rank: int):
+    """the ~1T-parameter MoE, experts sharded over the torchrun
+    ranks (expert parallelism), trunk replicated; one sequence decoded by the
+    whole job."""
+    import datetime
+    import torch
+    from strataflow_b200 import engine as E
+    from strataflow_b200 import lib as L
+
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    B = args.batch
+    prompt_n = args.prompt
+    metric = "decode tok/s, ~1T-parameter MoE (61L d7168 E384 top-8) Q4_K experts, expert-parallel"
+    cfg = E.trillion_config(n_ctx=prompt_n + args.warmup + args.steps + 16, max_batch=B, n_layer=args.layers,
+                            ep_size=world, ep_rank=rank)
+    t_load = time.perf_counter()
+    try:
+        eng = E.Engine.load(cfg, seed=5, device=local_rank)
+        ok = 1
+    except L.SfkError as ex:
+        eng, ok, why = None, 0, str(ex)
+    if dist:
+        t = torch.tensor([ok], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        ok = int(t.item())
+    if not ok:
+        if rank == 0:
+            print(json.dumps({"metric": metric, "n_gpus": world, "unavailable":
+                              f"the model does not fit: {world} GPU(s) -> {why if eng is None else 'another rank'}"}),
+                  flush=True)
+        if dist:
+            dist.destroy_process_group()
+        return
+    t_load = time.perf_counter() - t_load
+    if world > 1:
+        eng.ep_connect_group()
+    stream = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", local_rank))
+    rng = np.random.default_rng(5)   # the same prompt on every rank
+    prompt = rng.integers(0, cfg.n_vocab, (B, prompt_n)).astype(np.int32)
+    t_pf = time.perf_counter()
+    for p in range(prompt_n):
+        eng.forward_batch(prompt[:, p], np.full(B, p, np.int32), want_logits=False)
+    t_pf = time.perf_counter() - t_pf
+    eng.decode_greedy(args.warmup, B, want_tokens=False)
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        ev0.record(stream)
+        toks = eng.decode_greedy(args.steps, B, want_tokens=True)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    same = 1
+    if dist:
+        t = torch.tensor([ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        # every rank must have decoded the same tokens
+        tt = torch.from_numpy(toks.astype(np.int64)).cuda()
+        t0 = tt.clone()
+        dist.broadcast(t0, 0)
+        s_ = torch.tensor([int(torch.equal(tt, t0))], device="cuda")
+        dist.all_reduce(s_, op=dist.ReduceOp.MIN)
+        same = int(s_.item())
+    value = B * args.steps / (ms / 1000.0)
+    st = eng.stats()
+    peak, peak_kind = _peaks()
+    d, F, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
+    q8 = lambda K: K // 32 * 34   # noqa: E731
+    q4 = lambda K: K // 256 * 144   # noqa: E731
+    trunk = cfg.n_layer * ((cfg.n_head + 2 * cfg.n_head_kv) * 128 * q8(d) + d * q8(cfg.n_head * 128) + 4 * d * cfg.n_expert)
+    trunk += cfg.n_vocab * q8(d)
+    experts_rank = cfg.n_layer * B * k / world * (2 * F * q4(d) + d * q4(F))   # expected routed bytes per rank
+    rank_bytes = trunk + experts_rank
+    if rank == 0:
+        line = {
+            "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "q4_k experts / q8_0 trunk x int8 dot (dp4a), fp32 accum",
+            "data": "synthetic",
+            "config": {"workload": f"~1T-param MoE decode b={B}: {prompt_n}-token random prompt, then greedy decode",
+                       "model": "61L d7168 64q/8kv E384 top8 F2048 V160000", "global_batch": B,
+                       "seq_len": prompt_n, "parallelism": f"ep{world} (experts sharded, trunk replicated)"},
+            "clocks": clk.summary(), "ranks_agree": bool(same),
+            "gpu_launches": st["kernels_per_step"] * args.steps,
+            "step_roofline": {"achieved": rank_bytes * args.steps / (ms / 1000.0) / 1e9, "peak": peak,
+                              "unit": "GB/s per GPU", "frac": rank_bytes * args.steps / (ms / 1000.0) / 1e9 / peak,
+                              "bytes_per_token_per_gpu": rank_bytes, "peak_kind": peak_kind},
+            "weight_bytes_per_gpu": st["weight_bytes_hbm"], "load_s": t_load, "prefill_s": t_pf,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+    eng.close()
+    if dist:
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -310,12 +416,21 @@ def main():
     ap.add_argument("--layers", type=int, default=32, help="model depth (32 = the benchmark; fewer for profiling)")
     ap.add_argument("--no-kernel-times", action="store_true",
                     help="print only the device-timed decode rate (short profiling runs)")
+    ap.add_argument("--model", choices=["mixtral", "1t"], default="mixtral",
+                    help="1t: configs[4], experts sharded over the torchrun ranks")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.model == "1t":
+        if args.layers == 32:
+            args.layers = 61
+        if args.prompt == PROMPT:
+            args.prompt = 1024
+        run_ep(args, rank, world, local_rank)
         return
     run_ours(args, rank, world, local_rank)
 

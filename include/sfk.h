@@ -83,6 +83,14 @@ typedef struct sfk_hparams {
     int32_t type_embd, type_attn, type_ffn_gu, type_ffn_down, type_output;
     int32_t kv_type;
     int32_t max_batch;
+    /* Expert parallelism (experts sharded across the GPUs of one box).
+     * ep_size ranks, one engine per GPU; rank ep_rank holds
+     * experts [ep_rank * E / ep_size, (ep_rank + 1) * E / ep_size) of every
+     * layer and a full copy of everything else.  0 or 1: no sharding. */
+    int32_t ep_size, ep_rank;
+    /* Attention head width; 0 = n_embd / n_head (the reference's rule,
+     * engine.cpp:1161).  Set it when n_head * head_dim != n_embd. */
+    int32_t head_dim;
 } sfk_hparams;
 
 typedef struct sfk_engine sfk_engine;
@@ -230,6 +238,22 @@ SFK_API sfk_status sfk_moe_ffn_noalloc(int type_gu, int type_down, const void *d
                                        const void *dev_down, int32_t n_expert, int64_t d, int64_t F,
                                        const float *dev_x, const float *dev_res, const int32_t *dev_ids,
                                        const float *dev_w, int32_t b, int32_t k, float *dev_out, void *stream);
+
+/* ---- expert parallelism (no counterpart in the reference, which runs one
+ *      device; the north star shards the experts over the GPUs of a box) ----
+ * Every rank's engine exposes one exchange buffer (partial MoE outputs and
+ * flag words).  Each rank passes sfk_ep_handle's bytes (SFK_EP_HANDLE_BYTES,
+ * a CUDA IPC handle) to every other rank by its own means (e.g. a
+ * torch.distributed all-gather); sfk_ep_connect then opens every rank's
+ * buffer.  Connect before the first decode step.  All ranks must run the
+ * same steps (same tokens, positions and batch) in the same order: after
+ * every layer's expert FFN the ranks exchange partial outputs through peer
+ * memory and add them in rank order, so every rank holds the same hidden
+ * state and produces the same logits.  Waits for a peer are bounded (about a
+ * second) and end the step with SFK_ERR_RUNTIME. */
+#define SFK_EP_HANDLE_BYTES 64
+SFK_API sfk_status sfk_ep_handle(sfk_engine *eng, void *handle_out, size_t n_bytes);
+SFK_API sfk_status sfk_ep_connect(sfk_engine *eng, const void *handles, int32_t n_ranks);
 
 /* GQA decode attention over a paged KV cache (engine.cpp:1751-1761 math):
  * q [b][Hq][hd] f32; k_pages/v_pages [n_pages][Hkv][16][hd] (f16 or f32 per

@@ -234,6 +234,15 @@ struct sfk_engine {
   int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
   int* status = nullptr;
   bool fused_route = false;  // the gate/up kernel routes in its prologue (no router kernel)
+  // expert parallelism: this rank holds experts [e0, e0 + e_loc)
+  int ep_size = 1, ep_rank = 0, e_loc = 0, e0 = 0;
+  float* ep_buf = nullptr;      // [2][B][d] partial outputs (layer parity) | flags [MAXR] ints
+  int* ep_flags = nullptr;
+  int* ep_step = nullptr;
+  const float* ep_parts[MAXR] = {};
+  int* ep_peer_flags[MAXR] = {};
+  std::vector<void*> ep_opened;  // peer buffers opened through IPC
+  bool ep_connected = false;
   int attn_cluster = 8;
   int attn_max_chunk = 0;
   // pinned staging
@@ -271,8 +280,8 @@ int64_t tensor_rows(const sfk_engine* e, int tid) {
     case SFK_T_ATTN_K: case SFK_T_ATTN_V: return e->nk;
     case SFK_T_ATTN_OUT: return hp.n_embd;
     case SFK_T_FFN_GATE_INP: return hp.n_expert;
-    case SFK_T_FFN_GATE_EXPS: case SFK_T_FFN_UP_EXPS: return (int64_t)hp.n_expert * hp.n_ff;
-    case SFK_T_FFN_DOWN_EXPS: return (int64_t)hp.n_expert * hp.n_embd;
+    case SFK_T_FFN_GATE_EXPS: case SFK_T_FFN_UP_EXPS: return (int64_t)e->e_loc * hp.n_ff;  // local experts
+    case SFK_T_FFN_DOWN_EXPS: return (int64_t)e->e_loc * hp.n_embd;
     default: return 1;
   }
 }
@@ -383,6 +392,10 @@ StreamParams gateup_params(const sfk_engine* e, int l, int b) {
   p.row_align = 1;
   p.b = b; p.k = k; p.n_pairs = b * k; p.n_vec = b;
   p.route = e->route;
+  if (e->ep_size > 1) {
+    p.ep_e0 = e->e0;
+    p.ep_eloc = e->e_loc;
+  }
   if (e->fused_route) {
     p.pro = PRO_ROUTE;  // ffn_norm + quantize + router + top-k in the prologue
     p.x = e->ffn_inp;
@@ -430,6 +443,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       ep.pos_state = e->pos_state;
       ep.pos_cur = e->pos_cur;
       ep.x = e->x;
+      ep.ep_step = e->ep_step;
       ep.status = e->status;
       CK(launch_embed(ep, st, pdl));
       return SFK_OK;
@@ -515,6 +529,10 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       r.route = e->route;
       r.logits = e->router_logits;
       r.counter = e->router_counter;
+      if (e->ep_size > 1) {
+        r.ep_e0 = e->e0;
+        r.ep_eloc = e->e_loc;
+      }
       r.status = e->status;
       CK(launch_router(r, st, pdl));
       return SFK_OK;
@@ -545,6 +563,14 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.epi = EPI_DOWN;
       p.y = e->x;
       p.res = e->ffn_inp;
+      if (e->ep_size > 1) {
+        // this rank's experts into its exchange buffer (layer parity); the
+        // residual is added once, by rank 0; the combine writes x
+        p.ep_e0 = e->e0;
+        p.ep_eloc = e->e_loc;
+        p.y = e->ep_buf + (size_t)(l & 1) * e->hp.max_batch * d;
+        p.res = e->ep_rank == 0 ? e->ffn_inp : nullptr;
+      }
       p.y_stride = d;
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
@@ -591,6 +617,25 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
       if ((s = launch_one(e, c, l, b, greedy, true))) return s;
       ++nk;
     }
+    if (e->ep_size > 1) {  // add the ranks' expert outputs (peer memory)
+      EpParams q{};
+      for (int r = 0; r < e->ep_size; ++r) {
+        q.parts[r] = e->ep_parts[r];
+        q.peer_flags[r] = e->ep_peer_flags[r];
+      }
+      q.flags = e->ep_flags;
+      q.n_ranks = e->ep_size;
+      q.rank = e->ep_rank;
+      q.layer = l;
+      q.n_layer = e->hp.n_layer;
+      q.ep_step = e->ep_step;
+      q.half = e->hp.max_batch * e->hp.n_embd;
+      q.n = b * e->hp.n_embd;
+      q.x = e->x;
+      q.status = e->status;
+      CK(launch_ep_combine(q, e->stream, true));
+      ++nk;
+    }
   }
   if ((s = launch_one(e, K_LMHEAD, 0, b, greedy, true))) return s;
   ++nk;
@@ -599,6 +644,8 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
 }
 
 sfk_status get_graph(sfk_engine* e, int b, bool greedy, cudaGraphExec_t* out) {
+  if (e->ep_size > 1 && !e->ep_connected)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "expert-parallel engine: call sfk_ep_connect before decoding");
   const int key = b * 2 + (greedy ? 1 : 0);
   auto it = e->graphs.find(key);
   if (it != e->graphs.end()) {
@@ -628,9 +675,9 @@ sfk_status validate_hp(const sfk_hparams* hp) {
   if (hp->n_embd <= 0 || hp->n_head <= 0 || hp->n_head_kv <= 0 || hp->n_layer <= 0 || hp->n_ff <= 0 ||
       hp->n_expert <= 0 || hp->n_expert_used <= 0 || hp->n_vocab <= 0 || hp->n_ctx <= 0)
     return fail(SFK_ERR_INVALID_ARGUMENT, "hparams must be positive");
-  if (hp->n_head % hp->n_head_kv || hp->n_embd % hp->n_head)
+  if (hp->n_head % hp->n_head_kv || (hp->head_dim <= 0 && hp->n_embd % hp->n_head))
     return fail(SFK_ERR_INVALID_ARGUMENT, "n_head must divide by n_head_kv and n_embd by n_head");
-  const int hd = hp->n_embd / hp->n_head;
+  const int hd = hp->head_dim > 0 ? hp->head_dim : hp->n_embd / hp->n_head;
   if (hd != 32 && hd != 64 && hd != 128 && hd != 256)
     return fail(SFK_ERR_UNSUPPORTED, "head_dim %d not in {32,64,128,256}", hd);
   if (hp->n_embd % 256 || hp->n_ff % 256)
@@ -646,6 +693,11 @@ sfk_status validate_hp(const sfk_hparams* hp) {
     return fail(SFK_ERR_UNSUPPORTED, "embedding type %d not supported", hp->type_embd);
   if (hp->kv_type != SFK_KV_F32 && hp->kv_type != SFK_KV_F16)
     return fail(SFK_ERR_INVALID_ARGUMENT, "kv_type must be SFK_KV_F32 or SFK_KV_F16");
+  if (hp->ep_size > 1) {
+    if (hp->ep_size > MAXR || hp->n_expert % hp->ep_size || hp->ep_rank < 0 || hp->ep_rank >= hp->ep_size)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "ep_size must be in [2,%d] and divide n_expert; 0 <= ep_rank < ep_size",
+                  MAXR);
+  }
   return SFK_OK;
 }
 
@@ -674,6 +726,7 @@ void sfk_engine_free(sfk_engine* e) {
   cudaSetDevice(e->device);
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
+  for (void* p : e->ep_opened) cudaIpcCloseMemHandle(p);
   for (void* p : e->allocs) cudaFree(p);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_pos) cudaFreeHost(e->h_pos);
@@ -698,12 +751,16 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   if (!e) return fail(SFK_ERR_OUT_OF_MEMORY, "host alloc");
   e->device = device;
   e->hp = *hp;
-  e->hd = hp->n_embd / hp->n_head;
+  e->hd = hp->head_dim > 0 ? hp->head_dim : hp->n_embd / hp->n_head;
   e->nq = hp->n_head * e->hd;
   e->nk = hp->n_head_kv * e->hd;
   e->nqkv = e->nq + 2 * e->nk;
   e->sm_count = sm_count_of(device);
   e->seq_pos.assign(hp->max_batch, 0);
+  e->ep_size = hp->ep_size > 1 ? hp->ep_size : 1;
+  e->ep_rank = hp->ep_size > 1 ? hp->ep_rank : 0;
+  e->e_loc = hp->n_expert / e->ep_size;
+  e->e0 = e->ep_rank * e->e_loc;
 #define TRY(x)               \
   do {                       \
     sfk_status s_ = (x);     \
@@ -733,9 +790,10 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     TRY(e->alloc(&W.attn_norm, sizeof(float) * d, &e->weight_bytes));
     TRY(e->alloc(&W.ffn_norm, sizeof(float) * d, &e->weight_bytes));
     TRY(e->alloc(&W.router, sizeof(float) * d * E, &e->weight_bytes));
-    TRY(e->alloc(&W.gate, dev_row_bytes(hp->type_ffn_gu, d) * F * E, &e->weight_bytes));
-    TRY(e->alloc(&W.up, dev_row_bytes(hp->type_ffn_gu, d) * F * E, &e->weight_bytes));
-    TRY(e->alloc(&W.down, dev_row_bytes(hp->type_ffn_down, F) * d * E, &e->weight_bytes));
+    const int El = e->e_loc;  // this rank's experts
+    TRY(e->alloc(&W.gate, dev_row_bytes(hp->type_ffn_gu, d) * F * El, &e->weight_bytes));
+    TRY(e->alloc(&W.up, dev_row_bytes(hp->type_ffn_gu, d) * F * El, &e->weight_bytes));
+    TRY(e->alloc(&W.down, dev_row_bytes(hp->type_ffn_down, F) * d * El, &e->weight_bytes));
   }
   // paged KV: one pool per layer of B * ceil(n_ctx/16) pages [Hkv][16][hd];
   // pages are handed to sequences in a seeded permuted order (a fragmented
@@ -807,6 +865,20 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->pos_cur, sizeof(int) * B, sb));
   TRY(e->alloc(&e->tok_hist, sizeof(int) * B, sb));
   TRY(e->alloc(&e->status, sizeof(int), sb));
+  if (e->ep_size > 1) {
+    // exchange buffer: [2][B][d] partial outputs, then MAXR flag words; its own
+    // allocation so that its IPC handle exposes nothing else
+    const size_t part = sizeof(float) * 2 * (size_t)B * d;
+    TRY(e->alloc(&e->ep_buf, part + 256, sb));
+    e->ep_flags = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(e->ep_buf) + part);
+    TRY(e->alloc(&e->ep_step, sizeof(int), sb));
+    cudaError_t ce = cudaMemset(e->ep_buf, 0, part + 256);
+    if (ce == cudaSuccess) ce = cudaMemset(e->ep_step, 0, sizeof(int));
+    if (ce != cudaSuccess) {
+      sfk_engine_free(e);
+      return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
+    }
+  }
   {
     cudaError_t ce = cudaSuccess;
     ce = cudaMemset(e->router_counter, 0, 2 * sizeof(int));
@@ -906,6 +978,8 @@ sfk_status sfk_expert_put(sfk_engine* e, int layer, int expert, const void* bund
   const sfk_hparams& hp = e->hp;
   if (layer < 0 || layer >= hp.n_layer || expert < 0 || expert >= hp.n_expert)
     return fail(SFK_ERR_INVALID_ARGUMENT, "expert (%d,%d) out of range", layer, expert);
+  if (expert < e->e0 || expert >= e->e0 + e->e_loc) return SFK_OK;  // another rank's expert
+  expert -= e->e0;
   const size_t gl = dev_gguf_row_bytes(hp.type_ffn_gu, hp.n_embd) * hp.n_ff;
   const size_t dl = dev_gguf_row_bytes(hp.type_ffn_down, hp.n_ff) * hp.n_embd;
   if (n_bytes != 2 * gl + dl) return fail(SFK_ERR_INVALID_ARGUMENT, "bundle %zu bytes, expected %zu", n_bytes, 2 * gl + dl);
@@ -959,7 +1033,11 @@ sfk_status sfk_weights_synth(sfk_engine* e, uint64_t seed) {
         continue;
       }
       const int type = tensor_type(e, tid);
-      CK(launch_synth(type, tensor_seed(seed, tid, l), 0.02f, tmp, rows, (int)cols, e->stream));
+      // expert tensors: this rank's rows of the full stacked tensor
+      const int64_t row0 = tid == SFK_T_FFN_GATE_EXPS || tid == SFK_T_FFN_UP_EXPS ? (int64_t)e->e0 * e->hp.n_ff
+                           : tid == SFK_T_FFN_DOWN_EXPS                          ? (int64_t)e->e0 * e->hp.n_embd
+                                                                                  : 0;
+      CK(launch_synth(type, tensor_seed(seed, tid, l), 0.02f, tmp, rows, (int)cols, e->stream, row0));
       sfk_status s = put_gguf_device(e, tid, l, tmp);
       if (s) {
         cudaFreeAsync(tmp, e->stream);
@@ -1130,6 +1208,45 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
   cudaEventDestroy(z);
   if (s) return s;
   return engine_check(e);
+}
+
+sfk_status sfk_ep_handle(sfk_engine* e, void* handle_out, size_t n_bytes) {
+  if (!e || !handle_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  if (e->ep_size <= 1) return fail(SFK_ERR_INVALID_ARGUMENT, "engine is not expert-parallel");
+  if (n_bytes < sizeof(cudaIpcMemHandle_t) || n_bytes < SFK_EP_HANDLE_BYTES)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "handle buffer of %zu bytes", n_bytes);
+  CK(cudaSetDevice(e->device));
+  cudaIpcMemHandle_t h;
+  CK(cudaIpcGetMemHandle(&h, e->ep_buf));
+  memcpy(handle_out, &h, sizeof(h));
+  return SFK_OK;
+}
+
+sfk_status sfk_ep_connect(sfk_engine* e, const void* handles, int32_t n_ranks) {
+  if (!e || !handles) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  if (e->ep_size <= 1) return fail(SFK_ERR_INVALID_ARGUMENT, "engine is not expert-parallel");
+  if (n_ranks != e->ep_size) return fail(SFK_ERR_INVALID_ARGUMENT, "%d handles for %d ranks", n_ranks, e->ep_size);
+  if (e->ep_connected) return fail(SFK_ERR_INVALID_ARGUMENT, "already connected");
+  CK(cudaSetDevice(e->device));
+  const size_t part = sizeof(float) * 2 * (size_t)e->hp.max_batch * e->hp.n_embd;
+  for (int r = 0; r < n_ranks; ++r) {
+    uint8_t* base = nullptr;
+    if (r == e->ep_rank) {
+      base = reinterpret_cast<uint8_t*>(e->ep_buf);
+    } else {
+      cudaIpcMemHandle_t h;
+      memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * SFK_EP_HANDLE_BYTES, sizeof(h));
+      void* p = nullptr;
+      cudaError_t ce = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+      if (ce != cudaSuccess) return fail(SFK_ERR_RUNTIME, "rank %d buffer: %s", r, cudaGetErrorString(ce));
+      e->ep_opened.push_back(p);
+      base = static_cast<uint8_t*>(p);
+    }
+    e->ep_parts[r] = reinterpret_cast<const float*>(base);
+    e->ep_peer_flags[r] = reinterpret_cast<int*>(base + part);
+  }
+  e->ep_connected = true;
+  return SFK_OK;
 }
 
 // ---- operator-level -------------------------------------------------------

@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 #include <cooperative_groups.h>
 #include <cuda_fp16.h>
+#include <algorithm>
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
@@ -367,8 +368,18 @@ __device__ void epi_down(const StreamParams& p, const float* acc, int r0, int r1
     const int row = idx % nr, t = idx / nr;
     // experts * weights, then moe_out = e0 + e1 + ..., then + ffn_inp
     // (engine.cpp:1973-1986)
-    float a = __fmul_rn(acc[row * p.n_pairs + t * k], p.route->w[t * k]);
-    for (int j = 1; j < k; ++j) a = __fadd_rn(a, __fmul_rn(acc[row * p.n_pairs + t * k + j], p.route->w[t * k + j]));
+    float a;
+    if (p.ep_eloc == 0) {
+      a = __fmul_rn(acc[row * p.n_pairs + t * k], p.route->w[t * k]);
+      for (int j = 1; j < k; ++j) a = __fadd_rn(a, __fmul_rn(acc[row * p.n_pairs + t * k + j], p.route->w[t * k + j]));
+    } else {  // this rank's experts only; the ranks' partials are added by the combine
+      a = 0.0f;
+      for (int j = 0; j < k; ++j) {
+        const int id = p.route->ids[t * k + j];
+        if (id >= p.ep_e0 && id < p.ep_e0 + p.ep_eloc)
+          a = __fadd_rn(a, __fmul_rn(acc[row * p.n_pairs + t * k + j], p.route->w[t * k + j]));
+      }
+    }
     if (p.res) a = __fadd_rn(a, p.res[(int64_t)t * p.rows + r0 + row]);
     p.y[(int64_t)t * p.y_stride + r0 + row] = a;
   }
@@ -870,10 +881,10 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
     for (int t = warp; t < p.b; t += NWS)
       route_select(probs_s + t * p.n_expert, p.n_expert, p.k, &sroute->ids[t * p.k], &sroute->w[t * p.k], lane);
     consumer_sync<NWS>();
-    if (p.b * p.k <= 32 && p.n_expert <= 64) {
-      if (warp == 0) build_slots_warp(sroute->ids, p.b * p.k, sroute, lane);
+    if (p.b * p.k <= 32 && (p.ep_eloc > 0 ? p.ep_eloc : p.n_expert) <= 64) {
+      if (warp == 0) build_slots_warp(sroute->ids, p.b * p.k, sroute, lane, p.ep_e0, p.ep_eloc);
     } else if (threadIdx.x == 0) {
-      build_slots(sroute->ids, p.b * p.k, sroute);
+      build_slots(sroute->ids, p.b * p.k, sroute, p.ep_e0, p.ep_eloc);
     }
     if (threadIdx.x == 0) {
       sroute->k = p.k;
@@ -951,7 +962,7 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
       route_select(probs_s + t * p.n_expert, p.n_expert, p.k, &sroute->ids[t * p.k], &sroute->w[t * p.k], lane);
     consumer_sync<NWS>();
     if (tid == 0) {
-      build_slots(sroute->ids, p.b * p.k, sroute);
+      build_slots(sroute->ids, p.b * p.k, sroute, p.ep_e0, p.ep_eloc);
       sroute->k = p.k;
       sroute->b = p.b;
       // departure count; its result is looked at only when the CTA is done,
@@ -1474,7 +1485,7 @@ __global__ void __launch_bounds__(RT_THREADS) router_kernel(const RouterParams p
   const int np = p.b * p.k;
   int ids_l[MAXP];
   for (int i = 0; i < np; ++i) ids_l[i] = __ldcg(&r->ids[i]);
-  build_slots(ids_l, np, r);
+  build_slots(ids_l, np, r, p.ep_e0, p.ep_eloc);
   r->k = p.k;
   r->b = p.b;
   atomicExch(p.counter, 0);
@@ -1512,11 +1523,58 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
       p.tok_hist[tid] = tok;
     }
   }
+  if (blockIdx.x == 0 && tid == 0 && p.ep_step) *p.ep_step += 1;  // expert-parallel combine epochs
   __syncthreads();
   const int64_t rb = (int64_t)dev_gguf_row_bytes(p.type, p.d);
   const int i = blockIdx.x * 256 + tid;
   if (i < p.d) {
     for (int t = 0; t < p.b; ++t) p.x[(int64_t)t * p.d + i] = gguf_dequant_one(p.type, p.tok_embd + (int64_t)toks[t] * rb, i);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Expert-parallel combine (see EpParams): signal this rank's partial to every
+// rank, wait for every rank's, add them in rank order.  The waits are bounded
+// and report ERR_TIMEOUT; nothing traps.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
+  // the step counter was written by the embed kernel, two or more kernels back
+  const int epoch = *p.ep_step * p.n_layer + p.layer + 1;
+  pdl_wait();
+  pdl_launch_dependents();
+  if (blockIdx.x == 0 && (int)threadIdx.x < p.n_ranks) {
+    __threadfence_system();  // this rank's partial (the down kernel's output) before the flag
+    st_release_sys(p.peer_flags[threadIdx.x] + p.rank, epoch);
+  }
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    bool ok = true;
+    for (int r = 0; r < p.n_ranks && ok; ++r) {
+      while (ld_acquire_sys(p.flags + r) < epoch) {
+        __nanosleep(32);
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(p.status, ERR_TIMEOUT);
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int off = (p.layer & 1) * p.half;
+  for (int i = blockIdx.x * 256 + threadIdx.x; i < p.n; i += gridDim.x * 256) {
+    float a = __ldcv(p.parts[0] + off + i);
+    for (int r = 1; r < p.n_ranks; ++r) a = __fadd_rn(a, __ldcv(p.parts[r] + off + i));
+    p.x[i] = a;
   }
 }
 
@@ -1689,6 +1747,12 @@ int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_ch
     case 256: return f16 ? attn_active_clusters_t<256, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<256, 0>(gqa, cluster, max_chunk);
     default: return 0;
   }
+}
+
+cudaError_t launch_ep_combine(const EpParams& p, cudaStream_t st, bool pdl) {
+  if (p.n_ranks < 1 || p.n_ranks > MAXR || p.n < 1) return cudaErrorInvalidValue;
+  const int grid = std::min(64, (p.n + 255) / 256);
+  return launch_pdl(ep_combine_kernel, dim3(grid), dim3(256), 0, st, pdl, p);
 }
 
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl) {

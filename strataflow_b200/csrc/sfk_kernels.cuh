@@ -10,6 +10,7 @@ constexpr int MAXP = 128;  // max (token, expert) pairs per step  (b * k)
 constexpr int MAXB = 16;   // max tokens per step
 constexpr int NW = 8;      // consumer warps of the producer/consumer streaming kernel
 constexpr int RING_BYTES = 96 * 1024;
+constexpr int MAXR = 8;    // max expert-parallel ranks
 
 // Routing of one MoE step, written by the router kernel (device memory).
 // Pair p = t * k + j is token t's j-th routed expert.  Slots are the distinct
@@ -120,6 +121,10 @@ struct StreamParams {
   int s2_tile;
   int s2_stages;
   int s2_occ;  // 2: size the kernel for two CTAs per SM (half the shared memory and registers)
+  // expert parallelism: this rank holds experts [ep_e0, ep_e0 + ep_eloc)
+  // (ep_eloc = 0: all experts are local); routed tiles and the weighted
+  // combine skip the others
+  int ep_e0, ep_eloc;
   Plan2 pl;  // filled by the launcher
 };
 
@@ -146,6 +151,7 @@ struct RouterParams {
   Route* route;
   float* logits;           // [b][E] scratch
   int* counter;            // self-resetting
+  int ep_e0, ep_eloc;      // local experts (ep_eloc = 0: all)
   int* status;
 };
 
@@ -160,6 +166,25 @@ struct EmbedParams {
   int* pos_state;          // [b] persistent position counters (greedy loop)
   int* pos_cur;            // [b] position of this step (out)
   float* x;                // [b][d]
+  int* ep_step;            // expert parallelism: step counter the combine epochs derive from (or null)
+  int* status;
+};
+
+// Expert-parallel combine of one layer: every rank wrote its partial MoE
+// output (its local experts' weighted sum, plus the residual on rank 0) into
+// parts[rank] + (layer & 1) * half; x = sum of the ranks' partials in rank
+// order, identical on every rank.  Peers signal through each other's flag
+// words over peer memory (epoch = step * n_layer + layer + 1).
+struct EpParams {
+  const float* parts[MAXR];  // every rank's partial buffer (peer pointers; own buffer at [rank])
+  int* flags;                // this rank's flag words [MAXR] (peers write them)
+  int* peer_flags[MAXR];     // every rank's flag words
+  int n_ranks, rank;
+  int layer, n_layer;
+  const int* ep_step;
+  int half;                  // floats in one of the two partial buffers
+  int n;                     // floats to combine (b * d)
+  float* x;
   int* status;
 };
 
@@ -169,6 +194,7 @@ int stream2_smem_bytes(const StreamParams& p);  // the warp-tile kernel's shared
 int stream2_occupancy(const StreamParams& p);   // CTAs per SM its plan allows (0: the kernel cannot run it)
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
+cudaError_t launch_ep_combine(const EpParams& p, cudaStream_t st, bool pdl);
 // clusters of `cluster` attention CTAs that fit on the device at once (0 if
 // that cluster size cannot be launched)
 int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_chunk);
@@ -179,7 +205,7 @@ cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nr
 cudaError_t launch_unpack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);
 cudaError_t launch_dequant(int type, const uint8_t* src, float* dst, int64_t n, cudaStream_t st);
 cudaError_t launch_synth(int type, uint64_t seed, float std_, uint8_t* dst_gguf, int64_t nrows, int K,
-                         cudaStream_t st);
+                         cudaStream_t st, int64_t row0 = 0);
 cudaError_t launch_synth_f32(uint64_t seed, float std_, float* dst, int64_t n, cudaStream_t st);
 cudaError_t launch_quant_act(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t st);

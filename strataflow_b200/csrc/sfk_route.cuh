@@ -252,13 +252,15 @@ __device__ void route_one(const float* x, const float* norm_w, const float* w_r,
   sync();
 }
 
-// The same slot lists built by one warp when np <= 32 and every id < 64:
-// lane i holds pair i; the slot of an expert is the number of distinct
+// The same slot lists built by one warp when np <= 32 and every local id <
+// 64: lane i holds pair i; the slot of an expert is the number of distinct
 // smaller experts in use, a pair's place in its slot the number of earlier
-// pairs of the same expert.
-__device__ inline void build_slots_warp(const int* ids, int np, Route* r, int lane) {
-  const int id = lane < np ? ids[lane] : -1;
-  const unsigned act = __ballot_sync(0xffffffffu, lane < np);
+// pairs of the same expert.  Only experts [e0, e0 + eloc) get slots (eloc = 0:
+// all), numbered from e0.
+__device__ inline void build_slots_warp(const int* ids, int np, Route* r, int lane, int e0 = 0, int eloc = 0) {
+  int id = lane < np ? ids[lane] : -1;
+  if (eloc > 0 && id >= 0) id = (id >= e0 && id < e0 + eloc) ? id - e0 : -1;
+  const unsigned act = __ballot_sync(0xffffffffu, id >= 0);
   unsigned lo = 0, hi = 0;
   if (id >= 0 && id < 32) lo = 1u << id;
   if (id >= 32) hi = 1u << (id - 32);
@@ -271,34 +273,36 @@ __device__ inline void build_slots_warp(const int* ids, int np, Route* r, int la
   // pairs of each expert, and the pairs of all smaller experts before them
   const unsigned same = __match_any_sync(0xffffffffu, id) & act;
   const int slot = id < 0 ? 0 : (id < 32 ? __popc(lo & ((1u << id) - 1u)) : n_lo + __popc(hi & ((1u << (id - 32)) - 1u)));
-  int before = 0;  // pairs whose expert is smaller than mine
+  int before = 0;  // local pairs whose expert is smaller than mine
   for (int j = 0; j < np; ++j) {
     const int oj = __shfl_sync(0xffffffffu, id, j);
-    before += (oj < id) ? 1 : 0;
+    before += (oj >= 0 && oj < id) ? 1 : 0;
   }
   const int place = __popc(same & ((1u << lane) - 1u));
-  if (lane < np) r->slot_pairs[before + place] = lane;
-  // slot_off[s] = pairs of the s smallest experts: the first pair of slot s
-  // knows it, and the total closes the list
-  if (lane < np && place == 0) r->slot_off[slot] = before;
+  if (id >= 0) r->slot_pairs[before + place] = lane;
+  // slot_off[s] = local pairs of the s smallest experts: the first pair of
+  // slot s knows it, and the total closes the list
+  if (id >= 0 && place == 0) r->slot_off[slot] = before;
   if (lane == 0) {
-    r->slot_off[ns] = np;
+    r->slot_off[ns] = __popc(act);
     r->n_slots = ns;
   }
   __syncwarp();
 }
 
 // Slot lists from the pairs' expert ids: distinct experts ascending, each with
-// its pairs ascending.  One thread.
-__device__ inline void build_slots(const int* ids, int np, Route* r) {
-  int ns = 0, fill = 0, prev = -1;
+// its pairs ascending.  Only experts [e0, e0 + eloc) get slots (eloc = 0: all),
+// numbered from e0.  One thread.
+__device__ inline void build_slots(const int* ids, int np, Route* r, int e0 = 0, int eloc = 0) {
+  const int lo = eloc > 0 ? e0 : 0, hi = eloc > 0 ? e0 + eloc : 0x7fffffff;
+  int ns = 0, fill = 0, prev = lo - 1;
   r->slot_off[0] = 0;
   while (true) {
     int nxt = 0x7fffffff;
     for (int i = 0; i < np; ++i)
       if (ids[i] > prev && ids[i] < nxt) nxt = ids[i];
-    if (nxt == 0x7fffffff) break;
-    r->slot_expert[ns] = nxt;
+    if (nxt == 0x7fffffff || nxt >= hi) break;
+    r->slot_expert[ns] = nxt - lo;
     for (int i = 0; i < np; ++i)
       if (ids[i] == nxt) r->slot_pairs[fill++] = i;
     r->slot_off[++ns] = fill;

@@ -43,10 +43,14 @@ class ModelConfig:
     type_output: int = L.TYPE_Q8_0
     kv_type: int = L.KV_F32
     max_batch: int = 1
+    ep_size: int = 1   # expert-parallel ranks (one engine per GPU)
+    ep_rank: int = 0
+    head_dim: int = 0  # 0: n_embd / n_head
 
     @property
-    def head_dim(self) -> int:
-        return self.n_embd // self.n_head
+    def hd(self) -> int:
+        """The attention head width in use."""
+        return self.head_dim if self.head_dim > 0 else self.n_embd // self.n_head
 
     def to_c(self) -> L.Hparams:
         h = L.Hparams()
@@ -77,6 +81,19 @@ def mixtral_config(**kw) -> ModelConfig:
                     n_vocab=32000, n_ctx=1024, rms_eps=1e-5, freq_base=1e6, type_embd=L.TYPE_Q6_K,
                     type_attn=L.TYPE_Q6_K, type_ffn_gu=L.TYPE_Q4_K, type_ffn_down=L.TYPE_Q4_K,
                     type_output=L.TYPE_Q6_K, kv_type=L.KV_F16)
+    return c.replace(**kw)
+
+
+def trillion_config(**kw) -> ModelConfig:
+    """~1T-parameter llama-arch MoE -- 61 layers, d 7168, 64q/8kv
+    heads (hd 128), 384 experts top-8, FFN 2048, vocab 160000; experts Q4_K,
+    trunk Q8_0 (RoPE base unspecified there: 1e4), f16 KV, context 1280 (a
+    1024-token prompt + 128 decode steps); meant for expert parallelism
+    (ep_size 4 or 8: ~156 or ~84 GB per GPU)."""
+    c = ModelConfig(n_embd=7168, n_head=64, n_head_kv=8, n_layer=61, n_ff=2048, n_expert=384, n_expert_used=8,
+                    n_vocab=160000, n_ctx=1280, rms_eps=1e-5, freq_base=10000.0, head_dim=128, type_embd=L.TYPE_Q8_0,
+                    type_attn=L.TYPE_Q8_0, type_ffn_gu=L.TYPE_Q4_K, type_ffn_down=L.TYPE_Q4_K,
+                    type_output=L.TYPE_Q8_0, kv_type=L.KV_F16)
     return c.replace(**kw)
 
 
@@ -116,6 +133,25 @@ class Engine:
     def stream(self) -> int:
         """cudaStream_t (as an int) every call of this engine is ordered on."""
         return int(self._lib.sfk_engine_stream(self.h) or 0)
+
+    # -- expert parallelism ---------------------------------------------------
+    def ep_handle(self) -> bytes:
+        """This rank's exchange-buffer handle (to be passed to every rank)."""
+        buf = (C.c_uint8 * L.EP_HANDLE_BYTES)()
+        L.check(self._lib.sfk_ep_handle(self.h, buf, L.EP_HANDLE_BYTES))
+        return bytes(buf)
+
+    def ep_connect(self, handles) -> None:
+        """Open every rank's exchange buffer (handles in rank order)."""
+        blob = b"".join(handles)
+        L.check(self._lib.sfk_ep_connect(self.h, blob, len(handles)))
+
+    def ep_connect_group(self, group=None) -> None:
+        """Exchange handles over a torch.distributed group and connect."""
+        import torch.distributed as dist
+        hs = [None] * dist.get_world_size(group)
+        dist.all_gather_object(hs, self.ep_handle(), group=group)
+        self.ep_connect(hs)
 
     def time_kernels(self, n_seq: int = 1, iters: int = 32) -> dict:
         """Average device ms of each kernel class of one step (sfk_time_kernels)."""
@@ -189,7 +225,7 @@ class Engine:
         """Step buffers of the last layer (sfk_debug_get): 0 attention output,
         1 ffn_inp, 2 q after RoPE, 3 SwiGLU activation."""
         c = self.cfg
-        n = {0: c.n_head * c.head_dim, 1: c.n_embd, 2: c.n_head * c.head_dim,
+        n = {0: c.n_head * c.hd, 1: c.n_embd, 2: c.n_head * c.hd,
              3: c.n_expert_used * c.n_ff}[which] * n_seq
         out = np.empty(n, np.float32)
         L.check(self._lib.sfk_debug_get(self.h, which, out.ctypes.data_as(C.c_void_p), n))

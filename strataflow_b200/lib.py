@@ -31,7 +31,11 @@ class Hparams(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
         ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
-            "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_type", "max_batch")]
+            "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_type", "max_batch",
+            "ep_size", "ep_rank", "head_dim")]
+
+
+EP_HANDLE_BYTES = 64  # SFK_EP_HANDLE_BYTES
 
 
 class Stats(C.Structure):
@@ -71,6 +75,8 @@ _SIGS = {
     "sfk_moe_ffn": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
     "sfk_moe_ffn_noalloc": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
     "sfk_attn_decode_paged": (I32, [P, P, P, I32, I32, P, I32, P, I32, I32, I32, I32, P, P]),
+    "sfk_ep_handle": (I32, [P, P, SZ]),
+    "sfk_ep_connect": (I32, [P, P, I32]),
 }
 
 _lib = None

@@ -53,3 +53,14 @@ def test_engine_create_rejects_bad_hparams_without_touching_a_gpu(sfk):
     rc = sfk.sfk_engine_create(0, C.byref(hp), C.byref(out))   # all-zero shape
     assert rc == L.SFK_OK + 1 and not out.value
     assert b"positive" in sfk.sfk_last_error()
+
+
+def test_expert_parallel_shape_is_checked_before_any_gpu_work(sfk):
+    """ep_size must divide n_expert and ep_rank lie in [0, ep_size)."""
+    from strataflow_b200 import engine as E
+    out = C.c_void_p()
+    for kw in (dict(ep_size=3), dict(ep_size=2, ep_rank=2), dict(ep_size=16)):
+        hp = E.tiny_config(**kw).to_c()   # 8 experts
+        rc = sfk.sfk_engine_create(0, C.byref(hp), C.byref(out))
+        assert rc == L.SFK_OK + 1 and not out.value, kw
+        assert b"ep_size" in sfk.sfk_last_error()

@@ -1,0 +1,81 @@
+"""Expert parallelism over two GPUs of one box: each rank holds half of every
+layer's experts, the ranks add their expert outputs through peer memory after
+every layer, and the decode must match one GPU holding everything: the same
+greedy tokens, the same logits on both ranks (bit-identical: the ranks add
+the same partials in the same order), and logits within float rounding of
+the single-GPU engine (whose expert sum runs in one pass instead of two
+partials).  Skipped on a box with fewer than two GPUs.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    try:
+        torch.cuda.set_device(rank)
+        dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=120))
+        from strataflow_b200 import engine as E
+        cfg = E.tiny_config(**cfg_kw).replace(ep_size=world, ep_rank=rank)
+        eng = E.Engine.load(cfg, seed=seed, device=rank)
+        eng.ep_connect_group()
+        toks, logits = eng.generate(prompt, n_gen, host_loop=True)
+        dev = eng.decode_greedy(6, 1)[:, 0].tolist()   # device loop continues the sequence
+        q.put((rank, toks, np.stack(logits), dev, None))
+        dist.barrier()
+        eng.close()
+        dist.destroy_process_group()
+    except Exception as ex:  # report instead of hanging the parent
+        q.put((rank, None, None, None, repr(ex)))
+
+
+@pytest.mark.parametrize("cfg_kw", [
+    dict(n_layer=2),                                                               # routing inside gate/up
+    dict(n_layer=2, type_ffn_gu=12, type_ffn_down=12, n_expert=16, n_expert_used=4),
+    dict(n_layer=2, n_expert=72, n_expert_used=4),                                 # standalone router kernel
+])
+def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw):
+    import torch
+    import torch.multiprocessing as mp
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    from strataflow_b200 import engine as E
+    seed, n_gen = 11, 10
+    prompt = np.random.default_rng(3).integers(0, 4096, 8).tolist()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfg_kw, seed, prompt, n_gen, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(2):
+        rank, toks, logits, dev, err = q.get(timeout=300)
+        assert err is None, err
+        res[rank] = (toks, logits, dev)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    ref = E.Engine.load(E.tiny_config(**cfg_kw), seed=seed)
+    toks1, logits1 = ref.generate(prompt, n_gen, host_loop=True)
+    logits1 = np.stack(logits1)
+    dev1 = ref.decode_greedy(6, 1)[:, 0].tolist()
+    assert res[0][0] == res[1][0] == toks1
+    assert np.array_equal(res[0][1].view(np.uint32), res[1][1].view(np.uint32))
+    rel = np.linalg.norm(res[0][1] - logits1) / np.linalg.norm(logits1)
+    assert rel < 1e-5, rel
+    assert res[0][2] == res[1][2] == dev1
