@@ -897,13 +897,18 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
       return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
     }
   }
-  if (hp->n_expert <= 64) {
-    // fold the router into the gate/up kernel when its warp-tile form fits
-    // (larger expert counts keep the one-CTA router kernel)
-    e->fused_route = true;
+  {
+    // fold the router into the gate/up kernel when its warp-tile form fits:
+    // small routers are staged whole in every CTA, large ones (hundreds of
+    // experts) are scored a few logits per CTA and exchanged.
+    // SFK_ROUTER_KERNEL=1 keeps the separate router kernel.
+    const char* rk = getenv("SFK_ROUTER_KERNEL");
+    e->fused_route = !(rk && atoi(rk) == 1);
     StreamParams gp = gateup_params(e, 0, B);
     int grid = 0;
-    if (plan_stream(gp, e->sm_count, &grid) != SFK_OK || stream2_smem_bytes(gp) > SMEM_LIMIT) e->fused_route = false;
+    if (e->fused_route &&
+        (plan_stream(gp, e->sm_count, &grid) != SFK_OK || stream2_smem_bytes(gp) > SMEM_LIMIT))
+      e->fused_route = false;
   }
   {
     // RoPE cos/sin for every position (ggml rope cache, mode NORMAL,

@@ -190,10 +190,23 @@ def test_kernel_timing_entry_point(cuda):
     assert eng.stats()["kernels_per_step"] == 2 + 5 * cfg.n_layer
 
 
-def test_many_experts_standalone_router_parity(cuda):
-    """More than 64 experts: routing runs in its own kernel before gate/up."""
+def test_standalone_router_kernel_parity(cuda, monkeypatch):
+    """SFK_ROUTER_KERNEL=1: routing runs in its own kernel before gate/up."""
     from strataflow_b200 import engine as E
+    monkeypatch.setenv("SFK_ROUTER_KERNEL", "1")
     cfg = E.tiny_config(n_layer=2, n_expert=72, n_expert_used=4)
     prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, 8).tolist()
     eng, om, toks, worst = _run_parity(cfg, 9, prompt, 12)
     assert eng.stats()["kernels_per_step"] == 2 + 6 * cfg.n_layer
+
+
+@pytest.mark.parametrize("n_expert,k", [(72, 4), (160, 2)])
+def test_many_experts_fused_routing_parity(cuda, n_expert, k):
+    """Routing inside gate/up for larger expert counts: 72 experts fit the
+    ring (router staged in every CTA); 160 do not (each CTA scores a few
+    logits and the CTAs exchange them)."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=2, n_expert=n_expert, n_expert_used=k)
+    prompt = np.random.default_rng(n_expert).integers(0, cfg.n_vocab, 8).tolist()
+    eng, om, toks, worst = _run_parity(cfg, 9, prompt, 12)
+    assert eng.stats()["kernels_per_step"] == 2 + 5 * cfg.n_layer

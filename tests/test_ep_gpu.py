@@ -46,7 +46,8 @@ def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q):
 @pytest.mark.parametrize("cfg_kw", [
     dict(n_layer=2),                                                               # routing inside gate/up
     dict(n_layer=2, type_ffn_gu=12, type_ffn_down=12, n_expert=16, n_expert_used=4),
-    dict(n_layer=2, n_expert=72, n_expert_used=4),                                 # standalone router kernel
+    dict(n_layer=2, n_expert=72, n_expert_used=4),                                 # router staged per CTA
+    dict(n_layer=2, n_expert=160, n_expert_used=2),                                # logits exchanged between CTAs
 ])
 def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw):
     import torch
