@@ -236,6 +236,10 @@ struct sfk_engine {
   bool fused_route = false;  // the gate/up kernel routes in its prologue (no router kernel)
   // expert parallelism: this rank holds experts [e0, e0 + e_loc)
   int ep_size = 1, ep_rank = 0, e_loc = 0, e0 = 0;
+  // head parallelism (with expert parallelism when the heads divide): this
+  // rank computes query heads [q0, q0 + hq_loc) and kv heads [kv0, kv0 + hkv_loc)
+  bool head_par = false;
+  int hq_loc = 0, hkv_loc = 0, q0 = 0, kv0 = 0;
   float* ep_buf = nullptr;      // [2][B][d] partial outputs (layer parity) | flags [MAXR] ints
   int* ep_flags = nullptr;
   int* ep_step = nullptr;
@@ -366,7 +370,7 @@ KvView kv_view(const sfk_engine* e, int l) {
   kv.page_table = e->page_table;
   kv.max_pages = e->max_pages;
   kv.n_pages = e->n_pages;
-  kv.n_head_kv = hp.n_head_kv;
+  kv.n_head_kv = e->hkv_loc;
   kv.head_dim = e->hd;
   kv.f16 = hp.kv_type == SFK_KV_F16 ? 1 : 0;
   const size_t kv_elem = kv.f16 ? 2 : 4;
@@ -467,7 +471,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.epi = EPI_QKV;
       p.y = e->q;
       p.kv = kv_view(e, l);
-      p.n_head = hp.n_head;
+      p.n_head = e->hq_loc;
       p.rope = e->rope;
       p.pos = e->pos_cur;
       if (l == 0) {  // the embedding kernel has read the argmax keys by now
@@ -485,7 +489,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       a.kv = kv_view(e, l);
       a.pos = e->pos_cur;
       a.b = b;
-      a.n_head = hp.n_head;
+      a.n_head = e->hq_loc;
       a.cluster = e->attn_cluster;
       a.max_chunk = e->attn_max_chunk;
       a.out = e->attn_out;
@@ -510,6 +514,12 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.y = e->ffn_inp;
       p.res = e->x;
       p.y_stride = d;
+      if (e->head_par) {
+        // this rank's heads' share of the projection (its columns) into the
+        // exchange slot; the residual is added once, by rank 0
+        p.y = e->ep_buf + (size_t)((l & 1) * 2 + 0) * e->hp.max_batch * d;
+        p.res = e->ep_rank == 0 ? e->x : nullptr;
+      }
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
       CK(launch_stream(p, grid, st, pdl));
@@ -568,7 +578,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
         // residual is added once, by rank 0; the combine writes x
         p.ep_e0 = e->e0;
         p.ep_eloc = e->e_loc;
-        p.y = e->ep_buf + (size_t)(l & 1) * e->hp.max_batch * d;
+        p.y = e->ep_buf + (size_t)((l & 1) * 2 + 1) * e->hp.max_batch * d;
         p.res = e->ep_rank == 0 ? e->ffn_inp : nullptr;
       }
       p.y_stride = d;
@@ -606,6 +616,28 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
   }
 }
 
+// Combine of a layer stage across the expert-parallel ranks (peer memory).
+sfk_status launch_combine(sfk_engine* e, int l, int stage, int b, float* dst) {
+  EpParams q{};
+  for (int r = 0; r < e->ep_size; ++r) {
+    q.parts[r] = e->ep_parts[r];
+    q.peer_flags[r] = e->ep_peer_flags[r];
+  }
+  q.flags = e->ep_flags;
+  q.n_ranks = e->ep_size;
+  q.rank = e->ep_rank;
+  q.layer = l;
+  q.n_layer = e->hp.n_layer;
+  q.stage = stage;
+  q.ep_step = e->ep_step;
+  q.half = e->hp.max_batch * e->hp.n_embd;
+  q.n = b * e->hp.n_embd;
+  q.x = dst;
+  q.status = e->status;
+  CK(launch_ep_combine(q, e->stream, true));
+  return SFK_OK;
+}
+
 sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
   int nk = 0;
   sfk_status s = launch_one(e, K_EMBED, 0, b, greedy, true);
@@ -616,24 +648,13 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
       if (c == K_ROUTER && e->fused_route) continue;
       if ((s = launch_one(e, c, l, b, greedy, true))) return s;
       ++nk;
+      if (c == K_OPROJ && e->head_par) {  // add the ranks' attention projections
+        if ((s = launch_combine(e, l, 0, b, e->ffn_inp))) return s;
+        ++nk;
+      }
     }
     if (e->ep_size > 1) {  // add the ranks' expert outputs (peer memory)
-      EpParams q{};
-      for (int r = 0; r < e->ep_size; ++r) {
-        q.parts[r] = e->ep_parts[r];
-        q.peer_flags[r] = e->ep_peer_flags[r];
-      }
-      q.flags = e->ep_flags;
-      q.n_ranks = e->ep_size;
-      q.rank = e->ep_rank;
-      q.layer = l;
-      q.n_layer = e->hp.n_layer;
-      q.ep_step = e->ep_step;
-      q.half = e->hp.max_batch * e->hp.n_embd;
-      q.n = b * e->hp.n_embd;
-      q.x = e->x;
-      q.status = e->status;
-      CK(launch_ep_combine(q, e->stream, true));
+      if ((s = launch_combine(e, l, 1, b, e->x))) return s;
       ++nk;
     }
   }
@@ -752,8 +773,21 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   e->device = device;
   e->hp = *hp;
   e->hd = hp->head_dim > 0 ? hp->head_dim : hp->n_embd / hp->n_head;
-  e->nq = hp->n_head * e->hd;
-  e->nk = hp->n_head_kv * e->hd;
+  {
+    const int N = hp->ep_size > 1 ? hp->ep_size : 1;
+    // SFK_HEAD_PARALLEL=0 keeps the attention trunk replicated on every rank
+    const char* hpv = getenv("SFK_HEAD_PARALLEL");
+    e->head_par = N > 1 && hp->n_head % N == 0 && hp->n_head_kv % N == 0 &&
+                  (hp->n_head / N) * e->hd % 256 == 0 &&  // the projection's column slice is whole 256-blocks
+                  !(hpv && atoi(hpv) == 0);
+    const int R = e->head_par ? hp->ep_rank : 0, NP = e->head_par ? N : 1;
+    e->hq_loc = hp->n_head / NP;
+    e->hkv_loc = hp->n_head_kv / NP;
+    e->q0 = R * e->hq_loc;
+    e->kv0 = R * e->hkv_loc;
+  }
+  e->nq = e->hq_loc * e->hd;  // this rank's query rows (all of them without head parallelism)
+  e->nk = e->hkv_loc * e->hd;
   e->nqkv = e->nq + 2 * e->nk;
   e->sm_count = sm_count_of(device);
   e->seq_pos.assign(hp->max_batch, 0);
@@ -800,7 +834,7 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   // pool, as a page allocator produces).
   e->max_pages = (hp->n_ctx + 15) / 16;
   e->n_pages = B * e->max_pages;
-  e->kv_layer_elems = (int64_t)e->n_pages * hp->n_head_kv * 16 * e->hd;
+  e->kv_layer_elems = (int64_t)e->n_pages * e->hkv_loc * 16 * e->hd;
   const size_t kv_elem = hp->kv_type == SFK_KV_F16 ? 2 : 4;
   TRY(e->alloc(&e->k_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
   TRY(e->alloc(&e->v_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
@@ -825,11 +859,11 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     // forces 8 or 16
     int want = 0;
     if (const char* v = getenv("SFK_ATTN_CLUSTER")) want = atoi(v);
-    if (want == 0 && B * hp->n_head_kv <= 8 && e->max_pages >= 32) want = 16;
+    if (want == 0 && B * e->hkv_loc <= 8 && e->max_pages >= 32) want = 16;
     if (want == 16 && e->attn_cluster != 16) {
       const int mc16 = (e->max_pages + 15) / 16 * 16;
       if (attn_active_clusters(e->hd, hp->kv_type == SFK_KV_F16, hp->n_head / hp->n_head_kv, 16, mc16) >=
-          B * hp->n_head_kv) {
+          B * e->hkv_loc) {
         e->attn_cluster = 16;
         e->attn_max_chunk = mc16;
       }
@@ -866,9 +900,9 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->tok_hist, sizeof(int) * B, sb));
   TRY(e->alloc(&e->status, sizeof(int), sb));
   if (e->ep_size > 1) {
-    // exchange buffer: [2][B][d] partial outputs, then MAXR flag words; its own
-    // allocation so that its IPC handle exposes nothing else
-    const size_t part = sizeof(float) * 2 * (size_t)B * d;
+    // exchange buffer: [layer parity][stage][B][d] partial outputs, then MAXR
+    // flag words; its own allocation so that its IPC handle exposes nothing else
+    const size_t part = sizeof(float) * 4 * (size_t)B * d;
     TRY(e->alloc(&e->ep_buf, part + 256, sb));
     e->ep_flags = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(e->ep_buf) + part);
     TRY(e->alloc(&e->ep_step, sizeof(int), sb));
@@ -1039,10 +1073,19 @@ sfk_status sfk_weights_synth(sfk_engine* e, uint64_t seed) {
       }
       const int type = tensor_type(e, tid);
       // expert tensors: this rank's rows of the full stacked tensor
-      const int64_t row0 = tid == SFK_T_FFN_GATE_EXPS || tid == SFK_T_FFN_UP_EXPS ? (int64_t)e->e0 * e->hp.n_ff
-                           : tid == SFK_T_FFN_DOWN_EXPS                          ? (int64_t)e->e0 * e->hp.n_embd
-                                                                                  : 0;
-      CK(launch_synth(type, tensor_seed(seed, tid, l), 0.02f, tmp, rows, (int)cols, e->stream, row0));
+      // head-sharded tensors: this rank's rows of Q/K/V, its columns of the
+      // output projection
+      int64_t row0 = tid == SFK_T_FFN_GATE_EXPS || tid == SFK_T_FFN_UP_EXPS ? (int64_t)e->e0 * e->hp.n_ff
+                     : tid == SFK_T_FFN_DOWN_EXPS                          ? (int64_t)e->e0 * e->hp.n_embd
+                                                                            : 0;
+      int64_t col0 = 0, kfull = 0;
+      if (tid == SFK_T_ATTN_Q) row0 = (int64_t)e->q0 * e->hd;
+      if (tid == SFK_T_ATTN_K || tid == SFK_T_ATTN_V) row0 = (int64_t)e->kv0 * e->hd;
+      if (tid == SFK_T_ATTN_OUT) {
+        col0 = (int64_t)e->q0 * e->hd;
+        kfull = (int64_t)e->hp.n_head * e->hd;
+      }
+      CK(launch_synth(type, tensor_seed(seed, tid, l), 0.02f, tmp, rows, (int)cols, e->stream, row0, col0, kfull));
       sfk_status s = put_gguf_device(e, tid, l, tmp);
       if (s) {
         cudaFreeAsync(tmp, e->stream);
@@ -1233,7 +1276,7 @@ sfk_status sfk_ep_connect(sfk_engine* e, const void* handles, int32_t n_ranks) {
   if (n_ranks != e->ep_size) return fail(SFK_ERR_INVALID_ARGUMENT, "%d handles for %d ranks", n_ranks, e->ep_size);
   if (e->ep_connected) return fail(SFK_ERR_INVALID_ARGUMENT, "already connected");
   CK(cudaSetDevice(e->device));
-  const size_t part = sizeof(float) * 2 * (size_t)e->hp.max_batch * e->hp.n_embd;
+  const size_t part = sizeof(float) * 4 * (size_t)e->hp.max_batch * e->hp.n_embd;
   for (int r = 0; r < n_ranks; ++r) {
     uint8_t* base = nullptr;
     if (r == e->ep_rank) {

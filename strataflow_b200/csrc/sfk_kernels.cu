@@ -1548,7 +1548,7 @@ __device__ __forceinline__ int ld_acquire_sys(const int* p) {
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
   // the step counter was written by the embed kernel, two or more kernels back
-  const int epoch = *p.ep_step * p.n_layer + p.layer + 1;
+  const int epoch = (*p.ep_step * p.n_layer + p.layer) * 2 + p.stage + 1;
   pdl_wait();
   pdl_launch_dependents();
   if (blockIdx.x == 0 && (int)threadIdx.x < p.n_ranks) {
@@ -1570,7 +1570,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
     }
   }
   __syncthreads();
-  const int off = (p.layer & 1) * p.half;
+  const int off = ((p.layer & 1) * 2 + p.stage) * p.half;
   for (int i = blockIdx.x * 256 + threadIdx.x; i < p.n; i += gridDim.x * 256) {
     float a = __ldcv(p.parts[0] + off + i);
     for (int r = 1; r < p.n_ranks; ++r) a = __fadd_rn(a, __ldcv(p.parts[r] + off + i));

@@ -170,19 +170,22 @@ struct EmbedParams {
   int* status;
 };
 
-// Expert-parallel combine of one layer: every rank wrote its partial MoE
-// output (its local experts' weighted sum, plus the residual on rank 0) into
-// parts[rank] + (layer & 1) * half; x = sum of the ranks' partials in rank
-// order, identical on every rank.  Peers signal through each other's flag
-// words over peer memory (epoch = step * n_layer + layer + 1).
+// Combine of one layer stage across the ranks: every rank wrote its partial
+// (stage 1: its local experts' weighted sum; stage 0: its heads' share of the
+// output projection; plus the residual on rank 0) into slot
+// parts[rank] + ((layer & 1) * 2 + stage) * half; x = sum of the ranks'
+// partials in rank order, identical on every rank.  Peers signal through each
+// other's flag words over peer memory (epoch = (step * n_layer + layer) * 2 +
+// stage + 1).
 struct EpParams {
   const float* parts[MAXR];  // every rank's partial buffer (peer pointers; own buffer at [rank])
   int* flags;                // this rank's flag words [MAXR] (peers write them)
   int* peer_flags[MAXR];     // every rank's flag words
   int n_ranks, rank;
   int layer, n_layer;
+  int stage;                 // 0: attention output projection, 1: expert FFN
   const int* ep_step;
-  int half;                  // floats in one of the two partial buffers
+  int half;                  // floats in one partial slot ([layer parity][stage] slots)
   int n;                     // floats to combine (b * d)
   float* x;
   int* status;
@@ -205,7 +208,7 @@ cudaError_t launch_repack(int type, const uint8_t* src, uint8_t* dst, int64_t nr
 cudaError_t launch_unpack(int type, const uint8_t* src, uint8_t* dst, int64_t nrows, int K, cudaStream_t st);
 cudaError_t launch_dequant(int type, const uint8_t* src, float* dst, int64_t n, cudaStream_t st);
 cudaError_t launch_synth(int type, uint64_t seed, float std_, uint8_t* dst_gguf, int64_t nrows, int K,
-                         cudaStream_t st, int64_t row0 = 0);
+                         cudaStream_t st, int64_t row0 = 0, int64_t col0 = 0, int64_t kfull = 0);
 cudaError_t launch_synth_f32(uint64_t seed, float std_, float* dst, int64_t n, cudaStream_t st);
 cudaError_t launch_quant_act(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
 cudaError_t launch_fill_f32(float* dst, float v, int64_t n, cudaStream_t st);

@@ -226,7 +226,7 @@ __device__ void synth_blocks_q80(const float v[8], uint8_t* out, int lane) {
 
 // one warp per 256-column block of a [nrows x K] tensor; GGUF layout output
 __global__ void __launch_bounds__(256) synth_kernel(int type, uint64_t seed, float std_, uint8_t* dst, int64_t nrows,
-                                                     int K, int64_t row0) {
+                                                     int K, int64_t row0, int64_t col0, int64_t kfull) {
   __shared__ uint8_t sh[8][288];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t nb_row = K / 256;
@@ -234,7 +234,8 @@ __global__ void __launch_bounds__(256) synth_kernel(int type, uint64_t seed, flo
   const int64_t rb = dev_gguf_row_bytes(type, K);
   for (int64_t blk = (int64_t)blockIdx.x * 8 + warp; blk < total; blk += (int64_t)gridDim.x * 8) {
     const int64_t row = blk / nb_row, bc = blk % nb_row;
-    const int64_t e0 = (row0 + row) * K + bc * 256 + lane * 8;  // element index in the full tensor
+    // element index in the full tensor (rows row0.., columns col0.. of kfull)
+    const int64_t e0 = (row0 + row) * kfull + col0 + bc * 256 + lane * 8;
     float v[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) v[i] = synth_z(seed, e0 + i) * std_;
@@ -370,9 +371,10 @@ static int grid_for(int64_t work, int per_block) {
 }
 
 cudaError_t launch_synth(int type, uint64_t seed, float std_, uint8_t* dst, int64_t nrows, int K, cudaStream_t st,
-                         int64_t row0) {
+                         int64_t row0, int64_t col0, int64_t kfull) {
   if (K % 256) return cudaErrorInvalidValue;
-  synth_kernel<<<grid_for(nrows * (K / 256), 8), 256, 0, st>>>(type, seed, std_, dst, nrows, K, row0);
+  if (kfull <= 0) kfull = K;
+  synth_kernel<<<grid_for(nrows * (K / 256), 8), 256, 0, st>>>(type, seed, std_, dst, nrows, K, row0, col0, kfull);
   return cudaGetLastError();
 }
 cudaError_t launch_synth_f32(uint64_t seed, float std_, float* dst, int64_t n, cudaStream_t st) {

@@ -1,6 +1,7 @@
 """Expert parallelism over two GPUs of one box: each rank holds half of every
-layer's experts, the ranks add their expert outputs through peer memory after
-every layer, and the decode must match one GPU holding everything: the same
+layer's experts (and, when the heads split into whole 256-column blocks, half
+of the attention heads with their KV), the ranks add their partial outputs
+through peer memory after every layer, and the decode must match one GPU holding everything: the same
 greedy tokens, the same logits on both ranks (bit-identical: the ranks add
 the same partials in the same order), and logits within float rounding of
 the single-GPU engine (whose expert sum runs in one pass instead of two
@@ -21,8 +22,8 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q):
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q, env=None):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), **(env or {}))
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -43,13 +44,22 @@ def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q):
         q.put((rank, None, None, None, repr(ex)))
 
 
-@pytest.mark.parametrize("cfg_kw", [
-    dict(n_layer=2),                                                               # routing inside gate/up
-    dict(n_layer=2, type_ffn_gu=12, type_ffn_down=12, n_expert=16, n_expert_used=4),
-    dict(n_layer=2, n_expert=72, n_expert_used=4),                                 # router staged per CTA
-    dict(n_layer=2, n_expert=160, n_expert_used=2),                                # logits exchanged between CTAs
+WIDE = dict(n_layer=2, n_embd=512, n_head=16, n_head_kv=4)   # heads split into whole 256-column blocks
+
+
+@pytest.mark.parametrize("cfg_kw,env,tol", [
+    (dict(n_layer=2), {}, 1e-5),                                                   # routing inside gate/up
+    (dict(n_layer=2, type_ffn_gu=12, type_ffn_down=12, n_expert=16, n_expert_used=4), {}, 1e-5),
+    (dict(n_layer=2, n_expert=72, n_expert_used=4), {}, 1e-5),                     # router staged per CTA
+    (dict(n_layer=2, n_expert=160, n_expert_used=2), {}, 1e-5),                    # logits exchanged between CTAs
+    (WIDE, {"SFK_HEAD_PARALLEL": "0"}, 1e-5),                                      # trunk replicated
+    # heads split over the ranks too: the output projection's sum is cut at
+    # the rank boundary, a reduction-order change every step that moves
+    # activation-quantisation codes; bounded like the reference's own Q8_0
+    # engine-vs-ggml check (tests/test_engine_oracle.cpp:539, 2e-2)
+    (WIDE, {}, 2e-2),
 ])
-def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw):
+def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw, env, tol):
     import torch
     import torch.multiprocessing as mp
     if torch.cuda.device_count() < 2:
@@ -60,7 +70,7 @@ def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfg_kw, seed, prompt, n_gen, q)) for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(r, 2, port, cfg_kw, seed, prompt, n_gen, q, env)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -78,5 +88,5 @@ def test_expert_parallel_two_ranks_match_one_gpu(cuda, cfg_kw):
     assert res[0][0] == res[1][0] == toks1
     assert np.array_equal(res[0][1].view(np.uint32), res[1][1].view(np.uint32))
     rel = np.linalg.norm(res[0][1] - logits1) / np.linalg.norm(logits1)
-    assert rel < 1e-5, rel
+    assert rel < tol, rel
     assert res[0][2] == res[1][2] == dev1
