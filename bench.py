@@ -241,16 +241,19 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     kt = eng.time_kernels(B, iters=64)
     peak, peak_kind = _peaks()
     gu_row = 4096 // 256 * 144
-    uniq = 2 if B == 1 else None
-    if uniq is None:
-        uniq = min(8, 2 * B)
+    # distinct experts a step streams per layer: 2 at b=1; for b tokens the
+    # expectation of a uniform top-2 draw over 8 experts, 8 (1 - 0.75^b)
+    uniq = 2.0 if B == 1 else 8.0 * (1.0 - 0.75 ** B)
     # routed expert rows of gate and up; the routing prologue (F32 router
     # weights + the token's hidden state) rides along in the same kernel
     gu_bytes = uniq * 2 * 14336 * gu_row + (8 * 4096 * 4 + B * 4096 * 4 if kt["router"] == 0.0 else 0)
     gu_ms = kt["gate_up"]
     achieved = gu_bytes / (gu_ms * 1e-3) / 1e9
     kv_bytes_tok = 32 * 2 * 8 * 128 * 2 * (PROMPT + args.warmup + args.steps // 2)
-    step_bytes = st["active_bytes_per_token"] * B + kv_bytes_tok * B
+    # one step streams the trunk once and each distinct expert once
+    expert_bytes_tok = 32 * 2 * 3 * 14336 * gu_row   # two experts per layer, gate + up + down (Q4_K)
+    trunk_bytes = st["active_bytes_per_token"] - expert_bytes_tok
+    step_bytes = trunk_bytes + expert_bytes_tok * uniq / 2.0 + kv_bytes_tok * B
     step_gbs = step_bytes * args.steps / (ms / 1000.0) / 1e9
 
     cpu = None
@@ -292,9 +295,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the routed gate/up kernel at this shape, from an `ncu --set full` capture of
-# the same kernel (2-layer model, identical launch shape): 132.39 MB read +
-# 3.65 MB written.
-GU_TRAFFIC_BYTES = 136.04e6
+# the same kernel (2-layer model, identical launch shape): 132.40 MB read +
+# 3.17 MB written.
+GU_TRAFFIC_BYTES = 135.57e6
 
 
 def run_ep(args, rank: int, world: int, local_rank: int):
@@ -403,6 +406,67 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         dist.destroy_process_group()
 
 
+def run_sweep(args):
+    """configs[1] and configs[2] of BASELINE.json, through the engine's own
+    kernels (sfk_time_kernels: CUDA events around 64 back-to-back launches of
+    one kernel class, launch gaps included).  Prints one JSON line per case.
+
+    mul_mat_id: Mixtral-shape experts (E=8, gate/up 14336x4096, down
+    4096x14336) in Q4_K / Q6_K / Q8_0 at b in {1, 4, 16} tokens (16 is the
+    engine's largest step; 64 is not run).  Four layers are resident and the
+    launches rotate over them, so every launch streams experts that are not
+    in L2.  Bytes = unique routed experts x per-expert matrix bytes; the
+    router is a seeded random F32 matrix, so the expected unique count of a
+    uniform top-2 draw, 8 (1 - 0.75^b), is used (the last launch's measured
+    count is printed beside it).
+
+    attention: 32q/8kv heads, hd 128, f16 KV in 16-token pages handed out in
+    a permuted order, contexts {512, 4096, 32768}, b in {1, 8}; one layer, so
+    working sets under 126 MB stay in L2 between the back-to-back launches
+    (those cases are latency-bound; their GB/s is not an HBM figure)."""
+    from strataflow_b200 import engine as E
+    from strataflow_b200 import lib as L
+    peak, peak_kind = _peaks()
+    names = {L.TYPE_Q4_K: "Q4_K", L.TYPE_Q6_K: "Q6_K", L.TYPE_Q8_0: "Q8_0"}
+    row_bytes = {L.TYPE_Q4_K: lambda K: K // 256 * 144, L.TYPE_Q6_K: lambda K: K // 256 * 210,
+                 L.TYPE_Q8_0: lambda K: K // 32 * 34}
+    d, F = 4096, 14336
+    rng = np.random.default_rng(2)
+    for t in (L.TYPE_Q4_K, L.TYPE_Q6_K, L.TYPE_Q8_0):
+        cfg = E.mixtral_config(n_layer=4, n_ctx=64, max_batch=16, type_ffn_gu=t, type_ffn_down=t)
+        eng = E.Engine.load(cfg, seed=2)
+        for b in (1, 4, 16):
+            for p in range(2):
+                eng.forward_batch(rng.integers(0, cfg.n_vocab, b), np.full(b, p, np.int32), want_logits=False)
+            kt = eng.time_kernels(b, iters=64)
+            ids, _ = eng.route(b)
+            uniq = 8.0 * (1.0 - 0.75 ** b)
+            for kern, mb in (("gate_up", 2 * F * row_bytes[t](d)), ("down", d * row_bytes[t](F))):
+                byts = uniq * mb
+                gbs = byts / (kt[kern] * 1e-3) / 1e9
+                print(json.dumps({"sweep": "mul_mat_id", "kernel": kern, "wtype": names[t], "b": b,
+                                  "us": kt[kern] * 1e3, "bytes": byts, "GBps": gbs, "frac": gbs / peak,
+                                  "peak_kind": peak_kind, "unique_experts_expected": uniq,
+                                  "unique_experts_last_launch": int(np.unique(ids).size)}), flush=True)
+        eng.close()
+    ctxs = (512, 4096, 32768)
+    cfg = E.mixtral_config(n_layer=1, n_ctx=max(ctxs) + 16, max_batch=8)
+    eng = E.Engine.load(cfg, seed=3)
+    pos = 0
+    for ctx in ctxs:
+        while pos < ctx:   # fill the KV of all 8 sequences up to position ctx - 1
+            eng.forward_batch(rng.integers(0, cfg.n_vocab, 8), np.full(8, pos, np.int32), want_logits=False)
+            pos += 1
+        for b in (1, 8):
+            kt = eng.time_kernels(b, iters=64)
+            byts = b * ctx * 8 * 128 * 2 * 2
+            gbs = byts / (kt["attention"] * 1e-3) / 1e9
+            print(json.dumps({"sweep": "attention", "ctx": ctx, "b": b, "us": kt["attention"] * 1e3, "bytes": byts,
+                              "GBps": gbs, "frac": gbs / peak, "peak_kind": peak_kind,
+                              "l2_resident": byts < 126e6}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -418,12 +482,17 @@ def main():
                     help="print only the device-timed decode rate (short profiling runs)")
     ap.add_argument("--model", choices=["mixtral", "1t"], default="mixtral",
                     help="1t: configs[4], experts sharded over the torchrun ranks")
+    ap.add_argument("--sweep", action="store_true",
+                    help="operator sweeps (configs[1] mul_mat_id, configs[2] attention), one JSON line per case")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank)
+        return
+    if args.sweep:
+        run_sweep(args)
         return
     if args.model == "1t":
         if args.layers == 32:
