@@ -133,6 +133,39 @@ SFK_API sfk_status sfk_weights_synth(sfk_engine *eng, uint64_t seed);
 /* Bytes of a tensor in GGUF layout (0 for an unknown tensor). */
 SFK_API size_t sfk_tensor_bytes(const sfk_engine *eng, int tensor, int layer);
 
+/* ---- .strata files (src/tws/strata_format.h:77-177): the reader and the
+ *      HBM loader.  Host-only except sfk_strata_load. ---------------------- */
+typedef struct sfk_strata sfk_strata;
+/* StrataReader::open (src/tws/strata_file.cpp:30-230): superblock v1/v2/v3
+ * (header CRC32 checked), embedded GGUF metadata, expert index, optional trunk
+ * index (checked against the GGUF-order trunk walk).  Files whose expert blobs
+ * are LZ-compressed (v3 flag bit 3) are rejected with SFK_ERR_UNSUPPORTED. */
+SFK_API sfk_status sfk_strata_open(const char *path, sfk_strata **out);
+SFK_API void sfk_strata_close(sfk_strata *s);
+/* The model-shape fields of *hp from the GGUF keys and tensor shapes, as
+ * Engine::load reads them (src/model/engine/engine.cpp:1078-1087,1131-1137);
+ * kv_type, max_batch, ep_size, ep_rank are left as the caller set them, and
+ * n_ctx too unless it is <= 0 (then llama.context_length). */
+SFK_API sfk_status sfk_strata_hparams(const sfk_strata *s, sfk_hparams *hp);
+/* The GGUF tensor table: name, ggml type, ne, ggml_nbytes, and whether the
+ * tensor lives in the expert bundles rather than the trunk block. */
+SFK_API int64_t sfk_strata_n_tensors(const sfk_strata *s);
+SFK_API sfk_status sfk_strata_tensor_info(const sfk_strata *s, int64_t i, char *name, size_t name_cap, int32_t *type,
+                                          int64_t ne[4], uint64_t *n_bytes, int32_t *is_expert);
+/* One trunk tensor's verbatim bytes (StrataReader::read_at over the trunk
+ * block, engine.cpp:786-830: trunk tensors packed in GGUF order). */
+SFK_API sfk_status sfk_strata_read_trunk(const sfk_strata *s, const char *name, void *host_out, size_t n_bytes);
+/* StrataReader::read_bundle (src/tws/strata_file.cpp:368-444): the bundle
+ * gate|up|down of (layer, expert), each slice read at its *_rel offset. */
+SFK_API size_t sfk_strata_bundle_bytes(const sfk_strata *s, int32_t layer);
+SFK_API sfk_status sfk_strata_read_bundle(const sfk_strata *s, int32_t layer, int32_t expert, void *host_out,
+                                          size_t n_bytes);
+/* Engine::load_strata_weights (engine.cpp:556-830) for the HBM tier: every
+ * trunk tensor through sfk_weights_put, every bundle through sfk_expert_put
+ * (an expert-parallel engine keeps its own experts).  The engine must have
+ * been created with sfk_strata_hparams' shape. */
+SFK_API sfk_status sfk_strata_load(const sfk_strata *s, sfk_engine *eng);
+
 /* ---- decode: replaces Engine::forward / reset_kv (engine.h:241,245) ----- */
 /* Clear every sequence's KV so the next step starts at position 0. */
 SFK_API sfk_status sfk_kv_reset(sfk_engine *eng);

@@ -25,7 +25,7 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
           "-I", CSRC, "-I", os.path.join(ROOT, "include")] + ARCH
 # per-file extra flags: the synthetic generator must round exactly as written
 EXTRA = {"sfk_synth.cu": ["-fmad=false"]}
-SOURCES = ["sfk_kernels.cu", "sfk_synth.cu", "sfk_api.cu", "sfk_noalloc.cu"]
+SOURCES = ["sfk_kernels.cu", "sfk_synth.cu", "sfk_api.cu", "sfk_noalloc.cu", "sfk_strata.cpp"]
 HEADERS = ["sfk_device.cuh", "sfk_act.cuh", "sfk_dequant.cuh", "sfk_kernels.cuh", "sfk_route.cuh"]
 
 
@@ -50,7 +50,7 @@ def build(verbose: bool = False, ptxas_info: bool = False, force: bool = False) 
     objs = []
     for src in SOURCES:
         sp = os.path.join(CSRC, src)
-        obj = os.path.join(OBJ_DIR, src.replace(".cu", ".o"))
+        obj = os.path.join(OBJ_DIR, os.path.splitext(src)[0] + ".o")
         objs.append(obj)
         if force or ptxas_info or _stale(obj, [sp] + hdrs + [__file__]):
             cmd = [nvcc()] + COMMON + EXTRA.get(src, []) + (["-Xptxas", "-v"] if ptxas_info else []) + \

@@ -121,6 +121,28 @@ class Engine:
                 eng.put(tid, layer, qtype, ne, data)
         return eng
 
+    @classmethod
+    def load_strata(cls, path: str, n_ctx: int = 0, max_batch: int = 1, kv_type: int = L.KV_F16,
+                    ep_size: int = 1, ep_rank: int = 0, device: int = 0) -> "Engine":
+        """Engine::load of a .strata file (engine.cpp:983-1137 with
+        load_strata_weights): the model shape from the file's GGUF metadata,
+        every trunk tensor and expert bundle uploaded to the HBM tier.  n_ctx
+        <= 0 takes the file's llama.context_length."""
+        from .strata import StrataFile
+        with StrataFile(path) as f:
+            base = L.Hparams()
+            base.n_ctx, base.max_batch, base.kv_type, base.ep_size, base.ep_rank = n_ctx, max_batch, kv_type, \
+                ep_size, ep_rank
+            hp = f.hparams(base)
+            cfg = ModelConfig(**{n: getattr(hp, n) for n, _ in L.Hparams._fields_})
+            eng = cls(cfg, device)
+            try:
+                f.load_into(eng)
+            except Exception:
+                eng.close()
+                raise
+        return eng
+
     def close(self):
         if getattr(self, "h", None):
             self._lib.sfk_engine_free(self.h)

@@ -14,6 +14,7 @@ LIB_PATH = os.path.join(HERE, "_lib", "libsfk.so")
 HEADER = os.path.join(os.path.dirname(HERE), "include", "sfk.h")
 
 SFK_OK = 0
+SFK_ERR_INVALID_ARGUMENT, SFK_ERR_UNSUPPORTED, SFK_ERR_OUT_OF_MEMORY, SFK_ERR_RUNTIME = 1, 3, 4, 7
 TYPE_F32, TYPE_F16, TYPE_Q8_0, TYPE_Q4_K, TYPE_Q6_K, TYPE_Q8_K = 0, 1, 8, 12, 14, 15
 KV_F32, KV_F16 = 0, 1
 (T_TOK_EMBD, T_OUTPUT_NORM, T_OUTPUT, T_ATTN_NORM, T_ATTN_Q, T_ATTN_K, T_ATTN_V, T_ATTN_OUT,
@@ -77,6 +78,15 @@ _SIGS = {
     "sfk_attn_decode_paged": (I32, [P, P, P, I32, I32, P, I32, P, I32, I32, I32, I32, P, P]),
     "sfk_ep_handle": (I32, [P, P, SZ]),
     "sfk_ep_connect": (I32, [P, P, I32]),
+    "sfk_strata_open": (I32, [C.c_char_p, C.POINTER(P)]),
+    "sfk_strata_close": (None, [P]),
+    "sfk_strata_hparams": (I32, [P, C.POINTER(Hparams)]),
+    "sfk_strata_n_tensors": (I64, [P]),
+    "sfk_strata_tensor_info": (I32, [P, I64, C.c_char_p, SZ, C.POINTER(I32), P, C.POINTER(U64), C.POINTER(I32)]),
+    "sfk_strata_read_trunk": (I32, [P, C.c_char_p, P, SZ]),
+    "sfk_strata_bundle_bytes": (SZ, [P, I32]),
+    "sfk_strata_read_bundle": (I32, [P, I32, I32, P, SZ]),
+    "sfk_strata_load": (I32, [P, P]),
 }
 
 _lib = None
