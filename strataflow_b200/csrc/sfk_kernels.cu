@@ -1119,6 +1119,7 @@ constexpr int ATT_THREADS = ATT_NW * 32;
 constexpr int ATT_MAXG = 16;       // max query heads per kv head
 constexpr int ATT_MAXC = 16;       // max CTAs per cluster
 constexpr int ATT_RING = 64 * 1024;  // bytes of K + V page slots
+constexpr int ATT_PG = 4;            // pages between block barriers (slots refilled per group)
 
 struct AttnPlan {
   int ns, slot_bytes;
@@ -1260,65 +1261,71 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
     constexpr int LP = HD / 8;
     constexpr int PPW = 32 / LP;
     const int sub = lane / LP, dl = (lane % LP) * 8;
-    for (int i = 0; i < np; ++i) {
-      const int slot = i % pl.ns;
-      mbar_wait_bounded(&kfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
-      const uint8_t* kp = kring + (int64_t)slot * pl.slot_bytes;
-      for (int base = warp * PPW; base < 16; base += ATT_NW * PPW) {
-        const int jj = base + sub;
-        const int jl = i * 16 + jj;
-        float kf[8];
-        if constexpr (F16) {
-          const uint4 raw = lds128(kp + (jj * HD + dl) * 2);
-          const __half2* hv = reinterpret_cast<const __half2*>(&raw);
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float2 f = __half22float2(hv[e]);
-            kf[2 * e] = f.x;
-            kf[2 * e + 1] = f.y;
-          }
-        } else {
-          const uint4 r0 = lds128(kp + (jj * HD + dl) * 4);
-          const uint4 r1 = lds128(kp + (jj * HD + dl) * 4 + 16);
-          kf[0] = __uint_as_float(r0.x); kf[1] = __uint_as_float(r0.y);
-          kf[2] = __uint_as_float(r0.z); kf[3] = __uint_as_float(r0.w);
-          kf[4] = __uint_as_float(r1.x); kf[5] = __uint_as_float(r1.y);
-          kf[6] = __uint_as_float(r1.z); kf[7] = __uint_as_float(r1.w);
-        }
-        // four heads at a time, two accumulation chains each (the double
-        // sums are order-free at this length), so the chains overlap
-        for (int h0 = 0; h0 < gqa; h0 += 4) {
-          double r[4];
-#pragma unroll
-          for (int hh = 0; hh < 4; ++hh) {
-            r[hh] = 0.0;
-            if (h0 + hh < gqa) {
-              const float4 qa = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl);
-              const float4 qb = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl + 4);
-              double a0 = (double)__fmul_rn(kf[0], qa.x), a1 = (double)__fmul_rn(kf[1], qa.y);
-              a0 += (double)__fmul_rn(kf[2], qa.z);
-              a1 += (double)__fmul_rn(kf[3], qa.w);
-              a0 += (double)__fmul_rn(kf[4], qb.x);
-              a1 += (double)__fmul_rn(kf[5], qb.y);
-              a0 += (double)__fmul_rn(kf[6], qb.z);
-              a1 += (double)__fmul_rn(kf[7], qb.w);
-              r[hh] = a0 + a1;
+    const int pg = max(1, min(ATT_PG, pl.ns / 2));  // half the ring: the next group's copies are in flight
+    for (int i0 = 0; i0 < np; i0 += pg) {
+      const int ig = min(pg, np - i0);
+      for (int i = i0; i < i0 + ig; ++i) {
+        const int slot = i % pl.ns;
+        mbar_wait_bounded(&kfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
+        const uint8_t* kp = kring + (int64_t)slot * pl.slot_bytes;
+        for (int base = warp * PPW; base < 16; base += ATT_NW * PPW) {
+          const int jj = base + sub;
+          const int jl = i * 16 + jj;
+          float kf[8];
+          if constexpr (F16) {
+            const uint4 raw = lds128(kp + (jj * HD + dl) * 2);
+            const __half2* hv = reinterpret_cast<const __half2*>(&raw);
+  #pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float2 f = __half22float2(hv[e]);
+              kf[2 * e] = f.x;
+              kf[2 * e + 1] = f.y;
             }
+          } else {
+            const uint4 r0 = lds128(kp + (jj * HD + dl) * 4);
+            const uint4 r1 = lds128(kp + (jj * HD + dl) * 4 + 16);
+            kf[0] = __uint_as_float(r0.x); kf[1] = __uint_as_float(r0.y);
+            kf[2] = __uint_as_float(r0.z); kf[3] = __uint_as_float(r0.w);
+            kf[4] = __uint_as_float(r1.x); kf[5] = __uint_as_float(r1.y);
+            kf[6] = __uint_as_float(r1.z); kf[7] = __uint_as_float(r1.w);
           }
-#pragma unroll
-          for (int o = LP / 2; o > 0; o >>= 1)
-#pragma unroll
-            for (int hh = 0; hh < 4; ++hh) r[hh] += __shfl_xor_sync(0xffffffffu, r[hh], o);
-          if ((lane % LP) == 0 && jl < nloc) {
-#pragma unroll
-            for (int hh = 0; hh < 4; ++hh)
-              if (h0 + hh < gqa) sc[(h0 + hh) * mc + jl] = __fmul_rn((float)r[hh], scale);
+          // four heads at a time, two accumulation chains each (the double
+          // sums are order-free at this length), so the chains overlap
+          for (int h0 = 0; h0 < gqa; h0 += 4) {
+            double r[4];
+  #pragma unroll
+            for (int hh = 0; hh < 4; ++hh) {
+              r[hh] = 0.0;
+              if (h0 + hh < gqa) {
+                const float4 qa = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl);
+                const float4 qb = *reinterpret_cast<const float4*>(qs + (h0 + hh) * HD + dl + 4);
+                double a0 = (double)__fmul_rn(kf[0], qa.x), a1 = (double)__fmul_rn(kf[1], qa.y);
+                a0 += (double)__fmul_rn(kf[2], qa.z);
+                a1 += (double)__fmul_rn(kf[3], qa.w);
+                a0 += (double)__fmul_rn(kf[4], qb.x);
+                a1 += (double)__fmul_rn(kf[5], qb.y);
+                a0 += (double)__fmul_rn(kf[6], qb.z);
+                a1 += (double)__fmul_rn(kf[7], qb.w);
+                r[hh] = a0 + a1;
+              }
+            }
+  #pragma unroll
+            for (int o = LP / 2; o > 0; o >>= 1)
+  #pragma unroll
+              for (int hh = 0; hh < 4; ++hh) r[hh] += __shfl_xor_sync(0xffffffffu, r[hh], o);
+            if ((lane % LP) == 0 && jl < nloc) {
+  #pragma unroll
+              for (int hh = 0; hh < 4; ++hh)
+                if (h0 + hh < gqa) sc[(h0 + hh) * mc + jl] = __fmul_rn((float)r[hh], scale);
+            }
           }
         }
       }
-      if (i + pl.ns < np) {  // the slot is refilled: every warp must be done with it
+      if (i0 + pl.ns < np) {  // the group's slots are refilled: every warp must be done with them
         __syncthreads();
-        if (lane == 0 && warp == i % ATT_NW) issue(0, i + pl.ns);
+        if (lane == 0)
+          for (int i = i0 + warp; i < i0 + ig; i += ATT_NW)
+            if (i + pl.ns < np) issue(0, i + pl.ns);
       }
     }
   }
@@ -1376,39 +1383,45 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
   double acc[2 * NPAIR][2];  // two chains per output dim (order-free double sums)
 #pragma unroll
   for (int i = 0; i < 2 * NPAIR; ++i) acc[i][0] = acc[i][1] = 0.0;
-  for (int i = 0; i < np; ++i) {
-    const int slot = i % pl.ns;
-    mbar_wait_bounded(&vfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
-    const uint8_t* vp = vring + (int64_t)slot * pl.slot_bytes;
-    const int jn = min(16, nloc - i * 16);
-#pragma unroll
-    for (int q2 = 0; q2 < NPAIR; ++q2) {
-      const int pi = tid + q2 * ATT_THREADS;
-      if (pi < npairs) {
-        const int h = (pi * 2) / HD, dd = (pi * 2) % HD;
-        const float inv = invs[h];
-        const float* sh = sc + h * mc + i * 16;
-        auto step = [&](int jj, int c) {
-          const float pj = __fmul_rn(sh[jj], inv);
-          float2 v;
-          if constexpr (F16)
-            v = __half22float2(*reinterpret_cast<const __half2*>(vp + (jj * HD + dd) * 2));
-          else
-            v = *reinterpret_cast<const float2*>(vp + (jj * HD + dd) * 4);
-          acc[2 * q2][c] += (double)__fmul_rn(v.x, pj);
-          acc[2 * q2 + 1][c] += (double)__fmul_rn(v.y, pj);
-        };
-        if (jn == 16) {
-#pragma unroll
-          for (int jj = 0; jj < 16; ++jj) step(jj, jj & 1);
-        } else {
-          for (int jj = 0; jj < jn; ++jj) step(jj, jj & 1);
+  const int pgv = max(1, min(ATT_PG, pl.ns / 2));
+  for (int i0 = 0; i0 < np; i0 += pgv) {
+    const int ig = min(pgv, np - i0);
+    for (int i = i0; i < i0 + ig; ++i) {
+      const int slot = i % pl.ns;
+      mbar_wait_bounded(&vfull[slot], (uint32_t)((i / pl.ns) & 1), p.status);
+      const uint8_t* vp = vring + (int64_t)slot * pl.slot_bytes;
+      const int jn = min(16, nloc - i * 16);
+  #pragma unroll
+      for (int q2 = 0; q2 < NPAIR; ++q2) {
+        const int pi = tid + q2 * ATT_THREADS;
+        if (pi < npairs) {
+          const int h = (pi * 2) / HD, dd = (pi * 2) % HD;
+          const float inv = invs[h];
+          const float* sh = sc + h * mc + i * 16;
+          auto step = [&](int jj, int c) {
+            const float pj = __fmul_rn(sh[jj], inv);
+            float2 v;
+            if constexpr (F16)
+              v = __half22float2(*reinterpret_cast<const __half2*>(vp + (jj * HD + dd) * 2));
+            else
+              v = *reinterpret_cast<const float2*>(vp + (jj * HD + dd) * 4);
+            acc[2 * q2][c] += (double)__fmul_rn(v.x, pj);
+            acc[2 * q2 + 1][c] += (double)__fmul_rn(v.y, pj);
+          };
+          if (jn == 16) {
+  #pragma unroll
+            for (int jj = 0; jj < 16; ++jj) step(jj, jj & 1);
+          } else {
+            for (int jj = 0; jj < jn; ++jj) step(jj, jj & 1);
+          }
         }
       }
     }
-    if (i + pl.ns < np) {  // the slot is refilled: every thread must be done with it
+    if (i0 + pl.ns < np) {  // the group's slots are refilled: every thread must be done with them
       __syncthreads();
-      if (lane == 0 && warp == i % ATT_NW) issue(1, i + pl.ns);
+      if (lane == 0)
+        for (int i = i0 + warp; i < i0 + ig; i += ATT_NW)
+          if (i + pl.ns < np) issue(1, i + pl.ns);
     }
   }
   // ---- partial outputs: output o belongs to CTA o / per, which adds the C
