@@ -28,7 +28,6 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
-#include <type_traits>
 
 #include "sfk_act.cuh"
 #include "sfk_device.cuh"
@@ -1018,48 +1017,31 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
       float part[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) part[j] = 0.0f;
-      // the tile's unit dots for this pair; value j = rm * G + g lands in
-      // part[j].  Common shapes run a compile-time block: groups outer, so
-      // each activation group is loaded once per pair, and all dots of a
-      // group in one basic block, so their dp4a chains interleave.
-      auto dots = [&](auto gc, auto rc) {
-        constexpr int GG = decltype(gc)::value, RR = decltype(rc)::value;
-#pragma unroll
-        for (int g = 0; g < GG; ++g) {
-          const int ng = group_units(p.K, g);
-          if (vi * GG + g != cached) {
-            if (lane < ng) {
-              const uint8_t* xg = xbase + (int64_t)vi * xstride + qact_group_offset(g);
-              if (pl.xq_smem)
-                xc.load(xg, ng, lane);
-              else
-                xc.load_any(xg, ng, lane);
-            }
-            cached = vi * GG + g;
-          }
+      if (G == 1 && RM == 4) {
+        // the common tile (4 row-matrices of one 32-unit group): four
+        // independent unit dots in one basic block, so their dp4a chains
+        // interleave
+        const int ng = group_units(p.K, 0);
+        if (vi != cached) {
           if (lane < ng) {
+            const uint8_t* xg = xbase + (int64_t)vi * xstride;
+            if (pl.xq_smem)
+              xc.load(xg, ng, lane);
+            else
+              xc.load_any(xg, ng, lane);
+          }
+          cached = vi;
+        }
+        if (lane < ng) {
 #pragma unroll
-            for (int q = 0; q < RR; ++q)
-              if (q < RM) {
-                const int r = NMAT == 2 ? (q >> 1) : q, m = NMAT == 2 ? (q & 1) : 0;
-                part[q * GG + g] =
-                    unit_dot_x<WT>(tile + ((int64_t)m * R + r) * rs + group_offset(WT, p.K, g), xc, ng, lane);
-              }
+          for (int q = 0; q < 4; ++q) {
+            const int r = NMAT == 2 ? (q >> 1) : q, m = NMAT == 2 ? (q & 1) : 0;
+            part[q] = unit_dot_x<WT>(tile + ((int64_t)m * R + r) * rs, xc, ng, lane);
           }
         }
-      };
-      // (the multi-group blocks serve single-matrix kernels -- the down
-      // projection's 14336 columns, the 1T trunk's 7168 / 8192 -- and stay out
-      // of the two-matrix gate/up kernel, whose registers they would crowd)
-      if (G == 1 && RM <= 4) {
-        dots(std::integral_constant<int, 1>{}, std::integral_constant<int, 4>{});
-      } else if (NMAT == 1 && G == 2 && RM <= 4) {
-        if constexpr (NMAT == 1) dots(std::integral_constant<int, 2>{}, std::integral_constant<int, 4>{});
-      } else if (NMAT == 1 && G == 4 && RM <= 2) {
-        if constexpr (NMAT == 1) dots(std::integral_constant<int, 4>{}, std::integral_constant<int, 2>{});
       } else {
-      // other shapes: one unit dot in the loop body (a small hot loop stays in
-      // the instruction cache)
+      // one unit dot in the loop body (a small hot loop stays in the
+      // instruction cache); value j = rm * G + g lands in part[j]
       int j = 0;
 #pragma unroll 1
       for (int rm = 0; rm < RM; ++rm) {
