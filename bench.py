@@ -13,7 +13,8 @@ than the 126 MB L2, so no flush is needed between steps.
 value : decode tok/s with everything resident in HBM, CUDA events on the
         engine's stream around K device-side greedy steps (max over ranks).
 e2e   : the same metric through the C-ABI call a host uses (sfk_forward with
-        a host token in and host logits + argmax out every step, synchronized).
+        a host token in and host logits + argmax out every step, synchronized;
+        W untimed warm-up steps, then up to 128 timed ones).
 roofline : the dominant kernel (routed gate/up over the Q4_K experts), its
         algorithmic bytes per launch over its CUDA-event launch duration.
 cpu_baseline : the CPU oracle (a C restatement of the reference's ggml CPU
@@ -175,8 +176,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 
     B = args.batch
     PROMPT = args.prompt
-    e2e_steps = 0 if args.no_e2e else min(args.steps, 32)
-    n_ctx = PROMPT + args.warmup + args.steps + e2e_steps + 16
+    e2e_steps = 0 if args.no_e2e else min(args.steps, 128)
+    e2e_warm = 0 if args.no_e2e else args.warmup
+    n_ctx = PROMPT + args.warmup + args.steps + e2e_warm + e2e_steps + 16
     cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B, n_layer=args.layers)
     t_load = time.perf_counter()
     eng = E.Engine.load(cfg, seed=SEED, device=local_rank)
@@ -214,6 +216,9 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     # --- end to end through the C ABI with host buffers ----------------------
     pos0 = PROMPT + args.warmup + args.steps
     tok = prompt[:, 0].copy()
+    for i in range(e2e_warm):   # untimed warm-up of the host-buffer path
+        tok, _ = eng.forward_batch(tok, np.full(B, pos0 + i, np.int32), want_logits=True)
+    pos0 += e2e_warm
     torch.cuda.synchronize()
     if dist:
         dist.barrier()

@@ -171,10 +171,9 @@ sfk_status op_scratch(size_t need, size_t n_counters, OpScratch** out) {
   return SFK_OK;
 }
 
-sfk_status check_status_word(int* dev_status, cudaStream_t st) {
-  int h = 0;
-  CK(cudaMemcpyAsync(&h, dev_status, sizeof(int), cudaMemcpyDeviceToHost, st));
-  CK(cudaStreamSynchronize(st));
+// The host's answer to a status word already read back as h: OK, or the
+// error it records (the device word is cleared for the next call).
+sfk_status status_result(int* dev_status, int h) {
   if (h != ERR_NONE) {
     int z = 0;
     cudaMemcpy(dev_status, &z, sizeof(int), cudaMemcpyHostToDevice);
@@ -185,6 +184,13 @@ sfk_status check_status_word(int* dev_status, cudaStream_t st) {
                                     : "bad position");
   }
   return SFK_OK;
+}
+
+sfk_status check_status_word(int* dev_status, cudaStream_t st) {
+  int h = 0;
+  CK(cudaMemcpyAsync(&h, dev_status, sizeof(int), cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  return status_result(dev_status, h);
 }
 
 }  // namespace
@@ -230,9 +236,9 @@ struct sfk_engine {
   uint8_t *xq_ffn = nullptr, *hq = nullptr;
   Route* route = nullptr;
   int *router_counter = nullptr, *grp_counter = nullptr;
-  unsigned long long* argmax_key = nullptr;
+  unsigned long long* argmax_key = nullptr;  // [B] keys, then the status word: one read-back
   int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
-  int* status = nullptr;
+  int* status = nullptr;  // right after argmax_key[B]
   bool fused_route = false;  // the gate/up kernel routes in its prologue (no router kernel)
   // expert parallelism: this rank holds experts [e0, e0 + e_loc)
   int ep_size = 1, ep_rank = 0, e_loc = 0, e0 = 0;
@@ -249,11 +255,15 @@ struct sfk_engine {
   bool ep_connected = false;
   int attn_cluster = 8;
   int attn_max_chunk = 0;
-  // pinned staging
+  // pinned staging: tokens and positions side by side (tok_in / pos_in are
+  // side by side on the device too: one upload), keys then status (one
+  // read-back), the logits of a host-buffer step
   int* h_tok = nullptr;
-  int* h_pos = nullptr;
+  int* h_pos = nullptr;  // h_tok + B
   int* h_hist = nullptr;
   unsigned long long* h_keys = nullptr;
+  int* h_status = nullptr;  // right after h_keys[B]
+  float* h_logits = nullptr;
   // graphs: key = b * 2 + greedy
   std::map<int, cudaGraphExec_t> graphs;
   uint64_t steps = 0;
@@ -750,9 +760,9 @@ void sfk_engine_free(sfk_engine* e) {
   for (void* p : e->ep_opened) cudaIpcCloseMemHandle(p);
   for (void* p : e->allocs) cudaFree(p);
   if (e->h_tok) cudaFreeHost(e->h_tok);
-  if (e->h_pos) cudaFreeHost(e->h_pos);
   if (e->h_hist) cudaFreeHost(e->h_hist);
   if (e->h_keys) cudaFreeHost(e->h_keys);
+  if (e->h_logits) cudaFreeHost(e->h_logits);
   if (e->stream) cudaStreamDestroy(e->stream);
   delete e;
 }
@@ -892,13 +902,13 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   TRY(e->alloc(&e->route, sizeof(Route), sb));
   TRY(e->alloc(&e->router_counter, 2 * sizeof(int), sb));
   TRY(e->alloc(&e->grp_counter, sizeof(int) * (F / 256), sb));
-  TRY(e->alloc(&e->argmax_key, sizeof(unsigned long long) * B, sb));
-  TRY(e->alloc(&e->tok_in, sizeof(int) * B, sb));
-  TRY(e->alloc(&e->pos_in, sizeof(int) * B, sb));
+  TRY(e->alloc(&e->argmax_key, sizeof(unsigned long long) * B + 16, sb));
+  e->status = reinterpret_cast<int*>(e->argmax_key + B);
+  TRY(e->alloc(&e->tok_in, sizeof(int) * 2 * B, sb));
+  e->pos_in = e->tok_in + B;
   TRY(e->alloc(&e->pos_state, sizeof(int) * B, sb));
   TRY(e->alloc(&e->pos_cur, sizeof(int) * B, sb));
   TRY(e->alloc(&e->tok_hist, sizeof(int) * B, sb));
-  TRY(e->alloc(&e->status, sizeof(int), sb));
   if (e->ep_size > 1) {
     // exchange buffer: [layer parity][stage][B][d] partial outputs, then MAXR
     // flag words; its own allocation so that its IPC handle exposes nothing else
@@ -922,10 +932,12 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     if (ce == cudaSuccess) ce = cudaMemset(e->status, 0, sizeof(int));
     if (ce == cudaSuccess) ce = cudaMemset(e->k_pool, 0, kv_elem * e->kv_layer_elems * hp->n_layer);
     if (ce == cudaSuccess) ce = cudaMemset(e->v_pool, 0, kv_elem * e->kv_layer_elems * hp->n_layer);
-    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_tok, sizeof(int) * B);
-    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_pos, sizeof(int) * B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_tok, sizeof(int) * 2 * B);
+    if (ce == cudaSuccess) e->h_pos = e->h_tok + B;
     if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_hist, sizeof(int) * B);
-    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_keys, sizeof(unsigned long long) * B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_keys, sizeof(unsigned long long) * B + 16);
+    if (ce == cudaSuccess) e->h_status = reinterpret_cast<int*>(e->h_keys + B);
+    if (ce == cudaSuccess) ce = cudaMallocHost(&e->h_logits, sizeof(float) * B * hp->n_vocab);
     if (ce != cudaSuccess) {
       sfk_engine_free(e);
       return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
@@ -1131,18 +1143,26 @@ sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens
       return fail(SFK_ERR_INVALID_ARGUMENT, "token %d outside the vocabulary", tokens[t]);
   }
   CK(cudaSetDevice(e->device));
+  // one upload of tokens | positions, the step, then the logits and keys |
+  // status word into pinned memory and a single synchronisation
+  const int B = e->hp.max_batch;
   memcpy(e->h_tok, tokens, sizeof(int) * n_seq);
   memcpy(e->h_pos, positions, sizeof(int) * n_seq);
-  CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * n_seq, cudaMemcpyHostToDevice, e->stream));
-  CK(cudaMemcpyAsync(e->pos_in, e->h_pos, sizeof(int) * n_seq, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * 2 * B, cudaMemcpyHostToDevice, e->stream));
   sfk_status s = run_step(e, n_seq, false);
   if (s) return s;
+  const size_t n_logits = (size_t)n_seq * e->hp.n_vocab;
   if (logits_host)
-    CK(cudaMemcpyAsync(logits_host, e->logits, sizeof(float) * n_seq * e->hp.n_vocab, cudaMemcpyDeviceToHost,
-                       e->stream));
-  CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * n_seq, cudaMemcpyDeviceToHost, e->stream));
-  s = engine_check(e);
-  if (s) return s;
+    CK(cudaMemcpyAsync(e->h_logits, e->logits, sizeof(float) * n_logits, cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * B + sizeof(int), cudaMemcpyDeviceToHost,
+                     e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  if ((s = status_result(e->status, *e->h_status))) {
+    cudaMemset(e->router_counter, 0, 2 * sizeof(int));
+    cudaMemset(e->grp_counter, 0, sizeof(int) * (e->hp.n_ff / 256));
+    return s;
+  }
+  if (logits_host) memcpy(logits_host, e->h_logits, sizeof(float) * n_logits);
   for (int t = 0; t < n_seq; ++t) {
     e->seq_pos[t] = positions[t] + 1;
     if (argmax_out) argmax_out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(e->h_keys[t] & 0xFFFFFFFFull));
