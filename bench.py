@@ -301,8 +301,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of
 # the routed gate/up kernel at this shape, from an `ncu --set full` capture of
 # the same kernel (2-layer model, identical launch shape): 132.40 MB read +
-# 3.17 MB written.
-GU_TRAFFIC_BYTES = 135.57e6
+# 4.69 MB written.
+GU_TRAFFIC_BYTES = 137.09e6
 
 
 def run_ep(args, rank: int, world: int, local_rank: int):
