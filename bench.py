@@ -305,6 +305,26 @@ def run_ours(args, rank: int, world: int, local_rank: int):
 GU_TRAFFIC_BYTES = 137.09e6
 
 
+def ep_rank_bytes(cfg, world: int, B: int) -> tuple[float, bool]:
+    """Bytes one rank streams per step of the expert-parallel decode (Q8_0
+    trunk, Q4_K experts, head width 128) and whether the attention heads are
+    split over the ranks.  The heads split, as the engine decides at
+    creation, when both head counts divide by the ranks and a rank's query
+    columns are whole 256-column blocks (SFK_HEAD_PARALLEL=0 keeps them
+    replicated); the router (F32), the norms and the lm_head stay replicated,
+    and each rank streams its share of the expected routed experts."""
+    d, F, k, hd = cfg.n_embd, cfg.n_ff, cfg.n_expert_used, 128
+    q8 = lambda K: K // 32 * 34   # noqa: E731
+    q4 = lambda K: K // 256 * 144   # noqa: E731
+    split = (world > 1 and cfg.n_head % world == 0 and cfg.n_head_kv % world == 0 and
+             (cfg.n_head // world * hd) % 256 == 0 and os.environ.get("SFK_HEAD_PARALLEL", "1") != "0")
+    share = world if split else 1
+    attn = ((cfg.n_head + 2 * cfg.n_head_kv) * hd * q8(d) + d * q8(cfg.n_head * hd)) / share
+    trunk = cfg.n_layer * (attn + 4 * d * cfg.n_expert) + cfg.n_vocab * q8(d)
+    experts_rank = cfg.n_layer * B * k / world * (2 * F * q4(d) + d * q4(F))   # expected routed bytes per rank
+    return trunk + experts_rank, split
+
+
 def run_ep(args, rank: int, world: int, local_rank: int):
     """the ~1T-parameter MoE, experts sharded over the torchrun
     ranks (expert parallelism), trunk replicated; one sequence decoded by the
@@ -380,13 +400,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     value = B * args.steps / (ms / 1000.0)
     st = eng.stats()
     peak, peak_kind = _peaks()
-    d, F, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
-    q8 = lambda K: K // 32 * 34   # noqa: E731
-    q4 = lambda K: K // 256 * 144   # noqa: E731
-    trunk = cfg.n_layer * ((cfg.n_head + 2 * cfg.n_head_kv) * 128 * q8(d) + d * q8(cfg.n_head * 128) + 4 * d * cfg.n_expert)
-    trunk += cfg.n_vocab * q8(d)
-    experts_rank = cfg.n_layer * B * k / world * (2 * F * q4(d) + d * q4(F))   # expected routed bytes per rank
-    rank_bytes = trunk + experts_rank
+    rank_bytes, heads_split = ep_rank_bytes(cfg, world, B)
     if rank == 0:
         line = {
             "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -395,7 +409,9 @@ def run_ep(args, rank: int, world: int, local_rank: int):
             "data": "synthetic",
             "config": {"workload": f"~1T-param MoE decode b={B}: {prompt_n}-token random prompt, then greedy decode",
                        "model": "61L d7168 64q/8kv E384 top8 F2048 V160000", "global_batch": B,
-                       "seq_len": prompt_n, "parallelism": f"ep{world} (experts sharded, trunk replicated)"},
+                       "seq_len": prompt_n,
+                       "parallelism": f"ep{world} (experts sharded, "
+                                      f"{'attention heads split' if heads_split else 'trunk replicated'})"},
             "clocks": clk.summary(), "ranks_agree": bool(same),
             "gpu_launches": st["kernels_per_step"] * args.steps,
             "step_roofline": {"achieved": rank_bytes * args.steps / (ms / 1000.0) / 1e9, "peak": peak,
