@@ -20,6 +20,7 @@
 #include <fcntl.h>
 #include <unistd.h>
 
+#include <array>
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
@@ -56,16 +57,15 @@ constexpr uint64_t TRUNK_ENTRY = 80;  // TrunkIndexEntry (64-byte name + 2 x u64
 // CRC-32 (IEEE 802.3, reflected polynomial 0xEDB88320), as the header CRC
 // of strata_format.h specifies it; table-driven.
 uint32_t crc32_ieee(const uint8_t* p, size_t n) {
-  static uint32_t table[256];
-  static bool init = false;
-  if (!init) {
+  static const std::array<uint32_t, 256> table = [] {  // built once, thread-safe
+    std::array<uint32_t, 256> t{};
     for (uint32_t i = 0; i < 256; ++i) {
       uint32_t c = i;
       for (int k = 0; k < 8; ++k) c = (c & 1u) ? 0xEDB88320u ^ (c >> 1) : c >> 1;
-      table[i] = c;
+      t[i] = c;
     }
-    init = true;
-  }
+    return t;
+  }();
   uint32_t c = 0xFFFFFFFFu;
   for (size_t i = 0; i < n; ++i) c = table[(c ^ p[i]) & 0xFFu] ^ (c >> 8);
   return c ^ 0xFFFFFFFFu;
@@ -206,7 +206,10 @@ int parse_layer(const std::string& name, std::string* suffix) {
   size_t i = 4;
   int l = 0;
   if (i >= name.size() || name[i] < '0' || name[i] > '9') return -1;
-  while (i < name.size() && name[i] >= '0' && name[i] <= '9') l = l * 10 + (name[i++] - '0');
+  while (i < name.size() && name[i] >= '0' && name[i] <= '9') {
+    if (i >= 4 + 6) return -1;  // a layer index of at most six digits
+    l = l * 10 + (name[i++] - '0');
+  }
   if (i >= name.size() || name[i] != '.') return -1;
   *suffix = name.substr(i + 1);
   return l;
@@ -281,8 +284,7 @@ struct sfk_strata {
     if (it == kv.end()) return fallback;
     const uint32_t t = it->second.type;
     if (t == G_F32 || t == G_F64 || t == G_STR || t == G_ARR) return fallback;
-    if (t == G_I8 || t == G_I16 || t == G_I32 || t == G_I64) return (int64_t)it->second.u;
-    return (int64_t)it->second.u;
+    return (int64_t)it->second.u;  // signed types were stored sign-extended
   }
   double key_float(const std::string& k, double fallback) const {
     auto it = kv.find(k);
@@ -384,8 +386,11 @@ sfk_status parse_gguf(sfk_strata* s) {
     if (!type_block(t.type, &blk, &bb))
       return sfail(SFK_ERR_UNSUPPORTED, "%s: tensor %s has ggml type %d (F32, F16, Q8_0, Q4_K, Q6_K are read)",
                    s->path.c_str(), t.name.c_str(), t.type);
-    if (t.ne[0] <= 0 || t.ne[0] % blk || t.ne[1] <= 0 || t.ne[2] <= 0 || t.ne[3] <= 0)
-      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor %s shape", s->path.c_str(), t.name.c_str());
+    bool shape_ok = t.ne[0] > 0 && t.ne[0] % blk == 0;
+    for (int d = 0; d < 4; ++d) shape_ok = shape_ok && t.ne[d] > 0 && t.ne[d] < ((int64_t)1 << 31);
+    if (shape_ok)  // the byte count must stay far from overflow (no real tensor is near 2^50 bytes)
+      shape_ok = (double)(t.ne[0] / blk * bb) * (double)t.ne[1] * (double)t.ne[2] * (double)t.ne[3] < 0x1p50;
+    if (!shape_ok) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor %s shape", s->path.c_str(), t.name.c_str());
     t.nbytes = (uint64_t)(t.ne[0] / blk * bb) * (uint64_t)t.ne[1] * (uint64_t)t.ne[2] * (uint64_t)t.ne[3];
     t.expert = is_expert_name(t.name);
     if (!t.expert) {  // trunk tensors sit contiguously in GGUF order (engine.cpp:786-830)
