@@ -86,7 +86,11 @@ typedef struct sfk_hparams {
     /* Expert parallelism (experts sharded across the GPUs of one box).
      * ep_size ranks, one engine per GPU; rank ep_rank holds
      * experts [ep_rank * E / ep_size, (ep_rank + 1) * E / ep_size) of every
-     * layer and a full copy of everything else.  0 or 1: no sharding. */
+     * layer.  When both head counts divide by ep_size and a rank's query
+     * columns are whole 256-column blocks, the rank also holds only its share
+     * of the attention heads (their Q/K/V rows, output-projection columns and
+     * KV pages; the environment variable SFK_HEAD_PARALLEL=0 keeps them
+     * replicated); everything else is a full copy.  0 or 1: no sharding. */
     int32_t ep_size, ep_rank;
     /* Attention head width; 0 = n_embd / n_head (the reference's rule,
      * engine.cpp:1161).  Set it when n_head * head_dim != n_embd. */
@@ -161,8 +165,10 @@ SFK_API size_t sfk_strata_bundle_bytes(const sfk_strata *s, int32_t layer);
 SFK_API sfk_status sfk_strata_read_bundle(const sfk_strata *s, int32_t layer, int32_t expert, void *host_out,
                                           size_t n_bytes);
 /* Engine::load_strata_weights (engine.cpp:556-830) for the HBM tier: every
- * trunk tensor through sfk_weights_put, every bundle through sfk_expert_put
- * (an expert-parallel engine keeps its own experts).  The engine must have
+ * trunk tensor through sfk_weights_put, every bundle through sfk_expert_put.
+ * An expert-parallel engine reads only its own experts' bundles and, when its
+ * attention heads are split over the ranks, uploads its heads' rows of Q, K,
+ * V and its heads' columns of the output projection.  The engine must have
  * been created with sfk_strata_hparams' shape. */
 SFK_API sfk_status sfk_strata_load(const sfk_strata *s, sfk_engine *eng);
 

@@ -1236,6 +1236,26 @@ sfk_status sfk_hidden_get(sfk_engine* e, float* host_out, size_t n_floats) {
   return SFK_OK;
 }
 
+}  // extern "C"
+
+namespace sfk {
+// This engine's share of a sharded model (library-internal, for the .strata
+// loader): the head split (query heads [q0, q0 + hq_loc), kv heads
+// [kv0, kv0 + hkv_loc), head width hd) and the local experts [e0, e0 + e_loc).
+void engine_shard(const sfk_engine* e, EngineShard* out) {
+  out->head_split = e->head_par ? 1 : 0;
+  out->q0 = e->q0;
+  out->hq_loc = e->hq_loc;
+  out->kv0 = e->kv0;
+  out->hkv_loc = e->hkv_loc;
+  out->hd = e->hd;
+  out->e0 = e->e0;
+  out->e_loc = e->e_loc;
+}
+}  // namespace sfk
+
+extern "C" {
+
 sfk_status sfk_get_stats(const sfk_engine* e, sfk_stats* out) {
   if (!e || !out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
   const sfk_hparams& hp = e->hp;

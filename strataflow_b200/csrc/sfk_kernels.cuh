@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+struct sfk_engine;  // include/sfk.h
+
 namespace sfk {
 
 constexpr int MAXP = 128;  // max (token, expert) pairs per step  (b * k)
@@ -216,6 +218,12 @@ cudaError_t launch_route_build(const int* ids, const float* w, int b, int k, int
                                cudaStream_t st);
 // sets the message sfk_last_error() returns on the calling thread
 void set_last_error(const char* msg);
+
+// An engine's share of a sharded model (see engine_shard in sfk_api.cu).
+struct EngineShard {
+  int head_split, q0, hq_loc, kv0, hkv_loc, hd, e0, e_loc;
+};
+void engine_shard(const ::sfk_engine* e, EngineShard* out);
 cudaError_t launch_quant_act_gguf(int act_type, const float* x, int b, int K, uint8_t* dst, cudaStream_t st);
 
 }  // namespace sfk

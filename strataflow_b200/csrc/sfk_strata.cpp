@@ -581,7 +581,12 @@ SFK_API sfk_status sfk_strata_load(const sfk_strata* s, sfk_engine* eng) {
       if (!s->entry_of.count(((uint64_t)l << 32) | (uint64_t)e))
         return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: no bundle for layer %lld expert %lld", s->path.c_str(),
                      (long long)l, (long long)e);
-  std::vector<uint8_t> buf;
+  // an expert-parallel engine holds its own experts and, when the heads
+  // split, its query / kv heads' rows of Q, K, V and its heads' columns of
+  // the output projection (whole quant blocks: the split is 256-column aligned)
+  sfk::EngineShard sh{};
+  sfk::engine_shard(eng, &sh);
+  std::vector<uint8_t> buf, part;
   for (const TensorInfo& t : s->tensors) {
     if (t.expert) continue;
     int tid, layer;
@@ -591,10 +596,37 @@ SFK_API sfk_status sfk_strata_load(const sfk_strata* s, sfk_engine* eng) {
     buf.resize((size_t)t.nbytes);
     sfk_status st = sfk_strata_read_trunk(s, t.name.c_str(), buf.data(), buf.size());
     if (st) return st;
-    const int64_t ne[3] = {t.ne[0], t.ne[1], t.ne[2]};
-    if ((st = sfk_weights_put(eng, tid, layer, t.type, ne, buf.data(), buf.size()))) return st;
+    int64_t ne[3] = {t.ne[0], t.ne[1], t.ne[2]};
+    const uint8_t* src = buf.data();
+    size_t n = buf.size();
+    if (sh.head_split && (tid == SFK_T_ATTN_Q || tid == SFK_T_ATTN_K || tid == SFK_T_ATTN_V)) {
+      const int64_t h0 = tid == SFK_T_ATTN_Q ? sh.q0 : sh.kv0, hn = tid == SFK_T_ATTN_Q ? sh.hq_loc : sh.hkv_loc;
+      const uint64_t rowb = t.nbytes / (uint64_t)t.ne[1];  // one output row (head_dim rows per head)
+      if ((h0 + hn) * sh.hd > t.ne[1])
+        return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: %s has fewer heads than the engine", s->path.c_str(),
+                     t.name.c_str());
+      src = buf.data() + (uint64_t)(h0 * sh.hd) * rowb;
+      n = (size_t)((uint64_t)(hn * sh.hd) * rowb);
+      ne[1] = hn * sh.hd;
+    } else if (sh.head_split && tid == SFK_T_ATTN_OUT) {
+      int64_t blk, bb;
+      type_block(t.type, &blk, &bb);
+      const int64_t c0 = (int64_t)sh.q0 * sh.hd, cn = (int64_t)sh.hq_loc * sh.hd;
+      if (c0 % blk || cn % blk || c0 + cn > t.ne[0])
+        return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: %s columns do not split on quant blocks", s->path.c_str(),
+                     t.name.c_str());
+      const uint64_t rowb = (uint64_t)(t.ne[0] / blk * bb), off = (uint64_t)(c0 / blk * bb),
+                     len = (uint64_t)(cn / blk * bb);
+      part.resize((size_t)(len * (uint64_t)t.ne[1]));
+      for (int64_t r = 0; r < t.ne[1]; ++r) memcpy(part.data() + r * len, buf.data() + r * rowb + off, len);
+      src = part.data();
+      n = part.size();
+      ne[0] = cn;
+    }
+    if ((st = sfk_weights_put(eng, tid, layer, t.type, ne, src, n))) return st;
   }
   for (const ExpertEntry& x : s->index) {
+    if ((int)x.expert < sh.e0 || (int)x.expert >= sh.e0 + sh.e_loc) continue;  // another rank's expert
     const size_t n = sfk_strata_bundle_bytes(s, (int32_t)x.layer);
     if (!n) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: layer %u has no expert tensors", s->path.c_str(), x.layer);
     buf.resize(n);

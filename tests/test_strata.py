@@ -133,3 +133,38 @@ def test_strata_load_decodes_like_the_same_weights_put_directly(cuda, packed, ve
         assert float(np.linalg.norm(a - b) / np.linalg.norm(b)) < 1e-3 and float(np.abs(a - b).max()) < 1e-2
     eng.close()
     ref.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rank", [0, 1])
+def test_strata_load_into_an_expert_parallel_engine(cuda, tmp_path, rank):
+    """One rank of a two-rank engine loaded from a .strata file holds its own
+    experts and, with the heads split (16 query / 4 kv heads of width 32: a
+    rank's 8 query heads are 256 whole columns), its heads' rows of Q, K, V
+    and its heads' columns of the output projection; the rest in full.  (The
+    ranks are loaded one after the other on one GPU: loading needs no peer.)"""
+    from strataflow_b200 import engine as E
+    cfg = _cfg(n_embd=512, n_head=16, n_head_kv=4, n_layer=2, type_ffn_gu=O.Q4_K, type_ffn_down=O.Q8_0)
+    om = O.Model(cfg, seed=13)
+    path = tmp_path / "wide.strata"
+    write_strata(path, om, cfg, version=2)
+    eng = E.Engine.load_strata(str(path), kv_type=L.KV_F32, ep_size=2, ep_rank=rank)
+    hd, hq, hkv, E_loc = 32, 8, 2, 4
+    for l in range(cfg.n_layer):
+        for tid, h0, hn in ((O.T_ATTN_Q, rank * hq, hq), (O.T_ATTN_K, rank * hkv, hkv), (O.T_ATTN_V, rank * hkv, hkv)):
+            full, qtype, ne = om.tensor(tid, l)
+            rows = full.reshape(ne[1], -1)
+            assert np.array_equal(eng.get(tid, l), rows[h0 * hd:(h0 + hn) * hd].ravel()), (tid, l)
+        full, qtype, ne = om.tensor(O.T_ATTN_OUT, l)                 # [d rows][Hq*hd columns]
+        rb = O.row_bytes(qtype, hq * hd)
+        want = full.reshape(ne[1], -1)[:, rank * rb:(rank + 1) * rb].ravel()
+        assert np.array_equal(eng.get(O.T_ATTN_OUT, l), want), l
+        for tid in (O.T_FFN_GATE_EXPS, O.T_FFN_UP_EXPS, O.T_FFN_DOWN_EXPS):
+            full, _, _ = om.tensor(tid, l)
+            experts = full.reshape(cfg.n_expert, -1)
+            assert np.array_equal(eng.get(tid, l), experts[rank * E_loc:(rank + 1) * E_loc].ravel()), (tid, l)
+        for tid in (O.T_ATTN_NORM, O.T_FFN_NORM, O.T_FFN_GATE_INP):
+            assert np.array_equal(eng.get(tid, l), om.tensor(tid, l)[0]), (tid, l)
+    for tid in (O.T_TOK_EMBD, O.T_OUTPUT_NORM, O.T_OUTPUT):
+        assert np.array_equal(eng.get(tid, 0), om.tensor(tid, 0)[0]), tid
+    eng.close()
