@@ -307,13 +307,14 @@ GU_TRAFFIC_BYTES = 137.09e6
 
 def ep_rank_bytes(cfg, world: int, B: int) -> tuple[float, bool]:
     """Bytes one rank streams per step of the expert-parallel decode (Q8_0
-    trunk, Q4_K experts, head width 128) and whether the attention heads are
+    trunk, Q4_K experts, the config's head width) and whether the attention heads are
     split over the ranks.  The heads split, as the engine decides at
     creation, when both head counts divide by the ranks and a rank's query
     columns are whole 256-column blocks (SFK_HEAD_PARALLEL=0 keeps them
     replicated); the router (F32), the norms and the lm_head stay replicated,
     and each rank streams its share of the expected routed experts."""
-    d, F, k, hd = cfg.n_embd, cfg.n_ff, cfg.n_expert_used, 128
+    d, F, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
+    hd = cfg.head_dim if cfg.head_dim > 0 else cfg.n_embd // cfg.n_head   # as sfk_engine_create decides it
     q8 = lambda K: K // 32 * 34   # noqa: E731
     q4 = lambda K: K // 256 * 144   # noqa: E731
     split = (world > 1 and cfg.n_head % world == 0 and cfg.n_head_kv % world == 0 and

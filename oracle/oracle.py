@@ -40,7 +40,8 @@ class Hparams(C.Structure):
     _fields_ = [(n, C.c_int32) for n in (
         "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
         ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
-            "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_f16", "fp32_mode")]
+            "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_f16", "fp32_mode",
+            "head_dim")]
 
 
 _lib = None
@@ -230,6 +231,7 @@ class ModelConfig:
     type_output: int = Q8_0
     kv_f16: bool = False
     fp32_mode: bool = False
+    head_dim: int = 0   # 0: n_embd / n_head
 
     def to_c(self) -> Hparams:
         h = Hparams()

@@ -895,8 +895,12 @@ void sfo_seq_timing(const sfo_seq *s, double *layers_s, double *head_s) {
 
 static int tensor_layered(int tid) { return tid >= SFO_T_ATTN_NORM; }
 
+/* attention head width: n_embd / n_head (engine.cpp:1161) unless the model
+ * states its own (head_dim > 0, e.g. 64 heads x 128 over d = 7168) */
+static int hp_head_dim(const sfo_hparams *hp) { return hp->head_dim > 0 ? hp->head_dim : hp->n_embd / hp->n_head; }
+
 static void tensor_shape(const sfo_hparams *hp, int tid, int *type, int64_t ne[3]) {
-    const int64_t d = hp->n_embd, hd = d / hp->n_head;
+    const int64_t d = hp->n_embd, hd = hp_head_dim(hp);
     ne[0] = ne[1] = ne[2] = 1;
     switch (tid) {
     case SFO_T_TOK_EMBD: *type = hp->type_embd; ne[0] = d; ne[1] = hp->n_vocab; break;
@@ -918,7 +922,8 @@ static void tensor_shape(const sfo_hparams *hp, int tid, int *type, int64_t ne[3
 
 sfo_model *sfo_model_create(const sfo_hparams *hp) {
     if (hp->n_layer > 128 || hp->n_layer <= 0 || hp->n_head <= 0 || hp->n_head_kv <= 0 ||
-        hp->n_head % hp->n_head_kv || hp->n_embd % hp->n_head || hp->n_expert_used > hp->n_expert)
+        hp->n_head % hp->n_head_kv || (hp->head_dim <= 0 && hp->n_embd % hp->n_head) ||
+        hp->n_expert_used > hp->n_expert)
         return NULL;
     sfo_model *m = (sfo_model *)calloc(1, sizeof(sfo_model));
     m->hp = *hp;
@@ -984,7 +989,7 @@ int sfo_model_synth(sfo_model *m, uint64_t seed) {
 
 sfo_seq *sfo_seq_create(const sfo_model *m) {
     const sfo_hparams *hp = &m->hp;
-    const size_t hd = (size_t)(hp->n_embd / hp->n_head);
+    const size_t hd = (size_t)hp_head_dim(hp);
     const size_t kv = (size_t)hp->n_layer * hp->n_ctx * hp->n_head_kv * hd;
     sfo_seq *s = (sfo_seq *)calloc(1, sizeof(sfo_seq));
     s->m = m;
@@ -1010,7 +1015,7 @@ void sfo_seq_free(sfo_seq *s) {
 
 void sfo_seq_reset(sfo_seq *s) {
     const sfo_hparams *hp = &s->m->hp;
-    const size_t hd = (size_t)(hp->n_embd / hp->n_head);
+    const size_t hd = (size_t)hp_head_dim(hp);
     const size_t kv = (size_t)hp->n_layer * hp->n_ctx * hp->n_head_kv * hd;
     memset(s->k_cache, 0, kv * sizeof(float));
     memset(s->v_cache, 0, kv * sizeof(float));
@@ -1031,7 +1036,7 @@ static inline float kv_round(float v, int f16) { return f16 ? sfo_fp16_to_fp32(s
 /* engine::Engine::forward, engine.cpp:2498-3025, one token at `pos`. */
 int32_t sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t pos, float *logits) {
     const sfo_hparams *hp = &m->hp;
-    const int d = hp->n_embd, Hq = hp->n_head, Hkv = hp->n_head_kv, hd = d / Hq;
+    const int d = hp->n_embd, Hq = hp->n_head, Hkv = hp->n_head_kv, hd = hp_head_dim(hp);
     const int k = hp->n_expert_used, E = hp->n_expert, F = hp->n_ff;
     if (token < 0 || token >= hp->n_vocab || pos < 0 || pos >= hp->n_ctx) return -1;
     const int fp32 = hp->fp32_mode;

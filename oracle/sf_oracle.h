@@ -112,6 +112,7 @@ typedef struct sfo_hparams {
     int32_t type_embd, type_attn, type_ffn_gu, type_ffn_down, type_output;
     int32_t kv_f16;       /* round stored K/V through f16 (the paged-f16 KV mode) */
     int32_t fp32_mode;    /* diagnostic: dequantize weights, f32 activations */
+    int32_t head_dim;     /* 0: n_embd / n_head (engine.cpp:1161); else the stated head width */
 } sfo_hparams;
 
 /* tensor ids shared with the CUDA engine's C ABI (include/sfk.h) */

@@ -91,6 +91,10 @@ const StreamTuning& stream_tuning() {
   return t;
 }
 
+}  // namespace
+
+namespace sfk {
+// declared in sfk_kernels.cuh: also plans the no-allocation entry point's launches
 sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
   if (!p.s2_tile) p.s2_tile = stream_tuning().tile;
   if (!p.s2_stages) p.s2_stages = stream_tuning().stages;
@@ -126,6 +130,9 @@ sfk_status plan_stream(StreamParams& p, int sm_count, int* grid_out) {
   *grid_out = grid;
   return SFK_OK;
 }
+}  // namespace sfk
+
+namespace {
 
 // CTAs per (token, kv head) in the attention cluster: 8 (portable) unless a
 // CTA would own more than 2048 positions at the longest context
@@ -247,10 +254,10 @@ struct sfk_engine {
   bool head_par = false;
   int hq_loc = 0, hkv_loc = 0, q0 = 0, kv0 = 0;
   float* ep_buf = nullptr;      // [2][B][d] partial outputs (layer parity) | flags [MAXR] ints
-  int* ep_flags = nullptr;
-  int* ep_step = nullptr;
+  unsigned* ep_flags = nullptr;
+  unsigned* ep_step = nullptr;
   const float* ep_parts[MAXR] = {};
-  int* ep_peer_flags[MAXR] = {};
+  unsigned* ep_peer_flags[MAXR] = {};
   std::vector<void*> ep_opened;  // peer buffers opened through IPC
   bool ep_connected = false;
   int attn_cluster = 8;
@@ -914,10 +921,10 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     // flag words; its own allocation so that its IPC handle exposes nothing else
     const size_t part = sizeof(float) * 4 * (size_t)B * d;
     TRY(e->alloc(&e->ep_buf, part + 256, sb));
-    e->ep_flags = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(e->ep_buf) + part);
-    TRY(e->alloc(&e->ep_step, sizeof(int), sb));
+    e->ep_flags = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(e->ep_buf) + part);
+    TRY(e->alloc(&e->ep_step, sizeof(unsigned), sb));
     cudaError_t ce = cudaMemset(e->ep_buf, 0, part + 256);
-    if (ce == cudaSuccess) ce = cudaMemset(e->ep_step, 0, sizeof(int));
+    if (ce == cudaSuccess) ce = cudaMemset(e->ep_step, 0, sizeof(unsigned));
     if (ce != cudaSuccess) {
       sfk_engine_free(e);
       return fail(SFK_ERR_RUNTIME, "engine init: %s", cudaGetErrorString(ce));
@@ -1331,7 +1338,7 @@ sfk_status sfk_ep_connect(sfk_engine* e, const void* handles, int32_t n_ranks) {
       base = static_cast<uint8_t*>(p);
     }
     e->ep_parts[r] = reinterpret_cast<const float*>(base);
-    e->ep_peer_flags[r] = reinterpret_cast<int*>(base + part);
+    e->ep_peer_flags[r] = reinterpret_cast<unsigned*>(base + part);
   }
   e->ep_connected = true;
   return SFK_OK;

@@ -1550,18 +1550,18 @@ __global__ void __launch_bounds__(256) embed_kernel(const EmbedParams p) {
 // rank, wait for every rank's, add them in rank order.  The waits are bounded
 // and report ERR_TIMEOUT; nothing traps.
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ void st_release_sys(int* p, int v) {
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
-__device__ __forceinline__ int ld_acquire_sys(const int* p) {
-  int v;
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
   asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
 
 __global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
   // the step counter was written by the embed kernel, two or more kernels back
-  const int epoch = (*p.ep_step * p.n_layer + p.layer) * 2 + p.stage + 1;
+  const unsigned epoch = ep_epoch(*p.ep_step, p.n_layer, p.layer, p.stage);
   pdl_wait();
   pdl_launch_dependents();
   if (blockIdx.x == 0 && (int)threadIdx.x < p.n_ranks) {
@@ -1572,7 +1572,7 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
     const long long t0 = clock64();
     bool ok = true;
     for (int r = 0; r < p.n_ranks && ok; ++r) {
-      while (ld_acquire_sys(p.flags + r) < epoch) {
+      while (!ep_reached(ld_acquire_sys(p.flags + r), epoch)) {
         __nanosleep(32);
         if (clock64() - t0 > (1ll << 31)) {
           atomicExch(p.status, ERR_TIMEOUT);

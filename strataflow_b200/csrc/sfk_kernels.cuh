@@ -168,7 +168,7 @@ struct EmbedParams {
   int* pos_state;          // [b] persistent position counters (greedy loop)
   int* pos_cur;            // [b] position of this step (out)
   float* x;                // [b][d]
-  int* ep_step;            // expert parallelism: step counter the combine epochs derive from (or null)
+  unsigned* ep_step;       // expert parallelism: step counter the combine epochs derive from (or null)
   int* status;
 };
 
@@ -177,21 +177,35 @@ struct EmbedParams {
 // output projection; plus the residual on rank 0) into slot
 // parts[rank] + ((layer & 1) * 2 + stage) * half; x = sum of the ranks'
 // partials in rank order, identical on every rank.  Peers signal through each
-// other's flag words over peer memory (epoch = (step * n_layer + layer) * 2 +
-// stage + 1).
+// other's flag words over peer memory (epoch = ep_epoch(step, n_layer, layer,
+// stage)).
 struct EpParams {
   const float* parts[MAXR];  // every rank's partial buffer (peer pointers; own buffer at [rank])
-  int* flags;                // this rank's flag words [MAXR] (peers write them)
-  int* peer_flags[MAXR];     // every rank's flag words
+  unsigned* flags;           // this rank's flag words [MAXR] (peers write them)
+  unsigned* peer_flags[MAXR];  // every rank's flag words
   int n_ranks, rank;
   int layer, n_layer;
   int stage;                 // 0: attention output projection, 1: expert FFN
-  const int* ep_step;
+  const unsigned* ep_step;
   int half;                  // floats in one partial slot ([layer parity][stage] slots)
   int n;                     // floats to combine (b * d)
   float* x;
   int* status;
 };
+
+// Combine epochs are 32-bit unsigned and wrap (after about 2^32 / (2 * n_layer)
+// steps: ~35 M at 61 layers).  A flag has reached an epoch when the wrapped
+// difference is non-negative, which stays correct across the wrap because
+// ranks are never more than one stage apart (far less than 2^31 epochs).
+__host__ __device__ inline unsigned ep_epoch(unsigned step, int n_layer, int layer, int stage) {
+  return (step * (unsigned)n_layer + (unsigned)layer) * 2u + (unsigned)stage + 1u;
+}
+__host__ __device__ inline bool ep_reached(unsigned flag, unsigned epoch) { return (int)(flag - epoch) >= 0; }
+
+// Grid, rows per CTA, activation residency and ring plan of one streaming
+// launch (sfk_api.cu): the same plan for the engine, the operator calls and
+// the no-allocation entry point.  Returns an sfk_status (0 = SFK_OK).
+int plan_stream(StreamParams& p, int sm_count, int* grid_out);
 
 // launch helpers (implemented in sfk_kernels.cu)
 int stream_smem_bytes(const StreamParams& p, int* n_stages, int* stage_bytes, int* rows_per_warp);

@@ -68,19 +68,6 @@ size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
 int act_of(int wtype) { return wtype == T_Q8_0 ? T_Q8_0 : T_Q8_K; }
 bool quant_type(int t) { return t == T_Q4_K || t == T_Q6_K || t == T_Q8_0; }
 
-sfk_status plan(StreamParams& p, int sm_count, int* grid_out) {
-  int grid = std::min(sm_count, std::max(1, (p.rows + 15) / 16));
-  int rpc = (p.rows + grid - 1) / grid;
-  rpc = (rpc + p.row_align - 1) / p.row_align * p.row_align;
-  grid = (p.rows + rpc - 1) / rpc;
-  p.rows_per_cta = rpc;
-  p.xq_resident = (int64_t)p.n_vec * qact_bytes(p.K) <= 48 * 1024 ? 1 : 0;
-  const int smem = stream_smem_bytes(p, nullptr, nullptr, nullptr);
-  if (smem > 227 * 1024) return nfail(SFK_ERR_UNSUPPORTED, "stream kernel needs %d B of shared memory", smem);
-  *grid_out = grid;
-  return SFK_OK;
-}
-
 }  // namespace
 
 #define NCK(call)                                                                                 \
@@ -152,7 +139,7 @@ sfk_status sfk_moe_ffn_noalloc(int type_gu, int type_down, const void* gate, con
     p.grp_counter = counters;
     p.h_act_type = act_of(type_down);
     p.status = status;
-    if ((s = plan(p, sms, &grid))) return s;
+    if ((s = plan_stream(p, sms, &grid))) return s;
     NCK(launch_stream(p, grid, st, false));
   }
   {
@@ -177,7 +164,7 @@ sfk_status sfk_moe_ffn_noalloc(int type_gu, int type_down, const void* gate, con
     p.res = res;
     p.y_stride = d;
     p.status = status;
-    if ((s = plan(p, sms, &grid))) return s;
+    if ((s = plan_stream(p, sms, &grid))) return s;
     NCK(launch_stream(p, grid, st, false));
   }
   int host_status = 0;

@@ -23,3 +23,19 @@ def test_ep_rank_bytes_1t_shape(monkeypatch):
     assert not split and rep == 61 * (attn + router) + lm_head + 61 * 8 / 4 * expert
     one, split = bench.ep_rank_bytes(cfg, 1, 1)                     # one GPU holds everything
     assert not split and one == 61 * (attn + router) + lm_head + 61 * 8 * expert
+
+
+def test_ep_rank_bytes_uses_config_head_width(monkeypatch):
+    """A head width other than 128 (the tiny shape: d 256 / 8 heads = 32) is
+    taken from the config, as the engine takes it."""
+    monkeypatch.delenv("SFK_HEAD_PARALLEL", raising=False)
+    cfg = E.tiny_config(type_ffn_gu=12, type_ffn_down=12)
+    q8 = lambda K: K // 32 * 34   # noqa: E731
+    q4 = lambda K: K // 256 * 144   # noqa: E731
+    hd = 32
+    attn = (8 + 2 * 4) * hd * q8(256) + 256 * q8(8 * hd)
+    expert = 2 * 512 * q4(256) + 256 * q4(512)
+    got, split = bench.ep_rank_bytes(cfg, 2, 1)
+    # 4 query heads x 32 columns per rank = 128 columns: not whole 256-column blocks, so no split
+    assert not split
+    assert got == 4 * (attn + 4 * 256 * 8) + 4096 * q8(256) + 4 * 2 / 2 * expert

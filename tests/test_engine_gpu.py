@@ -12,22 +12,8 @@ from oracle import oracle as O
 
 pytestmark = pytest.mark.gpu
 
-REL_L2, MAX_ABS = 1e-3, 1e-2
 
-
-def _oracle_cfg(cfg, **kw):
-    d = {k: getattr(cfg, k) for k in ("n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used",
-                                      "n_vocab", "n_ctx", "rms_eps", "freq_base", "type_embd", "type_attn",
-                                      "type_ffn_gu", "type_ffn_down", "type_output")}
-    d["kv_f16"] = cfg.kv_type == 1
-    d.update(kw)
-    return O.ModelConfig(**d)
-
-
-def _close(a, b):
-    rel = float(np.linalg.norm(a - b) / np.linalg.norm(b))
-    mx = float(np.abs(a - b).max())
-    return rel < REL_L2 and mx < MAX_ABS, rel, mx
+from parity_util import oracle_cfg as _oracle_cfg, close as _close  # noqa: E402
 
 
 def _run_parity(cfg, seed, prompt, n_gen, oracle_model=None):
