@@ -28,6 +28,7 @@
 #include "sfk_dequant.cuh"
 #include "sfk_device.cuh"
 #include "sfk_kernels.cuh"
+#include "sfk_mega.cuh"
 
 using namespace sfk;
 
@@ -271,6 +272,17 @@ struct sfk_engine {
   unsigned long long* h_keys = nullptr;
   int* h_status = nullptr;  // right after h_keys[B]
   float* h_logits = nullptr;
+  // persistent step kernel (sfk_mega.cu): one cooperative launch per step
+  // when the shape fits its plan; otherwise the launch chain below
+  bool mega = false;
+  MegaLayer* d_layers = nullptr;  // per-layer weight pointers on the device
+  float *att_y = nullptr, *att_cmax = nullptr, *att_stat = nullptr;
+  double* att_opart = nullptr;
+  int* att_cnt = nullptr;
+  unsigned* att_ready = nullptr;
+  unsigned* gbar = nullptr;
+  int att_nc = 0;
+  bool last_step_mega = false;
   // graphs: key = b * 2 + greedy
   std::map<int, cudaGraphExec_t> graphs;
   uint64_t steps = 0;
@@ -372,12 +384,19 @@ enum KernelClass { K_EMBED = 0, K_QKV, K_ATTN, K_OPROJ, K_ROUTER, K_GATEUP, K_DO
 // The device status word after a step; on a device error the counters that
 // CTAs hand between launches (routing arrivals, SwiGLU group counters) may be
 // left mid-count, so they are cleared before the engine is used again.
+void reset_counters(sfk_engine* e) {
+  cudaMemset(e->router_counter, 0, 2 * sizeof(int));
+  cudaMemset(e->grp_counter, 0, sizeof(int) * (e->hp.n_ff / 256));
+  if (e->mega) {  // a failed persistent step may leave its barrier and attention words mid-count
+    cudaMemset(e->gbar, 0, 2 * sizeof(unsigned));
+    cudaMemset(e->att_cnt, 0, sizeof(int) * 2 * e->hp.max_batch * e->hkv_loc);
+    cudaMemset(e->att_ready, 0, sizeof(unsigned) * e->hp.max_batch * e->hkv_loc);
+  }
+}
+
 sfk_status engine_check(sfk_engine* e) {
   sfk_status s = check_status_word(e->status, e->stream);
-  if (s != SFK_OK) {
-    cudaMemset(e->router_counter, 0, 2 * sizeof(int));
-    cudaMemset(e->grp_counter, 0, sizeof(int) * (e->hp.n_ff / 256));
-  }
+  if (s != SFK_OK) reset_counters(e);
   return s;
 }
 
@@ -655,7 +674,155 @@ sfk_status launch_combine(sfk_engine* e, int l, int stage, int b, float* dst) {
   return SFK_OK;
 }
 
+// Plan of the persistent step kernel for b sequences: rows per CTA, ring
+// slot size, tile rows per phase, shared-memory layout.  False when the shape
+// does not fit it (the step then runs as the launch chain).
+constexpr int MEGA_CH = 64;  // attention positions per work item
+
+bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* grid_out) {
+  if (!e->mega || b < 1 || b > e->hp.max_batch) return false;
+  const sfk_hparams& hp = e->hp;
+  const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used, V = hp.n_vocab;
+  const int hd = e->hd, gqa = hp.n_head / hp.n_head_kv;
+  if (b * k > 32) return false;
+  const int grid = e->sm_count;
+  MegaParams p{};
+  p.layers = e->d_layers;
+  p.n_layer = hp.n_layer;
+  p.d = d; p.nq = e->nq; p.nk = e->nk; p.nqkv = e->nqkv; p.hd = hd; p.n_head = hp.n_head; p.n_head_kv = hp.n_head_kv;
+  p.gqa = gqa; p.F = F; p.E = E; p.k = k; p.V = V; p.b = b; p.n_ctx = hp.n_ctx;
+  p.eps = hp.rms_eps;
+  p.att_scale = 1.0f / sqrtf((float)hd);
+  p.t_embd = hp.type_embd; p.t_attn = hp.type_attn; p.t_gu = hp.type_ffn_gu; p.t_down = hp.type_ffn_down;
+  p.t_out = hp.type_output;
+  p.a_attn = act_for(hp.type_attn); p.a_gu = act_for(hp.type_ffn_gu); p.a_down = act_for(hp.type_ffn_down);
+  p.a_out = act_for(hp.type_output);
+  p.rs_attn = dev_row_bytes(hp.type_attn, d);
+  p.rs_o = dev_row_bytes(hp.type_attn, e->nq);
+  p.rs_gu = dev_row_bytes(hp.type_ffn_gu, d);
+  p.rs_down = dev_row_bytes(hp.type_ffn_down, F);
+  p.rs_out = dev_row_bytes(hp.type_output, d);
+  auto rpc = [&](int rows, int align) {
+    int r = (rows + grid - 1) / grid;
+    return (r + align - 1) / align * align;
+  };
+  p.rpc_qkv = rpc(e->nqkv, 2);
+  p.rpc_o = rpc(d, 1);
+  p.rpc_gu = rpc(F, 1);
+  p.rpc_down = rpc(d, 1);
+  p.rpc_out = rpc(V, 1);
+  // router rows: pieces of d / parts columns (a multiple of 128), one tile per warp
+  int parts = 1;
+  if (E < MEGA_NWS)
+    while (parts * 2 * E <= MEGA_NWS && d % (parts * 2 * 128) == 0) parts *= 2;
+  if (d % (parts * 128)) return false;
+  p.rt_parts = parts;
+  const int items = E * parts;
+  const int64_t rt_bytes = (int64_t)((items + MEGA_NWS - 1) / MEGA_NWS) * (d / parts) * 4;
+  // shared memory
+  auto al = [](int64_t v, int a) { return (v + a - 1) / a * a; };
+  const int kvb = hp.kv_type == SFK_KV_F16 ? 2 : 4;
+  const int64_t qd = qact_bytes(d), qq = qact_bytes(e->nq), qf = qact_bytes(F);
+  int64_t xq = std::max<int64_t>(b * qd, b * qq);
+  xq = std::max<int64_t>(xq, (int64_t)b * k * qf);
+  xq = std::max<int64_t>(xq, al(b * qd, 16) + (int64_t)b * d * 4 + (int64_t)b * E * 4);
+  xq = std::max<int64_t>(xq, 2ll * MEGA_CH * hd * kvb);
+  xq = al(xq, 128);
+  int64_t acc = std::max<int64_t>((int64_t)p.rpc_qkv * b, (int64_t)p.rpc_o * b);
+  acc = std::max<int64_t>(acc, (int64_t)p.rpc_gu * b * k * 2);
+  acc = std::max<int64_t>(acc, (int64_t)p.rpc_down * b * k);
+  acc = std::max<int64_t>(acc, (int64_t)p.rpc_out * b);
+  acc = al(acc * 4, 16);
+  const int64_t route = al(sizeof(Route), 16);
+  const int64_t red = MEGA_RED * 8;
+  const int64_t probs = al((int64_t)b * items * 8, 16);
+  const int64_t att = al((int64_t)gqa * hd * 4 + 2ll * gqa * MEGA_CH * 4 + gqa * 8, 16);
+  const int64_t misc = al((2 * MAXB + 4) * 4, 16);
+  const int64_t bars = al(MEGA_NWS * MEGA_MAXS * 8 + 3 * 8, 128);
+  const int64_t fixed = bars + xq + acc + route + red + probs + att + misc;
+  int S = 1;
+  if (const char* v = getenv("SFK_MEGA_STAGES")) S = std::max(1, std::min(MEGA_MAXS, atoi(v)));
+  int64_t slot = (SMEM_LIMIT - fixed) / (MEGA_NWS * S);
+  slot = std::min<int64_t>(slot, 32 * 1024) / 128 * 128;
+  if (const char* v = getenv("SFK_MEGA_SLOT")) slot = std::min<int64_t>(slot, atoi(v) / 128 * 128);
+  if (slot <= 0 || rt_bytes > slot) return false;
+  // rows per tile: <= 4 (row, matrix) unit dots of one group, or <= 8 values
+  // (row, matrix, group) for longer rows
+  auto rows_per_tile = [&](int64_t rs, int nmat, int K) {
+    const int G = n_groups(K);
+    const int rmax = G == 1 ? 4 / nmat : 8 / (nmat * G);
+    return (int)std::min<int64_t>(rmax, slot / (nmat * rs));
+  };
+  p.R_qkv = rows_per_tile(p.rs_attn, 1, d);
+  p.R_o = rows_per_tile(p.rs_o, 1, e->nq);
+  p.R_gu = rows_per_tile(p.rs_gu, 2, d);
+  p.R_down = rows_per_tile(p.rs_down, 1, F);
+  p.R_out = rows_per_tile(p.rs_out, 1, d);
+  if (p.R_qkv < 1 || p.R_o < 1 || p.R_gu < 1 || p.R_down < 1 || p.R_out < 1) return false;
+  p.S = S;
+  p.slot = (int)slot;
+  p.att_ch = MEGA_CH;
+  p.att_nc = e->att_nc;
+  p.off_ring = (int)bars;
+  p.off_xq = p.off_ring + (int)(MEGA_NWS * S * slot);
+  p.off_acc = p.off_xq + (int)xq;
+  p.off_route = p.off_acc + (int)acc;
+  p.off_red = p.off_route + (int)route;
+  p.off_probs = p.off_red + (int)red;
+  p.off_att = p.off_probs + (int)probs;
+  p.off_misc = p.off_att + (int)att;
+  p.smem = p.off_misc + (int)misc;
+  p.xq_bytes = (int)xq;
+  if (p.smem > SMEM_LIMIT) return false;
+  p.tok_embd = e->tok_embd;
+  p.out_norm = e->out_norm;
+  p.output = e->output;
+  p.tok_in = e->tok_in;
+  p.pos_in = greedy ? nullptr : e->pos_in;
+  p.greedy = greedy ? 1 : 0;
+  p.pos_state = e->pos_state;
+  p.pos_cur = e->pos_cur;
+  p.tok_hist = e->tok_hist;
+  p.argmax_key = e->argmax_key;
+  p.k_pool = e->k_pool;
+  p.v_pool = e->v_pool;
+  p.kv_layer_bytes = e->kv_layer_elems * kvb;
+  p.page_table = e->page_table;
+  p.max_pages = e->max_pages;
+  p.n_pages = e->n_pages;
+  p.kv_f16 = hp.kv_type == SFK_KV_F16 ? 1 : 0;
+  p.rope = e->rope;
+  p.x = e->x;
+  p.ffn_inp = e->ffn_inp;
+  p.q = e->q;
+  p.attn_out = e->attn_out;
+  p.h = e->h;
+  p.hq = e->hq;
+  p.logits = e->logits;
+  p.grp_counter = e->grp_counter;
+  p.route_out = e->route;
+  p.att_y = e->att_y;
+  p.att_cmax = e->att_cmax;
+  p.att_stat = e->att_stat;
+  p.att_opart = e->att_opart;
+  p.att_cnt = e->att_cnt;
+  p.att_ready = e->att_ready;
+  p.gbar = e->gbar;
+  p.status = e->status;
+  p.store_logits = 1;
+  *out = p;
+  *grid_out = grid;
+  return true;
+}
+
 sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
+  MegaParams mp;
+  int mgrid = 0;
+  if (mega_params(e, b, greedy, &mp, &mgrid)) {
+    CK(launch_mega(mp, mgrid, e->stream));
+    e->kernels_per_step = 1;
+    return SFK_OK;
+  }
   int nk = 0;
   sfk_status s = launch_one(e, K_EMBED, 0, b, greedy, true);
   if (s) return s;
@@ -964,6 +1131,42 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
       e->fused_route = false;
   }
   {
+    // the persistent step kernel: single-GPU engines whose types, expert
+    // count and GQA group it covers (SFK_PERSISTENT=0 keeps the launch chain)
+    const char* pv = getenv("SFK_PERSISTENT");
+    const int gqa = hp->n_head / hp->n_head_kv;
+    int coop = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
+    if (!(pv && atoi(pv) == 0) && coop && e->ep_size == 1 && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
+        (gqa & (gqa - 1)) == 0 &&
+        mega_types_supported(hp->type_attn, hp->type_ffn_gu, hp->type_ffn_down, hp->type_output)) {
+      const int Hq = hp->n_head, Hkv = hp->n_head_kv;
+      e->att_nc = (e->max_pages * 16 + MEGA_CH - 1) / MEGA_CH;
+      TRY(e->alloc(&e->d_layers, sizeof(MegaLayer) * hp->n_layer, sb));
+      TRY(e->alloc(&e->att_y, sizeof(float) * (size_t)B * Hq * hp->n_ctx, sb));
+      TRY(e->alloc(&e->att_cmax, sizeof(float) * (size_t)B * Hkv * e->att_nc * gqa, sb));
+      TRY(e->alloc(&e->att_stat, sizeof(float) * (size_t)B * Hq * 2, sb));
+      TRY(e->alloc(&e->att_opart, sizeof(double) * (size_t)B * Hkv * e->att_nc * gqa * e->hd, sb));
+      TRY(e->alloc(&e->att_cnt, sizeof(int) * 2 * B * Hkv, sb));
+      TRY(e->alloc(&e->att_ready, sizeof(unsigned) * B * Hkv, sb));
+      TRY(e->alloc(&e->gbar, 2 * sizeof(unsigned), sb));
+      std::vector<MegaLayer> tab(hp->n_layer);
+      for (int l = 0; l < hp->n_layer; ++l) {
+        const LayerW& W = e->L[l];
+        tab[l] = MegaLayer{W.qkv, W.wo, W.attn_norm, W.ffn_norm, W.router, W.gate, W.up, W.down};
+      }
+      cudaError_t ce = cudaMemcpy(e->d_layers, tab.data(), sizeof(MegaLayer) * tab.size(), cudaMemcpyHostToDevice);
+      if (ce == cudaSuccess) ce = cudaMemset(e->att_cnt, 0, sizeof(int) * 2 * B * Hkv);
+      if (ce == cudaSuccess) ce = cudaMemset(e->att_ready, 0, sizeof(unsigned) * B * Hkv);
+      if (ce == cudaSuccess) ce = cudaMemset(e->gbar, 0, 2 * sizeof(unsigned));
+      if (ce != cudaSuccess) {
+        sfk_engine_free(e);
+        return fail(SFK_ERR_RUNTIME, "persistent kernel init: %s", cudaGetErrorString(ce));
+      }
+      e->mega = true;
+    }
+  }
+  {
     // RoPE cos/sin for every position (ggml rope cache, mode NORMAL,
     // freq_scale 1, ext_factor 0): theta_0 = pos, theta_{i+1} = theta_i *
     // powf(base, -2/n_dims), evaluated with the host libm
@@ -1165,8 +1368,7 @@ sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens
                      e->stream));
   CK(cudaStreamSynchronize(e->stream));
   if ((s = status_result(e->status, *e->h_status))) {
-    cudaMemset(e->router_counter, 0, 2 * sizeof(int));
-    cudaMemset(e->grp_counter, 0, sizeof(int) * (e->hp.n_ff / 256));
+    reset_counters(e);
     return s;
   }
   if (logits_host) memcpy(logits_host, e->h_logits, sizeof(float) * n_logits);

@@ -159,9 +159,12 @@ def test_forward_rejects_out_of_range_inputs(cuda):
     assert 0 <= am < cfg.n_vocab
 
 
-def test_kernel_timing_entry_point(cuda):
+def test_kernel_timing_entry_point(cuda, monkeypatch):
+    """The launch chain's per-kernel timing (the persistent step kernel is
+    switched off so the step runs as the chain of 2 + 5L launches)."""
     from strataflow_b200 import engine as E
     import ctypes as C
+    monkeypatch.setenv("SFK_PERSISTENT", "0")
     cfg = E.tiny_config(n_layer=2)
     eng = E.Engine.load(cfg, seed=0)
     eng.forward(3, 0)
@@ -177,9 +180,11 @@ def test_kernel_timing_entry_point(cuda):
 
 
 def test_standalone_router_kernel_parity(cuda, monkeypatch):
-    """SFK_ROUTER_KERNEL=1: routing runs in its own kernel before gate/up."""
+    """SFK_ROUTER_KERNEL=1: routing runs in its own kernel before gate/up
+    (launch chain)."""
     from strataflow_b200 import engine as E
     monkeypatch.setenv("SFK_ROUTER_KERNEL", "1")
+    monkeypatch.setenv("SFK_PERSISTENT", "0")
     cfg = E.tiny_config(n_layer=2, n_expert=72, n_expert_used=4)
     prompt = np.random.default_rng(8).integers(0, cfg.n_vocab, 8).tolist()
     eng, om, toks, worst = _run_parity(cfg, 9, prompt, 12)
@@ -187,12 +192,36 @@ def test_standalone_router_kernel_parity(cuda, monkeypatch):
 
 
 @pytest.mark.parametrize("n_expert,k", [(72, 4), (160, 2)])
-def test_many_experts_fused_routing_parity(cuda, n_expert, k):
-    """Routing inside gate/up for larger expert counts: 72 experts fit the
-    ring (router staged in every CTA); 160 do not (each CTA scores a few
-    logits and the CTAs exchange them)."""
+def test_many_experts_fused_routing_parity(cuda, n_expert, k, monkeypatch):
+    """Routing inside gate/up for larger expert counts (launch chain): 72
+    experts fit the ring (router staged in every CTA); 160 do not (each CTA
+    scores a few logits and the CTAs exchange them)."""
     from strataflow_b200 import engine as E
+    monkeypatch.setenv("SFK_PERSISTENT", "0")
     cfg = E.tiny_config(n_layer=2, n_expert=n_expert, n_expert_used=k)
     prompt = np.random.default_rng(n_expert).integers(0, cfg.n_vocab, 8).tolist()
     eng, om, toks, worst = _run_parity(cfg, 9, prompt, 12)
     assert eng.stats()["kernels_per_step"] == 2 + 5 * cfg.n_layer
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(type_ffn_gu=12, type_ffn_down=12, type_attn=14, type_output=14,
+                                             type_embd=14, kv_type=1)])
+def test_persistent_step_matches_launch_chain(cuda, monkeypatch, kw):
+    """The persistent step kernel (one cooperative launch per step) and the
+    launch chain produce the same greedy tokens and logits within float
+    rounding of each other, and both match the oracle (checked by
+    _run_parity on the persistent path)."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_layer=3, **kw)
+    prompt = np.random.default_rng(12).integers(0, cfg.n_vocab, 10).tolist()
+    eng, om, toks, worst = _run_parity(cfg, 21, prompt, 16)
+    assert eng.stats()["kernels_per_step"] == 1
+    monkeypatch.setenv("SFK_PERSISTENT", "0")
+    chain = E.Engine.load(cfg, seed=21)
+    toks_c, logits_c = chain.generate(prompt, 16, host_loop=True)
+    assert chain.stats()["kernels_per_step"] == 2 + 5 * cfg.n_layer
+    assert toks_c == toks
+    eng.reset_kv()
+    toks_p, logits_p = eng.generate(prompt, 16, host_loop=True)
+    for a, b in zip(logits_p, logits_c):
+        assert np.abs(a - b).max() <= 1e-5 * np.abs(b).max()

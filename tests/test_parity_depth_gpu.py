@@ -38,17 +38,21 @@ def _check_seq(eng, om, prompt, n_gen):
     return toks, worst
 
 
-def test_mixtral_full_depth_greedy_parity(cuda):
+@pytest.mark.parametrize("persistent", ["1", "0"])
+def test_mixtral_full_depth_greedy_parity(cuda, monkeypatch, persistent):
     """The benchmark's model at full depth: 32 layers, 32-token prompt, 16
-    greedy tokens, every step's logits against the oracle."""
+    greedy tokens, every step's logits against the oracle; on the persistent
+    step kernel (the benchmarked path) and on the launch chain."""
     from strataflow_b200 import engine as E
+    monkeypatch.setenv("SFK_PERSISTENT", persistent)
     cfg = E.mixtral_config(n_ctx=64)
     eng = E.Engine.load(cfg, seed=4)
     try:
         om = oracle_from_engine(eng)
         prompt = np.random.default_rng(4).integers(0, cfg.n_vocab, 32).tolist()
         toks, worst = _check_seq(eng, om, prompt, 16)
-        print("mixtral 32L worst rel/max-abs", worst)
+        assert eng.stats()["kernels_per_step"] == (1 if persistent == "1" else 2 + 5 * cfg.n_layer)
+        print("mixtral 32L persistent=%s worst rel/max-abs" % persistent, worst)
         # the device greedy loop continues the same sequence as the host loop
         eng.reset_kv()
         dev, _ = eng.generate(prompt, 16, host_loop=False)
