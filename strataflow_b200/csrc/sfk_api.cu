@@ -711,14 +711,13 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   p.rpc_gu = rpc(F, 1);
   p.rpc_down = rpc(d, 1);
   p.rpc_out = rpc(V, 1);
-  // router rows: pieces of d / parts columns (a multiple of 128), one tile per warp
+  // router rows: pieces of d / parts columns (a multiple of 128); the pieces
+  // are dealt to the warps like row blocks, one piece per ring slot.  At
+  // least one piece per warp when the columns allow it; pieces are cut
+  // further below until one fits a slot (checked once the slot is known).
   int parts = 1;
-  if (E < MEGA_NWS)
-    while (parts * 2 * E <= MEGA_NWS && d % (parts * 2 * 128) == 0) parts *= 2;
+  while (E * parts < MEGA_NWS && d % (parts * 2 * 128) == 0) parts *= 2;
   if (d % (parts * 128)) return false;
-  p.rt_parts = parts;
-  const int items = E * parts;
-  const int64_t rt_bytes = (int64_t)((items + MEGA_NWS - 1) / MEGA_NWS) * (d / parts) * 4;
   // shared memory
   auto al = [](int64_t v, int a) { return (v + a - 1) / a * a; };
   const int kvb = hp.kv_type == SFK_KV_F16 ? 2 : 4;
@@ -735,30 +734,53 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   acc = al(acc * 4, 16);
   const int64_t route = al(sizeof(Route), 16);
   const int64_t red = MEGA_RED * 8;
-  const int64_t probs = al((int64_t)b * items * 8, 16);
+  const int64_t probs = al((int64_t)b * E * (d / 128) * 8, 16);  // partial logits, any piece count
   const int64_t att = al((int64_t)gqa * hd * 4 + 2ll * gqa * MEGA_CH * 4 + gqa * 8, 16);
-  const int64_t misc = al((2 * MAXB + 4) * 4, 16);
+  const int64_t misc = al((2 * MAXB + 4) * 4, 16);  // tokens | positions | routed layer | flag | phase limit
   const int64_t bars = al(MEGA_NWS * MEGA_MAXS * 8 + 3 * 8, 128);
-  const int64_t fixed = bars + xq + acc + route + red + probs + att + misc;
+  const int64_t layers = al((int64_t)hp.n_layer * sizeof(MegaLayer), 16);
+  const int64_t fixed = bars + xq + acc + route + red + probs + att + misc + layers;
+  // ring slots per warp, a power of two (SFK_MEGA_STAGES / SFK_MEGA_SLOT
+  // override the ring shape)
   int S = 1;
-  if (const char* v = getenv("SFK_MEGA_STAGES")) S = std::max(1, std::min(MEGA_MAXS, atoi(v)));
+  if (const char* v = getenv("SFK_MEGA_STAGES")) S = atoi(v);
+  if (S != 1 && S != 2 && S != 4) return false;
+  p.S_log2 = S == 1 ? 0 : (S == 2 ? 1 : 2);
+  p.lookahead = 1 << 20;  // unlimited: rings run ahead across every phase boundary
+  if (const char* v = getenv("SFK_MEGA_LOOKAHEAD")) p.lookahead = atoi(v);
   int64_t slot = (SMEM_LIMIT - fixed) / (MEGA_NWS * S);
   slot = std::min<int64_t>(slot, 32 * 1024) / 128 * 128;
   if (const char* v = getenv("SFK_MEGA_SLOT")) slot = std::min<int64_t>(slot, atoi(v) / 128 * 128);
-  if (slot <= 0 || rt_bytes > slot) return false;
-  // rows per tile: <= 4 (row, matrix) unit dots of one group, or <= 8 values
-  // (row, matrix, group) for longer rows
-  auto rows_per_tile = [&](int64_t rs, int nmat, int K) {
+  if (slot <= 0) return false;
+  while ((int64_t)(d / parts) * 4 > slot && d % (parts * 2 * 128) == 0) parts *= 2;
+  if ((int64_t)(d / parts) * 4 > slot) return false;
+  p.rt_parts = parts;
+  // Tiles per weight phase: R whole rows (at most four (row, matrix) unit dots
+  // of a one-group row, or eight (row, matrix, group) values), or, for a row
+  // longer than a slot (one matrix only), column-group ranges of one row
+  auto plan_tiles = [&](int k, int64_t rs, int nmat, int wt, int K) {
     const int G = n_groups(K);
-    const int rmax = G == 1 ? 4 / nmat : 8 / (nmat * G);
-    return (int)std::min<int64_t>(rmax, slot / (nmat * rs));
+    // (row, matrix) values per tile: up to four for one-group rows, two for
+    // longer rows, and at most eight (row, matrix, group) values
+    const int rmax = G == 1 ? 4 / nmat : std::min(2 / nmat, 8 / (nmat * G));
+    p.R[k] = (int)std::min<int64_t>(std::max(rmax, 1), slot / (nmat * rs));
+    p.H[k] = 1;
+    p.gpp[k] = 8;
+    if (p.R[k] >= 1 && rmax >= 1) return true;
+    if (nmat != 1) return false;
+    const int64_t gb = group_bytes(wt, GROUP_UNITS);  // a full group; the last may be shorter
+    const int gpp = (int)std::min<int64_t>(8, slot / gb);
+    if (gpp < 1) return false;
+    p.R[k] = 1;
+    p.gpp[k] = gpp;
+    p.H[k] = (G + gpp - 1) / gpp;
+    return true;
   };
-  p.R_qkv = rows_per_tile(p.rs_attn, 1, d);
-  p.R_o = rows_per_tile(p.rs_o, 1, e->nq);
-  p.R_gu = rows_per_tile(p.rs_gu, 2, d);
-  p.R_down = rows_per_tile(p.rs_down, 1, F);
-  p.R_out = rows_per_tile(p.rs_out, 1, d);
-  if (p.R_qkv < 1 || p.R_o < 1 || p.R_gu < 1 || p.R_down < 1 || p.R_out < 1) return false;
+  if (!plan_tiles(MEGA_PK_QKV, p.rs_attn, 1, hp.type_attn, d) || !plan_tiles(MEGA_PK_O, p.rs_o, 1, hp.type_attn, e->nq) ||
+      !plan_tiles(MEGA_PK_GU, p.rs_gu, 2, hp.type_ffn_gu, d) ||
+      !plan_tiles(MEGA_PK_DN, p.rs_down, 1, hp.type_ffn_down, F) ||
+      !plan_tiles(MEGA_PK_OUT, p.rs_out, 1, hp.type_output, d))
+    return false;
   p.S = S;
   p.slot = (int)slot;
   p.att_ch = MEGA_CH;
@@ -771,7 +793,8 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   p.off_probs = p.off_red + (int)red;
   p.off_att = p.off_probs + (int)probs;
   p.off_misc = p.off_att + (int)att;
-  p.smem = p.off_misc + (int)misc;
+  p.off_layers = p.off_misc + (int)misc;
+  p.smem = p.off_layers + (int)layers;
   p.xq_bytes = (int)xq;
   if (p.smem > SMEM_LIMIT) return false;
   p.tok_embd = e->tok_embd;

@@ -51,11 +51,15 @@ constexpr int NT = NWS * 32;
 enum : int { SP_QKV = 0, SP_O = 1, SP_RT = 2, SP_GU = 3, SP_DN = 4, SP_N = 5 };
 enum : int { K_DENSE = 0, K_ROUTED = 1, K_ROUTER = 2 };
 
+extern __shared__ __align__(128) uint8_t mega_smem[];
+
 struct SDesc {
   const uint8_t* w0;
   const uint8_t* w1;
   int64_t rs, es;
   int r0, r1, R, nmat, kind;
+  int H, gpp;  // tiles per row (cut into column-group ranges) and groups per such tile
+  int wt, K;   // weight type and row length (columns)
 };
 
 __device__ __forceinline__ SDesc stream_desc(const MegaParams& p, int gp) {
@@ -64,56 +68,80 @@ __device__ __forceinline__ SDesc stream_desc(const MegaParams& p, int gp) {
   s.es = 0;
   s.nmat = 1;
   s.kind = K_DENSE;
+  s.H = 1;
+  s.gpp = 8;
   const int c = blockIdx.x;
   if (gp >= p.n_layer * SP_N) {  // lm_head
     s.w0 = p.output;
     s.rs = p.rs_out;
-    s.R = p.R_out;
+    s.R = p.R[MEGA_PK_OUT];
+    s.H = p.H[MEGA_PK_OUT];
+    s.gpp = p.gpp[MEGA_PK_OUT];
+    s.wt = p.t_out;
+    s.K = p.d;
     s.r0 = c * p.rpc_out;
     s.r1 = min(p.V, s.r0 + p.rpc_out);
     return s;
   }
   const int l = gp / SP_N, ph = gp - l * SP_N;
-  const MegaLayer* L = p.layers + l;
+  const MegaLayer* L = reinterpret_cast<const MegaLayer*>(mega_smem + p.off_layers) + l;  // copied at launch
   switch (ph) {
     case SP_QKV:
-      s.w0 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->qkv)));
+      s.w0 = reinterpret_cast<const uint8_t*>(L->qkv);
       s.rs = p.rs_attn;
-      s.R = p.R_qkv;
+      s.R = p.R[MEGA_PK_QKV];
+      s.H = p.H[MEGA_PK_QKV];
+      s.gpp = p.gpp[MEGA_PK_QKV];
+      s.wt = p.t_attn;
+      s.K = p.d;
       s.r0 = c * p.rpc_qkv;
       s.r1 = min(p.nqkv, s.r0 + p.rpc_qkv);
       break;
     case SP_O:
-      s.w0 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->wo)));
+      s.w0 = reinterpret_cast<const uint8_t*>(L->wo);
       s.rs = p.rs_o;
-      s.R = p.R_o;
+      s.R = p.R[MEGA_PK_O];
+      s.H = p.H[MEGA_PK_O];
+      s.gpp = p.gpp[MEGA_PK_O];
+      s.wt = p.t_attn;
+      s.K = p.nq;
       s.r0 = c * p.rpc_o;
       s.r1 = min(p.d, s.r0 + p.rpc_o);
       break;
     case SP_RT:
-      s.w0 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->router)));
+      s.w0 = reinterpret_cast<const uint8_t*>(L->router);
       s.rs = 0;
       s.R = 1;
       s.r0 = 0;
       s.r1 = 0;
       s.kind = K_ROUTER;
+      s.wt = T_F32;
+      s.K = p.d;
       break;
     case SP_GU:
-      s.w0 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->gate)));
-      s.w1 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->up)));
+      s.w0 = reinterpret_cast<const uint8_t*>(L->gate);
+      s.w1 = reinterpret_cast<const uint8_t*>(L->up);
       s.rs = p.rs_gu;
       s.es = (int64_t)p.F * p.rs_gu;
-      s.R = p.R_gu;
+      s.R = p.R[MEGA_PK_GU];
+      s.H = p.H[MEGA_PK_GU];
+      s.gpp = p.gpp[MEGA_PK_GU];
+      s.wt = p.t_gu;
+      s.K = p.d;
       s.r0 = c * p.rpc_gu;
       s.r1 = min(p.F, s.r0 + p.rpc_gu);
       s.nmat = 2;
       s.kind = K_ROUTED;
       break;
     default:  // SP_DN
-      s.w0 = reinterpret_cast<const uint8_t*>(__ldg(reinterpret_cast<const unsigned long long*>(&L->down)));
+      s.w0 = reinterpret_cast<const uint8_t*>(L->down);
       s.rs = p.rs_down;
       s.es = (int64_t)p.d * p.rs_down;
-      s.R = p.R_down;
+      s.R = p.R[MEGA_PK_DN];
+      s.H = p.H[MEGA_PK_DN];
+      s.gpp = p.gpp[MEGA_PK_DN];
+      s.wt = p.t_down;
+      s.K = p.F;
       s.r0 = c * p.rpc_down;
       s.r1 = min(p.d, s.r0 + p.rpc_down);
       s.kind = K_ROUTED;
@@ -122,16 +150,17 @@ __device__ __forceinline__ SDesc stream_desc(const MegaParams& p, int gp) {
   return s;
 }
 
-// tiles of a phase in this CTA: row blocks (x routed experts), or one router
-// piece per warp
-__device__ __forceinline__ int n_tiles(const MegaParams& p, const SDesc& s, int n_slots) {
-  if (s.kind == K_ROUTER) return min(NWS, p.E * p.rt_parts);
+// Work units of a phase in this CTA: row blocks (x routed experts), or the
+// router's row pieces (every CTA takes all of them).  Unit u belongs to warp u % NWS and streams as H
+// consecutive tiles (column-group ranges of its row when a row is longer than
+// a ring slot, else the whole row block).
+__device__ __forceinline__ int n_units(const MegaParams& p, const SDesc& s, int n_slots) {
+  if (s.kind == K_ROUTER) return p.E * p.rt_parts;
   const int n_rb = s.r0 < s.r1 ? (s.r1 - s.r0 + s.R - 1) / s.R : 0;
   return s.kind == K_ROUTED ? n_rb * n_slots : n_rb;
 }
 
 // Shared memory of one CTA; the offsets come from the host plan (MegaParams).
-extern __shared__ __align__(128) uint8_t mega_smem[];
 
 struct Smem {
   const MegaParams& p;
@@ -153,10 +182,12 @@ struct Smem {
   __device__ int* pos() const { return toks() + MAXB; }
   __device__ int* route_layer() const { return toks() + 2 * MAXB; }
   __device__ int* flag() const { return toks() + 2 * MAXB + 1; }
+  __device__ int* gp_limit() const { return toks() + 2 * MAXB + 2; }  // last streamed phase a ring may issue
 };
 
-// The issue side of a warp's ring: the next tile (phase gp, tile warp + j*NWS)
-// and the counts of tiles issued and consumed.  Warp-uniform; lane 0 issues.
+// The issue side of a warp's ring: the next tile (phase gp, this warp's j-th
+// tile of the phase: unit warp + (j / H) * NWS, part j % H) and the counts of
+// tiles issued and consumed.  Warp-uniform; lane 0 issues.
 struct Ring {
   uint32_t n_iss, n_con;
   int gp, j;
@@ -176,6 +207,25 @@ __device__ __forceinline__ bool spin_ge(const unsigned* addr, unsigned target, i
         return false;
       }
       if (*(volatile int*)status != ERR_NONE) return false;
+    }
+  }
+}
+
+// Bounded mbarrier wait that backs off between polls: a warp waiting for a
+// tile sleeps instead of spinning through issue slots the computing warps need.
+// ~2^31 cycles (about a second) then ERR_TIMEOUT in *status and false.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t* bar, uint32_t parity, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(i < 8 ? 32 : 128);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(status, ERR_TIMEOUT);
+        return false;
+      }
+      if (*(volatile int*)status == ERR_TIMEOUT) return false;
     }
   }
 }
@@ -204,27 +254,30 @@ __device__ __forceinline__ bool grid_sync(const MegaParams& p, unsigned& target,
   return *(volatile int*)flag != 0;
 }
 
-__device__ __forceinline__ void issue_tile(const MegaParams& p, const SDesc& s, int it, int n_slots, const Route* rt,
-                                           uint64_t* bar, uint8_t* dst, uint64_t pol) {
-  if (s.kind == K_ROUTER) {
-    const int items = p.E * p.rt_parts;
+__device__ __forceinline__ void issue_tile(const MegaParams& p, const SDesc& s, int it, int part, int n_slots,
+                                           const Route* rt, uint64_t* bar, uint8_t* dst, uint64_t pol) {
+  if (s.kind == K_ROUTER) {  // piece `it`: columns [part * piece, +piece) of router row e
     const int piece = p.d / p.rt_parts;  // floats
-    uint32_t bytes = 0;
-    for (int i = it; i < items; i += NWS) bytes += (uint32_t)(piece * 4);
-    mbar_arrive_expect_tx(bar, bytes);
-    int jj = 0;
-    for (int i = it; i < items; i += NWS, ++jj) {
-      const int e = i / p.rt_parts, part = i - e * p.rt_parts;
-      bulk_g2s(dst + (int64_t)jj * piece * 4, s.w0 + ((int64_t)e * p.d + (int64_t)part * piece) * 4,
-               (uint32_t)(piece * 4), bar);
-    }
+    const int e = it / p.rt_parts, pt = it - e * p.rt_parts;
+    mbar_arrive_expect_tx(bar, (uint32_t)(piece * 4));
+    bulk_g2s(dst, s.w0 + ((int64_t)e * p.d + (int64_t)pt * piece) * 4, (uint32_t)(piece * 4), bar);
     return;
   }
   const int rb = it / n_slots, si = it - rb * n_slots;
   const int rbase = s.r0 + rb * s.R;
-  const uint32_t bytes = (uint32_t)(min(s.R, s.r1 - rbase) * s.rs);
   const int expert = s.kind == K_ROUTED ? rt->slot_expert[si] : 0;
-  const int64_t eoff = (int64_t)expert * s.es + (int64_t)rbase * s.rs;
+  int64_t eoff = (int64_t)expert * s.es + (int64_t)rbase * s.rs;
+  uint32_t bytes;
+  if (s.H > 1) {  // column groups [g0, g1) of one row
+    const int G = n_groups(s.K);
+    const int g0 = part * s.gpp, g1 = min(G, g0 + s.gpp);
+    const int64_t o0 = group_offset(s.wt, s.K, g0);
+    const int64_t o1 = g1 == G ? dev_row_bytes(s.wt, s.K) : group_offset(s.wt, s.K, g1);
+    eoff += o0;
+    bytes = (uint32_t)(o1 - o0);
+  } else {
+    bytes = (uint32_t)(min(s.R, s.r1 - rbase) * s.rs);
+  }
   mbar_arrive_expect_tx(bar, bytes * s.nmat);
   bulk_g2s_hint(dst, s.w0 + eoff, bytes, bar, pol);
   if (s.nmat == 2) bulk_g2s_hint(dst + (int64_t)s.R * s.rs, s.w1 + eoff, bytes, bar, pol);
@@ -236,23 +289,24 @@ __device__ __forceinline__ void issue_tile(const MegaParams& p, const SDesc& s, 
 __device__ __forceinline__ void issue_ahead(const MegaParams& p, Ring& rg, const Smem& sm, int warp, int lane,
                                             uint64_t pol) {
   const int NP = p.n_layer * SP_N + 1;
-  while (rg.n_iss - rg.n_con < (uint32_t)p.S && rg.gp < NP) {
+  const int limit = *(volatile int*)sm.gp_limit();
+  while (rg.n_iss - rg.n_con < (uint32_t)p.S && rg.gp < NP && rg.gp <= limit) {
     const SDesc s = stream_desc(p, rg.gp);
     int ns = 1;
     if (s.kind == K_ROUTED) {
       if (*(volatile int*)sm.route_layer() != rg.gp / SP_N) break;  // routing of that layer not known yet
       ns = sm.route()->n_slots;
     }
-    const int it = warp + rg.j * NWS;
-    if (it >= n_tiles(p, s, ns)) {
+    const int ju = rg.j / s.H, part = rg.j - ju * s.H;
+    const int u = warp + ju * NWS;
+    if (u >= n_units(p, s, ns)) {
       ++rg.gp;
       rg.j = 0;
       continue;
     }
-    const int slot = (int)(rg.n_iss % (uint32_t)p.S);
+    const int slot = (int)(rg.n_iss & (uint32_t)(p.S - 1));
     if (lane == 0)
-      issue_tile(p, s, it, ns, sm.route(), &sm.full()[warp * p.S + slot],
-                 sm.slot(warp, slot), pol);
+      issue_tile(p, s, u, part, ns, sm.route(), &sm.full()[warp * p.S + slot], sm.slot(warp, slot), pol);
     ++rg.n_iss;
     ++rg.j;
   }
@@ -262,26 +316,9 @@ __device__ __forceinline__ void issue_ahead(const MegaParams& p, Ring& rg, const
 // Let every copy this warp has in flight land (error exit).
 __device__ void drain(const MegaParams& p, Ring& rg, const Smem& sm, int warp) {
   while (rg.n_con < rg.n_iss) {
-    const int slot = (int)(rg.n_con % (uint32_t)p.S);
-    mbar_wait_bounded(&sm.full()[warp * p.S + slot], (rg.n_con / (uint32_t)p.S) & 1, p.status);
+    const int slot = (int)(rg.n_con & (uint32_t)(p.S - 1));
+    mbar_wait_backoff(&sm.full()[warp * p.S + slot], (rg.n_con >> p.S_log2) & 1, p.status);
     ++rg.n_con;
-  }
-}
-
-// One unit dot (32 units per warp, one per lane) for the weight type wt.
-__device__ __forceinline__ float unit_dot_rt(int wt, const uint8_t* wg, const XQ8& x, int ng, int lane) {
-  if (wt == T_Q4_K) {
-    WQ4K w;
-    w.load(wg, ng, lane);
-    return dot_unit_q4k(w, x, lane);
-  } else if (wt == T_Q6_K) {
-    WQ6K w;
-    w.load(wg, ng, lane);
-    return dot_unit_q6k(w, x);
-  } else {
-    WQ80 w;
-    w.load(wg, ng, lane);
-    return dot_unit_q80(w, x);
   }
 }
 
@@ -312,23 +349,83 @@ __device__ __forceinline__ float reduce8m(const float v[8], int lane) {
   return y;
 }
 
+template <int WT>
+__device__ __forceinline__ float unit_dot_t(const uint8_t* wg, const XQ8& x, int ng, int lane) {
+  if constexpr (WT == T_Q4_K) {
+    WQ4K w;
+    w.load(wg, ng, lane);
+    return dot_unit_q4k(w, x, lane);
+  } else if constexpr (WT == T_Q6_K) {
+    WQ6K w;
+    w.load(wg, ng, lane);
+    return dot_unit_q6k(w, x);
+  } else {
+    WQ80 w;
+    w.load(wg, ng, lane);
+    return dot_unit_q80(w, x);
+  }
+}
+
+// The unit dots of one tile for one activation vector xv: value v = rm * Gp +
+// g ((row, matrix) rm, local column group g) lands in pv[v].  One-group rows
+// (the common case) run up to four independent dots in one basic block.
+template <int WT>
+__device__ __forceinline__ void tile_dots(const uint8_t* tile, int64_t rs, int R, int nmat, int RM, int K, int g0,
+                                          int Gp, const uint8_t* xv, float pv[8], int lane) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) pv[j] = 0.0f;
+  const int64_t tbase = group_offset(WT, K, g0);
+  if (Gp == 1) {
+    const int ng = group_units(K, g0);
+    if (lane < ng) {
+      XQ8 xc;
+      xc.load(xv + qact_group_offset(g0), ng, lane);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (q < RM) {
+          const int r = nmat == 2 ? (q >> 1) : q, m = nmat == 2 ? (q & 1) : 0;
+          pv[q] = unit_dot_t<WT>(tile + ((int64_t)m * R + r) * rs, xc, ng, lane);
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int g = 0; g < Gp; ++g) {
+    const int ng = group_units(K, g0 + g);
+    const int64_t goff = group_offset(WT, K, g0 + g) - tbase;
+    float d[2] = {0.0f, 0.0f};
+    if (lane < ng) {
+      XQ8 xc;
+      xc.load(xv + qact_group_offset(g0 + g), ng, lane);
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        if (q < RM) {
+          const int r = nmat == 2 ? (q >> 1) : q, m = nmat == 2 ? (q & 1) : 0;
+          d[q] = unit_dot_t<WT>(tile + ((int64_t)m * R + r) * rs + goff, xc, ng, lane);
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) pv[q] = (q == g) ? d[0] : ((q == Gp + g && RM > 1) ? d[1] : pv[q]);
+  }
+}
+
 // Consume this warp's tiles of one phase (dense or routed): dot every tile
 // row against the phase's activation vectors in xq and store the row sums in
 // acc[((row - r0) * n_pairs + pair) * nmat + m].  After each tile the freed
 // slot is refilled with the warp's next tile of the stream.  One copy of this
 // loop serves every phase (the weight type is a run-time switch per unit dot).
-__device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDesc& s, int wt, int n_slots, int K,
-                        int xq_vec, int by_pair, int n_pairs, int warp, int lane, uint64_t pol) {
+__device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDesc& s, int n_slots, int xq_vec,
+                        int by_pair, int n_pairs, int warp, int lane, uint64_t pol) {
   const Route* rt = sm.route();
+  const int wt = s.wt, K = s.K;
   const int G = n_groups(K);
-  const int nt = n_tiles(p, s, n_slots);
+  const int nu = n_units(p, s, n_slots);
   const int64_t rs = s.rs;
   const int nmat = s.nmat;
-  for (int it = warp; it < nt; it += NWS) {
-    const int slot = (int)(rg.n_con % (uint32_t)p.S);
-    if (!mbar_wait_bounded(&sm.full()[warp * p.S + slot], (rg.n_con / (uint32_t)p.S) & 1, p.status)) return false;
-    const uint8_t* tile = sm.slot(warp, slot);
-    const int rb = it / n_slots, si = it - rb * n_slots;
+  for (int u = warp; u < nu; u += NWS) {
+    const int rb = u / n_slots, si = u - rb * n_slots;
     const int rbase = s.r0 + rb * s.R;
     const int nrows = min(s.R, s.r1 - rbase);
     const int RM = nrows * nmat;
@@ -337,52 +434,42 @@ __device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDe
       pb = rt->slot_off[si];
       pe = rt->slot_off[si + 1];
     }
-    for (int pi = pb; pi < pe; ++pi) {
-      const int pair = s.kind == K_ROUTED ? rt->slot_pairs[pi] : pi;
-      const int vi = by_pair ? pair : (s.kind == K_ROUTED ? pair / p.k : pair);
-      float part[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) part[j] = 0.0f;
-      // value j = rm * G + g ((row, matrix) rm, column group g) lands in part[j]
-      int j = 0;
-      XQ8 xc;
-#pragma unroll 1
-      for (int g = 0; g < G; ++g) {
-        const int ng = group_units(K, g);
-        if (lane < ng) xc.load(sm.xq() + (int64_t)vi * xq_vec + qact_group_offset(g), ng, lane);
-#pragma unroll 1
-        for (int rm = 0; rm < RM; rm += 2) {
-          // two (row, matrix) unit dots per pass: their dp4a chains interleave
-          const int r0 = nmat == 2 ? (rm >> 1) : rm, m0 = nmat == 2 ? (rm & 1) : 0;
-          const int r1 = nmat == 2 ? ((rm + 1) >> 1) : rm + 1, m1 = nmat == 2 ? ((rm + 1) & 1) : 0;
-          float d0 = 0.0f, d1 = 0.0f;
-          if (lane < ng) {
-            d0 = unit_dot_rt(wt, tile + ((int64_t)m0 * s.R + r0) * rs + group_offset(wt, K, g), xc, ng, lane);
-            if (rm + 1 < RM)
-              d1 = unit_dot_rt(wt, tile + ((int64_t)m1 * s.R + r1) * rs + group_offset(wt, K, g), xc, ng, lane);
-          }
-          const int j0 = rm * G + g, j1 = (rm + 1) * G + g;
-#pragma unroll
-          for (int q = 0; q < 8; ++q) part[q] = (q == j0) ? d0 : ((q == j1 && rm + 1 < RM) ? d1 : part[q]);
-        }
-        j += RM;
-      }
-      (void)j;
-      const float sum = reduce8m(part, lane);
-      float tot = 0.0f;
-      for (int g = 0; g < G; ++g) {
-        const int v = lane * G + g;
-        const int src = ((v >> 2) & 1) << 2 | ((v >> 1) & 1) << 3 | (v & 1) << 4;
-        tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sum, src));
-      }
-      if (lane < RM) {
+    for (int part = 0; part < s.H; ++part) {
+      const int slot = (int)(rg.n_con & (uint32_t)(p.S - 1));
+      if (!mbar_wait_backoff(&sm.full()[warp * p.S + slot], (rg.n_con >> p.S_log2) & 1, p.status)) return false;
+      const uint8_t* tile = sm.slot(warp, slot);
+      // this tile's column groups [g0, g0 + Gp); a cut row (H > 1) has one row
+      const int g0 = part * s.gpp, Gp = min(G - g0, s.gpp);
+      for (int pi = pb; pi < pe; ++pi) {
+        const int pair = s.kind == K_ROUTED ? rt->slot_pairs[pi] : pi;
+        const int vi = by_pair ? pair : (s.kind == K_ROUTED ? pair / p.k : pair);
+        const uint8_t* xv = sm.xq() + (int64_t)vi * xq_vec;
+        float pv[8];
+        // the weight type is fixed for the whole tile: one straight-line dot
+        // block per type, so independent unit dots interleave
+        if (wt == T_Q4_K)
+          tile_dots<T_Q4_K>(tile, rs, s.R, nmat, RM, K, g0, Gp, xv, pv, lane);
+        else if (wt == T_Q6_K)
+          tile_dots<T_Q6_K>(tile, rs, s.R, nmat, RM, K, g0, Gp, xv, pv, lane);
+        else
+          tile_dots<T_Q8_0>(tile, rs, s.R, nmat, RM, K, g0, Gp, xv, pv, lane);
+        const float sum = reduce8m(pv, lane);
+        // (row, matrix) rm = lane adds its group sums in column order; a cut
+        // row continues the sum its previous tile left in acc
         const int r = nmat == 2 ? (lane >> 1) : lane, m = nmat == 2 ? (lane & 1) : 0;
-        sm.acc()[((rbase - s.r0 + r) * n_pairs + pair) * nmat + m] = tot;
+        float* ap = &sm.acc()[((rbase - s.r0 + r) * n_pairs + pair) * nmat + m];
+        float tot = (part > 0 && lane < RM) ? *ap : 0.0f;
+        for (int g = 0; g < Gp; ++g) {
+          const int v = (lane * Gp + g) & 7;
+          const int src = ((v >> 2) & 1) << 2 | ((v >> 1) & 1) << 3 | (v & 1) << 4;
+          tot = __fadd_rn(tot, __shfl_sync(0xffffffffu, sum, src));
+        }
+        if (lane < RM) *ap = tot;
       }
+      __syncwarp();
+      ++rg.n_con;
+      issue_ahead(p, rg, sm, warp, lane, pol);
     }
-    __syncwarp();
-    ++rg.n_con;
-    issue_ahead(p, rg, sm, warp, lane, pol);
   }
   return true;
 }
@@ -391,31 +478,19 @@ __device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDe
 // activation type `act` into xq (vector stride xq_vec), as ggml: squares
 // summed in double, mean = (float)(sum / K), scale = 1/sqrtf(mean + eps),
 // y = (x * scale) * w.  norm_w == null: no norm.  The source is global memory
-// written by other CTAs (read through L2), or with `emb` set the token
-// embedding rows, dequantized on the fly.  xn (optional): the normalised
-// values in shared memory [b][K].
-__device__ __noinline__ void emb_load8(int type, const uint8_t* row, int c0, float* v) {
-#pragma unroll 1
-  for (int i = 0; i < 8; ++i) v[i] = gguf_dequant_one(type, row, c0 + i);
-}
-
-__device__ void pro_quant(const MegaParams& p, const float* src, bool emb, const int* toks, const float* norm_w,
-                          int K, int act, uint8_t* xq, int xq_vec, float* xn, double* red) {
+// written by other CTAs (read through L2, one round trip for x and the norm
+// weight).  xn (optional): the normalised values in shared memory [b][K].
+__device__ void pro_quant(const MegaParams& p, const float* src, const float* norm_w, int K, int act, uint8_t* xq,
+                          int xq_vec, float* xn, double* red) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nblk = K / QK_K;
-  const int64_t erb = emb ? dev_gguf_row_bytes(p.t_embd, p.d) : 0;
   for (int t = 0; t < p.b; ++t) {
     const float* x = src + (int64_t)t * K;
-    const uint8_t* erow = emb ? p.tok_embd + (int64_t)toks[t] * erb : nullptr;
     auto load8 = [&](int blk, float v[8]) {
       const int c0 = blk * QK_K + lane * 8;
-      if (emb) {
-        emb_load8(p.t_embd, erow, c0, v);
-      } else {
-        const float4 a = __ldcg(reinterpret_cast<const float4*>(x + c0));
-        const float4 b = __ldcg(reinterpret_cast<const float4*>(x + c0 + 4));
-        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-      }
+      const float4 a = __ldcg(reinterpret_cast<const float4*>(x + c0));
+      const float4 b = __ldcg(reinterpret_cast<const float4*>(x + c0 + 4));
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
     };
     float scale = 1.0f;
     if (norm_w) {
@@ -438,7 +513,7 @@ __device__ void pro_quant(const MegaParams& p, const float* src, bool emb, const
     uint8_t* qa = xq + (int64_t)t * xq_vec;
     for (int blk = warp; blk < nblk; blk += NWS) {
       float v[8];
-      load8(blk, v);
+      load8(blk, v);  // an L2 hit: the first pass brought the lines in
       if (norm_w) {
         const float4 wa = __ldg(reinterpret_cast<const float4*>(norm_w + blk * QK_K + lane * 8));
         const float4 wb = __ldg(reinterpret_cast<const float4*>(norm_w + blk * QK_K + lane * 8 + 4));
@@ -547,7 +622,7 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
     }
     for (int i = tid; i < gqa * hd; i += NT) qs[i] = __ldcg(p.q + (int64_t)a.t * p.nq + (int64_t)a.h * gqa * hd + i);
     __syncthreads();
-    if (!mbar_wait_bounded(sm.kbar(), kph & 1, p.status)) return false;
+    if (!mbar_wait_backoff(sm.kbar(), kph & 1, p.status)) return false;
     ++kph;
     // y[g][j]: one (position, head) dot per thread, four double chains, the
     // dimensions walked from a per-thread rotation (fewer bank conflicts)
@@ -648,7 +723,7 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
       ps[g * CH + jj] = __fmul_rn(sfk_expf(__fsub_rn(y, st[2 * g])), st[2 * g + 1]);
     }
     __syncthreads();
-    if (!mbar_wait_bounded(sm.vbar(), vph & 1, p.status)) return false;
+    if (!mbar_wait_backoff(sm.vbar(), vph & 1, p.status)) return false;
     ++vph;
     double* op = p.att_opart + (((int64_t)a.t * p.n_head_kv + a.h) * p.att_nc + a.c) * gqa * hd;
     for (int w = tid; w < gqa * hd; w += NT) {
@@ -690,22 +765,21 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
 // follows directly.  The lm_head step closes the launch.
 enum : int { ST_QKV = 0, ST_ATT = 1, ST_O = 2, ST_RT = 3, ST_GU = 4, ST_DN = 5, ST_N = 6 };
 
-// The F32 router rows of this warp (its ring slot) against the normalised
-// inputs xn [b][d]: double partial logits part[t * items + i].
+// The F32 router pieces of this warp (one per ring slot, in stream order)
+// against the normalised inputs xn [b][d]: double partial logits
+// part[t * items + i].
 __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, const float* xn, double* part, int warp,
                                 int lane, uint64_t pol) {
   const int items = p.E * p.rt_parts, piece = p.d / p.rt_parts;
-  const int slot = (int)(rg.n_con % (uint32_t)p.S);
-  if (!mbar_wait_bounded(&sm.full()[warp * p.S + slot], (rg.n_con / (uint32_t)p.S) & 1, p.status)) return false;
-  const float* wt = reinterpret_cast<const float*>(sm.slot(warp, slot));
-  int jj = 0;
-  for (int i = warp; i < items; i += NWS, ++jj) {
+  for (int i = warp; i < items; i += NWS) {
+    const int slot = (int)(rg.n_con & (uint32_t)(p.S - 1));
+    if (!mbar_wait_backoff(&sm.full()[warp * p.S + slot], (rg.n_con >> p.S_log2) & 1, p.status)) return false;
+    const float* ws = reinterpret_cast<const float*>(sm.slot(warp, slot));
     const int pt = i % p.rt_parts;
     for (int t = 0; t < p.b; ++t) {
       // logit = sum_c (double)(w_r[e][c] * xn[c]) (ggml's F32 mul_mat): four
-      // chains per lane; the parts of a row are added in order afterwards
+      // chains per lane; the pieces of a row are added in order afterwards
       const float* xs = xn + (int64_t)t * p.d + pt * piece;
-      const float* ws = wt + (int64_t)jj * piece;
       double a0 = 0.0, a1 = 0.0, a2 = 0.0, a3 = 0.0;
       for (int c = lane * 4; c < piece; c += 128) {
         const float4 w4 = *reinterpret_cast<const float4*>(ws + c);
@@ -718,10 +792,10 @@ __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, c
       const double a = warp_sum_d((a0 + a1) + (a2 + a3));
       if (lane == 0) part[t * items + i] = a;
     }
+    __syncwarp();
+    ++rg.n_con;
+    issue_ahead(p, rg, sm, warp, lane, pol);
   }
-  __syncwarp();
-  ++rg.n_con;
-  issue_ahead(p, rg, sm, warp, lane, pol);
   return true;
 }
 
@@ -853,9 +927,8 @@ __device__ bool route_layer(const MegaParams& p, int l, Ring& rg, const Smem& sm
                             uint64_t pol) {
   const int tid = threadIdx.x;
   double* part = reinterpret_cast<double*>(sm.probs());
-  const SDesc s = stream_desc(p, l * SP_N + SP_RT);
   bool ok = true;
-  if (warp < n_tiles(p, s, 1) && !router_partials(p, rg, sm, xn, part, warp, lane, pol)) ok = false;
+  if (!router_partials(p, rg, sm, xn, part, warp, lane, pol)) ok = false;
   __syncthreads();
   if (!ok) return false;
   const int items = p.E * p.rt_parts;
@@ -896,6 +969,12 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
   const int cta = blockIdx.x;
   const uint64_t pol = l2_evict_first_policy();
 
+  {  // the per-layer weight pointers, read on every tile issue, live in shared memory
+    const int n = p.n_layer * (int)(sizeof(MegaLayer) / 8);
+    unsigned long long* dst = reinterpret_cast<unsigned long long*>(mega_smem + p.off_layers);
+    const unsigned long long* src = reinterpret_cast<const unsigned long long*>(p.layers);
+    for (int i = tid; i < n; i += NT) dst[i] = __ldg(src + i);
+  }
   if (tid == 0) {
     for (int i = 0; i < NWS * p.S; ++i) mbar_init(&sm.full()[i], 1);
     mbar_init(sm.pro_bar(), 1);
@@ -903,6 +982,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     mbar_init(sm.vbar(), 1);
     fence_mbar_init();
     *sm.route_layer() = -1;
+    *sm.gp_limit() = p.lookahead;  // the first step streams QKV of layer 0
   }
   // tokens and positions of the step (the embed kernel's duties)
   if (tid < p.b) {
@@ -928,21 +1008,38 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
   __syncthreads();
   Ring rg{0u, 0u, 0, 0};
   issue_ahead(p, rg, sm, warp, lane, pol);  // the first tiles go out at once
-  if (cta == 0) {  // the embedding rows (layer 0's residual)
+  unsigned target = 0;
+  {  // the embedding rows (ggml_get_rows, engine.cpp:2708-2723), a column slice per CTA
     const int64_t erb = dev_gguf_row_bytes(p.t_embd, p.d);
+    const int per = (p.d + gridDim.x - 1) / gridDim.x;
+    const int c0 = cta * per, c1 = min(p.d, c0 + per);
     for (int t = 0; t < p.b; ++t)
-      for (int i = tid; i < p.d; i += NT)
+      for (int i = c0 + tid; i < c1; i += NT)
         p.x[(int64_t)t * p.d + i] = gguf_dequant_one(p.t_embd, p.tok_embd + (int64_t)toks[t] * erb, i);
   }
-  unsigned target = 0;
   uint32_t pro_ph = 0, kph = 0, vph = 0;
   const int n_steps = p.n_layer * ST_N + 1;
   const int np = p.b * p.k;
-  bool ok = true;
+  bool ok = grid_sync(p, target, flag);  // x holds the embeddings
+  if (cta == 0 && tid < p.b) {  // every CTA has read the argmax keys by now
+    p.argmax_key[tid] = 0ull;
+    p.pos_cur[tid] = pos_s[tid];
+    if (p.pos_state) p.pos_state[tid] = pos_s[tid] + 1;
+    p.tok_hist[tid] = toks[tid];
+  }
   for (int gs = 0; gs < n_steps && ok; ++gs) {
     const int l = gs / ST_N;
     const int st = gs == n_steps - 1 ? -1 : gs - l * ST_N;  // -1: lm_head
-    const MegaLayer* LW = p.layers + (l < p.n_layer ? l : 0);
+    const MegaLayer* LW = reinterpret_cast<const MegaLayer*>(mega_smem + p.off_layers) + (l < p.n_layer ? l : 0);
+    {  // how far the rings may run ahead: this step's streamed phase + lookahead
+      const int cur = st == -1 ? SP_N * p.n_layer
+                               : l * SP_N + (st <= ST_QKV ? SP_QKV : st <= ST_O ? SP_O : st == ST_RT ? SP_RT
+                                                                   : st == ST_GU ? SP_GU : SP_DN);
+      __syncthreads();
+      if (tid == 0) *sm.gp_limit() = cur + p.lookahead;
+      __syncthreads();
+      issue_ahead(p, rg, sm, warp, lane, pol);
+    }
     if (st == ST_ATT) {  // attention over the paged KV (engine.cpp:1751-1761)
       ok = attention(p, l, sm, pos_s, kph, vph) && grid_sync(p, target, flag);
       continue;
@@ -958,7 +1055,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
         for (int pr = 0; pr < np; ++pr)
           bulk_g2s(sm.xq() + (int64_t)pr * xv, p.hq + (int64_t)pr * xv, (uint32_t)xv, sm.pro_bar());
       }
-      if (!mbar_wait_bounded(sm.pro_bar(), pro_ph & 1, p.status)) { ok = false; break; }
+      if (!mbar_wait_backoff(sm.pro_bar(), pro_ph & 1, p.status)) { ok = false; break; }
       ++pro_ph;
     } else if (st != ST_GU) {
       // attn_norm (QKV), none (O), ffn_norm (routing), output_norm (lm_head)
@@ -966,8 +1063,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
       const float* nw = st == ST_QKV ? LW->attn_norm : (st == ST_RT ? LW->ffn_norm : (st == -1 ? p.out_norm : nullptr));
       const int K = st == ST_O ? p.nq : p.d;
       const int act = st == ST_RT ? p.a_gu : (st == -1 ? p.a_out : p.a_attn);
-      pro_quant(p, src, st == ST_QKV && l == 0, toks, nw, K, act, sm.xq(), (int)qact_bytes(K),
-                st == ST_RT ? xn : nullptr, sm.red());
+      pro_quant(p, src, nw, K, act, sm.xq(), (int)qact_bytes(K), st == ST_RT ? xn : nullptr, sm.red());
     }
     if (st == ST_RT) {
       if (!route_layer(p, l, rg, sm, xn, warp, lane, pol)) { ok = false; break; }
@@ -978,10 +1074,8 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
                             : l * SP_N + (st == ST_QKV ? SP_QKV : st == ST_O ? SP_O : st == ST_GU ? SP_GU : SP_DN);
     const SDesc s = stream_desc(p, sp);
     {
-      const int wt = st == -1 ? p.t_out : (st == ST_GU ? p.t_gu : (st == ST_DN ? p.t_down : p.t_attn));
-      const int K = st == ST_O ? p.nq : (st == ST_DN ? p.F : p.d);
       const bool routed = st == ST_GU || st == ST_DN;
-      if (!consume(p, rg, sm, s, wt, routed ? sm.route()->n_slots : 1, K, (int)qact_bytes(K), st == ST_DN ? 1 : 0,
+      if (!consume(p, rg, sm, s, routed ? sm.route()->n_slots : 1, (int)qact_bytes(s.K), st == ST_DN ? 1 : 0,
                    routed ? np : p.b, warp, lane, pol)) {
         ok = false;
         break;
@@ -1016,12 +1110,6 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
       break;  // the last step: no barrier
     }
     if (!grid_sync(p, target, flag)) { ok = false; break; }
-    if (gs == 0 && cta == 0 && tid < p.b) {  // every CTA has read the keys by now
-      p.argmax_key[tid] = 0ull;
-      p.pos_cur[tid] = pos_s[tid];
-      if (p.pos_state) p.pos_state[tid] = pos_s[tid] + 1;
-      p.tok_hist[tid] = toks[tid];
-    }
   }
   if (!ok) {  // let this warp's copies land, then leave; the host clears the counters
     drain(p, rg, sm, warp);

@@ -19,6 +19,8 @@ constexpr int MEGA_MAXS = 4;        // ring slots per warp (at most)
 constexpr int MEGA_MAXE = 64;       // experts the kernel routes itself
 constexpr int MEGA_MAXGQA = 16;     // query heads per kv head
 constexpr int MEGA_RED = 128;       // doubles of reduction scratch
+// weight phases of the tile plan
+enum : int { MEGA_PK_QKV = 0, MEGA_PK_O = 1, MEGA_PK_GU = 2, MEGA_PK_DN = 3, MEGA_PK_OUT = 4 };
 
 // Per-layer weights (device array, read-only).
 struct MegaLayer {
@@ -43,12 +45,16 @@ struct MegaParams {
   int64_t rs_attn, rs_o, rs_gu, rs_down, rs_out;  // device row strides
   // plan (host): ring, tile rows, rows per CTA, shared-memory offsets
   int S, slot;
-  int R_qkv, R_o, R_gu, R_down, R_out;
+  // per weight phase (MEGA_PK_*): rows per tile R; a row longer than a slot
+  // is cut into H tiles of gpp column groups each (then R = 1)
+  int R[5], H[5], gpp[5];
   int rpc_qkv, rpc_o, rpc_gu, rpc_down, rpc_out;
   int rt_parts;       // router: parts per expert row (items = E * rt_parts)
   int att_ch;         // attention positions per work item (multiple of 16)
   int att_nc;         // chunks per (sequence, kv head) at n_ctx
-  int off_ring, off_xq, off_acc, off_route, off_red, off_probs, off_att, off_misc, smem;
+  int S_log2;         // S = 1 << S_log2 ring slots per warp
+  int lookahead;      // streamed phases a warp's ring may run ahead of the CTA's current step
+  int off_ring, off_xq, off_acc, off_route, off_red, off_probs, off_att, off_misc, off_layers, smem;
   int xq_bytes;       // bytes of the xq region (activations; attention staging)
   // embedding / head
   const uint8_t* tok_embd;  // GGUF layout
