@@ -79,6 +79,7 @@ def lib():
             "sfo_seq_create": (P, [P]),
             "sfo_seq_free": (None, [P]),
             "sfo_seq_reset": (None, [P]),
+            "sfo_seq_fill_kv": (I, [P, I, U64]),
             "sfo_forward": (C.c_int32, [P, P, C.c_int32, C.c_int32, P]),
             "sfo_seq_hidden": (P, [P, I]),
             "sfo_seq_ids": (P, [P, I]),
@@ -291,6 +292,11 @@ class Seq:
 
     def reset(self):
         lib().sfo_seq_reset(self.h)
+
+    def fill_kv(self, n_pos: int, seed: int = 0) -> None:
+        """Positions 0..n_pos-1 of the KV cache get seeded values (a stand-in
+        for a fed prompt, for timing decode steps at a long context)."""
+        assert lib().sfo_seq_fill_kv(self.h, int(n_pos), C.c_uint64(seed)) == 0
 
     def forward(self, token: int, pos: int) -> tuple[int, np.ndarray]:
         logits = np.empty(self.m.cfg.n_vocab, np.float32)

@@ -1021,6 +1021,26 @@ void sfo_seq_reset(sfo_seq *s) {
     memset(s->v_cache, 0, kv * sizeof(float));
 }
 
+/* Timing support: positions 0..n_pos-1 of every layer's K/V cache receive
+ * seeded pseudo-random values in [-1, 1) (rounded through f16 in the f16-KV
+ * mode), as if a prompt had been fed, so a decode step at position n_pos
+ * attends over a full context without running the prompt. */
+int sfo_seq_fill_kv(sfo_seq *s, int n_pos, uint64_t seed) {
+    const sfo_hparams *hp = &s->m->hp;
+    if (n_pos < 0 || n_pos > hp->n_ctx) return -1;
+    const size_t hd = (size_t)hp_head_dim(hp);
+    const size_t row = (size_t)hp->n_head_kv * hd, per_layer = (size_t)hp->n_ctx * row;
+    for (int il = 0; il < hp->n_layer; ++il)
+        for (size_t i = 0; i < (size_t)n_pos * row; ++i) {
+            const uint64_t z = splitmix64(seed ^ (((uint64_t)il << 40) + i));
+            const float a = (float)((double)(z >> 40) / (double)(1ull << 24) * 2.0 - 1.0);
+            const float b = (float)((double)(z & 0xFFFFFFull) / (double)(1ull << 24) * 2.0 - 1.0);
+            s->k_cache[(size_t)il * per_layer + i] = hp->kv_f16 ? sfo_fp16_to_fp32(sfo_fp32_to_fp16(a)) : a;
+            s->v_cache[(size_t)il * per_layer + i] = hp->kv_f16 ? sfo_fp16_to_fp32(sfo_fp32_to_fp16(b)) : b;
+        }
+    return 0;
+}
+
 const float *sfo_seq_hidden(const sfo_seq *s, int il) { return s->hidden + (size_t)il * s->m->hp.n_embd; }
 const int32_t *sfo_seq_ids(const sfo_seq *s, int il) { return s->ids + (size_t)il * s->m->hp.n_expert_used; }
 const float *sfo_seq_debug(const sfo_seq *s, int il, int which) {

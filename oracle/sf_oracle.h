@@ -138,6 +138,9 @@ void       sfo_seq_free(sfo_seq *s);
 void       sfo_seq_reset(sfo_seq *s);
 /* one token at `pos` (causal over 0..pos); logits [n_vocab]; returns argmax or <0 */
 int32_t    sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t pos, float *logits);
+/* timing support: positions 0..n_pos-1 of the KV cache filled with seeded
+ * values in [-1, 1) (a stand-in for a fed prompt); returns 0 or -1 */
+int        sfo_seq_fill_kv(sfo_seq *s, int n_pos, uint64_t seed);
 /* per-layer hooks for tests: hidden state after layer `il` of the last forward */
 const float *sfo_seq_hidden(const sfo_seq *s, int il);
 const int32_t *sfo_seq_ids(const sfo_seq *s, int il);

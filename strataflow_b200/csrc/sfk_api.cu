@@ -716,7 +716,7 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   // least one piece per warp when the columns allow it; pieces are cut
   // further below until one fits a slot (checked once the slot is known).
   int parts = 1;
-  while (E * parts < MEGA_NWS && d % (parts * 2 * 128) == 0) parts *= 2;
+  while (E * parts < MEGA_NC && d % (parts * 2 * 128) == 0) parts *= 2;
   if (d % (parts * 128)) return false;
   // shared memory
   auto al = [](int64_t v, int a) { return (v + a - 1) / a * a; };
@@ -732,12 +732,12 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   acc = std::max<int64_t>(acc, (int64_t)p.rpc_down * b * k);
   acc = std::max<int64_t>(acc, (int64_t)p.rpc_out * b);
   acc = al(acc * 4, 16);
-  const int64_t route = al(sizeof(Route), 16);
+  const int64_t route = al(2 * sizeof(Route), 16);  // double-buffered by layer parity
   const int64_t red = MEGA_RED * 8;
   const int64_t probs = al((int64_t)b * E * (d / 128) * 8, 16);  // partial logits, any piece count
   const int64_t att = al((int64_t)gqa * hd * 4 + 2ll * gqa * MEGA_CH * 4 + gqa * 8, 16);
   const int64_t misc = al((2 * MAXB + 4) * 4, 16);  // tokens | positions | routed layer | flag | phase limit
-  const int64_t bars = al(MEGA_NWS * MEGA_MAXS * 8 + 3 * 8, 128);
+  const int64_t bars = al(2 * MEGA_NWS * MEGA_MAXS * 8 + 3 * 8, 128);  // full | empty slot barriers, prologue barriers
   const int64_t layers = al((int64_t)hp.n_layer * sizeof(MegaLayer), 16);
   const int64_t fixed = bars + xq + acc + route + red + probs + att + misc + layers;
   // ring slots per warp, a power of two (SFK_MEGA_STAGES / SFK_MEGA_SLOT
@@ -748,7 +748,7 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   p.S_log2 = S == 1 ? 0 : (S == 2 ? 1 : 2);
   p.lookahead = 1 << 20;  // unlimited: rings run ahead across every phase boundary
   if (const char* v = getenv("SFK_MEGA_LOOKAHEAD")) p.lookahead = atoi(v);
-  int64_t slot = (SMEM_LIMIT - fixed) / (MEGA_NWS * S);
+  int64_t slot = (SMEM_LIMIT - fixed) / (MEGA_NC * S);
   slot = std::min<int64_t>(slot, 32 * 1024) / 128 * 128;
   if (const char* v = getenv("SFK_MEGA_SLOT")) slot = std::min<int64_t>(slot, atoi(v) / 128 * 128);
   if (slot <= 0) return false;
@@ -786,7 +786,7 @@ bool mega_params(const sfk_engine* e, int b, bool greedy, MegaParams* out, int* 
   p.att_ch = MEGA_CH;
   p.att_nc = e->att_nc;
   p.off_ring = (int)bars;
-  p.off_xq = p.off_ring + (int)(MEGA_NWS * S * slot);
+  p.off_xq = p.off_ring + (int)(MEGA_NC * S * slot);
   p.off_acc = p.off_xq + (int)xq;
   p.off_route = p.off_acc + (int)acc;
   p.off_red = p.off_route + (int)route;
@@ -1154,13 +1154,14 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
       e->fused_route = false;
   }
   {
-    // the persistent step kernel: single-GPU engines whose types, expert
-    // count and GQA group it covers (SFK_PERSISTENT=0 keeps the launch chain)
+    // the persistent step kernel (SFK_PERSISTENT=1): single-GPU engines whose
+    // types, expert count and GQA group it covers; by default a step runs as
+    // the launch chain, which is faster at the Mixtral shape today
     const char* pv = getenv("SFK_PERSISTENT");
     const int gqa = hp->n_head / hp->n_head_kv;
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-    if (!(pv && atoi(pv) == 0) && coop && e->ep_size == 1 && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
+    if (pv && atoi(pv) == 1 && coop && e->ep_size == 1 && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
         (gqa & (gqa - 1)) == 0 &&
         mega_types_supported(hp->type_attn, hp->type_ffn_gu, hp->type_ffn_down, hp->type_output)) {
       const int Hq = hp->n_head, Hkv = hp->n_head_kv;

@@ -46,6 +46,10 @@ namespace {
 
 constexpr int NWS = MEGA_NWS;
 constexpr int NT = NWS * 32;
+constexpr int NC = NWS - 1;   // consumer warps; warp NC (the producer) issues every weight tile
+constexpr int NCT = NC * 32;  // consumer threads
+// the consumer warps' CTA barrier (the producer warp never joins it)
+__device__ __forceinline__ void csync() { asm volatile("bar.sync 1, %0;" ::"n"(NCT) : "memory"); }
 
 // streamed phases of a layer (attention streams no weights)
 enum : int { SP_QKV = 0, SP_O = 1, SP_RT = 2, SP_GU = 3, SP_DN = 4, SP_N = 5 };
@@ -151,7 +155,7 @@ __device__ __forceinline__ SDesc stream_desc(const MegaParams& p, int gp) {
 }
 
 // Work units of a phase in this CTA: row blocks (x routed experts), or the
-// router's row pieces (every CTA takes all of them).  Unit u belongs to warp u % NWS and streams as H
+// router's row pieces (every CTA takes all of them).  Unit u belongs to consumer warp u % NC and streams as H
 // consecutive tiles (column-group ranges of its row when a row is longer than
 // a ring slot, else the whole row block).
 __device__ __forceinline__ int n_units(const MegaParams& p, const SDesc& s, int n_slots) {
@@ -165,8 +169,10 @@ __device__ __forceinline__ int n_units(const MegaParams& p, const SDesc& s, int 
 struct Smem {
   const MegaParams& p;
   __device__ explicit Smem(const MegaParams& pp) : p(pp) {}
-  __device__ uint64_t* full() const { return reinterpret_cast<uint64_t*>(mega_smem); }  // [NWS][S]
-  __device__ uint64_t* pro_bar() const { return reinterpret_cast<uint64_t*>(mega_smem) + NWS * MEGA_MAXS; }
+  // consumer warp c's ring slot s: full[c * S + s] (tile landed), empty[c * S + s] (slot released)
+  __device__ uint64_t* full() const { return reinterpret_cast<uint64_t*>(mega_smem); }
+  __device__ uint64_t* empty() const { return reinterpret_cast<uint64_t*>(mega_smem) + NWS * MEGA_MAXS; }
+  __device__ uint64_t* pro_bar() const { return reinterpret_cast<uint64_t*>(mega_smem) + 2 * NWS * MEGA_MAXS; }
   __device__ uint64_t* kbar() const { return pro_bar() + 1; }
   __device__ uint64_t* vbar() const { return pro_bar() + 2; }
   __device__ uint8_t* slot(int warp, int s) const {
@@ -174,23 +180,22 @@ struct Smem {
   }
   __device__ uint8_t* xq() const { return mega_smem + p.off_xq; }
   __device__ float* acc() const { return reinterpret_cast<float*>(mega_smem + p.off_acc); }
-  __device__ Route* route() const { return reinterpret_cast<Route*>(mega_smem + p.off_route); }
+  // the routing of layer l lives in buffer l & 1 (the producer may still read a
+  // layer's routing while the consumers route the next one)
+  __device__ Route* route(int l) const { return reinterpret_cast<Route*>(mega_smem + p.off_route) + (l & 1); }
   __device__ double* red() const { return reinterpret_cast<double*>(mega_smem + p.off_red); }
   __device__ float* probs() const { return reinterpret_cast<float*>(mega_smem + p.off_probs); }
   __device__ uint8_t* att() const { return mega_smem + p.off_att; }
   __device__ int* toks() const { return reinterpret_cast<int*>(mega_smem + p.off_misc); }
   __device__ int* pos() const { return toks() + MAXB; }
-  __device__ int* route_layer() const { return toks() + 2 * MAXB; }
-  __device__ int* flag() const { return toks() + 2 * MAXB + 1; }
-  __device__ int* gp_limit() const { return toks() + 2 * MAXB + 2; }  // last streamed phase a ring may issue
+  __device__ int* route_layer(int l) const { return toks() + 2 * MAXB + (l & 1); }  // layer routed into buffer l & 1
+  __device__ int* flag() const { return toks() + 2 * MAXB + 2; }
+  __device__ int* gp_limit() const { return toks() + 2 * MAXB + 3; }  // last streamed phase the producer may issue
 };
 
-// The issue side of a warp's ring: the next tile (phase gp, this warp's j-th
-// tile of the phase: unit warp + (j / H) * NWS, part j % H) and the counts of
-// tiles issued and consumed.  Warp-uniform; lane 0 issues.
+// A consumer warp's count of the tiles it has consumed (its ring position).
 struct Ring {
-  uint32_t n_iss, n_con;
-  int gp, j;
+  uint32_t n_con;
 };
 
 __device__ __forceinline__ bool spin_ge(const unsigned* addr, unsigned target, int* status) {
@@ -240,7 +245,7 @@ __device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.p
 // Grid barrier: every CTA arrives once; returns false when the step failed
 // (a bounded wait ran out or a CTA reported an error).
 __device__ __forceinline__ bool grid_sync(const MegaParams& p, unsigned& target, int* flag) {
-  __syncthreads();
+  csync();
   target += gridDim.x;
   if (threadIdx.x == 0) {
     __threadfence();
@@ -250,7 +255,7 @@ __device__ __forceinline__ bool grid_sync(const MegaParams& p, unsigned& target,
     fence_proxy_async_global();  // bulk copies after the barrier read what other CTAs stored before it
     *flag = ok && *(volatile int*)p.status == ERR_NONE;
   }
-  __syncthreads();
+  csync();
   return *(volatile int*)flag != 0;
 }
 
@@ -283,43 +288,78 @@ __device__ __forceinline__ void issue_tile(const MegaParams& p, const SDesc& s, 
   if (s.nmat == 2) bulk_g2s_hint(dst + (int64_t)s.R * s.rs, s.w1 + eoff, bytes, bar, pol);
 }
 
-// Fill this warp's free ring slots with its next tiles, across phases, until
-// the ring is full, the stream ends, or the next tile is a routed tile of a
-// layer whose routing is not known yet.
-__device__ __forceinline__ void issue_ahead(const MegaParams& p, Ring& rg, const Smem& sm, int warp, int lane,
-                                            uint64_t pol) {
-  const int NP = p.n_layer * SP_N + 1;
-  const int limit = *(volatile int*)sm.gp_limit();
-  while (rg.n_iss - rg.n_con < (uint32_t)p.S && rg.gp < NP && rg.gp <= limit) {
-    const SDesc s = stream_desc(p, rg.gp);
-    int ns = 1;
-    if (s.kind == K_ROUTED) {
-      if (*(volatile int*)sm.route_layer() != rg.gp / SP_N) break;  // routing of that layer not known yet
-      ns = sm.route()->n_slots;
-    }
-    const int ju = rg.j / s.H, part = rg.j - ju * s.H;
-    const int u = warp + ju * NWS;
-    if (u >= n_units(p, s, ns)) {
-      ++rg.gp;
-      rg.j = 0;
-      continue;
-    }
-    const int slot = (int)(rg.n_iss & (uint32_t)(p.S - 1));
-    if (lane == 0)
-      issue_tile(p, s, u, part, ns, sm.route(), &sm.full()[warp * p.S + slot], sm.slot(warp, slot), pol);
-    ++rg.n_iss;
-    ++rg.j;
-  }
-  __syncwarp();
+__device__ __forceinline__ bool mbar_test(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
 }
 
-// Let every copy this warp has in flight land (error exit).
-__device__ void drain(const MegaParams& p, Ring& rg, const Smem& sm, int warp) {
-  while (rg.n_con < rg.n_iss) {
-    const int slot = (int)(rg.n_con & (uint32_t)(p.S - 1));
-    mbar_wait_backoff(&sm.full()[warp * p.S + slot], (rg.n_con >> p.S_log2) & 1, p.status);
-    ++rg.n_con;
+// The producer warp.  Lane c < NC feeds consumer warp c: it walks that warp's
+// tiles in stream order (phase gp, the warp's j-th tile of the phase: unit
+// c + (j / H) * NC, part j % H) and issues each tile's bulk copies into the
+// warp's next ring slot as soon as the warp has released it (empty barrier),
+// running ahead across phase boundaries up to the CTA's phase limit; routed
+// tiles wait until their layer's routing is in shared memory.  The lanes work
+// independently, so one slow consumer does not hold up the others' copies.
+// Returns once every tile of the step is issued (or the step failed), after
+// letting its last copies land.
+__device__ void producer(const MegaParams& p, const Smem& sm, int lane) {
+  const int NP = p.n_layer * SP_N + 1;
+  const uint64_t pol = l2_evict_first_policy();
+  const int c = lane;
+  uint32_t n_iss = 0;
+  int gp = c < NC ? 0 : NP, j = 0;
+  const long long t0 = clock64();
+  int idle = 0;
+  while (true) {
+    bool did = false;
+    if (gp < NP && gp <= *(volatile int*)sm.gp_limit()) {
+      const int slot = (int)(n_iss & (uint32_t)(p.S - 1));
+      // the slot's previous tile (n_iss - S) must have been consumed
+      const bool free_slot = n_iss < (uint32_t)p.S || mbar_test(&sm.empty()[c * p.S + slot], ((n_iss >> p.S_log2) + 1) & 1);
+      if (free_slot) {
+        const SDesc s = stream_desc(p, gp);
+        const int l = gp / SP_N;
+        int ns = 1;
+        bool ready = true;
+        if (s.kind == K_ROUTED) {
+          ready = *(volatile int*)sm.route_layer(l) == l;  // routing of that layer known
+          if (ready) ns = sm.route(l)->n_slots;
+        }
+        if (ready) {
+          const int ju = j / s.H, part = j - ju * s.H;
+          const int u = c + ju * NC;
+          if (u >= n_units(p, s, ns)) {
+            ++gp;
+            j = 0;
+            did = true;  // progress: look again at once
+          } else {
+            issue_tile(p, s, u, part, ns, sm.route(l), &sm.full()[c * p.S + slot], sm.slot(c, slot), pol);
+            ++n_iss;
+            ++j;
+            did = true;
+          }
+        }
+      }
+    }
+    const unsigned any = __ballot_sync(0xffffffffu, did);
+    const unsigned live = __ballot_sync(0xffffffffu, gp < NP);
+    if (!live) break;
+    if (!any) {
+      if ((++idle & 63) == 0) {
+        if (*(volatile int*)p.status != ERR_NONE) break;  // the step failed: stop issuing
+        if (clock64() - t0 > (1ll << 33)) break;          // far beyond any step (bounded loop)
+      }
+      __nanosleep(64);
+    }
   }
+  // let this lane's copies in flight land before the CTA may exit
+  for (uint32_t k = n_iss > (uint32_t)p.S ? n_iss - p.S : 0u; k < n_iss; ++k)
+    mbar_wait_backoff(&sm.full()[c * p.S + (int)(k & (uint32_t)(p.S - 1))], (k >> p.S_log2) & 1, p.status);
 }
 
 // The 32-lane butterfly of 8 lane-distributed values (value v ends in the
@@ -413,18 +453,17 @@ __device__ __forceinline__ void tile_dots(const uint8_t* tile, int64_t rs, int R
 
 // Consume this warp's tiles of one phase (dense or routed): dot every tile
 // row against the phase's activation vectors in xq and store the row sums in
-// acc[((row - r0) * n_pairs + pair) * nmat + m].  After each tile the freed
-// slot is refilled with the warp's next tile of the stream.  One copy of this
+// acc[((row - r0) * n_pairs + pair) * nmat + m].  After each tile the warp
+// releases its slot to the producer.  One copy of this
 // loop serves every phase (the weight type is a run-time switch per unit dot).
-__device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDesc& s, int n_slots, int xq_vec,
-                        int by_pair, int n_pairs, int warp, int lane, uint64_t pol) {
-  const Route* rt = sm.route();
+__device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDesc& s, const Route* rt, int n_slots,
+                        int xq_vec, int by_pair, int n_pairs, int warp, int lane) {
   const int wt = s.wt, K = s.K;
   const int G = n_groups(K);
   const int nu = n_units(p, s, n_slots);
   const int64_t rs = s.rs;
   const int nmat = s.nmat;
-  for (int u = warp; u < nu; u += NWS) {
+  for (int u = warp; u < nu; u += NC) {
     const int rb = u / n_slots, si = u - rb * n_slots;
     const int rbase = s.r0 + rb * s.R;
     const int nrows = min(s.R, s.r1 - rbase);
@@ -467,8 +506,8 @@ __device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDe
         if (lane < RM) *ap = tot;
       }
       __syncwarp();
+      if (lane == 0) mbar_arrive(&sm.empty()[warp * p.S + slot]);  // the producer may refill the slot
       ++rg.n_con;
-      issue_ahead(p, rg, sm, warp, lane, pol);
     }
   }
   return true;
@@ -495,7 +534,7 @@ __device__ void pro_quant(const MegaParams& p, const float* src, const float* no
     float scale = 1.0f;
     if (norm_w) {
       double s = 0.0;
-      for (int blk = warp; blk < nblk; blk += NWS) {
+      for (int blk = warp; blk < nblk; blk += NC) {
         float v[8];
         load8(blk, v);
 #pragma unroll
@@ -503,15 +542,15 @@ __device__ void pro_quant(const MegaParams& p, const float* src, const float* no
       }
       s = warp_sum_d(s);
       if (lane == 0) red[warp] = s;
-      __syncthreads();
+      csync();
       double tot = 0.0;
-      for (int w = 0; w < NWS; ++w) tot += red[w];  // every thread, same order
+      for (int w = 0; w < NC; ++w) tot += red[w];  // every thread, same order
       const float mean = (float)(tot / (double)K);
       scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, p.eps)));
-      __syncthreads();  // red is reused
+      csync();  // red is reused
     }
     uint8_t* qa = xq + (int64_t)t * xq_vec;
-    for (int blk = warp; blk < nblk; blk += NWS) {
+    for (int blk = warp; blk < nblk; blk += NC) {
       float v[8];
       load8(blk, v);  // an L2 hit: the first pass brought the lines in
       if (norm_w) {
@@ -529,7 +568,7 @@ __device__ void pro_quant(const MegaParams& p, const float* src, const float* no
       qact_put(act, qa, K, blk, v, lane);
     }
   }
-  __syncthreads();
+  csync();
 }
 
 __device__ __forceinline__ float kv_load(const MegaParams& p, const uint8_t* base, int64_t idx) {
@@ -615,18 +654,18 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
     const int n_kv = pos_s[a.t] + 1;
     const int j0 = a.c * CH, nj = min(CH, n_kv - j0);
     fence_proxy_async_smem();  // the staging buffer was last read by generic loads
-    __syncthreads();
+    csync();
     if (tid == 0) {
       att_issue(p, l, a, pos_s, 0, kst, sm.kbar());
       if (single) att_issue(p, l, a, pos_s, 1, vst, sm.vbar());
     }
-    for (int i = tid; i < gqa * hd; i += NT) qs[i] = __ldcg(p.q + (int64_t)a.t * p.nq + (int64_t)a.h * gqa * hd + i);
-    __syncthreads();
+    for (int i = tid; i < gqa * hd; i += NCT) qs[i] = __ldcg(p.q + (int64_t)a.t * p.nq + (int64_t)a.h * gqa * hd + i);
+    csync();
     if (!mbar_wait_backoff(sm.kbar(), kph & 1, p.status)) return false;
     ++kph;
     // y[g][j]: one (position, head) dot per thread, four double chains, the
     // dimensions walked from a per-thread rotation (fewer bank conflicts)
-    for (int w = tid; w < nj * gqa; w += NT) {
+    for (int w = tid; w < nj * gqa; w += NCT) {
       const int jj = w / gqa, g = w - jj * gqa;
       const int rot = (2 * jj + 8 * g) % hd;
       const float* qg = qs + g * hd;
@@ -653,7 +692,7 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
       ys[g * CH + jj] = y;
       p.att_y[((int64_t)a.t * p.n_head + a.h * gqa + g) * p.n_ctx + j0 + jj] = y;
     }
-    __syncthreads();
+    csync();
     if (warp < gqa) {
       float m = -INFINITY;
       for (int jj = lane; jj < nj; jj += 32) m = fmaxf(m, ys[warp * CH + jj]);
@@ -661,9 +700,9 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
       if (lane == 0) p.att_cmax[(((int64_t)a.t * p.n_head_kv + a.h) * p.att_nc + a.c) * gqa + warp] = m;
     }
     __threadfence();
-    __syncthreads();
+    csync();
     if (tid == 0) *flag = atomicAdd(&cnt1[a.t * p.n_head_kv + a.h], 1u) == (unsigned)(a.nc - 1);
-    __syncthreads();
+    csync();
     if (*(volatile int*)flag) {
       __threadfence();
       // M_g over the chunk maxima, S_g over every score of the context
@@ -674,8 +713,8 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
         m = warp_max(m);
         if (lane == 0) st[2 * warp] = m;
       }
-      __syncthreads();
-      const int tpg = NT / gqa;  // threads per head (a multiple of 32: gqa <= 16)
+      csync();
+      const int tpg = (NC / gqa) * 32;  // threads per head: whole warps (gqa <= 8)
       const int g = tid / tpg, r = tid - g * tpg;
       double s = 0.0;
       if (g < gqa) {
@@ -685,16 +724,16 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
       }
       s = warp_sum_d(s);
       if (lane == 0) sm.red()[warp] = s;
-      __syncthreads();
+      csync();
       if (tid < gqa) {
         double S = 0.0;
-        for (int w = tid * (tpg / 32); w < (tid + 1) * (tpg / 32); ++w) S += sm.red()[w];
+        for (int w = tid * (tpg / 32); w < (tid + 1) * (tpg / 32); ++w) S += sm.red()[w];  // this head's warps, in order
         float* sp = p.att_stat + ((int64_t)a.t * p.n_head + a.h * gqa + tid) * 2;
         sp[0] = st[2 * tid];
         sp[1] = (float)(1.0 / S);
       }
       __threadfence();
-      __syncthreads();
+      csync();
       if (tid == 0) {
         cnt1[a.t * p.n_head_kv + a.h] = 0u;
         st_release_gpu(&p.att_ready[a.t * p.n_head_kv + a.h], (unsigned)(l + 1));
@@ -708,25 +747,25 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
     const int j0 = a.c * CH, nj = min(CH, n_kv - j0);
     if (!single) {
       fence_proxy_async_smem();
-      __syncthreads();
+      csync();
       if (tid == 0) att_issue(p, l, a, pos_s, 1, vst, sm.vbar());
     }
     if (tid == 0) *flag = spin_ge(&p.att_ready[a.t * p.n_head_kv + a.h], (unsigned)(l + 1), p.status) ? 1 : 0;
-    __syncthreads();
+    csync();
     if (!*(volatile int*)flag) return false;
     if (tid < 2 * gqa) st[tid] = __ldcg(p.att_stat + ((int64_t)a.t * p.n_head + a.h * gqa) * 2 + tid);
-    __syncthreads();
-    for (int w = tid; w < nj * gqa; w += NT) {
+    csync();
+    for (int w = tid; w < nj * gqa; w += NCT) {
       const int g = w / nj, jj = w - g * nj;
       const float y = single ? ys[g * CH + jj]
                              : __ldcg(p.att_y + ((int64_t)a.t * p.n_head + a.h * gqa + g) * p.n_ctx + j0 + jj);
       ps[g * CH + jj] = __fmul_rn(sfk_expf(__fsub_rn(y, st[2 * g])), st[2 * g + 1]);
     }
-    __syncthreads();
+    csync();
     if (!mbar_wait_backoff(sm.vbar(), vph & 1, p.status)) return false;
     ++vph;
     double* op = p.att_opart + (((int64_t)a.t * p.n_head_kv + a.h) * p.att_nc + a.c) * gqa * hd;
-    for (int w = tid; w < gqa * hd; w += NT) {
+    for (int w = tid; w < gqa * hd; w += NCT) {
       const int g = w / hd, i = w - g * hd;
       const float* pg = ps + g * CH;
       double s0 = 0.0, s1 = 0.0;
@@ -740,20 +779,20 @@ __device__ bool attention(const MegaParams& p, int l, const Smem& sm, const int*
       op[w] = s0 + s1;
     }
     __threadfence();
-    __syncthreads();
+    csync();
     if (tid == 0) *flag = atomicAdd(&cnt2[a.t * p.n_head_kv + a.h], 1u) == (unsigned)(a.nc - 1);
-    __syncthreads();
+    csync();
     if (*(volatile int*)flag) {
       __threadfence();
       const double* base = p.att_opart + ((int64_t)a.t * p.n_head_kv + a.h) * p.att_nc * gqa * hd;
-      for (int w = tid; w < gqa * hd; w += NT) {
+      for (int w = tid; w < gqa * hd; w += NCT) {
         double s = 0.0;
         for (int c = 0; c < a.nc; ++c) s += __ldcg(base + (int64_t)c * gqa * hd + w);
         p.attn_out[(int64_t)a.t * p.nq + (int64_t)a.h * gqa * hd + w] = (float)s;
       }
       if (tid == 0) cnt2[a.t * p.n_head_kv + a.h] = 0u;
     }
-    __syncthreads();
+    csync();
   }
   return true;
 }
@@ -769,9 +808,9 @@ enum : int { ST_QKV = 0, ST_ATT = 1, ST_O = 2, ST_RT = 3, ST_GU = 4, ST_DN = 5, 
 // against the normalised inputs xn [b][d]: double partial logits
 // part[t * items + i].
 __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, const float* xn, double* part, int warp,
-                                int lane, uint64_t pol) {
+                                int lane) {
   const int items = p.E * p.rt_parts, piece = p.d / p.rt_parts;
-  for (int i = warp; i < items; i += NWS) {
+  for (int i = warp; i < items; i += NC) {
     const int slot = (int)(rg.n_con & (uint32_t)(p.S - 1));
     if (!mbar_wait_backoff(&sm.full()[warp * p.S + slot], (rg.n_con >> p.S_log2) & 1, p.status)) return false;
     const float* ws = reinterpret_cast<const float*>(sm.slot(warp, slot));
@@ -793,8 +832,8 @@ __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, c
       if (lane == 0) part[t * items + i] = a;
     }
     __syncwarp();
+    if (lane == 0) mbar_arrive(&sm.empty()[warp * p.S + slot]);
     ++rg.n_con;
-    issue_ahead(p, rg, sm, warp, lane, pol);
   }
   return true;
 }
@@ -804,7 +843,7 @@ __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, c
 __device__ void epi_qkv(const MegaParams& p, int l, const float* acc, int r0, int r1, const int* pos_s) {
   const int hd = p.hd, nq = p.nq, nk = p.nk;
   const int npr = (r1 - r0) / 2;
-  for (int idx = threadIdx.x; idx < npr * p.b; idx += NT) {
+  for (int idx = threadIdx.x; idx < npr * p.b; idx += NCT) {
     const int t = idx / npr;
     const int r = r0 + 2 * (idx - t * npr);
     const float x0 = acc[(r - r0) * p.b + t];
@@ -850,7 +889,7 @@ __device__ void epi_qkv(const MegaParams& p, int l, const float* acc, int r0, in
 __device__ void epi_gateup(const MegaParams& p, const Smem& sm, const float* acc, int r0, int r1) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int np = p.b * p.k, nr = r1 - r0;
-  for (int idx = tid; idx < nr * np; idx += NT) {
+  for (int idx = tid; idx < nr * np; idx += NCT) {
     const int row = idx % nr, pr = idx / nr;
     const float g = acc[(row * np + pr) * 2 + 0];
     const float u = acc[(row * np + pr) * 2 + 1];
@@ -858,7 +897,7 @@ __device__ void epi_gateup(const MegaParams& p, const Smem& sm, const float* acc
     p.h[(int64_t)pr * p.F + r0 + row] = __fmul_rn(sl, u);
   }
   __threadfence();
-  __syncthreads();
+  csync();
   int* gflag = reinterpret_cast<int*>(sm.red());
   const int q0 = r0 / QK_K, q1 = (r1 - 1) / QK_K;
   if (tid == 0) {
@@ -868,11 +907,11 @@ __device__ void epi_gateup(const MegaParams& p, const Smem& sm, const float* acc
       gflag[q - q0] = (old + (hi - lo) == QK_K) ? 1 : 0;
     }
   }
-  __syncthreads();
+  csync();
   for (int q = q0; q <= q1; ++q) {
     if (!gflag[q - q0]) continue;
     __threadfence();
-    for (int pr = warp; pr < np; pr += NWS) {
+    for (int pr = warp; pr < np; pr += NC) {
       const float* hp = p.h + (int64_t)pr * p.F + q * QK_K + lane * 8;
       const float4 a4 = __ldcg(reinterpret_cast<const float4*>(hp));
       const float4 b4 = __ldcg(reinterpret_cast<const float4*>(hp + 4));
@@ -892,7 +931,7 @@ __device__ void epi_lmhead(const MegaParams& p, const Smem& sm, const float* acc
   for (int t = 0; t < p.b; ++t) {
     float best = -INFINITY;
     int bi = 0x7fffffff;
-    for (int row = tid; row < nr; row += NT) {
+    for (int row = tid; row < nr; row += NCT) {
       const float v = acc[row * p.b + t];
       if (p.store_logits) p.logits[(int64_t)t * p.V + r0 + row] = v;
       if (v > best) { best = v; bi = r0 + row; }
@@ -910,53 +949,51 @@ __device__ void epi_lmhead(const MegaParams& p, const Smem& sm, const float* acc
                        ? 0ull
                        : (((unsigned long long)ord << 32) | (unsigned long long)(0xFFFFFFFFu - (unsigned)bi));
     }
-    __syncthreads();
+    csync();
     if (tid == 0) {
       unsigned long long m = 0;
-      for (int w = 0; w < NWS; ++w) m = kred[w] > m ? kred[w] : m;
+      for (int w = 0; w < NC; ++w) m = kred[w] > m ? kred[w] : m;
       if (m) atomicMax(&p.argmax_key[t], m);
     }
-    __syncthreads();
+    csync();
   }
 }
 
 // Routing of layer l (engine.cpp:1913-1924): logits from the router rows in
-// the ring, softmax, top-k, renormalised weights, slot lists; then the routed
-// gate/up tiles may be issued.
-__device__ bool route_layer(const MegaParams& p, int l, Ring& rg, const Smem& sm, const float* xn, int warp, int lane,
-                            uint64_t pol) {
+// the ring, softmax, top-k, renormalised weights, slot lists; then the
+// producer may issue the routed gate/up tiles.
+__device__ bool route_layer(const MegaParams& p, int l, Ring& rg, const Smem& sm, const float* xn, int warp, int lane) {
   const int tid = threadIdx.x;
   double* part = reinterpret_cast<double*>(sm.probs());
   bool ok = true;
-  if (!router_partials(p, rg, sm, xn, part, warp, lane, pol)) ok = false;
-  __syncthreads();
+  if (!router_partials(p, rg, sm, xn, part, warp, lane)) ok = false;
+  csync();
   if (!ok) return false;
   const int items = p.E * p.rt_parts;
   float* probs = const_cast<float*>(xn) + (int64_t)p.b * p.d;  // [b][E]
-  for (int i = tid; i < p.b * p.E; i += NT) {
+  for (int i = tid; i < p.b * p.E; i += NCT) {
     const int t = i / p.E, e = i - t * p.E;
     double a = 0.0;
     for (int pt = 0; pt < p.rt_parts; ++pt) a += part[t * items + e * p.rt_parts + pt];
     probs[i] = (float)a;
   }
-  __syncthreads();
-  Route* rt = sm.route();
-  for (int t = warp; t < p.b; t += NWS) route_select(probs + t * p.E, p.E, p.k, &rt->ids[t * p.k], &rt->w[t * p.k], lane);
-  __syncthreads();
+  csync();
+  Route* rt = sm.route(l);
+  for (int t = warp; t < p.b; t += NC) route_select(probs + t * p.E, p.E, p.k, &rt->ids[t * p.k], &rt->w[t * p.k], lane);
+  csync();
   if (warp == 0) build_slots_warp(rt->ids, p.b * p.k, rt, lane);
   if (tid == 0) {
     rt->k = p.k;
     rt->b = p.b;
   }
-  __syncthreads();
-  if (tid == 0) *sm.route_layer() = l;
+  csync();
+  if (tid == 0) *(volatile int*)sm.route_layer(l) = l;  // the producer may issue this layer's routed tiles
   if (blockIdx.x == 0) {  // the routing of the last layer, for the host
     const int* src = reinterpret_cast<const int*>(rt);
     int* dst = reinterpret_cast<int*>(p.route_out);
-    for (int i = tid; i < (int)(sizeof(Route) / 4); i += NT) dst[i] = src[i];
+    for (int i = tid; i < (int)(sizeof(Route) / 4); i += NCT) dst[i] = src[i];
   }
-  __syncthreads();
-  issue_ahead(p, rg, sm, warp, lane, pol);  // the routed gate/up tiles
+  csync();
   return true;
 }
 
@@ -967,7 +1004,6 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
   int* pos_s = sm.pos();
   int* flag = sm.flag();
   const int cta = blockIdx.x;
-  const uint64_t pol = l2_evict_first_policy();
 
   {  // the per-layer weight pointers, read on every tile issue, live in shared memory
     const int n = p.n_layer * (int)(sizeof(MegaLayer) / 8);
@@ -976,12 +1012,16 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     for (int i = tid; i < n; i += NT) dst[i] = __ldg(src + i);
   }
   if (tid == 0) {
-    for (int i = 0; i < NWS * p.S; ++i) mbar_init(&sm.full()[i], 1);
+    for (int i = 0; i < NC * p.S; ++i) {
+      mbar_init(&sm.full()[i], 1);   // the producer lane's arrival + the copies' bytes
+      mbar_init(&sm.empty()[i], 1);  // the consumer warp's release
+    }
     mbar_init(sm.pro_bar(), 1);
     mbar_init(sm.kbar(), 1);
     mbar_init(sm.vbar(), 1);
     fence_mbar_init();
-    *sm.route_layer() = -1;
+    *sm.route_layer(0) = -1;
+    *sm.route_layer(1) = -1;
     *sm.gp_limit() = p.lookahead;  // the first step streams QKV of layer 0
   }
   // tokens and positions of the step (the embed kernel's duties)
@@ -1005,16 +1045,19 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     toks[tid] = tok;
     pos_s[tid] = pos;
   }
-  __syncthreads();
-  Ring rg{0u, 0u, 0, 0};
-  issue_ahead(p, rg, sm, warp, lane, pol);  // the first tiles go out at once
+  __syncthreads();  // the last barrier of the whole CTA: the producer warp leaves here
+  if (warp == NC) {
+    producer(p, sm, lane);
+    return;
+  }
+  Ring rg{0u};
   unsigned target = 0;
   {  // the embedding rows (ggml_get_rows, engine.cpp:2708-2723), a column slice per CTA
     const int64_t erb = dev_gguf_row_bytes(p.t_embd, p.d);
     const int per = (p.d + gridDim.x - 1) / gridDim.x;
     const int c0 = cta * per, c1 = min(p.d, c0 + per);
     for (int t = 0; t < p.b; ++t)
-      for (int i = c0 + tid; i < c1; i += NT)
+      for (int i = c0 + tid; i < c1; i += NCT)
         p.x[(int64_t)t * p.d + i] = gguf_dequant_one(p.t_embd, p.tok_embd + (int64_t)toks[t] * erb, i);
   }
   uint32_t pro_ph = 0, kph = 0, vph = 0;
@@ -1035,10 +1078,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
       const int cur = st == -1 ? SP_N * p.n_layer
                                : l * SP_N + (st <= ST_QKV ? SP_QKV : st <= ST_O ? SP_O : st == ST_RT ? SP_RT
                                                                    : st == ST_GU ? SP_GU : SP_DN);
-      __syncthreads();
-      if (tid == 0) *sm.gp_limit() = cur + p.lookahead;
-      __syncthreads();
-      issue_ahead(p, rg, sm, warp, lane, pol);
+      if (tid == 0) *(volatile int*)sm.gp_limit() = cur + p.lookahead;
     }
     if (st == ST_ATT) {  // attention over the paged KV (engine.cpp:1751-1761)
       ok = attention(p, l, sm, pos_s, kph, vph) && grid_sync(p, target, flag);
@@ -1049,7 +1089,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     if (st == ST_DN) {  // the quantized SwiGLU activations of every pair
       const int xv = (int)qact_bytes(p.F);
       fence_proxy_async_smem();
-      __syncthreads();
+      csync();
       if (tid == 0) {
         mbar_arrive_expect_tx(sm.pro_bar(), (uint32_t)(np * xv));
         for (int pr = 0; pr < np; ++pr)
@@ -1066,7 +1106,7 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
       pro_quant(p, src, nw, K, act, sm.xq(), (int)qact_bytes(K), st == ST_RT ? xn : nullptr, sm.red());
     }
     if (st == ST_RT) {
-      if (!route_layer(p, l, rg, sm, xn, warp, lane, pol)) { ok = false; break; }
+      if (!route_layer(p, l, rg, sm, xn, warp, lane)) { ok = false; break; }
       continue;  // gate/up follows without a barrier
     }
     // ---- the step's weight tiles
@@ -1075,20 +1115,21 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     const SDesc s = stream_desc(p, sp);
     {
       const bool routed = st == ST_GU || st == ST_DN;
-      if (!consume(p, rg, sm, s, routed ? sm.route()->n_slots : 1, (int)qact_bytes(s.K), st == ST_DN ? 1 : 0,
-                   routed ? np : p.b, warp, lane, pol)) {
+      const Route* rt = sm.route(l);
+      if (!consume(p, rg, sm, s, rt, routed ? rt->n_slots : 1, (int)qact_bytes(s.K), st == ST_DN ? 1 : 0,
+                   routed ? np : p.b, warp, lane)) {
         ok = false;
         break;
       }
     }
-    __syncthreads();
+    csync();
     // ---- epilogue
     const int nr = s.r0 < s.r1 ? s.r1 - s.r0 : 0;
     const float* acc = sm.acc();
     if (st == ST_QKV) {
       epi_qkv(p, l, acc, s.r0, s.r0 + nr, pos_s);
     } else if (st == ST_O) {  // + residual (engine.cpp:1905-1906)
-      for (int idx = tid; idx < nr * p.b; idx += NT) {
+      for (int idx = tid; idx < nr * p.b; idx += NCT) {
         const int t = idx / nr, row = idx - t * nr;
         const int64_t o = (int64_t)t * p.d + s.r0 + row;
         p.ffn_inp[o] = __fadd_rn(acc[row * p.b + t], __ldcg(p.x + o));
@@ -1096,9 +1137,9 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     } else if (st == ST_GU) {
       if (nr > 0) epi_gateup(p, sm, acc, s.r0, s.r1);
     } else if (st == ST_DN) {  // experts * weights, moe_out = e0 + e1 + ..., + ffn_inp (engine.cpp:1973-1986)
-      const Route* rt = sm.route();
+      const Route* rt = sm.route(l);
       const int k = p.k;
-      for (int idx = tid; idx < nr * p.b; idx += NT) {
+      for (int idx = tid; idx < nr * p.b; idx += NCT) {
         const int row = idx % nr, t = idx / nr;
         float a = __fmul_rn(acc[row * np + t * k], rt->w[t * k]);
         for (int j = 1; j < k; ++j) a = __fadd_rn(a, __fmul_rn(acc[row * np + t * k + j], rt->w[t * k + j]));
@@ -1111,12 +1152,9 @@ __global__ void __launch_bounds__(NT, 1) mega_kernel(const __grid_constant__ Meg
     }
     if (!grid_sync(p, target, flag)) { ok = false; break; }
   }
-  if (!ok) {  // let this warp's copies land, then leave; the host clears the counters
-    drain(p, rg, sm, warp);
-    return;
-  }
+  if (!ok) return;  // the producer lets the copies it issued land; the host clears the counters
   // the last CTA out re-arms the barrier words and the attention flags for the next launch
-  __syncthreads();
+  csync();
   if (tid == 0) {
     __threadfence();
     const unsigned old = atomicAdd(p.gbar + 1, 1u);

@@ -14,10 +14,11 @@
 
 namespace sfk {
 
-constexpr int MEGA_NWS = 16;        // warps per CTA
+constexpr int MEGA_NWS = 16;        // warps per CTA: 15 consumer warps and the producer warp
+constexpr int MEGA_NC = MEGA_NWS - 1;  // consumer warps (each owns a ring of weight-tile slots)
 constexpr int MEGA_MAXS = 4;        // ring slots per warp (at most)
 constexpr int MEGA_MAXE = 64;       // experts the kernel routes itself
-constexpr int MEGA_MAXGQA = 16;     // query heads per kv head
+constexpr int MEGA_MAXGQA = 8;      // query heads per kv head (whole warps per head in the softmax sums)
 constexpr int MEGA_RED = 128;       // doubles of reduction scratch
 // weight phases of the tile plan
 enum : int { MEGA_PK_QKV = 0, MEGA_PK_O = 1, MEGA_PK_GU = 2, MEGA_PK_DN = 3, MEGA_PK_OUT = 4 };

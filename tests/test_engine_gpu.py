@@ -214,6 +214,7 @@ def test_persistent_step_matches_launch_chain(cuda, monkeypatch, kw):
     from strataflow_b200 import engine as E
     cfg = E.tiny_config(n_layer=3, **kw)
     prompt = np.random.default_rng(12).integers(0, cfg.n_vocab, 10).tolist()
+    monkeypatch.setenv("SFK_PERSISTENT", "1")
     eng, om, toks, worst = _run_parity(cfg, 21, prompt, 16)
     assert eng.stats()["kernels_per_step"] == 1
     monkeypatch.setenv("SFK_PERSISTENT", "0")

@@ -199,3 +199,19 @@ def test_forward_rejects_bad_inputs():
         s.forward(64, 0)
     with pytest.raises(ValueError):
         s.forward(1, 4)
+
+
+def test_fill_kv_is_seeded_and_finite():
+    """The timing helper fills a context deterministically; a decode step at
+    the next position over it yields finite, reproducible logits."""
+    cfg = O.ModelConfig(n_embd=256, n_head=8, n_head_kv=4, n_layer=2, n_ff=512, n_expert=4, n_expert_used=2,
+                        n_vocab=512, n_ctx=40, kv_f16=True)
+    m = O.Model(cfg, seed=3)
+    outs = []
+    for _ in range(2):
+        s = m.new_seq()
+        s.fill_kv(32, seed=7)
+        _, lg = s.forward(5, 32)
+        outs.append(lg)
+    assert np.all(np.isfinite(outs[0]))
+    assert np.array_equal(outs[0], outs[1])
