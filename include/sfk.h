@@ -241,6 +241,16 @@ SFK_API sfk_status sfk_quantize_act(int act_type, const float *dev_x, int32_t b,
 SFK_API sfk_status sfk_mul_mat(int ggml_type, const void *dev_w, int64_t rows, int64_t K, const float *dev_x, int32_t b,
                        float *dev_y, void *stream);
 
+/* The same product for many activation rows at once on the tensor cores
+ * (tcgen05 kind::i8): y[t][r] = W[r,:] . x[t], t < n (any n >= 1), the
+ * activations quantized the ggml way and the sub-block integer dots exact; the
+ * fp32 sum over 256-column blocks is taken in block order.  For prefill and
+ * large batches (the reference feeds a prompt one position per call,
+ * tests/test_engine_oracle.cpp:182-187; this is the batched form of
+ * ggml_mul_mat, engine.cpp:1882-1889). */
+SFK_API sfk_status sfk_mul_mat_tc(int ggml_type, const void *dev_w, int64_t rows, int64_t K, const float *dev_x,
+                                  int32_t n, float *dev_y, void *stream);
+
 /* ggml_mul_mat_id for the routed experts (engine.cpp:1967-1970):
  * w: stacked [E][rows][K] (device layout), x: [b][K] (one row per token,
  * broadcast over its k experts) or [b][k][K] when x_per_pair,

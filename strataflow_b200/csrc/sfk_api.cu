@@ -29,6 +29,7 @@
 #include "sfk_device.cuh"
 #include "sfk_kernels.cuh"
 #include "sfk_mega.cuh"
+#include "sfk_tc.cuh"
 
 using namespace sfk;
 
@@ -1603,6 +1604,38 @@ sfk_status sfk_quantize_act(int act_type, const float* x, int32_t b, int64_t K, 
   if (b == 0) return SFK_OK;
   CK(launch_quant_act_gguf(act_type, x, b, (int)K, (uint8_t*)out, (cudaStream_t)stream));
   return SFK_OK;
+}
+
+sfk_status sfk_mul_mat_tc(int t, const void* w, int64_t rows, int64_t K, const float* x, int32_t n, float* y,
+                          void* stream) {
+  if (!quant_ok(t) || K % 256 || !w || !x || !y || n < 1 || rows < 1 || rows > (1 << 30))
+    return fail(SFK_ERR_INVALID_ARGUMENT, "mul_mat_tc arguments");
+  const int act = act_for(t);
+  size_t odx = 0, obs = 0;
+  const size_t need = tc_act_bytes(act, n, (int)K, &odx, &obs);
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(need, 1, &sc);
+  if (s) return s;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* buf = static_cast<uint8_t*>(sc->buf);
+  CK(launch_tc_quant(act, x, n, (int)K, buf, st));
+  TcGemmParams p{};
+  p.w = (const uint8_t*)w;
+  p.rowstride = dev_row_bytes(t, (int)K);
+  p.rows = (int)rows;
+  p.K = (int)K;
+  p.wtype = t;
+  p.act_type = act;
+  p.xq = reinterpret_cast<const int8_t*>(buf);
+  p.dx = reinterpret_cast<const float*>(buf + odx);
+  p.bs = reinterpret_cast<const int16_t*>(buf + obs);
+  p.n = n;
+  p.npad = (n + TC_TT - 1) / TC_TT * TC_TT;
+  p.y = y;
+  p.ldy = rows;
+  p.status = sc->status;
+  CK(launch_tc_gemm(p, st));
+  return check_status_word(sc->status, st);
 }
 
 sfk_status sfk_mul_mat(int t, const void* w, int64_t rows, int64_t K, const float* x, int32_t b, float* y,

@@ -72,6 +72,7 @@ _SIGS = {
     "sfk_dequantize": (I32, [C.c_int, P, P, I64, P]),
     "sfk_quantize_act": (I32, [C.c_int, P, I32, I64, P, P]),
     "sfk_mul_mat": (I32, [C.c_int, P, I64, I64, P, I32, P, P]),
+    "sfk_mul_mat_tc": (I32, [C.c_int, P, I64, I64, P, I32, P, P]),
     "sfk_mul_mat_id": (I32, [C.c_int, P, I32, I64, I64, P, I32, P, I32, I32, P, P]),
     "sfk_moe_ffn": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
     "sfk_moe_ffn_noalloc": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),

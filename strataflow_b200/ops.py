@@ -63,6 +63,15 @@ def mul_mat(qtype: int, w_dev: torch.Tensor, rows: int, K: int, x: torch.Tensor)
     return y
 
 
+def mul_mat_tc(qtype: int, w_dev: torch.Tensor, rows: int, K: int, x: torch.Tensor) -> torch.Tensor:
+    """The same product for any number of activation rows on the tensor cores
+    (sfk_mul_mat_tc): y [n][rows]."""
+    n = x.shape[0]
+    y = torch.empty((n, rows), dtype=torch.float32, device=x.device)
+    L.check(L.load().sfk_mul_mat_tc(qtype, _ptr(w_dev), rows, K, _ptr(x), n, _ptr(y), _stream(x)))
+    return y
+
+
 def mul_mat_id(qtype: int, w_dev: torch.Tensor, n_expert: int, rows: int, K: int, x: torch.Tensor,
                ids: torch.Tensor) -> torch.Tensor:
     """x: [b][K] (broadcast over each token's experts) or [b][k][K]."""
