@@ -189,6 +189,20 @@ SFK_API sfk_status sfk_forward_batch(sfk_engine *eng, int32_t n_seq, const int32
  * The loop runs on the device as one captured CUDA graph per step, with no
  * host round trip; tokens_out: [n_steps][n_seq] (host). */
 SFK_API sfk_status sfk_decode_greedy(sfk_engine *eng, int32_t n_seq, int32_t n_steps, int32_t *tokens_out);
+/* Batched prompt prefill: tokens[0..n) of sequence `seq` at positions
+ * pos0 .. pos0 + n - 1 (pos0 + n <= n_ctx), every layer run over a chunk of
+ * up to 512 prompt tokens at once (tensor-core GEMMs; routed pairs grouped by
+ * expert; each token attends over its own prefix).  It replaces feeding the
+ * prompt one position per Engine::forward call (tests/test_engine_oracle.cpp:
+ * 182-187): the KV cache, the next position and the argmax key end as they
+ * would after the last prompt token's forward, so sfk_decode_greedy
+ * continues from it.  logits_host (optional, n_vocab floats) and argmax_out
+ * (optional) receive the last prompt token's logits and greedy token.  The
+ * GEMMs add the 256-column blocks of a row in order, so values differ from
+ * token-by-token decode in fp32 rounding only.  One GPU (no expert
+ * parallelism). */
+SFK_API sfk_status sfk_prefill(sfk_engine *eng, int32_t seq, const int32_t *tokens, int32_t n, int32_t pos0,
+                               float *logits_host, int32_t *argmax_out);
 
 /* Routing of the last layer of the last step: ids [n_seq][k] and weights
  * [n_seq][k] (host) -- the router segment's read-back (engine.cpp:2823-2833). */

@@ -73,6 +73,7 @@ def lib():
             "sfo_attn_decode": (None, [P, P, P, I, I, I, I, P]),
             "sfo_model_create": (P, [P]),
             "sfo_model_free": (None, [P]),
+            "sfo_set_fp32_mode": (None, [P, I]),
             "sfo_tensor_bytes": (SZ, [P, I, I, P, P]),
             "sfo_tensor_data": (P, [P, I, I]),
             "sfo_model_synth": (I, [P, U64]),
@@ -277,6 +278,10 @@ class Model:
     def new_seq(self) -> "Seq":
         return Seq(self)
 
+    def set_fp32_mode(self, mode: int) -> None:
+        """fp32 order of later forwards' quantized mul_mats (sfo_set_fp32_mode)."""
+        lib().sfo_set_fp32_mode(self.h, int(mode))
+
 
 class Seq:
     def __init__(self, model: Model):
@@ -326,17 +331,25 @@ class Seq:
                                      shape=(self.m.cfg.n_expert_used,)).copy()
 
 
-def greedy(model: Model, prompt: list[int], n_gen: int, want_logits=False):
+def greedy(model: Model, prompt: list[int], n_gen: int, want_logits=False, prompt_fp32_mode=None):
     """Prompt one token per position, then n_gen greedy tokens (the reference's
-    tests/test_engine_oracle.cpp:182-207 drive pattern)."""
+    tests/test_engine_oracle.cpp:182-207 drive pattern).  prompt_fp32_mode:
+    the fp32 order of the prompt tokens' mul_mats (2: the per-block order of a
+    batched prefill), the model's own order for the generated tokens."""
     seq = model.new_seq()
     pos = 0
     logits_all = []
     tok = None
     last = None
-    for t in prompt:
-        tok, last = seq.forward(t, pos)
-        pos += 1
+    if prompt_fp32_mode is not None:
+        model.set_fp32_mode(prompt_fp32_mode)
+    try:
+        for t in prompt:
+            tok, last = seq.forward(t, pos)
+            pos += 1
+    finally:
+        if prompt_fp32_mode is not None:
+            model.set_fp32_mode(int(model.cfg.fp32_mode))
     if want_logits:
         logits_all.append(last)
     out = []

@@ -940,6 +940,10 @@ sfo_model *sfo_model_create(const sfo_hparams *hp) {
     return m;
 }
 
+void sfo_set_fp32_mode(sfo_model *m, int mode) {
+    if (m) m->hp.fp32_mode = mode;
+}
+
 void sfo_model_free(sfo_model *m) {
     if (!m) return;
     for (int tid = 0; tid < SFO_T_COUNT; ++tid)

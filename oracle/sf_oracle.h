@@ -128,6 +128,10 @@ typedef struct sfo_seq   sfo_seq;
 
 sfo_model *sfo_model_create(const sfo_hparams *hp);
 void       sfo_model_free(sfo_model *m);
+/* fp32 accumulation order of the quantized mul_mats of later forwards: 0 the
+ * decode kernels' unit order, 2 ggml's generic per-block order (the order of
+ * the tensor-core prefill GEMMs), 1 the dequantize-and-dot diagnostic. */
+void       sfo_set_fp32_mode(sfo_model *m, int mode);
 /* shape/type/size of tensor (tid, layer) in GGUF bytes; returns bytes or 0 */
 size_t     sfo_tensor_bytes(const sfo_model *m, int tid, int layer, int *type, int64_t ne[3]);
 void      *sfo_tensor_data(sfo_model *m, int tid, int layer);

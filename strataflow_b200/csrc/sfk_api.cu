@@ -29,6 +29,7 @@
 #include "sfk_device.cuh"
 #include "sfk_kernels.cuh"
 #include "sfk_mega.cuh"
+#include "sfk_prefill.cuh"
 #include "sfk_tc.cuh"
 
 using namespace sfk;
@@ -290,6 +291,19 @@ struct sfk_engine {
   int kernels_per_step = 0;
   int last_b = 0;
   std::vector<int> seq_pos;  // host mirror of the next position per sequence
+  // batched prompt prefill (sfk_prefill): buffers for a chunk of `cap` prompt
+  // tokens, allocated at the first prefill
+  struct Prefill {
+    int cap = 0;  // prompt tokens per chunk
+    int mt = 0;   // 64-row tiles of the routed pairs (expert-grouped, padded)
+    int *tok = nullptr, *pos = nullptr, *pt = nullptr;
+    float *x = nullptr, *ffn = nullptr, *xn = nullptr, *qkv = nullptr, *q = nullptr, *att = nullptr;
+    float *h = nullptr, *yd = nullptr, *w = nullptr;
+    float* score = nullptr;     // attention score rows (pf_attn scratch)
+    size_t score_bytes = 0;
+    uint8_t *act = nullptr, *xqd = nullptr;
+    int *ids = nullptr, *pos_of_pair = nullptr, *rows_tok = nullptr, *rows_self = nullptr, *tile_expert = nullptr;
+  } pf;
 
   template <typename T>
   sfk_status alloc(T** p, size_t bytes, uint64_t* acct) {
@@ -1408,6 +1422,255 @@ sfk_status sfk_forward(sfk_engine* e, int32_t token, int32_t pos, float* logits_
   return sfk_forward_batch(e, 1, &token, &pos, logits_host, argmax_out);
 }
 
+namespace {
+
+constexpr int PF_CHUNK = 512;  // prompt tokens per prefill pass
+
+sfk_status prefill_alloc(sfk_engine* e) {
+  if (e->pf.cap) return SFK_OK;
+  const sfk_hparams& hp = e->hp;
+  const int C = std::min(PF_CHUNK, hp.n_ctx);
+  const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
+  const int np = C * k;
+  const int mt = (np + TC_TT - 1) / TC_TT + std::min(E, np);
+  const int rows_pad = mt * TC_TT, cpad = (C + TC_TT - 1) / TC_TT * TC_TT;
+  const size_t act = std::max(std::max(tc_act_bytes(cpad, d), tc_act_bytes(cpad, e->nq)),
+                              std::max(tc_act_bytes(rows_pad, d), tc_act_bytes(rows_pad, F)));
+  sfk_engine::Prefill& f = e->pf;
+  uint64_t* acct = &e->scratch_bytes;
+  sfk_status s;
+  if ((s = e->alloc(&f.tok, sizeof(int) * C, acct)) || (s = e->alloc(&f.pos, sizeof(int) * C, acct)) ||
+      (s = e->alloc(&f.pt, sizeof(int) * (size_t)C * e->max_pages, acct)) ||
+      (s = e->alloc(&f.x, sizeof(float) * (size_t)C * d, acct)) ||
+      (s = e->alloc(&f.ffn, sizeof(float) * (size_t)C * d, acct)) ||
+      (s = e->alloc(&f.xn, sizeof(float) * (size_t)C * d, acct)) ||
+      (s = e->alloc(&f.qkv, sizeof(float) * (size_t)C * e->nqkv, acct)) ||
+      (s = e->alloc(&f.q, sizeof(float) * (size_t)C * e->nq, acct)) ||
+      (s = e->alloc(&f.att, sizeof(float) * (size_t)C * e->nq, acct)) ||
+      (s = e->alloc(&f.h, sizeof(float) * (size_t)rows_pad * F, acct)) ||
+      (s = e->alloc(&f.yd, sizeof(float) * (size_t)rows_pad * d, acct)) ||
+      (s = e->alloc(&f.w, sizeof(float) * np, acct)) || (s = e->alloc(&f.act, act, acct)) ||
+      (s = e->alloc(&f.xqd, (size_t)C * qact_bytes(d), acct)) || (s = e->alloc(&f.ids, sizeof(int) * np, acct)) ||
+      (s = e->alloc(&f.pos_of_pair, sizeof(int) * np, acct)) ||
+      (s = e->alloc(&f.rows_tok, sizeof(int) * rows_pad, acct)) ||
+      (s = e->alloc(&f.rows_self, sizeof(int) * rows_pad, acct)) ||
+      (s = e->alloc(&f.tile_expert, sizeof(int) * mt, acct)))
+    return s;
+  if (pf_attn_supported(e->hd, e->hq_loc, e->hkv_loc)) {
+    // score rows of a whole chunk at the longest context, at most 256 MB
+    // (longer contexts run the attention in token sub-batches of whole tiles)
+    const int qt = 64 / (e->hq_loc / e->hkv_loc);
+    const size_t want = pf_attn_scratch_bytes(C, hp.n_ctx - C, e->hq_loc, e->hkv_loc);
+    const size_t cap = std::max((size_t)256 << 20, pf_attn_scratch_bytes(qt, hp.n_ctx - qt, e->hq_loc, e->hkv_loc));
+    f.score_bytes = std::min(want, cap);
+    if ((s = e->alloc(&f.score, f.score_bytes, acct))) return s;
+  }
+  f.cap = C;
+  f.mt = mt;
+  return SFK_OK;
+}
+
+// One layer over m prompt tokens at positions pos0 .. pos0 + m - 1 of
+// sequence `seq`: the reference's per-token layer (engine.cpp:1878-1986) with
+// the matrices as tensor-core GEMMs over all m tokens (the routed experts
+// grouped by expert) and the attention of every token over its own prefix.
+sfk_status prefill_layer(sfk_engine* e, int l, int seq, int m, int pos0) {
+  const sfk_hparams& hp = e->hp;
+  const LayerW& W = e->L[l];
+  sfk_engine::Prefill& f = e->pf;
+  cudaStream_t st = e->stream;
+  const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
+  const int mpad = (m + TC_TT - 1) / TC_TT * TC_TT;
+  const int act_attn = act_for(hp.type_attn);
+  // attn_norm -> QKV (engine.cpp:1878-1889)
+  CK(launch_pf_norm(f.x, W.attn_norm, m, d, hp.rms_eps, f.xn, st));
+  CK(launch_tc_quant(act_attn, f.xn, d, nullptr, m, mpad, d, f.act, st));
+  TcGemmParams g{};
+  g.w = W.qkv;
+  g.rowstride = dev_row_bytes(hp.type_attn, d);
+  g.rows = e->nqkv;
+  g.K = d;
+  g.wtype = hp.type_attn;
+  g.act_type = act_attn;
+  g.xq = f.act;
+  g.n = m;
+  g.ntile = mpad / TC_TT;
+  g.y = f.qkv;
+  g.ldy = e->nqkv;
+  g.epi = TC_EPI_STORE;
+  g.status = e->status;
+  CK(launch_tc_gemm(g, st));
+  // RoPE, KV append (engine.cpp:1892-1901,1646-1656)
+  KvView kv = kv_view(e, l);
+  const int* pt_row = e->page_table + (size_t)seq * e->max_pages;
+  CK(launch_pf_rope_kv(f.qkv, m, e->hq_loc, kv, pt_row, e->rope, pos0, f.q, e->status, st));
+  // attention of token t over positions 0 .. pos0 + t (engine.cpp:1751-1761)
+  if (f.score) {
+    // token sub-batches (whole 64-row tiles) whose score rows fit the scratch
+    const int qt = 64 / (e->hq_loc / e->hkv_loc);
+    const size_t tile_bytes = pf_attn_scratch_bytes(qt, pos0 + m - qt, e->hq_loc, e->hkv_loc);
+    const int step = std::max(1, (int)(f.score_bytes / tile_bytes)) * qt;
+    for (int c = 0; c < m; c += step) {
+      const int mc = std::min(step, m - c);
+      CK(launch_pf_attn(f.q + (size_t)c * e->nq, kv, pt_row, mc, pos0 + c, e->hq_loc, f.att + (size_t)c * e->nq,
+                        f.score, e->status, st));
+    }
+  } else {  // other head shapes: the decode kernel, one page-table row per prompt token
+    AttnParams a{};
+    a.q = f.q;
+    a.kv = kv;
+    a.kv.page_table = f.pt;
+    a.pos = f.pos;
+    a.b = m;
+    a.n_head = e->hq_loc;
+    a.cluster = e->attn_cluster;
+    a.max_chunk = e->attn_max_chunk;
+    a.out = f.att;
+    a.status = e->status;
+    CK(launch_attn(a, st, false));
+  }
+  // O projection + residual (engine.cpp:1905-1906)
+  CK(launch_tc_quant(act_attn, f.att, e->nq, nullptr, m, mpad, e->nq, f.act, st));
+  g = TcGemmParams{};
+  g.w = W.wo;
+  g.rowstride = dev_row_bytes(hp.type_attn, e->nq);
+  g.rows = d;
+  g.K = e->nq;
+  g.wtype = hp.type_attn;
+  g.act_type = act_attn;
+  g.xq = f.act;
+  g.n = m;
+  g.ntile = mpad / TC_TT;
+  g.y = f.ffn;
+  g.ldy = d;
+  g.res = f.x;
+  g.ldres = d;
+  g.epi = TC_EPI_RESID;
+  g.status = e->status;
+  CK(launch_tc_gemm(g, st));
+  // ffn_norm, router, top-k (engine.cpp:1909-1924); pairs grouped by expert
+  const int act_gu = act_for(hp.type_ffn_gu), act_dn = act_for(hp.type_ffn_down);
+  CK(launch_pf_route(f.ffn, W.ffn_norm, W.router, m, d, E, k, hp.rms_eps, act_gu, f.xqd, f.xn, f.ids, f.w, e->status,
+                     st));
+  CK(launch_pf_group(f.ids, m * k, k, E, f.mt, f.pos_of_pair, f.rows_tok, f.rows_self, f.tile_expert, e->status, st));
+  // gate / up + SwiGLU of every routed pair (engine.cpp:1967-1969)
+  CK(launch_tc_quant(act_gu, f.xn, d, f.rows_tok, m, f.mt * TC_TT, d, f.act, st));
+  g = TcGemmParams{};
+  g.w = W.gate;
+  g.w2 = W.up;
+  g.rowstride = dev_row_bytes(hp.type_ffn_gu, d);
+  g.expert_stride = (int64_t)F * g.rowstride;
+  g.rows = F;
+  g.K = d;
+  g.wtype = hp.type_ffn_gu;
+  g.act_type = act_gu;
+  g.xq = f.act;
+  g.ntile = f.mt;
+  g.tile_expert = f.tile_expert;
+  g.y = f.h;
+  g.ldy = F;
+  g.epi = TC_EPI_SWIGLU;
+  g.status = e->status;
+  CK(launch_tc_gemm(g, st));
+  // down of every routed pair, then the weighted combine + residual
+  // (engine.cpp:1970-1986)
+  CK(launch_tc_quant(act_dn, f.h, F, f.rows_self, f.mt * TC_TT, f.mt * TC_TT, F, f.act, st));
+  g = TcGemmParams{};
+  g.w = W.down;
+  g.rowstride = dev_row_bytes(hp.type_ffn_down, F);
+  g.expert_stride = (int64_t)d * g.rowstride;
+  g.rows = d;
+  g.K = F;
+  g.wtype = hp.type_ffn_down;
+  g.act_type = act_dn;
+  g.xq = f.act;
+  g.ntile = f.mt;
+  g.tile_expert = f.tile_expert;
+  g.y = f.yd;
+  g.ldy = d;
+  g.epi = TC_EPI_STORE;
+  g.status = e->status;
+  CK(launch_tc_gemm(g, st));
+  CK(launch_pf_combine(f.yd, f.pos_of_pair, f.w, k, m, d, f.ffn, f.x, st));
+  return SFK_OK;
+}
+
+// output_norm + lm_head + argmax of one hidden row into sequence seq's logits
+// row and argmax key (engine.cpp:2988-3006)
+sfk_status lmhead_row(sfk_engine* e, const float* x_row, int seq) {
+  const sfk_hparams& hp = e->hp;
+  CK(cudaMemsetAsync(e->argmax_key + seq, 0, sizeof(unsigned long long), e->stream));
+  StreamParams p{};
+  p.w0 = e->output;
+  p.rowstride = dev_row_bytes(hp.type_output, hp.n_embd);
+  p.rows = hp.n_vocab;
+  p.K = hp.n_embd;
+  p.wtype = hp.type_output;
+  p.nmat = 1;
+  p.act_type = act_for(hp.type_output);
+  p.row_align = 1;
+  p.b = 1; p.k = 1; p.n_pairs = 1; p.n_vec = 1;
+  p.pro = PRO_QUANT;
+  p.x = x_row;
+  p.norm_w = e->out_norm;
+  p.eps = hp.rms_eps;
+  p.epi = EPI_LMHEAD;
+  p.y = e->logits + (size_t)seq * hp.n_vocab;
+  p.y_stride = hp.n_vocab;
+  p.argmax_key = e->argmax_key + seq;
+  p.store_logits = 1;
+  p.status = e->status;
+  int grid = 0;
+  sfk_status s = plan_stream(p, e->sm_count, &grid);
+  if (s) return s;
+  CK(launch_stream(p, grid, e->stream, false));
+  return SFK_OK;
+}
+
+}  // namespace
+
+sfk_status sfk_prefill(sfk_engine* e, int32_t seq, const int32_t* tokens, int32_t n, int32_t pos0, float* logits_host,
+                       int32_t* argmax_out) {
+  if (!e || !tokens) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  const sfk_hparams& hp = e->hp;
+  if (seq < 0 || seq >= hp.max_batch) return fail(SFK_ERR_INVALID_ARGUMENT, "sequence %d", seq);
+  if (n < 1 || pos0 < 0 || (int64_t)pos0 + n > hp.n_ctx)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "positions [%d, %d) outside [0, n_ctx=%d)", pos0, pos0 + n, hp.n_ctx);
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] < 0 || tokens[i] >= hp.n_vocab)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "token %d outside the vocabulary", tokens[i]);
+  if (e->ep_size > 1) return fail(SFK_ERR_UNSUPPORTED, "batched prefill runs on one GPU (no expert parallelism)");
+  CK(cudaSetDevice(e->device));
+  sfk_status s = prefill_alloc(e);
+  if (s) return s;
+  sfk_engine::Prefill& f = e->pf;
+  for (int c0 = 0; c0 < n; c0 += f.cap) {
+    const int m = std::min(f.cap, n - c0);
+    CK(cudaMemcpyAsync(f.tok, tokens + c0, sizeof(int) * m, cudaMemcpyHostToDevice, e->stream));
+    CK(launch_pf_embed(e->tok_embd, hp.type_embd, hp.n_embd, hp.n_vocab, f.tok, m, pos0 + c0, f.x, f.pos,
+                       e->pos_state + seq, e->status, e->stream));
+    CK(launch_pf_pt(e->page_table + (size_t)seq * e->max_pages, e->max_pages, m, f.pt, e->stream));
+    for (int l = 0; l < hp.n_layer; ++l)
+      if ((s = prefill_layer(e, l, seq, m, pos0 + c0))) return s;
+    if (c0 + m == n && (s = lmhead_row(e, f.x + (size_t)(m - 1) * hp.n_embd, seq))) return s;
+  }
+  const int B = hp.max_batch;
+  if (logits_host)
+    CK(cudaMemcpyAsync(e->h_logits, e->logits + (size_t)seq * hp.n_vocab, sizeof(float) * hp.n_vocab,
+                       cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * B + sizeof(int), cudaMemcpyDeviceToHost,
+                     e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  if ((s = status_result(e->status, *e->h_status))) {
+    reset_counters(e);
+    return s;
+  }
+  if (logits_host) memcpy(logits_host, e->h_logits, sizeof(float) * hp.n_vocab);
+  if (argmax_out) *argmax_out = (int32_t)(0xFFFFFFFFu - (uint32_t)(e->h_keys[seq] & 0xFFFFFFFFull));
+  e->seq_pos[seq] = pos0 + n;
+  return SFK_OK;
+}
+
 sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int32_t* tokens_out) {
   if (!e) return fail(SFK_ERR_INVALID_ARGUMENT, "null engine");
   if (n_seq < 1 || n_seq > e->hp.max_batch || n_steps < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "n_seq / n_steps");
@@ -1611,14 +1874,14 @@ sfk_status sfk_mul_mat_tc(int t, const void* w, int64_t rows, int64_t K, const f
   if (!quant_ok(t) || K % 256 || !w || !x || !y || n < 1 || rows < 1 || rows > (1 << 30))
     return fail(SFK_ERR_INVALID_ARGUMENT, "mul_mat_tc arguments");
   const int act = act_for(t);
-  size_t odx = 0, obs = 0;
-  const size_t need = tc_act_bytes(act, n, (int)K, &odx, &obs);
+  const int npad = (n + TC_TT - 1) / TC_TT * TC_TT;
+  const size_t need = tc_act_bytes(npad, (int)K);
   OpScratch* sc = nullptr;
   sfk_status s = op_scratch(need, 1, &sc);
   if (s) return s;
   cudaStream_t st = (cudaStream_t)stream;
   uint8_t* buf = static_cast<uint8_t*>(sc->buf);
-  CK(launch_tc_quant(act, x, n, (int)K, buf, st));
+  CK(launch_tc_quant(act, x, K, nullptr, n, npad, (int)K, buf, st));
   TcGemmParams p{};
   p.w = (const uint8_t*)w;
   p.rowstride = dev_row_bytes(t, (int)K);
@@ -1626,13 +1889,12 @@ sfk_status sfk_mul_mat_tc(int t, const void* w, int64_t rows, int64_t K, const f
   p.K = (int)K;
   p.wtype = t;
   p.act_type = act;
-  p.xq = reinterpret_cast<const int8_t*>(buf);
-  p.dx = reinterpret_cast<const float*>(buf + odx);
-  p.bs = reinterpret_cast<const int16_t*>(buf + obs);
+  p.xq = buf;
   p.n = n;
-  p.npad = (n + TC_TT - 1) / TC_TT * TC_TT;
+  p.ntile = npad / TC_TT;
   p.y = y;
   p.ldy = rows;
+  p.epi = TC_EPI_STORE;
   p.status = sc->status;
   CK(launch_tc_gemm(p, st));
   return check_status_word(sc->status, st);

@@ -569,6 +569,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
         if (lane == 0) acc[((row - r0) * p.n_pairs + pair) * p.nmat + m] += part;
       }
     }
+    // the slot's generic reads are ordered before the bulk copy that refills it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[s]);
   }

@@ -505,6 +505,7 @@ __device__ bool consume(const MegaParams& p, Ring& rg, const Smem& sm, const SDe
         }
         if (lane < RM) *ap = tot;
       }
+      fence_proxy_async_smem();  // the slot's generic reads before the bulk copy that refills it
       __syncwarp();
       if (lane == 0) mbar_arrive(&sm.empty()[warp * p.S + slot]);  // the producer may refill the slot
       ++rg.n_con;
@@ -831,6 +832,7 @@ __device__ bool router_partials(const MegaParams& p, Ring& rg, const Smem& sm, c
       const double a = warp_sum_d((a0 + a1) + (a2 + a3));
       if (lane == 0) part[t * items + i] = a;
     }
+    fence_proxy_async_smem();  // the slot's generic reads before the bulk copy that refills it
     __syncwarp();
     if (lane == 0) mbar_arrive(&sm.empty()[warp * p.S + slot]);
     ++rg.n_con;

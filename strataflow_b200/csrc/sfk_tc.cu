@@ -1,29 +1,39 @@
-// sfk_tc.cu -- tensor-core (tcgen05, kind::i8) quantized GEMM for many tokens
-// at once: prefill and large batches.
+// sfk_tc.cu -- tensor-core (tcgen05, kind::i8) quantized GEMM for many
+// activation rows at once: prompt prefill, and the routed pairs of a prefill
+// chunk grouped by expert.
 //
-// Y[t][r] = W[r,:] . x[t] for a Q4_K / Q6_K / Q8_0 weight matrix in the HBM
+// Y[i][r] = W[r,:] . x[i] for a Q4_K / Q6_K / Q8_0 weight matrix in the HBM
 // layout and activations quantized the ggml way (Q8_K for the K-quants, Q8_0
 // for Q8_0): the arithmetic of ggml's vec_dot_*_q8_K / q8_0 reached from
 // src/model/engine/engine.cpp:1882-1889,1905,1967-1970 of the reference, with
-// the integer sub-block dot products on the tensor cores.
+// the integer dot products on the tensor cores.
 //
 //  * A operand (weights): one CTA takes 128 rows (the 128 TMEM lanes); for each
-//    256-column block its threads unpack their row's codes into shared memory
-//    as signed bytes (Q4_K q in 0..15, Q6_K q - 32, Q8_0 q), in the canonical
-//    K-major no-swizzle layout (8-row x 16-byte core matrices, the two 16-byte
-//    halves of a 32-column chunk 128 bytes apart, row groups 256 bytes apart).
-//  * B operand (activations): the codes of 64 tokens, written by tc_quant in
-//    the same core-matrix layout, so a (token tile, 256-block) slab is one
-//    contiguous 16 KB bulk copy.
-//  * One MMA (M=128, K=32) per scale sub-block writes that sub-block's exact
-//    int32 dot products into its own TMEM columns (Q6_K's 16-column
-//    sub-blocks use two MMAs on half-masked copies of the chunk).
-//  * The epilogue reads the sub-block sums with tcgen05.ld and applies the
-//    ggml scale arithmetic: Q4_K d*dx*sum_j sc_j*D_j - dmin*dx*sum_j m_j*bsums,
-//    Q6_K d*dx*sum_m sc_m*D_m, Q8_0 sum_j (d_j*dx_j)*D_j, accumulated in fp32.
-// The integer parts are exact; only the fp32 order of adding blocks differs
-// from the decode kernels.  Every wait is bounded; the TMEM columns are freed
-// on every exit path.
+//    256-column block its thread r unpacks row r's codes into shared memory as
+//    signed bytes in the canonical K-major no-swizzle layout (8-row x 16-byte
+//    core matrices, the two 16-byte halves of a 32-column chunk 128 bytes
+//    apart, row groups 256 bytes apart).  The raw bytes of the next block are
+//    loaded into registers while the current block is on the tensor core.
+//  * B operand (activations): a (64-row tile, 256-column block) slab -- codes
+//    in the same core-matrix layout followed by the block's scales -- is one
+//    contiguous bulk copy; two slab buffers, the next copy in flight.
+//  * Q4_K: the 6-bit sub-block scale sc_j is split into two 3-bit digits,
+//    sc_j = 8 h_j + l_j, and the A tile holds h_j q and l_j q (each <= 105, a
+//    signed byte).  Two K = 256 accumulations then give sum_j sc_j D_j =
+//    8 D_hi + D_lo exactly: two TMEM accumulators per block instead of eight.
+//    The min term sum_j m_j S_j is two more K = 32 MMAs: a tile holding the
+//    row's eight mins against the activation's 32-column code sums split as
+//    S_j = 128 hi_j + lo_j.  Two threads per row (256 threads), each
+//    unpacking half the sub-blocks and finishing half the tokens.
+//    Q6_K keeps one accumulator per 16-column sub-block (two MMAs per
+//    32-column chunk on half-masked copies), Q8_0 one per 32-column block (its
+//    scales are f16 per block on both sides).
+//  * The epilogue reads the accumulators with tcgen05.ld and applies ggml's
+//    scale arithmetic block by block, summing the blocks in order in fp32:
+//    Q4_K d*dx*sum_j sc_j D_j - dmin*dx*sum_j m_j S_j, Q6_K d*dx*sum_m sc_m D_m,
+//    Q8_0 sum_j (d_j*dx_j)*D_j.  The integer parts are exact.
+// Every wait is bounded; on a timeout the CTA records ERR_TIMEOUT, waits
+// (bounded) for its copies and MMAs in flight, frees its TMEM and returns.
 #include <cuda_runtime.h>
 #include <cuda_fp16.h>
 
@@ -37,8 +47,8 @@
 namespace sfk {
 namespace {
 
-constexpr int TC_M = 128;       // weight rows per CTA
-constexpr int TC_THREADS = 128; // one warpgroup: thread r owns row r (TMEM lane r)
+constexpr int TC_M = 128;        // weight rows per CTA
+constexpr int TC_THREADS = 128;  // one warpgroup: thread r owns row r (TMEM lane r)
 
 // ---- tcgen05 wrappers --------------------------------------------------------
 __device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
@@ -67,12 +77,61 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");
 }
-__device__ __forceinline__ void tmem_ld8(uint32_t taddr, int (&v)[8]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
-               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
-               : "r"(taddr));
+// TMEM loads and their wait in ONE asm statement: the destination registers
+// of tcgen05.ld are written asynchronously, and an arithmetic use of them
+// does not depend on a separate wait statement, so the compiler could move the
+// use above it.  Here the registers are only defined once the wait is done.
+// Four 8-column loads (lanes of this warp's quadrant), then the wait.
+__device__ __forceinline__ void tmem_ld8x4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int (&v0)[8],
+                                           int (&v1)[8], int (&v2)[8], int (&v3)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%34];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%24,%25,%26,%27,%28,%29,%30,%31}, [%35];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
+        "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
+        "=r"(v2[0]), "=r"(v2[1]), "=r"(v2[2]), "=r"(v2[3]), "=r"(v2[4]), "=r"(v2[5]), "=r"(v2[6]), "=r"(v2[7]),
+        "=r"(v3[0]), "=r"(v3[1]), "=r"(v3[2]), "=r"(v3[3]), "=r"(v3[4]), "=r"(v3[5]), "=r"(v3[6]), "=r"(v3[7])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3)
+      : "memory");
 }
-__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// Two 16-column loads, then the wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t a0, uint32_t a1, int (&v0)[16], int (&v1)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+      "[%33];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
+        "=r"(v0[8]), "=r"(v0[9]), "=r"(v0[10]), "=r"(v0[11]), "=r"(v0[12]), "=r"(v0[13]), "=r"(v0[14]), "=r"(v0[15]),
+        "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
+        "=r"(v1[8]), "=r"(v1[9]), "=r"(v1[10]), "=r"(v1[11]), "=r"(v1[12]), "=r"(v1[13]), "=r"(v1[14]), "=r"(v1[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+}
+// One 16-column load, then the wait.
+__device__ __forceinline__ void tmem_ld16w(uint32_t taddr, int (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// A compiler-level use of 32 values: the loads producing them are complete
+// before whatever follows is issued.
+__device__ __forceinline__ void use32(const float (&v)[32]) {
+  asm volatile(
+      "" ::"f"(v[0]), "f"(v[1]), "f"(v[2]), "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7]), "f"(v[8]),
+      "f"(v[9]), "f"(v[10]), "f"(v[11]), "f"(v[12]), "f"(v[13]), "f"(v[14]), "f"(v[15]), "f"(v[16]), "f"(v[17]),
+      "f"(v[18]), "f"(v[19]), "f"(v[20]), "f"(v[21]), "f"(v[22]), "f"(v[23]), "f"(v[24]), "f"(v[25]), "f"(v[26]),
+      "f"(v[27]), "f"(v[28]), "f"(v[29]), "f"(v[30]), "f"(v[31])
+      : "memory");
+}
 
 // shared-memory matrix descriptor, K-major, no swizzle: start, leading byte
 // offset (between the two 16-byte K halves of a core matrix pair), stride byte
@@ -101,170 +160,318 @@ __device__ __forceinline__ bool mbar_wait_tc(uint64_t* bar, uint32_t parity, int
   }
 }
 
-// ---- the 256-column block of one weight row, back in GGUF byte order ---------
-// (the inverse of the HBM layout's lane-interleaved groups, sfk_synth.cu)
-__device__ __forceinline__ void load16(uint8_t* dst, const uint8_t* src) {
-  *reinterpret_cast<uint4*>(dst) = __ldg(reinterpret_cast<const uint4*>(src));
+__device__ __forceinline__ uint4 ldg16(const uint8_t* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+__device__ __forceinline__ float half_lo(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w & 0xFFFF))); }
+__device__ __forceinline__ float half_hi(uint32_t w) { return __half2float(__ushort_as_half((unsigned short)(w >> 16))); }
+__device__ __forceinline__ uint32_t byte_of(const uint4& v, int i) {
+  const uint32_t w = i < 4 ? v.x : (i < 8 ? v.y : (i < 12 ? v.z : v.w));
+  return (w >> (8 * (i & 3))) & 0xFF;
 }
-__device__ void gguf_block(int type, const uint8_t* row, int K, int b, uint8_t* out) {
+__device__ __forceinline__ void sts16(uint8_t* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(a, b, c, d);
+}
+
+// ---- one 256-column block of a weight row: raw bytes (registers) ------------
+// The HBM layout keeps a row as lane-interleaved groups of 32 units of 128
+// columns (sfk_synth.cu); block b is units 2b and 2b + 1.
+struct BlockAddr {
+  const uint8_t* base;
+  int ng, l0;
+};
+__device__ __forceinline__ BlockAddr block_addr(int type, const uint8_t* row, int K, int b) {
   const int u0 = 2 * b;
-  const int g = u0 / GROUP_UNITS, l0 = u0 % GROUP_UNITS, ng = group_units(K, g);
-  const uint8_t* base = row + group_offset(type, K, g);
-  if (type == T_Q4_K) {  // d | dmin | scales[12] | qs[128]
-    load16(out, base + 4 * ng * 16 + (l0 >> 1) * 16);
-    for (int h = 0; h < 2; ++h)
-      for (int i = 0; i < 4; ++i) load16(out + 16 + 64 * h + 16 * i, base + (i * ng + l0 + h) * 16);
-  } else if (type == T_Q6_K) {  // ql[128] | qh[64] | scales[16] | d
+  const int g = u0 / GROUP_UNITS;
+  BlockAddr a;
+  a.l0 = u0 % GROUP_UNITS;
+  a.ng = group_units(K, g);
+  a.base = row + group_offset(type, K, g);
+  return a;
+}
+
+template <int TYPE>
+struct RawBlock;
+
+// Q4_K, one half of the block for one of the row's two threads: the header
+// (d, dmin, 12 scale bytes) and the 128-column unit h of qs (qs bytes
+// 64 h + 16 i .. + 15 in q[i]).
+struct RawQ4Half {
+  uint4 hdr, q[4];
+  __device__ __forceinline__ void load(const uint8_t* row, int K, int b, int h) {
+    const BlockAddr a = block_addr(T_Q4_K, row, K, b);
+    hdr = ldg16(a.base + 4 * a.ng * 16 + (a.l0 >> 1) * 16);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = ldg16(a.base + (i * a.ng + a.l0 + h) * 16);
+  }
+};
+// Q6_K: ql[128] (8 x 16), qh[64] (4 x 16), scales[16], d
+template <>
+struct RawBlock<T_Q6_K> {
+  uint4 ql[8], qh[4];
+  uint2 sc[2];
+  uint32_t d;
+  __device__ __forceinline__ void load(const uint8_t* row, int K, int b) {
+    const BlockAddr a = block_addr(T_Q6_K, row, K, b);
+#pragma unroll
     for (int h = 0; h < 2; ++h) {
-      for (int i = 0; i < 4; ++i) load16(out + 64 * h + 16 * i, base + (i * ng + l0 + h) * 16);
-      for (int i = 4; i < 6; ++i) load16(out + 128 + 32 * h + 16 * (i - 4), base + (i * ng + l0 + h) * 16);
-      *reinterpret_cast<uint2*>(out + 192 + 8 * h) = __ldg(reinterpret_cast<const uint2*>(base + 6 * ng * 16 + (l0 + h) * 8));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) ql[h * 4 + i] = ldg16(a.base + (i * a.ng + a.l0 + h) * 16);
+#pragma unroll
+      for (int i = 4; i < 6; ++i) qh[h * 2 + i - 4] = ldg16(a.base + (i * a.ng + a.l0 + h) * 16);
+      sc[h] = __ldg(reinterpret_cast<const uint2*>(a.base + 6 * a.ng * 16 + (a.l0 + h) * 8));
     }
-    const uint16_t dv = __ldg(reinterpret_cast<const unsigned short*>(base + 6 * ng * 16 + (ng / 2) * 16 + (l0 >> 1) * 2));
-    out[208] = (uint8_t)(dv & 0xFF);
-    out[209] = (uint8_t)(dv >> 8);
+    d = __ldg(reinterpret_cast<const unsigned short*>(a.base + 6 * a.ng * 16 + (a.ng / 2) * 16 + (a.l0 >> 1) * 2));
   }
-}
-
-__device__ __forceinline__ float half_bits(const uint8_t* p) {
-  return __half2float(__ushort_as_half((unsigned short)(p[0] | (p[1] << 8))));
-}
-
-// ggml get_scale_min_k4: 6-bit scale and min of Q4_K sub-block j
-__device__ __forceinline__ void scale_min_k4(int j, const uint8_t* q, int* sc, int* m) {
-  if (j < 4) {
-    *sc = q[j] & 63;
-    *m = q[j + 4] & 63;
-  } else {
-    *sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-    *m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+};
+// Q8_0: the block's two 128-column units: chunk i of unit h is the 16-byte
+// half (i & 1) of 32-column block 4h + i / 2; four f16 scales per unit
+template <>
+struct RawBlock<T_Q8_0> {
+  uint4 q[16];
+  uint2 sc[2];
+  __device__ __forceinline__ void load(const uint8_t* row, int K, int b) {
+    const BlockAddr a = block_addr(T_Q8_0, row, K, b);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) q[h * 8 + i] = ldg16(a.base + (i * a.ng + a.l0 + h) * 16);
+      sc[h] = __ldg(reinterpret_cast<const uint2*>(a.base + 8 * a.ng * 16 + (a.l0 + h) * 8));
+    }
   }
-}
-
-// Row scales of one block (per sub-block), in shared memory per row:
-//   Q4_K: f[0] = d, f[1] = dmin, i8 sc[8], m[8]
-//   Q6_K: f[0] = d, i8 sc[16]
-//   Q8_0: f[0..7] = d_j
-struct RowScales {
-  float f[8];
-  int8_t s[16];
-  uint8_t m[8];
 };
 
-// Q8_0 rows go straight from the HBM layout into the A tile: unit h of the
-// block holds 32-column blocks 4h..4h+3, chunk i of a unit is the 16-byte
-// half (i & 1) of block 4h + i / 2, and the unit's four f16 scales follow.
-__device__ void unpack_row_q80(const uint8_t* row, int K, int b, int r, uint8_t* A, RowScales* rs) {
-  const int u0 = 2 * b;
-  const int g = u0 / GROUP_UNITS, l0 = u0 % GROUP_UNITS, ng = group_units(K, g);
-  const uint8_t* base = row + group_offset(T_Q8_0, K, g);
-  uint8_t* rowbase = A + (r >> 3) * 256 + (r & 7) * 16;
+// Row scales kept in the unpacking thread's registers for its epilogue.
+template <int TYPE>
+struct RowScales;
+template <>
+struct RowScales<T_Q6_K> {
+  float d;
+  uint2 sc0, sc1;  // the 16 int8 sub-block scales
+};
+template <>
+struct RowScales<T_Q8_0> {
+  float d[8];
+};
+
+// ---- unpack: raw block -> A tile row + row scales ---------------------------
+// A row r lives at (r >> 3) * 256 + (r & 7) * 16 within each 4 KB chunk.
+// Q4_K half h of row r: sub-blocks 4h .. 4h + 3 into the A_hi / A_lo tiles
+// (sub-block j = 2c + hi holds the low (hi = 0) or high nibbles of qs chunk c,
+// its K half kh in q[2 (c - 2h) + kh]); the header's d and dmin out; half 0
+// also writes the row's mins into K half 0 of the min tile (columns 0..7).
+__device__ __forceinline__ void unpack_q4k_half(const RawQ4Half& raw, int h, uint8_t* Arow, uint8_t* Amrow,
+                                                float* d, float* dmin) {
+  *d = half_lo(raw.hdr.x);
+  *dmin = half_hi(raw.hdr.x);
+  // ggml get_scale_min_k4 over the 12 scale bytes (header bytes 4..15)
+  uint32_t sb[12];
+#pragma unroll
+  for (int i = 0; i < 12; ++i) sb[i] = byte_of(raw.hdr, 4 + i);
+  uint32_t sc[8], mn[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j < 4) {
+      sc[j] = sb[j] & 63;
+      mn[j] = sb[j + 4] & 63;
+    } else {
+      sc[j] = (sb[j + 4] & 0xF) | ((sb[j - 4] >> 6) << 4);
+      mn[j] = (sb[j + 4] >> 4) | ((sb[j] >> 6) << 4);
+    }
+  }
+  if (h == 0)
+    sts16(Amrow, mn[0] | (mn[1] << 8) | (mn[2] << 16) | (mn[3] << 24), mn[4] | (mn[5] << 8) | (mn[6] << 16) | (mn[7] << 24),
+          0u, 0u);
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    const int j = 4 * h + jj;
+    const uint32_t sh = sc[j] >> 3, sl = sc[j] & 7;
+#pragma unroll
+    for (int kh = 0; kh < 2; ++kh) {
+      const uint4 v = raw.q[2 * (jj >> 1) + kh];
+      const int s = (jj & 1) ? 4 : 0;
+      const uint32_t c0 = (v.x >> s) & 0x0F0F0F0Fu, c1 = (v.y >> s) & 0x0F0F0F0Fu;
+      const uint32_t c2 = (v.z >> s) & 0x0F0F0F0Fu, c3 = (v.w >> s) & 0x0F0F0F0Fu;
+      // bytes <= 15 * 7: the products stay inside their bytes
+      sts16(Arow + j * 4096 + kh * 128, c0 * sh, c1 * sh, c2 * sh, c3 * sh);
+      sts16(Arow + 32768 + j * 4096 + kh * 128, c0 * sl, c1 * sl, c2 * sl, c3 * sl);
+    }
+  }
+}
+
+// Q6_K codes q - 32 as signed bytes, four at a time: q = low nibble | (2 high
+// bits << 4) in 0..63, and (q + 0x60) ^ 0x80 is q - 32 in two's complement
+// without carries between bytes.
+__device__ __forceinline__ uint32_t q6_word(uint32_t lo4, uint32_t hi2) {
+  return (((lo4 & 0x0F0F0F0Fu) | (hi2 & 0x30303030u)) + 0x60606060u) ^ 0x80808080u;
+}
+__device__ __forceinline__ void unpack(const RawBlock<T_Q6_K>& raw, uint8_t* Arow, RowScales<T_Q6_K>& rs) {
+  rs.d = half_lo(raw.d);
+  rs.sc0 = raw.sc[0];
+  rs.sc1 = raw.sc[1];
+  // ggml dequantize_row_q6_K: in half n (128 values) with l in 0..31,
+  // y[l] = ql[l] lo | qh[l] bits 0-1, y[l+32] = ql[l+32] lo | bits 2-3,
+  // y[l+64] = ql[l] hi | bits 4-5, y[l+96] = ql[l+32] hi | bits 6-7.
+  // 16-column sub-block m = 8n + 2 part + (l >= 16) goes to masked chunk m,
+  // K half m & 1 (the other half is zero, written once).
+#pragma unroll
+  for (int n = 0; n < 2; ++n)
+#pragma unroll
+    for (int hl = 0; hl < 2; ++hl) {
+      const uint4 L = raw.ql[4 * n + hl], L2 = raw.ql[4 * n + 2 + hl], H = raw.qh[2 * n + hl];
+      const int m0 = 8 * n + hl;
+      uint8_t* a = Arow + hl * 128;
+      sts16(a + (m0 + 0) * 4096, q6_word(L.x, H.x << 4), q6_word(L.y, H.y << 4), q6_word(L.z, H.z << 4),
+            q6_word(L.w, H.w << 4));
+      sts16(a + (m0 + 2) * 4096, q6_word(L2.x, H.x << 2), q6_word(L2.y, H.y << 2), q6_word(L2.z, H.z << 2),
+            q6_word(L2.w, H.w << 2));
+      sts16(a + (m0 + 4) * 4096, q6_word(L.x >> 4, H.x), q6_word(L.y >> 4, H.y), q6_word(L.z >> 4, H.z),
+            q6_word(L.w >> 4, H.w));
+      sts16(a + (m0 + 6) * 4096, q6_word(L2.x >> 4, H.x >> 2), q6_word(L2.y >> 4, H.y >> 2),
+            q6_word(L2.z >> 4, H.z >> 2), q6_word(L2.w >> 4, H.w >> 2));
+    }
+}
+
+__device__ __forceinline__ void unpack(const RawBlock<T_Q8_0>& raw, uint8_t* Arow, RowScales<T_Q8_0>& rs) {
+#pragma unroll
   for (int h = 0; h < 2; ++h) {
-    const int lu = l0 + h;
-    for (int i = 0; i < 8; ++i)
-      *reinterpret_cast<uint4*>(rowbase + (4 * h + i / 2) * 4096 + (i & 1) * 128) =
-          __ldg(reinterpret_cast<const uint4*>(base + (i * ng + lu) * 16));
-    const uint2 dh = __ldg(reinterpret_cast<const uint2*>(base + 8 * ng * 16 + lu * 8));
-    rs->f[4 * h + 0] = __half2float(__ushort_as_half((unsigned short)(dh.x & 0xFFFF)));
-    rs->f[4 * h + 1] = __half2float(__ushort_as_half((unsigned short)(dh.x >> 16)));
-    rs->f[4 * h + 2] = __half2float(__ushort_as_half((unsigned short)(dh.y & 0xFFFF)));
-    rs->f[4 * h + 3] = __half2float(__ushort_as_half((unsigned short)(dh.y >> 16)));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) *reinterpret_cast<uint4*>(Arow + (4 * h + i / 2) * 4096 + (i & 1) * 128) = raw.q[h * 8 + i];
+    rs.d[4 * h + 0] = half_lo(raw.sc[h].x);
+    rs.d[4 * h + 1] = half_hi(raw.sc[h].x);
+    rs.d[4 * h + 2] = half_lo(raw.sc[h].y);
+    rs.d[4 * h + 3] = half_hi(raw.sc[h].y);
   }
 }
 
-// unpack one row's Q4_K / Q6_K block (GGUF bytes in `blk`) into the A tile
-// (chunk-major core-matrix layout) and its scales
-__device__ void unpack_row(int type, const uint8_t* blk, int r, uint8_t* A, RowScales* rs) {
-  uint8_t* rowbase = A + (r >> 3) * 256 + (r & 7) * 16;  // + chunk * 4096 (Q6_K: masked chunk * 4096) + half * 128
-  if (type == T_Q4_K) {
-    rs->f[0] = half_bits(blk);
-    rs->f[1] = half_bits(blk + 2);
-    for (int j = 0; j < 8; ++j) {
-      int sc, m;
-      scale_min_k4(j, blk + 4, &sc, &m);
-      rs->s[j] = (int8_t)sc;
-      rs->m[j] = (uint8_t)m;
+template <int TYPE>
+struct TcShape;
+template <>
+struct TcShape<T_Q6_K> {  // sixteen accumulators of 32 rows
+  static constexpr int N = 32, A_BYTES = 65536, MINB = 1;
+  static constexpr uint32_t NCOL = 512;
+};
+template <>
+struct TcShape<T_Q8_0> {  // eight accumulators of 64 rows
+  static constexpr int N = 64, A_BYTES = 32768, MINB = 1;
+  static constexpr uint32_t NCOL = 512;
+};
+
+// ---- MMAs of one block ----------------------------------------------------------
+// Bs: the slab's codes, already offset to this CTA's N rows of the tile.
+template <int TYPE>
+__device__ __forceinline__ void issue_mmas(uint32_t tmem, const uint8_t* A, const uint8_t* Bs) {
+  constexpr int N = TcShape<TYPE>::N;
+  constexpr uint32_t idesc = idesc_i8(TC_M, N);
+  if (TYPE == T_Q6_K) {
+#pragma unroll 1
+    for (int m = 0; m < 16; ++m)
+      mma_i8(tmem + (uint32_t)(m * N), smem_desc(A + m * 4096, 128, 256), smem_desc(Bs + (m >> 1) * 2048, 128, 256),
+             idesc, 0u);
+  } else {
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c)
+      mma_i8(tmem + (uint32_t)(c * N), smem_desc(A + c * 4096, 128, 256), smem_desc(Bs + c * 2048, 128, 256), idesc,
+             0u);
+  }
+}
+
+// ---- epilogue of one block: acc[i] += this block's dot of row r, row i ------
+// tb: this warp's TMEM lane base; slab: the block's slab; i0: first
+// activation row of the CTA within the tile.
+__device__ __forceinline__ int sbyte(uint2 v, int i) {
+  const uint32_t w = i < 4 ? v.x : v.y;
+  return (int)(int8_t)((w >> (8 * (i & 3))) & 0xFF);
+}
+__device__ __forceinline__ void block_epilogue(const RowScales<T_Q6_K>& s, uint32_t tb, const uint8_t* slab, int i0,
+                                               float (&acc)[32]) {
+  const float* dxs = reinterpret_cast<const float*>(slab + TC_SLAB_DX) + i0;
+#pragma unroll
+  for (int t0 = 0; t0 < 32; t0 += 16) {
+    int isum[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) isum[i] = 0;
+#pragma unroll
+    for (int m = 0; m < 16; m += 2) {
+      int D0[16], D1[16];
+      tmem_ld16x2(tb + (uint32_t)(m * 32 + t0), tb + (uint32_t)((m + 1) * 32 + t0), D0, D1);
+      const uint2 sv = m < 8 ? s.sc0 : s.sc1;
+      const int s0 = sbyte(sv, m & 7), s1 = sbyte(sv, (m + 1) & 7);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) isum[i] += s0 * D0[i] + s1 * D1[i];
     }
-    const uint8_t* qs = blk + 16;
-    // sub-block j = 2c (low nibbles of qs chunk c) and 2c + 1 (high nibbles)
-    for (int c = 0; c < 4; ++c)
-      for (int hi = 0; hi < 2; ++hi) {
-        const int j = 2 * c + hi;
-        for (int kh = 0; kh < 2; ++kh) {
-          uint32_t w[4];
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t v = *reinterpret_cast<const uint32_t*>(qs + 32 * c + 16 * kh + 4 * q);
-            w[q] = hi ? ((v >> 4) & 0x0F0F0F0Fu) : (v & 0x0F0F0F0Fu);
-          }
-          *reinterpret_cast<uint4*>(rowbase + j * 4096 + kh * 128) = make_uint4(w[0], w[1], w[2], w[3]);
-        }
-      }
-  } else if (type == T_Q6_K) {
-    rs->f[0] = half_bits(blk + 208);
-    for (int m = 0; m < 16; ++m) rs->s[m] = (int8_t)blk[192 + m];
-    const uint8_t* ql = blk;
-    const uint8_t* qh = blk + 128;
-    // ggml dequantize_row_q6_K: two halves of 128; in half n, l in 0..31:
-    // y[l] = q1, y[l+32] = q2, y[l+64] = q3, y[l+96] = q4 (each q - 32)
-    __align__(16) uint8_t codes[256];
-    for (int n = 0; n < 2; ++n)
-      for (int l = 0; l < 32; ++l) {
-        const uint8_t a = ql[64 * n + l], b = ql[64 * n + l + 32], h = qh[32 * n + l];
-        codes[128 * n + l] = (uint8_t)(int8_t)(((a & 0xF) | ((h & 3) << 4)) - 32);
-        codes[128 * n + l + 32] = (uint8_t)(int8_t)(((b & 0xF) | (((h >> 2) & 3) << 4)) - 32);
-        codes[128 * n + l + 64] = (uint8_t)(int8_t)(((a >> 4) | (((h >> 4) & 3) << 4)) - 32);
-        codes[128 * n + l + 96] = (uint8_t)(int8_t)(((b >> 4) | (((h >> 6) & 3) << 4)) - 32);
-      }
-    // 16-column sub-block m = e / 16 sits in masked chunk m: its codes in the
-    // K half (m & 1) of 32-column chunk m / 2, zeros in the other half
-    const uint4 z = make_uint4(0, 0, 0, 0);
-    for (int m = 0; m < 16; ++m) {
-      const uint4 v = *reinterpret_cast<const uint4*>(codes + 16 * m);
-      *reinterpret_cast<uint4*>(rowbase + m * 4096 + (m & 1) * 128) = v;
-      *reinterpret_cast<uint4*>(rowbase + m * 4096 + ((m & 1) ^ 1) * 128) = z;
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      acc[t0 + i] = __fadd_rn(acc[t0 + i], __fmul_rn(__fmul_rn(s.d, dxs[t0 + i]), (float)isum[i]));
+  }
+}
+
+__device__ __forceinline__ void block_epilogue(const RowScales<T_Q8_0>& s, uint32_t tb, const uint8_t* slab, int i0,
+                                               float (&acc)[64]) {
+  const float* dxs = reinterpret_cast<const float*>(slab + TC_SLAB_DX) + i0 * 8;
+  // ggml vec_dot_q8_0_q8_0: each 32-column block added in order
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+#pragma unroll
+    for (int t0 = 0; t0 < 64; t0 += 16) {
+      int D[16];
+      tmem_ld16w(tb + (uint32_t)(c * 64 + t0), D);
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        acc[t0 + i] = __fadd_rn(acc[t0 + i], __fmul_rn((float)D[i], __fmul_rn(s.d[c], dxs[(t0 + i) * 8 + c])));
     }
   }
 }
 
-__device__ __forceinline__ void zero_row(int type, int r, uint8_t* A, RowScales* rs) {
-  uint8_t* rowbase = A + (r >> 3) * 256 + (r & 7) * 16;
-  const int nch = type == T_Q6_K ? 16 : 8;
-  const uint4 z = make_uint4(0, 0, 0, 0);
-  for (int c = 0; c < nch; ++c)
-    for (int kh = 0; kh < 2; ++kh) *reinterpret_cast<uint4*>(rowbase + c * 4096 + kh * 128) = z;
-  for (int i = 0; i < 8; ++i) rs->f[i] = 0.0f;
-  for (int i = 0; i < 16; ++i) rs->s[i] = 0;
-  for (int i = 0; i < 8; ++i) rs->m[i] = 0;
+// Q6_K: the zero K half of every masked chunk of row r
+__device__ __forceinline__ void zero_masked_halves(uint8_t* Arow) {
+#pragma unroll
+  for (int m = 0; m < 16; ++m) sts16(Arow + m * 4096 + ((m & 1) ^ 1) * 128, 0u, 0u, 0u, 0u);
 }
 
 // ---- activations -------------------------------------------------------------
-// Codes of token t, column k in the tile layout: tile t / 64, 32-column chunk
-// k / 32, token group (t % 64) / 8, K half, token row, byte.
-__device__ __forceinline__ int64_t xq_off(int t, int k, int KC) {
-  const int64_t tile = t / TC_TT, tg = (t % TC_TT) >> 3;
-  return ((tile * KC + k / 32) * 8 + tg) * 256 + ((k % 32) / 16) * 128 + (t & 7) * 16 + (k % 16);
-}
-
-// One warp per (token, 256-column block): ggml quantize_row_q8_K_ref (or
-// quantize_row_q8_0_ref) of x[t][256 blk .. +256), codes into the tile layout,
-// the block scale (Q8_K d, or the eight f16-rounded Q8_0 scales) and the
-// 16-column sums (Q8_K).  Tokens n..npad-1 get zeros.
-__global__ void __launch_bounds__(256) tc_quant_kernel(int act_type, const float* x, int n, int npad, int K,
-                                                       int8_t* xq, float* dx, int16_t* bs) {
+// One warp per (activation row, 256-column block): ggml quantize_row_q8_K_ref
+// (or quantize_row_q8_0_ref) of the block, codes into the slab's core-matrix
+// layout, the scale(s), and for Q8_K the 32-column code sums (high and low
+// parts, the min term's B operand).
+__global__ void __launch_bounds__(256) tc_quant_kernel(int act_type, const float* x, int64_t ldx, const int* rows,
+                                                       int n_src, int npad, int K, uint8_t* out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nb = K / 256, KC = K / 32;
+  const int nb = K / 256;
   for (int w = blockIdx.x * 8 + warp; w < npad * nb; w += gridDim.x * 8) {
     const int t = w / nb, blk = w % nb;
+    const int src = rows ? rows[t] : t;
+    const bool valid = src >= 0 && src < n_src;
     float v[8];
+    if (valid) {
+      const float4* xp = reinterpret_cast<const float4*>(x + (int64_t)src * ldx + blk * 256 + lane * 8);
+      const float4 a = xp[0], b = xp[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) v[i] = t < n ? x[(int64_t)t * K + blk * 256 + lane * 8 + i] : 0.0f;
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    }
+    uint8_t* slab = out + ((int64_t)(t / TC_TT) * nb + blk) * TC_SLAB;
+    const int tl = t % TC_TT;
     int q[8];
     if (act_type == T_Q8_K) {
       float d;
-      int s;
-      q8k_block(v, lane, q, &d, &s);
-      if (lane == 0) dx[(int64_t)t * nb + blk] = d;
-      if ((lane & 1) == 0) bs[(int64_t)t * (K / 16) + blk * 16 + (lane >> 1)] = (int16_t)s;
+      int s16;
+      q8k_block(v, lane, q, &d, &s16);
+      int s = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) s += q[i];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if (lane == 0) reinterpret_cast<float*>(slab + TC_SLAB_DX)[tl] = d;
+      // S_j = 128 hi + lo as column j of the two sum chunks (row tl, K half 0)
+      const int rowoff = (tl >> 3) * 256 + (tl & 7) * 16;
+      if ((lane & 3) == 0) {
+        slab[TC_SLAB_SHI + rowoff + (lane >> 2)] = (uint8_t)(int8_t)(s >> 7);
+        slab[TC_SLAB_SLO + rowoff + (lane >> 2)] = (uint8_t)(s & 127);
+      }
+      if (lane == 0) {
+        *reinterpret_cast<uint2*>(slab + TC_SLAB_SHI + rowoff + 8) = make_uint2(0u, 0u);
+        *reinterpret_cast<uint2*>(slab + TC_SLAB_SLO + rowoff + 8) = make_uint2(0u, 0u);
+      }
     } else {
       float amax = 0.0f;
 #pragma unroll
@@ -275,41 +482,46 @@ __global__ void __launch_bounds__(256) tc_quant_kernel(int act_type, const float
       const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
 #pragma unroll
       for (int i = 0; i < 8; ++i) q[i] = (int)roundf(__fmul_rn(v[i], id));
-      if ((lane & 3) == 0) dx[(int64_t)t * (K / 32) + blk * 8 + (lane >> 2)] = __half2float(__float2half_rn(d));
+      if ((lane & 3) == 0)
+        reinterpret_cast<float*>(slab + TC_SLAB_DX)[tl * 8 + (lane >> 2)] = __half2float(__float2half_rn(d));
     }
-    const int k0 = blk * 256 + lane * 8;
-    const uint32_t lo = (uint32_t)(q[0] & 0xFF) | ((uint32_t)(q[1] & 0xFF) << 8) | ((uint32_t)(q[2] & 0xFF) << 16) |
-                        ((uint32_t)(q[3] & 0xFF) << 24);
-    const uint32_t hi = (uint32_t)(q[4] & 0xFF) | ((uint32_t)(q[5] & 0xFF) << 8) | ((uint32_t)(q[6] & 0xFF) << 16) |
-                        ((uint32_t)(q[7] & 0xFF) << 24);
-    *reinterpret_cast<uint2*>(xq + xq_off(t, k0, KC)) = make_uint2(lo, hi);
+    // columns lane*8 .. +7: chunk lane / 4, K half (lane / 2) & 1, byte (lane & 1) * 8
+    *reinterpret_cast<uint2*>(slab + (lane >> 2) * 2048 + (tl >> 3) * 256 + ((lane >> 1) & 1) * 128 + (tl & 7) * 16 +
+                              (lane & 1) * 8) = pack8(q);
   }
 }
 
 // ---- the GEMM ----------------------------------------------------------------
-// grid.x: 128-row weight tiles; grid.y: token tiles of N tokens (N = 64, or 32
-// for Q6_K whose 16 sub-block accumulators per block need twice the columns).
-template <int TYPE, int N>
-__global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(TcGemmParams p) {
-  constexpr int NCH = TYPE == T_Q6_K ? 16 : 8;       // accumulators (sub-blocks) per 256-block
-  constexpr uint32_t NCOL = (uint32_t)(NCH * N);     // TMEM columns: 512
-  static_assert(NCOL <= 512, "TMEM holds 512 columns");
+// grid.x: activation tiles x (64 / N) (the CTAs that share a weight tile run
+// together); grid.y: 128-row weight tiles.
+template <int TYPE>
+__global__ void __launch_bounds__(TC_THREADS, TcShape<TYPE>::MINB) tc_gemm_kernel(const __grid_constant__ TcGemmParams p) {
+  constexpr int N = TcShape<TYPE>::N;
+  constexpr uint32_t NCOL = TcShape<TYPE>::NCOL;
+  constexpr int SUB = TC_TT / N;
   extern __shared__ __align__(1024) uint8_t smem[];
-  uint8_t* A = smem;                                 // NCH x 4 KB
-  uint8_t* B = smem + NCH * 4096;                    // 16 KB: one (64-token tile, 256-block) slab
-  RowScales* rsc = reinterpret_cast<RowScales*>(B + 16384);
-  float* dxs = reinterpret_cast<float*>(rsc + TC_M);        // [N] (Q8_K) or [N][8] (Q8_0)
-  int16_t* bss = reinterpret_cast<int16_t*>(dxs + N * 8);  // [N][16]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(bss + N * 16);  // [0] B copy, [1] MMA done
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 2);
+  uint8_t* A = smem;
+  uint8_t* B = smem + TcShape<TYPE>::A_BYTES;                     // [2][TC_SLAB]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(B + 2 * TC_SLAB);  // [0..1] slab full, [2] MMAs done
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 3);
 
+  const int t64 = blockIdx.x / SUB, sub = blockIdx.x % SUB;
+  if (t64 >= p.ntile) return;
+  int expert = 0;
+  if (p.tile_expert) {
+    expert = p.tile_expert[t64];
+    if (expert < 0) return;  // uniform: the whole CTA leaves before any allocation
+  }
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int r = tid;
-  const int row = blockIdx.x * TC_M + r;
-  const int tt = blockIdx.y;                 // token tile of N tokens
-  const int t64 = (tt * N) / TC_TT;          // 64-token activation tile
-  const int half = ((tt * N) % TC_TT) / 32;  // Q6_K: which 32 tokens of it
-  const int KC = p.K / 32, nb = p.K / 256;
+  const int row = blockIdx.y * TC_M + tid;
+  const bool live = row < p.rows;
+  const int nb = p.K / 256;
+  const int nmat = p.epi == TC_EPI_SWIGLU ? 2 : 1;
+  const int total = nmat * nb;
+  const uint8_t* slabs = p.xq + (int64_t)t64 * nb * TC_SLAB;
+  uint8_t* Arow = A + (tid >> 3) * 256 + (tid & 7) * 16;
+  // rows past the matrix compute row 0 again; their results are not stored
+  const int64_t woff = (int64_t)expert * p.expert_stride + (int64_t)(live ? row : 0) * p.rowstride;
 
   if (warp == 0) {
     tmem_alloc(tslot, NCOL);
@@ -318,162 +530,410 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_gemm_kernel(TcGemmParams p) 
   if (tid == 0) {
     mbar_init(&bars[0], 1);
     mbar_init(&bars[1], 1);
+    mbar_init(&bars[2], 1);
     fence_mbar_init();
   }
+  if (TYPE == T_Q6_K) zero_masked_halves(Arow);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
+  const uint32_t tb = tmem + ((uint32_t)(warp * 32) << 16);
 
+  if (tid == 0) {
+    mbar_arrive_expect_tx(&bars[0], TC_SLAB);
+    bulk_g2s(B, slabs, TC_SLAB, &bars[0]);
+  }
+  RawBlock<TYPE> raw;
+  raw.load(p.w + woff, p.K, 0);
   float acc[N];
 #pragma unroll
   for (int i = 0; i < N; ++i) acc[i] = 0.0f;
-  const uint32_t idesc = idesc_i8(TC_M, N);
   bool ok = true;
-  __align__(16) uint8_t blk[224];
-  for (int b = 0; b < nb && ok; ++b) {
-    // activations of this (token tile, block): one bulk copy + scales
-    if (tid == 0) {
-      mbar_arrive_expect_tx(&bars[0], 16384u);
-      bulk_g2s(B, p.xq + ((int64_t)t64 * KC + b * 8) * 2048, 16384u, &bars[0]);
+  bool mma_pending = false;
+  int g = 0;
+  for (; g < total; ++g) {
+    const int mat = g >= nb ? 1 : 0, b = g - mat * nb;
+    if (tid == 0 && g + 1 < total) {  // the next slab into the other buffer (its last readers are done)
+      mbar_arrive_expect_tx(&bars[(g + 1) & 1], TC_SLAB);
+      bulk_g2s(B + ((g + 1) & 1) * TC_SLAB, slabs + (int64_t)((g + 1) % nb) * TC_SLAB, TC_SLAB, &bars[(g + 1) & 1]);
     }
-    for (int i = tid; i < N; i += TC_THREADS) {
-      const int t = tt * N + i;
-      if (p.act_type == T_Q8_K) {
-        dxs[i] = p.dx[(int64_t)t * nb + b];
-      } else {
-        for (int j = 0; j < 8; ++j) dxs[i * 8 + j] = p.dx[(int64_t)t * (p.K / 32) + b * 8 + j];
-      }
-    }
-    if (p.act_type == T_Q8_K)
-      for (int i = tid; i < N * 16; i += TC_THREADS)
-        bss[i] = p.bs[(int64_t)(tt * N + i / 16) * (p.K / 16) + b * 16 + (i % 16)];
-    // this thread's weight row: GGUF block bytes -> A codes + scales
-    if (row < p.rows) {
-      if (TYPE == T_Q8_0) {
-        unpack_row_q80(p.w + (int64_t)row * p.rowstride, p.K, b, r, A, &rsc[r]);
-      } else {
-        gguf_block(TYPE, p.w + (int64_t)row * p.rowstride, p.K, b, blk);
-        unpack_row(TYPE, blk, r, A, &rsc[r]);
-      }
-    } else {
-      zero_row(TYPE, r, A, &rsc[r]);
+    RowScales<TYPE> rs;
+    unpack(raw, Arow, rs);
+    if (g + 1 < total) {
+      const int nm = (g + 1) >= nb ? 1 : 0;
+      raw.load((nm ? p.w2 : p.w) + woff, p.K, (g + 1) - nm * nb);
     }
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the generic stores -> the tensor core's reads
     __syncthreads();
-    ok = mbar_wait_tc(&bars[0], b & 1, p.status);
+    ok = mbar_wait_tc(&bars[g & 1], (uint32_t)((g >> 1) & 1), p.status);
     ok = __syncthreads_and(ok) != 0;  // every thread leaves together
+    if (!ok) break;
     tc_fence_after();
-    if (ok && tid == 0) {
-      // one K = 32 MMA per accumulator: sub-block c's dots -> columns [c*N, c*N + N)
-#pragma unroll 1
-      for (int c = 0; c < NCH; ++c) {
-        const int chunk = TYPE == T_Q6_K ? (c >> 1) : c;  // the 32-column chunk of the activations
-        const uint64_t ad = smem_desc(A + c * 4096, 128, 256);
-        const uint64_t bd = smem_desc(B + chunk * 2048 + half * 1024, 128, 256);
-        mma_i8(tmem + (uint32_t)(c * N), ad, bd, idesc, 0u);
-      }
-      mma_commit(&bars[1]);
+    const uint8_t* slab = B + (g & 1) * TC_SLAB;
+    if (tid == 0) {
+      issue_mmas<TYPE>(tmem, A, slab + sub * N * 32);
+      mma_commit(&bars[2]);
     }
-    if (ok) ok = mbar_wait_tc(&bars[1], b & 1, p.status);
+    mma_pending = true;
+    ok = mbar_wait_tc(&bars[2], (uint32_t)(g & 1), p.status);
     ok = __syncthreads_and(ok) != 0;
+    if (!ok) break;
+    mma_pending = false;
     tc_fence_after();
-    if (ok) {
-      // epilogue: the sub-block sums of row r (TMEM lane r) for 8 tokens at a time
-      const RowScales& s = rsc[r];
-      const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+    block_epilogue(rs, tb, slab, sub * N, acc);
+    // this slab buffer's generic reads before the bulk copy that refills it
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();  // A, this slab buffer and TMEM are rewritten next
+    if (b == nb - 1) {
+      if (live) {
 #pragma unroll
-      for (int t0 = 0; t0 < N; t0 += 8) {
-        int isum[8], D[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) isum[i] = 0;
-#pragma unroll 1
-        for (int c = 0; c < NCH; ++c) {
-          tmem_ld8(lane_base + (uint32_t)(c * N + t0), D);
-          tmem_wait_ld();
-          if (TYPE == T_Q8_0) {  // ggml vec_dot_q8_0_q8_0: each 32-block added in order
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              acc[t0 + i] = __fadd_rn(acc[t0 + i], __fmul_rn((float)D[i], __fmul_rn(s.f[c], dxs[(t0 + i) * 8 + c])));
+        for (int i = 0; i < N; ++i) {
+          const int ir = t64 * TC_TT + sub * N + i;
+          if (!p.tile_expert && ir >= p.n) continue;
+          float* yp = p.y + (int64_t)ir * p.ldy + row;
+          if (p.epi == TC_EPI_RESID) {
+            *yp = __fadd_rn(acc[i], p.res[(int64_t)ir * p.ldres + row]);
+          } else if (p.epi == TC_EPI_SWIGLU && mat == 1) {
+            // h = silu(gate) * up (ggml_swiglu_split, engine.cpp:1969); this
+            // thread stored the gate value here at the end of matrix 0
+            const float gv = *yp;
+            *yp = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, sfk_expf(-gv))), acc[i]);
           } else {
-            const int sc = s.s[c];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) isum[i] += sc * D[i];
+            *yp = acc[i];
           }
-        }
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int t = t0 + i;
-          float v = 0.0f;
-          if (TYPE == T_Q4_K) {
-            int imin = 0;
-            for (int j = 0; j < 8; ++j) imin += (int)s.m[j] * ((int)bss[t * 16 + 2 * j] + (int)bss[t * 16 + 2 * j + 1]);
-            const float d = __fmul_rn(s.f[0], dxs[t]), dmin = __fmul_rn(s.f[1], dxs[t]);
-            v = __fsub_rn(__fmul_rn(d, (float)isum[i]), __fmul_rn(dmin, (float)imin));
-          } else if (TYPE == T_Q6_K) {
-            v = __fmul_rn(__fmul_rn(s.f[0], dxs[t]), (float)isum[i]);
-          }
-          if (TYPE != T_Q8_0) acc[t] = __fadd_rn(acc[t], v);
         }
       }
-    }
-    tc_fence_before();
-    __syncthreads();  // A, B, the scales and TMEM are rewritten by the next block
-  }
-  if (ok && row < p.rows) {
 #pragma unroll
-    for (int i = 0; i < N; ++i) {
-      const int t = tt * N + i;
-      if (t < p.n) p.y[(int64_t)t * p.ldy + row] = acc[i];
+      for (int i = 0; i < N; ++i) acc[i] = 0.0f;
     }
+  }
+  if (!ok && tid == 0) {
+    // drain what is still in flight before the TMEM and shared memory go:
+    // the MMAs of block g (when issued) and the slab copies g and g + 1
+    if (mma_pending) mbar_wait_tc(&bars[2], (uint32_t)(g & 1), p.status);
+    else mbar_wait_tc(&bars[g & 1], (uint32_t)((g >> 1) & 1), p.status);
+    if (g + 1 < total) mbar_wait_tc(&bars[(g + 1) & 1], (uint32_t)(((g + 1) >> 1) & 1), p.status);
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, NCOL);
 }
 
-template <int TYPE, int N>
+// ---- Q4_K: warp-specialized pipeline ------------------------------------------
+// One CTA per (64-row activation tile, 128 weight rows), 14 warps:
+//   warps 0-3   unpack: thread r turns row r's next block into A_hi / A_lo and
+//               the min tile, in one of two A stages;
+//   warps 4-11  epilogue: two warps per TMEM lane quadrant (tokens 0-31 and
+//               32-63 of the tile) apply the block's scales to the four
+//               accumulators of one of two TMEM stages; they copy the
+//               activation scales out of the slab first and release it;
+//   warp 12     MMA issue (one thread): 18 MMAs per block, then commits that
+//               free the A stage and fill the TMEM stage;
+//   warp 13     activation slabs (one thread): bulk copies into three stages.
+// Each hand-off is an mbarrier (full / empty per stage), so the unpack of
+// block b + 2, the MMAs of block b + 1 and the epilogue of block b overlap.
+// The MMAs of a block are committed once, to acc_full: the epilogue waits on
+// it for the accumulators and the unpack warps for the A stage.
+// TMEM stage columns: D_hi [0, 64), D_lo [64, 128), M_hi [128, 192),
+// M_lo [192, 256); sum_j sc_j D_j = 8 D_hi + D_lo, sum_j m_j S_j =
+// 128 M_hi + M_lo.  Every wait is bounded; a role that gives up raises the
+// CTA's abort flag, the others leave at their next wait, and the copies and
+// MMAs still in flight are drained before TMEM is freed.
+constexpr int Q4_UNPACK_WARPS = 4, Q4_EPI_WARPS = 8;
+constexpr int Q4_MMA_WARP = Q4_UNPACK_WARPS + Q4_EPI_WARPS, Q4_TMA_WARP = Q4_MMA_WARP + 1;
+constexpr int Q4_THREADS = (Q4_TMA_WARP + 1) * 32;
+constexpr uint32_t Q4_NCOL = 512;          // two TMEM stages of 256 columns
+constexpr int Q4_ASTAGE = 65536 + 4096;    // A_hi | A_lo | min tile
+constexpr int Q4_ASTAGES = 2;  // A tiles and TMEM accumulator sets
+constexpr int Q4_BSTAGES = 3;  // activation slabs
+constexpr int Q4_SMEM = Q4_ASTAGES * Q4_ASTAGE + Q4_BSTAGES * TC_SLAB + 16 * 8 + 16;  // + barriers, TMEM slot, abort flag
+
+struct Q4Bars {
+  uint64_t a_full[Q4_ASTAGES], b_full[Q4_BSTAGES], b_empty[Q4_BSTAGES], acc_full[Q4_ASTAGES], acc_empty[Q4_ASTAGES];
+};
+
+// bounded wait that also leaves when another role raised the abort flag
+__device__ __forceinline__ bool q4_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* status) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15) == 0) {
+      if (*abort_flag) return false;
+      if (clock64() - t0 > (1ll << 31)) {
+        atomicExch(status, ERR_TIMEOUT);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(Q4_THREADS, 1) tc_gemm_q4k_kernel(const __grid_constant__ TcGemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  uint8_t* Ast = smem;                                           // [Q4_ASTAGES][Q4_ASTAGE]
+  uint8_t* Bst = smem + Q4_ASTAGES * Q4_ASTAGE;                  // [Q4_BSTAGES][TC_SLAB]
+  Q4Bars* bars = reinterpret_cast<Q4Bars*>(Bst + Q4_BSTAGES * TC_SLAB);
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bars + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tslot + 1);
+
+  const int t64 = blockIdx.x;
+  if (t64 >= p.ntile) return;
+  int expert = 0;
+  if (p.tile_expert) {
+    expert = p.tile_expert[t64];
+    if (expert < 0) return;  // uniform: the whole CTA leaves before any allocation
+  }
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int nb = p.K / 256;
+  const int nmat = p.epi == TC_EPI_SWIGLU ? 2 : 1;
+  const int total = nmat * nb;
+  const uint8_t* slabs = p.xq + (int64_t)t64 * nb * TC_SLAB;
+
+  if (warp == 0) {
+    tmem_alloc(tslot, Q4_NCOL);
+    tmem_relinquish();
+  }
+  if (tid == 0) {
+    for (int i = 0; i < Q4_ASTAGES; ++i) {
+      mbar_init(&bars->a_full[i], Q4_UNPACK_WARPS * 32);
+      mbar_init(&bars->acc_full[i], 1);
+      mbar_init(&bars->acc_empty[i], Q4_EPI_WARPS);
+    }
+    for (int i = 0; i < Q4_BSTAGES; ++i) {
+      mbar_init(&bars->b_full[i], 1);
+      mbar_init(&bars->b_empty[i], Q4_EPI_WARPS * 32);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp < Q4_UNPACK_WARPS) {  // min tile columns 16..31 stay zero in both stages
+    const int r = tid;
+    for (int st = 0; st < Q4_ASTAGES; ++st)
+      sts16(Ast + st * Q4_ASTAGE + 65536 + (r >> 3) * 256 + (r & 7) * 16 + 128, 0u, 0u, 0u, 0u);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+
+  if (warp < Q4_UNPACK_WARPS) {
+    // ---- unpack -------------------------------------------------------------
+    const int r = tid;
+    const int row = blockIdx.y * TC_M + r;
+    const int64_t woff = (int64_t)expert * p.expert_stride + (int64_t)(row < p.rows ? row : 0) * p.rowstride;
+    const int rowoff = (r >> 3) * 256 + (r & 7) * 16;
+    RawQ4Half lo, hi;  // the block's two 128-column units
+    lo.load(p.w + woff, p.K, 0, 0);
+    hi.load(p.w + woff, p.K, 0, 1);
+    for (int g = 0; g < total; ++g) {
+      const int st = g % Q4_ASTAGES;
+      // A stage st is free once the MMAs of block g - Q4_ASTAGES have
+      // completed: the one commit per block, on acc_full, is waited on here too
+      if (g >= Q4_ASTAGES &&
+          !q4_wait(&bars->acc_full[st], (uint32_t)((g / Q4_ASTAGES + 1) & 1), abort_flag, p.status))
+        break;
+      uint8_t* A = Ast + st * Q4_ASTAGE;
+      float dd, dm;
+      unpack_q4k_half(lo, 0, A + rowoff, A + 65536 + rowoff, &dd, &dm);
+      unpack_q4k_half(hi, 1, A + rowoff, A + 65536 + rowoff, &dd, &dm);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor core's reads
+      mbar_arrive(&bars->a_full[st]);
+      if (g + 1 < total) {
+        const int nm = (g + 1) >= nb ? 1 : 0;
+        const uint8_t* w = (nm ? p.w2 : p.w) + woff;
+        lo.load(w, p.K, (g + 1) - nm * nb, 0);
+        hi.load(w, p.K, (g + 1) - nm * nb, 1);
+      }
+    }
+  } else if (warp < Q4_MMA_WARP) {
+    // ---- epilogue -------------------------------------------------------------
+    const int ew = warp - Q4_UNPACK_WARPS;
+    const int quad = warp & 3, th = ew >> 2;  // TMEM lanes 32 quad .. +31; tokens 32 th .. +31
+    const int r = quad * 32 + lane;
+    const int row = blockIdx.y * TC_M + r;
+    const bool live = row < p.rows;
+    const int64_t woff = (int64_t)expert * p.expert_stride + (int64_t)(live ? row : 0) * p.rowstride;
+    const uint32_t lane_base = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(32 * th);
+    uint4 hdr;  // this block's header (d, dmin) for row r
+    {
+      const BlockAddr a = block_addr(T_Q4_K, p.w + woff, p.K, 0);
+      hdr = ldg16(a.base + 4 * a.ng * 16 + (a.l0 >> 1) * 16);
+    }
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+    for (int g = 0; g < total; ++g) {
+      const int mat = g >= nb ? 1 : 0, b = g - mat * nb;
+      const float rd = half_lo(hdr.x), rdmin = half_hi(hdr.x);
+      if (g + 1 < total) {
+        const int nm = (g + 1) >= nb ? 1 : 0;
+        const BlockAddr a = block_addr(T_Q4_K, (nm ? p.w2 : p.w) + woff, p.K, (g + 1) - nm * nb);
+        hdr = ldg16(a.base + 4 * a.ng * 16 + (a.l0 >> 1) * 16);
+      }
+      const int ts = g % Q4_ASTAGES, bs = g % Q4_BSTAGES;
+      if (!q4_wait(&bars->acc_full[ts], (uint32_t)((g / Q4_ASTAGES) & 1), abort_flag, p.status)) break;
+      // the slab's scales are read here too: observe its copy's completion
+      if (!q4_wait(&bars->b_full[bs], (uint32_t)((g / Q4_BSTAGES) & 1), abort_flag, p.status)) break;
+      // the lanes left their waits one by one: reconverge before the
+      // warp-collective (.sync.aligned) TMEM loads
+      __syncwarp();
+      tc_fence_after();
+      // the block's activation scales into registers, then the slab goes back
+      // to the copy warp: each thread's reads complete (use32) and are ordered
+      // before the async proxy's next write into the stage (proxy fence), and
+      // every thread arrives for itself
+      const float* dxsm = reinterpret_cast<const float*>(Bst + bs * TC_SLAB + TC_SLAB_DX) + 32 * th;
+      float dxs[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) dxs[i] = dxsm[i];
+      use32(dxs);
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      mbar_arrive(&bars->b_empty[bs]);
+      const uint32_t tb = lane_base + (uint32_t)(ts * 256);
+      // ggml vec_dot_q4_K_q8_K per block: (d dx) sum_j sc_j D_j - (dmin dx) sum_j m_j S_j
+#pragma unroll
+      for (int t0 = 0; t0 < 32; t0 += 8) {
+        int Dh[8], Dl[8], Mh[8], Ml[8];
+        tmem_ld8x4(tb + (uint32_t)t0, tb + 64u + (uint32_t)t0, tb + 128u + (uint32_t)t0, tb + 192u + (uint32_t)t0, Dh,
+                   Dl, Mh, Ml);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int isum = Dh[i] * 8 + Dl[i];
+          const int imin = Mh[i] * 128 + Ml[i];
+          const float dx = dxs[t0 + i];
+          const float d = __fmul_rn(rd, dx), dmn = __fmul_rn(rdmin, dx);
+          acc[t0 + i] = __fadd_rn(acc[t0 + i], __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dmn, (float)imin)));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&bars->acc_empty[ts]);
+      }
+      if (b == nb - 1) {
+        if (live) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int ir = t64 * TC_TT + 32 * th + i;
+            if (!p.tile_expert && ir >= p.n) continue;
+            float* yp = p.y + (int64_t)ir * p.ldy + row;
+            if (p.epi == TC_EPI_RESID) {
+              *yp = __fadd_rn(acc[i], p.res[(int64_t)ir * p.ldres + row]);
+            } else if (p.epi == TC_EPI_SWIGLU && mat == 1) {
+              // h = silu(gate) * up (ggml_swiglu_split, engine.cpp:1969); this
+              // thread stored the gate value here at the end of matrix 0
+              const float gv = *yp;
+              *yp = __fmul_rn(__fdiv_rn(gv, __fadd_rn(1.0f, sfk_expf(-gv))), acc[i]);
+            } else {
+              *yp = acc[i];
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.0f;
+      }
+    }
+  } else if (warp == Q4_MMA_WARP) {
+    // ---- MMA issue ----------------------------------------------------------------
+    int issued = 0;  // blocks whose MMAs were committed
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_i8(TC_M, 64);
+      for (int g = 0; g < total; ++g) {
+        const int as = g % Q4_ASTAGES, bs = g % Q4_BSTAGES, ts = as;
+        if (!q4_wait(&bars->a_full[as], (uint32_t)((g / Q4_ASTAGES) & 1), abort_flag, p.status)) break;
+        if (!q4_wait(&bars->b_full[bs], (uint32_t)((g / Q4_BSTAGES) & 1), abort_flag, p.status)) break;
+        if (!q4_wait(&bars->acc_empty[ts], (uint32_t)((g / Q4_ASTAGES + 1) & 1), abort_flag, p.status)) break;
+        tc_fence_after();
+        const uint8_t* A = Ast + as * Q4_ASTAGE;
+        const uint8_t* slab = Bst + bs * TC_SLAB;
+        const uint32_t d0 = tmem + (uint32_t)(ts * 256);
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          const uint64_t bd = smem_desc(slab + c * 2048, 128, 256);
+          mma_i8(d0, smem_desc(A + c * 4096, 128, 256), bd, idesc, c > 0 ? 1u : 0u);
+          mma_i8(d0 + 64u, smem_desc(A + 32768 + c * 4096, 128, 256), bd, idesc, c > 0 ? 1u : 0u);
+        }
+        const uint64_t ad = smem_desc(A + 65536, 128, 256);
+        mma_i8(d0 + 128u, ad, smem_desc(slab + TC_SLAB_SHI, 128, 256), idesc, 0u);
+        mma_i8(d0 + 192u, ad, smem_desc(slab + TC_SLAB_SLO, 128, 256), idesc, 0u);
+        mma_commit(&bars->acc_full[ts]);  // frees A stage `as` and fills TMEM stage `ts`
+        issued = g + 1;
+      }
+      // before TMEM goes: the last committed MMAs have completed
+      if (issued > 0) {
+        const int g = issued - 1;
+        mbar_wait_tc(&bars->acc_full[g % Q4_ASTAGES], (uint32_t)((g / Q4_ASTAGES) & 1), p.status);
+      }
+    }
+  } else {
+    // ---- activation slabs ----------------------------------------------------------
+    if (lane == 0) {
+      int copied = 0;
+      for (int g = 0; g < total; ++g) {
+        const int bs = g % Q4_BSTAGES;
+        if (!q4_wait(&bars->b_empty[bs], (uint32_t)(((g / Q4_BSTAGES) + 1) & 1), abort_flag, p.status)) break;
+        mbar_arrive_expect_tx(&bars->b_full[bs], TC_SLAB);
+        bulk_g2s(Bst + bs * TC_SLAB, slabs + (int64_t)(g % nb) * TC_SLAB, TC_SLAB, &bars->b_full[bs]);
+        copied = g + 1;
+      }
+      // before shared memory goes: every copy issued has landed
+      for (int g = (copied > Q4_BSTAGES ? copied - Q4_BSTAGES : 0); g < copied; ++g)
+        mbar_wait_tc(&bars->b_full[g % Q4_BSTAGES], (uint32_t)((g / Q4_BSTAGES) & 1), p.status);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, Q4_NCOL);
+}
+
+cudaError_t launch_gemm_q4k(const TcGemmParams& p, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(tc_gemm_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Q4_SMEM);
+  if (e != cudaSuccess) return e;
+  const dim3 grid((unsigned)p.ntile, (unsigned)((p.rows + TC_M - 1) / TC_M));
+  tc_gemm_q4k_kernel<<<grid, Q4_THREADS, Q4_SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <int TYPE>
 cudaError_t launch_gemm_t(const TcGemmParams& p, cudaStream_t st) {
-  constexpr int NCH = TYPE == T_Q6_K ? 16 : 8;
-  const size_t smem = (size_t)NCH * 4096 + 16384 + sizeof(RowScales) * TC_M + (size_t)N * 8 * 4 + (size_t)N * 16 * 2 +
-                      2 * 8 + 16;
-  auto kern = tc_gemm_kernel<TYPE, N>;
+  constexpr int N = TcShape<TYPE>::N;
+  size_t smem = (size_t)TcShape<TYPE>::A_BYTES + 2 * TC_SLAB + 3 * 8 + 16;
+  // the 512-column kinds take all of an SM's TMEM: one CTA per SM
+  if (TcShape<TYPE>::NCOL == 512 && smem < 120 * 1024) smem = 120 * 1024;
+  auto kern = tc_gemm_kernel<TYPE>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int tiles = (p.npad + N - 1) / N;
-  kern<<<dim3((unsigned)((p.rows + TC_M - 1) / TC_M), (unsigned)tiles), TC_THREADS, smem, st>>>(p);
+  const dim3 grid((unsigned)(p.ntile * (TC_TT / N)), (unsigned)((p.rows + TC_M - 1) / TC_M));
+  kern<<<grid, TC_THREADS, smem, st>>>(p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
-size_t tc_act_bytes(int act_type, int n, int K, size_t* off_dx, size_t* off_bs) {
-  const int npad = (n + TC_TT - 1) / TC_TT * TC_TT;
-  const size_t codes = (size_t)npad * K;
-  const size_t dxn = act_type == T_Q8_K ? (size_t)npad * (K / 256) : (size_t)npad * (K / 32);
-  const size_t a = (codes + 255) & ~(size_t)255;
-  const size_t b = (a + dxn * 4 + 255) & ~(size_t)255;
-  if (off_dx) *off_dx = a;
-  if (off_bs) *off_bs = b;
-  return b + (size_t)npad * (K / 16) * 2;
+size_t tc_act_bytes(int rows, int K) {
+  const size_t tiles = (size_t)(rows + TC_TT - 1) / TC_TT;
+  return tiles * (size_t)(K / 256) * TC_SLAB;
 }
 
-cudaError_t launch_tc_quant(int act_type, const float* x, int n, int K, uint8_t* buf, cudaStream_t st) {
-  size_t odx = 0, obs = 0;
-  tc_act_bytes(act_type, n, K, &odx, &obs);
-  const int npad = (n + TC_TT - 1) / TC_TT * TC_TT;
+cudaError_t launch_tc_quant(int act_type, const float* x, int64_t ldx, const int* rows, int n_src, int npad, int K,
+                            uint8_t* buf, cudaStream_t st) {
+  if (npad % TC_TT || K % 256 || npad <= 0) return cudaErrorInvalidValue;
   const int items = npad * (K / 256);
-  tc_quant_kernel<<<(items + 7) / 8 < 4096 ? (items + 7) / 8 : 4096, 256, 0, st>>>(
-      act_type, x, n, npad, K, reinterpret_cast<int8_t*>(buf), reinterpret_cast<float*>(buf + odx),
-      reinterpret_cast<int16_t*>(buf + obs));
+  const int blocks = (items + 7) / 8 < 8192 ? (items + 7) / 8 : 8192;
+  tc_quant_kernel<<<blocks, 256, 0, st>>>(act_type, x, ldx, rows, n_src, npad, K, buf);
   return cudaGetLastError();
 }
 
 cudaError_t launch_tc_gemm(const TcGemmParams& p, cudaStream_t st) {
+  if (p.epi == TC_EPI_SWIGLU && !p.w2) return cudaErrorInvalidValue;
+  if (p.K % 256 || p.rows < 1 || p.ntile < 1) return cudaErrorInvalidValue;
   switch (p.wtype) {
-    case T_Q4_K: return launch_gemm_t<T_Q4_K, 64>(p, st);
-    case T_Q6_K: return launch_gemm_t<T_Q6_K, 32>(p, st);
-    case T_Q8_0: return launch_gemm_t<T_Q8_0, 64>(p, st);
+    case T_Q4_K: return launch_gemm_q4k(p, st);
+    case T_Q6_K: return launch_gemm_t<T_Q6_K>(p, st);
+    case T_Q8_0: return launch_gemm_t<T_Q8_0>(p, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -226,6 +226,17 @@ class Engine:
                                             am.ctypes.data_as(C.c_void_p)))
         return am, logits
 
+    def prefill(self, tokens, pos0: int = 0, seq: int = 0, want_logits: bool = True):
+        """Batched prompt prefill (sfk_prefill): tokens at positions pos0..;
+        returns (argmax, logits) of the last prompt token.  Decoding then
+        continues with decode_greedy / forward."""
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        logits = np.empty(self.cfg.n_vocab, np.float32) if want_logits else None
+        am = C.c_int32()
+        L.check(self._lib.sfk_prefill(self.h, int(seq), tokens.ctypes.data_as(C.c_void_p), int(tokens.size), int(pos0),
+                                      logits.ctypes.data_as(C.c_void_p) if want_logits else None, C.byref(am)))
+        return am.value, logits
+
     def decode_greedy(self, n_steps: int, n_seq: int = 1, want_tokens: bool = True):
         """Greedy loop on the device; returns the tokens fed at each step
         ([n_steps][n_seq]); the first is the argmax of the previous step."""

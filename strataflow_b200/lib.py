@@ -61,6 +61,7 @@ _SIGS = {
     "sfk_forward": (I32, [P, I32, I32, P, P]),
     "sfk_forward_batch": (I32, [P, I32, P, P, P, P]),
     "sfk_decode_greedy": (I32, [P, I32, I32, P]),
+    "sfk_prefill": (I32, [P, I32, P, I32, I32, P, P]),
     "sfk_hidden_get": (I32, [P, P, SZ]),
     "sfk_route_get": (I32, [P, P, P, SZ]),
     "sfk_debug_get": (I32, [P, I32, P, SZ]),
