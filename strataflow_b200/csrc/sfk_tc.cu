@@ -111,6 +111,33 @@ __device__ __forceinline__ void tmem_ld16x2(uint32_t a0, uint32_t a1, int (&v0)[
       : "r"(a0), "r"(a1)
       : "memory");
 }
+// Four 8-column loads without the wait; tmem_wait8x4 (which takes the
+// same registers as operands, so their uses cannot move above it) completes
+// them.  Lets the next group's loads overlap this group's arithmetic.
+__device__ __forceinline__ void tmem_issue8x4(uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, int (&v0)[8],
+                                              int (&v1)[8], int (&v2)[8], int (&v3)[8]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%8,%9,%10,%11,%12,%13,%14,%15}, [%33];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%16,%17,%18,%19,%20,%21,%22,%23}, [%34];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%24,%25,%26,%27,%28,%29,%30,%31}, [%35];\n"
+      : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
+        "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
+        "=r"(v2[0]), "=r"(v2[1]), "=r"(v2[2]), "=r"(v2[3]), "=r"(v2[4]), "=r"(v2[5]), "=r"(v2[6]), "=r"(v2[7]),
+        "=r"(v3[0]), "=r"(v3[1]), "=r"(v3[2]), "=r"(v3[3]), "=r"(v3[4]), "=r"(v3[5]), "=r"(v3[6]), "=r"(v3[7])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait8x4(int (&v0)[8], int (&v1)[8], int (&v2)[8], int (&v3)[8]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n"
+               : "+r"(v0[0]), "+r"(v0[1]), "+r"(v0[2]), "+r"(v0[3]), "+r"(v0[4]), "+r"(v0[5]), "+r"(v0[6]),
+                 "+r"(v0[7]), "+r"(v1[0]), "+r"(v1[1]), "+r"(v1[2]), "+r"(v1[3]), "+r"(v1[4]), "+r"(v1[5]),
+                 "+r"(v1[6]), "+r"(v1[7]), "+r"(v2[0]), "+r"(v2[1]), "+r"(v2[2]), "+r"(v2[3]), "+r"(v2[4]),
+                 "+r"(v2[5]), "+r"(v2[6]), "+r"(v2[7]), "+r"(v3[0]), "+r"(v3[1]), "+r"(v3[2]), "+r"(v3[3]),
+                 "+r"(v3[4]), "+r"(v3[5]), "+r"(v3[6]), "+r"(v3[7])
+               :
+               : "memory");
+}
 // One 16-column load, then the wait.
 __device__ __forceinline__ void tmem_ld16w(uint32_t taddr, int (&v)[16]) {
   asm volatile(
@@ -698,13 +725,13 @@ __global__ void __launch_bounds__(Q4_THREADS, 1) tc_gemm_q4k_kernel(const __grid
   }
   if (tid == 0) {
     for (int i = 0; i < Q4_ASTAGES; ++i) {
-      mbar_init(&bars->a_full[i], Q4_UNPACK_WARPS * 32);
+      mbar_init(&bars->a_full[i], Q4_UNPACK_WARPS);  // one arrival per unpack warp
       mbar_init(&bars->acc_full[i], 1);
       mbar_init(&bars->acc_empty[i], Q4_EPI_WARPS);
     }
     for (int i = 0; i < Q4_BSTAGES; ++i) {
       mbar_init(&bars->b_full[i], 1);
-      mbar_init(&bars->b_empty[i], Q4_EPI_WARPS * 32);
+      mbar_init(&bars->b_empty[i], Q4_EPI_WARPS);  // one arrival per epilogue warp
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -739,8 +766,11 @@ __global__ void __launch_bounds__(Q4_THREADS, 1) tc_gemm_q4k_kernel(const __grid
       float dd, dm;
       unpack_q4k_half(lo, 0, A + rowoff, A + 65536 + rowoff, &dd, &dm);
       unpack_q4k_half(hi, 1, A + rowoff, A + 65536 + rowoff, &dd, &dm);
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic stores -> the tensor core's reads
-      mbar_arrive(&bars->a_full[st]);
+      // each thread orders its generic stores before the tensor core's reads
+      // (proxy fence); the warp then arrives once
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->a_full[st]);
       if (g + 1 < total) {
         const int nm = (g + 1) >= nb ? 1 : 0;
         const uint8_t* w = (nm ? p.w2 : p.w) + woff;
@@ -783,26 +813,33 @@ __global__ void __launch_bounds__(Q4_THREADS, 1) tc_gemm_q4k_kernel(const __grid
       tc_fence_after();
       // the block's activation scales into registers, then the slab goes back
       // to the copy warp: each thread's reads complete (use32) and are ordered
-      // before the async proxy's next write into the stage (proxy fence), and
-      // every thread arrives for itself
+      // before the async proxy's next write into the stage (proxy fence); the
+      // warp then arrives once
       const float* dxsm = reinterpret_cast<const float*>(Bst + bs * TC_SLAB + TC_SLAB_DX) + 32 * th;
       float dxs[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) dxs[i] = dxsm[i];
       use32(dxs);
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      mbar_arrive(&bars->b_empty[bs]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bars->b_empty[bs]);
       const uint32_t tb = lane_base + (uint32_t)(ts * 256);
-      // ggml vec_dot_q4_K_q8_K per block: (d dx) sum_j sc_j D_j - (dmin dx) sum_j m_j S_j
+      // ggml vec_dot_q4_K_q8_K per block: (d dx) sum_j sc_j D_j - (dmin dx) sum_j m_j S_j;
+      // the loads of the next 8 tokens are in flight during this group's math
+      int Dh[2][8], Dl[2][8], Mh[2][8], Ml[2][8];
+      tmem_issue8x4(tb, tb + 64u, tb + 128u, tb + 192u, Dh[0], Dl[0], Mh[0], Ml[0]);
 #pragma unroll
-      for (int t0 = 0; t0 < 32; t0 += 8) {
-        int Dh[8], Dl[8], Mh[8], Ml[8];
-        tmem_ld8x4(tb + (uint32_t)t0, tb + 64u + (uint32_t)t0, tb + 128u + (uint32_t)t0, tb + 192u + (uint32_t)t0, Dh,
-                   Dl, Mh, Ml);
+      for (int grp = 0; grp < 4; ++grp) {
+        const int cb = grp & 1, t0 = grp * 8;
+        tmem_wait8x4(Dh[cb], Dl[cb], Mh[cb], Ml[cb]);
+        if (grp < 3) {
+          const uint32_t a = tb + (uint32_t)(t0 + 8);
+          tmem_issue8x4(a, a + 64u, a + 128u, a + 192u, Dh[cb ^ 1], Dl[cb ^ 1], Mh[cb ^ 1], Ml[cb ^ 1]);
+        }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int isum = Dh[i] * 8 + Dl[i];
-          const int imin = Mh[i] * 128 + Ml[i];
+          const int isum = Dh[cb][i] * 8 + Dl[cb][i];
+          const int imin = Mh[cb][i] * 128 + Ml[cb][i];
           const float dx = dxs[t0 + i];
           const float d = __fmul_rn(rd, dx), dmn = __fmul_rn(rdmin, dx);
           acc[t0 + i] = __fadd_rn(acc[t0 + i], __fsub_rn(__fmul_rn(d, (float)isum), __fmul_rn(dmn, (float)imin)));
@@ -847,18 +884,19 @@ __global__ void __launch_bounds__(Q4_THREADS, 1) tc_gemm_q4k_kernel(const __grid
         if (!q4_wait(&bars->b_full[bs], (uint32_t)((g / Q4_BSTAGES) & 1), abort_flag, p.status)) break;
         if (!q4_wait(&bars->acc_empty[ts], (uint32_t)((g / Q4_ASTAGES + 1) & 1), abort_flag, p.status)) break;
         tc_fence_after();
-        const uint8_t* A = Ast + as * Q4_ASTAGE;
-        const uint8_t* slab = Bst + bs * TC_SLAB;
+        // descriptors: the start field is the address >> 4, so +4096 bytes
+        // (next A chunk) is +256 and +2048 (next B chunk) is +128; all
+        // addresses stay below 256 KB, the field never carries
+        const uint64_t da = smem_desc(Ast + as * Q4_ASTAGE, 128, 256);
+        const uint64_t db = smem_desc(Bst + bs * TC_SLAB, 128, 256);
         const uint32_t d0 = tmem + (uint32_t)(ts * 256);
-#pragma unroll 1
+#pragma unroll
         for (int c = 0; c < 8; ++c) {
-          const uint64_t bd = smem_desc(slab + c * 2048, 128, 256);
-          mma_i8(d0, smem_desc(A + c * 4096, 128, 256), bd, idesc, c > 0 ? 1u : 0u);
-          mma_i8(d0 + 64u, smem_desc(A + 32768 + c * 4096, 128, 256), bd, idesc, c > 0 ? 1u : 0u);
+          mma_i8(d0, da + (uint64_t)(c * 256), db + (uint64_t)(c * 128), idesc, c > 0 ? 1u : 0u);
+          mma_i8(d0 + 64u, da + (uint64_t)(2048 + c * 256), db + (uint64_t)(c * 128), idesc, c > 0 ? 1u : 0u);
         }
-        const uint64_t ad = smem_desc(A + 65536, 128, 256);
-        mma_i8(d0 + 128u, ad, smem_desc(slab + TC_SLAB_SHI, 128, 256), idesc, 0u);
-        mma_i8(d0 + 192u, ad, smem_desc(slab + TC_SLAB_SLO, 128, 256), idesc, 0u);
+        mma_i8(d0 + 128u, da + (uint64_t)4096, db + (uint64_t)(TC_SLAB_SHI >> 4), idesc, 0u);
+        mma_i8(d0 + 192u, da + (uint64_t)4096, db + (uint64_t)(TC_SLAB_SLO >> 4), idesc, 0u);
         mma_commit(&bars->acc_full[ts]);  // frees A stage `as` and fills TMEM stage `ts`
         issued = g + 1;
       }
