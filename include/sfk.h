@@ -204,6 +204,44 @@ SFK_API sfk_status sfk_decode_greedy(sfk_engine *eng, int32_t n_seq, int32_t n_s
 SFK_API sfk_status sfk_prefill(sfk_engine *eng, int32_t seq, const int32_t *tokens, int32_t n, int32_t pos0,
                                float *logits_host, int32_t *argmax_out);
 
+/* Sampling of the generate loop: the reference's sf_sampling_params
+ * (include/strataflow/strataflow.h:193-199) plus the end-of-sequence token
+ * (the reference asks its model; -1: none).  temperature <= 0 is greedy (the
+ * argmax, first maximum wins); otherwise p_i = exp((l_i - max l) / T), the
+ * top_k largest kept (<= 0: all; ties by the lower index), then the shortest
+ * prefix in (p descending, index ascending) order whose mass reaches top_p
+ * of the kept mass (>= 1: all), drawn by inverse CDF in index order with
+ * u = splitmix64(seed + (step + 1) * 0x9E3779B97F4A7C15) / 2^64 (53 bits),
+ * step = the generated token's index.  On the device. */
+typedef struct sfk_sampling {
+  float temperature;
+  float top_p;
+  int32_t top_k;
+  uint64_t seed;
+  int32_t max_tokens; /* <= 0: 256, the reference's default cap */
+  int32_t eos_token;
+} sfk_sampling;
+/* The reference's defaults (strataflow_api.cpp:89-97): greedy, top_p 1,
+ * top_k 0, seed 0, 256 tokens; eos_token -1. */
+SFK_API sfk_sampling sfk_sampling_defaults(void);
+/* Called with each generated token; a nonzero return stops the loop. */
+typedef int (*sfk_token_cb)(int32_t token, void *user);
+/* The reference's sf_generate drive (strataflow_api.cpp:308-335) on sequence
+ * 0, with its prompt defect fixed: EVERY prompt token is fed at its position
+ * (batched, sfk_prefill) continuing from the sequence's next position, not
+ * only the last one.  Then up to max_tokens tokens (and at most cap_out, and
+ * n_ctx) are generated one decode step at a time; the loop stops before
+ * emitting eos_token, or after the callback (optional) returns nonzero.
+ * tokens_out (optional) receives the generated tokens, *n_out their count. */
+SFK_API sfk_status sfk_generate(sfk_engine *eng, const int32_t *prompt, int32_t n_prompt, const sfk_sampling *sampling,
+                                int32_t *tokens_out, int32_t cap_out, int32_t *n_out, sfk_token_cb cb, void *user);
+
+/* The generate loop's sampler as an operator: one token from n_vocab device
+ * logits (f32) under `sampling` (temperature > 0) at generated-token index
+ * `step`; *token_out (host) receives it. */
+SFK_API sfk_status sfk_sample_logits(const float *dev_logits, int32_t n_vocab, const sfk_sampling *sampling,
+                                     int32_t step, int32_t *token_out, void *stream);
+
 /* Routing of the last layer of the last step: ids [n_seq][k] and weights
  * [n_seq][k] (host) -- the router segment's read-back (engine.cpp:2823-2833). */
 SFK_API sfk_status sfk_route_get(sfk_engine *eng, int32_t *ids_out, float *w_out, size_t n);

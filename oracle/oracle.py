@@ -74,6 +74,7 @@ def lib():
             "sfo_model_create": (P, [P]),
             "sfo_model_free": (None, [P]),
             "sfo_set_fp32_mode": (None, [P, I]),
+            "sfo_sample": (C.c_int32, [P, I64, C.c_float, C.c_int32, C.c_float, U64, C.c_int32]),
             "sfo_tensor_bytes": (SZ, [P, I, I, P, P]),
             "sfo_tensor_data": (P, [P, I, I]),
             "sfo_model_synth": (I, [P, U64]),
@@ -329,6 +330,13 @@ class Seq:
         ptr = lib().sfo_seq_ids(self.h, il)
         return np.ctypeslib.as_array(C.cast(ptr, C.POINTER(C.c_int32)),
                                      shape=(self.m.cfg.n_expert_used,)).copy()
+
+
+def sample(logits: np.ndarray, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0,
+           step: int = 0) -> int:
+    """Token sampling of the generate loop (sfo_sample)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    return int(lib().sfo_sample(_p(lg), lg.size, float(temperature), int(top_k), float(top_p), int(seed), int(step)))
 
 
 def greedy(model: Model, prompt: list[int], n_gen: int, want_logits=False, prompt_fp32_mode=None):

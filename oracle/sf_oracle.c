@@ -773,6 +773,76 @@ int32_t sfo_argmax(const float *v, int n) {
     return best;
 }
 
+/* Token sampling of the generate loop (the reference declares
+ * sf_sampling_params, include/strataflow/strataflow.h:193-199, and never
+ * reads them: src/api/strataflow_api.cpp:308-335 always takes the argmax).
+ * Defined here and on the device (csrc/sfk_sample.cu) as: temperature <= 0
+ * -> the argmax (first maximum); else p_i = exp((l_i - max) * (1 / T)),
+ * keep the top_k largest p (ties: lower index first; top_k <= 0: all), then
+ * the shortest prefix in (p desc, index asc) order whose mass reaches
+ * top_p times the kept mass (top_p >= 1: all), and return the first kept
+ * index, in index order, whose running mass exceeds u times the kept mass,
+ * u = splitmix64(seed + (step + 1) * golden) / 2^64 (53 bits). */
+static uint64_t sfo_splitmix64(uint64_t z) {
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+static const float *g_sort_p;
+static int sfo_cmp_p_desc(const void *a, const void *b) {
+    const int32_t i = *(const int32_t *)a, j = *(const int32_t *)b;
+    const float pi = g_sort_p[i], pj = g_sort_p[j];
+    if (pi > pj) return -1;
+    if (pi < pj) return 1;
+    return i < j ? -1 : (i > j);
+}
+int32_t sfo_sample(const float *logits, int64_t V, float temperature, int32_t top_k, float top_p, uint64_t seed,
+                   int32_t step) {
+    if (!(temperature > 0.0f)) return sfo_argmax(logits, (int)V);
+    float mx = -INFINITY;
+    for (int64_t i = 0; i < V; ++i) mx = logits[i] > mx ? logits[i] : mx;
+    const float invT = 1.0f / temperature;
+    float *p = (float *)malloc(sizeof(float) * (size_t)V);
+    int32_t *idx = (int32_t *)malloc(sizeof(int32_t) * (size_t)V);
+    uint8_t *keep = (uint8_t *)calloc((size_t)V, 1);
+    for (int64_t i = 0; i < V; ++i) {
+        p[i] = sfo_expf((logits[i] - mx) * invT);
+        idx[i] = (int32_t)i;
+    }
+    g_sort_p = p;
+    qsort(idx, (size_t)V, sizeof(int32_t), sfo_cmp_p_desc);
+    const int64_t nk = (top_k > 0 && top_k < V) ? top_k : V;
+    double mk = 0.0;
+    for (int64_t j = 0; j < nk; ++j) mk += (double)p[idx[j]];
+    int64_t nkeep = nk;
+    if (top_p < 1.0f) {
+        const double target = (double)top_p * mk;
+        double a = 0.0;
+        for (int64_t j = 0; j < nk; ++j) {
+            a += (double)p[idx[j]];
+            if (a >= target) { nkeep = j + 1; break; }
+        }
+    }
+    for (int64_t j = 0; j < nkeep; ++j) keep[idx[j]] = 1;
+    const uint64_t z = sfo_splitmix64(seed + (uint64_t)(step + 1) * 0x9E3779B97F4A7C15ull);
+    const double u = (double)(z >> 11) * (1.0 / 9007199254740992.0);
+    double total = 0.0;
+    for (int64_t i = 0; i < V; ++i) if (keep[i]) total += (double)p[i];
+    const double target = u * total;
+    double a = 0.0;
+    int32_t pick = -1, last = -1;
+    for (int64_t i = 0; i < V && pick < 0; ++i) {
+        if (!keep[i]) continue;
+        last = (int32_t)i;
+        a += (double)p[i];
+        if (a > target) pick = (int32_t)i;
+    }
+    free(p);
+    free(idx);
+    free(keep);
+    return pick >= 0 ? pick : last;
+}
+
 /* Router: engine.cpp:1913-1924 (mul_mat gate_inp, soft_max, argsort_top_k,
  * get_rows, sum_rows (double accumulation, ggml_vec_sum_f32), clamp, div). */
 void sfo_router(const float *w_r, int n_expert, int d, const float *x, int k,

@@ -75,6 +75,10 @@ float sfo_expf(float x);
  * order (fp32_mode 2, for comparison). */
 int  sfo_mul_mat(int type, const void *w, int64_t nrows, int64_t ncols,
                  const float *x, float *y, int fp32_mode);
+/* Token sampling of the generate loop (greedy when temperature <= 0; see
+ * sf_oracle.c for the definition shared with the device sampler). */
+int32_t sfo_sample(const float *logits, int64_t V, float temperature, int32_t top_k, float top_p, uint64_t seed,
+                   int32_t step);
 void sfo_rms_norm(const float *x, const float *w, int64_t n, float eps, float *y);
 void sfo_rope_normal(float *x, int n_head, int head_dim, int pos, float freq_base);
 void sfo_soft_max(const float *x, float *y, int64_t n, float scale);

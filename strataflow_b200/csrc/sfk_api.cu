@@ -30,6 +30,7 @@
 #include "sfk_kernels.cuh"
 #include "sfk_mega.cuh"
 #include "sfk_prefill.cuh"
+#include "sfk_sample.cuh"
 #include "sfk_tc.cuh"
 
 using namespace sfk;
@@ -304,6 +305,9 @@ struct sfk_engine {
     uint8_t *act = nullptr, *xqd = nullptr;
     int *ids = nullptr, *pos_of_pair = nullptr, *rows_tok = nullptr, *rows_self = nullptr, *tile_expert = nullptr;
   } pf;
+  // generate loop: the sampler's probabilities [V] and its token
+  float* sample_p = nullptr;
+  int* sample_tok = nullptr;
 
   template <typename T>
   sfk_status alloc(T** p, size_t bytes, uint64_t* acct) {
@@ -1671,6 +1675,76 @@ sfk_status sfk_prefill(sfk_engine* e, int32_t seq, const int32_t* tokens, int32_
   return SFK_OK;
 }
 
+sfk_sampling sfk_sampling_defaults(void) {
+  sfk_sampling s{};
+  s.temperature = 0.0f;
+  s.top_p = 1.0f;
+  s.top_k = 0;
+  s.seed = 0;
+  s.max_tokens = 256;
+  s.eos_token = -1;
+  return s;
+}
+
+sfk_status sfk_generate(sfk_engine* e, const int32_t* prompt, int32_t n_prompt, const sfk_sampling* sampling,
+                        int32_t* tokens_out, int32_t cap_out, int32_t* n_out, sfk_token_cb cb, void* user) {
+  if (!e || !prompt || !n_out) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  if (n_prompt < 1) return fail(SFK_ERR_INVALID_ARGUMENT, "empty prompt");
+  if (tokens_out && cap_out < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "cap_out");
+  const sfk_sampling sp = sampling ? *sampling : sfk_sampling_defaults();
+  const sfk_hparams& hp = e->hp;
+  *n_out = 0;
+  const int pos0 = e->seq_pos[0];
+  if ((int64_t)pos0 + n_prompt > hp.n_ctx)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "prompt of %d tokens at position %d exceeds n_ctx=%d", n_prompt, pos0,
+                hp.n_ctx);
+  const bool greedy = !(sp.temperature > 0.0f);
+  if (!greedy && !e->sample_p) {
+    sfk_status s;
+    if ((s = e->alloc(&e->sample_p, sizeof(float) * hp.n_vocab, &e->scratch_bytes)) ||
+        (s = e->alloc(&e->sample_tok, sizeof(int), &e->scratch_bytes)))
+      return s;
+  }
+  int32_t am = 0;
+  sfk_status s = sfk_prefill(e, 0, prompt, n_prompt, pos0, nullptr, &am);
+  if (s) return s;
+  int limit = sp.max_tokens > 0 ? sp.max_tokens : 256;
+  if (tokens_out) limit = std::min(limit, cap_out);
+  SampleArgs a{};
+  a.temperature = sp.temperature;
+  a.top_p = sp.top_p;
+  a.top_k = sp.top_k;
+  a.seed = sp.seed;
+  int n = 0;
+  for (int i = 0; i < limit; ++i) {
+    // the token after the last forward: its argmax, or a sample of its logits
+    // written over the argmax key (the next step's input either way)
+    int32_t tok = 0;
+    if (greedy) {
+      unsigned long long key = 0;
+      CK(cudaMemcpyAsync(&key, e->argmax_key, sizeof(key), cudaMemcpyDeviceToHost, e->stream));
+      CK(cudaStreamSynchronize(e->stream));
+      tok = (int32_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+    } else {
+      CK(launch_sample(e->logits, hp.n_vocab, a, i, e->sample_p, e->argmax_key, e->sample_tok, e->stream));
+      CK(cudaMemcpyAsync(&tok, e->sample_tok, sizeof(int), cudaMemcpyDeviceToHost, e->stream));
+      CK(cudaStreamSynchronize(e->stream));
+    }
+    if (tok == sp.eos_token) break;
+    if (tok < 0 || tok >= hp.n_vocab) return fail(SFK_ERR_RUNTIME, "sampled token %d outside the vocabulary", tok);
+    if (tokens_out) tokens_out[n] = tok;
+    ++n;
+    if (cb && cb(tok, user) != 0) break;
+    if (i + 1 == limit || e->seq_pos[0] + 1 > hp.n_ctx) break;
+    // one decode step on the token (device greedy-loop form: the key holds it)
+    if ((s = run_step(e, 1, true))) return s;
+    if ((s = engine_check(e))) return s;
+    e->seq_pos[0] += 1;
+  }
+  *n_out = n;
+  return SFK_OK;
+}
+
 sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int32_t* tokens_out) {
   if (!e) return fail(SFK_ERR_INVALID_ARGUMENT, "null engine");
   if (n_seq < 1 || n_seq > e->hp.max_batch || n_steps < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "n_seq / n_steps");
@@ -1898,6 +1972,33 @@ sfk_status sfk_mul_mat_tc(int t, const void* w, int64_t rows, int64_t K, const f
   p.status = sc->status;
   CK(launch_tc_gemm(p, st));
   return check_status_word(sc->status, st);
+}
+
+sfk_status sfk_sample_logits(const float* logits, int32_t V, const sfk_sampling* sp, int32_t step, int32_t* token_out,
+                             void* stream) {
+  if (!logits || !sp || !token_out || V < 1 || step < 0 || !(sp->temperature > 0.0f))
+    return fail(SFK_ERR_INVALID_ARGUMENT, "sample_logits arguments");
+  // scratch: V floats, the key, the token
+  const size_t need = ((sizeof(float) * (size_t)V + 15) & ~(size_t)15) + 16 + 16;
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(need, 1, &sc);
+  if (s) return s;
+  uint8_t* buf = static_cast<uint8_t*>(sc->buf);
+  float* p = reinterpret_cast<float*>(buf);
+  unsigned long long* key = reinterpret_cast<unsigned long long*>(buf + ((sizeof(float) * (size_t)V + 15) & ~(size_t)15));
+  int* tok = reinterpret_cast<int*>(key + 2);
+  SampleArgs a{};
+  a.temperature = sp->temperature;
+  a.top_p = sp->top_p;
+  a.top_k = sp->top_k;
+  a.seed = sp->seed;
+  cudaStream_t st = (cudaStream_t)stream;
+  CK(launch_sample(logits, V, a, step, p, key, tok, st));
+  int h = 0;
+  CK(cudaMemcpyAsync(&h, tok, sizeof(int), cudaMemcpyDeviceToHost, st));
+  if ((s = check_status_word(sc->status, st))) return s;
+  *token_out = h;
+  return SFK_OK;
 }
 
 sfk_status sfk_mul_mat(int t, const void* w, int64_t rows, int64_t K, const float* x, int32_t b, float* y,

@@ -274,6 +274,21 @@ class Engine:
         L.check(self._lib.sfk_get_stats(self.h, C.byref(s)))
         return {n: int(getattr(s, n)) for n, _ in L.Stats._fields_}
 
+    def generate_api(self, prompt, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 0, seed: int = 0,
+                     max_tokens: int = 256, eos_token: int = -1, callback=None) -> list[int]:
+        """sfk_generate: the reference's sf_generate on sequence 0 with every
+        prompt token prefilled, then tokens greedy (temperature <= 0) or
+        sampled on the device.  callback(token) -> truthy stops the loop."""
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        sp = L.Sampling(float(temperature), float(top_p), int(top_k), int(seed), int(max_tokens), int(eos_token))
+        cap = max_tokens if max_tokens > 0 else 256
+        out = np.empty(cap, np.int32)
+        n = C.c_int32()
+        cb = L.TOKEN_CB(lambda tok, _u: 1 if (callback is not None and callback(int(tok))) else 0)
+        L.check(self._lib.sfk_generate(self.h, prompt.ctypes.data_as(C.c_void_p), int(prompt.size), C.byref(sp),
+                                       out.ctypes.data_as(C.c_void_p), cap, C.byref(n), cb, None))
+        return out[:n.value].tolist()
+
     def generate(self, prompt, n_gen: int, host_loop: bool = False):
         """The reference drive pattern (tests/test_engine_oracle.cpp:182-207):
         prompt tokens one position at a time, then n_gen greedy tokens.

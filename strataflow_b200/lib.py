@@ -45,6 +45,14 @@ class Stats(C.Structure):
         "active_bytes_per_token")]
 
 
+class Sampling(C.Structure):
+    """sfk_sampling: the reference's sf_sampling_params plus the eos token."""
+    _fields_ = [("temperature", C.c_float), ("top_p", C.c_float), ("top_k", C.c_int32), ("seed", C.c_uint64),
+                ("max_tokens", C.c_int32), ("eos_token", C.c_int32)]
+
+
+TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
+
 P, I32, I64, U64, SZ, F = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
 _SIGS = {
     "sfk_last_error": (C.c_char_p, []),
@@ -62,6 +70,9 @@ _SIGS = {
     "sfk_forward_batch": (I32, [P, I32, P, P, P, P]),
     "sfk_decode_greedy": (I32, [P, I32, I32, P]),
     "sfk_prefill": (I32, [P, I32, P, I32, I32, P, P]),
+    "sfk_sampling_defaults": (Sampling, []),
+    "sfk_generate": (I32, [P, P, I32, C.POINTER(Sampling), P, I32, C.POINTER(I32), TOKEN_CB, P]),
+    "sfk_sample_logits": (I32, [P, I32, C.POINTER(Sampling), I32, C.POINTER(I32), P]),
     "sfk_hidden_get": (I32, [P, P, SZ]),
     "sfk_route_get": (I32, [P, P, P, SZ]),
     "sfk_debug_get": (I32, [P, I32, P, SZ]),

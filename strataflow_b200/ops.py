@@ -104,3 +104,13 @@ def attn_decode_paged(q: torch.Tensor, k_pages: torch.Tensor, v_pages: torch.Ten
                                            page_table.shape[1], _ptr(positions), b, n_head, n_head_kv, head_dim,
                                            _ptr(out), _stream(q)))
     return out
+
+
+def sample_logits(logits: torch.Tensor, temperature: float, top_k: int = 0, top_p: float = 1.0, seed: int = 0,
+                  step: int = 0) -> int:
+    """The generate loop's device sampler on f32 logits [V] (sfk_sample_logits)."""
+    sp = L.Sampling(float(temperature), float(top_p), int(top_k), int(seed), 0, -1)
+    tok = C.c_int32()
+    L.check(L.load().sfk_sample_logits(_ptr(logits), int(logits.numel()), C.byref(sp), int(step), C.byref(tok),
+                                       _stream(logits)))
+    return tok.value
