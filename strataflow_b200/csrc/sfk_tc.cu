@@ -82,6 +82,20 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
 // separate wait statement, so the compiler could move the use above it.  The
 // helpers below either issue the loads and the wait in one asm statement, or
 // make the wait take the loaded registers as operands.
+// Two 16-column loads, then the wait.
+__device__ __forceinline__ void tmem_ld16x2(uint32_t a0, uint32_t a1, int (&v0)[16], int (&v1)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%32];\n"
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, "
+      "[%33];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(v0[0]), "=r"(v0[1]), "=r"(v0[2]), "=r"(v0[3]), "=r"(v0[4]), "=r"(v0[5]), "=r"(v0[6]), "=r"(v0[7]),
+        "=r"(v0[8]), "=r"(v0[9]), "=r"(v0[10]), "=r"(v0[11]), "=r"(v0[12]), "=r"(v0[13]), "=r"(v0[14]), "=r"(v0[15]),
+        "=r"(v1[0]), "=r"(v1[1]), "=r"(v1[2]), "=r"(v1[3]), "=r"(v1[4]), "=r"(v1[5]), "=r"(v1[6]), "=r"(v1[7]),
+        "=r"(v1[8]), "=r"(v1[9]), "=r"(v1[10]), "=r"(v1[11]), "=r"(v1[12]), "=r"(v1[13]), "=r"(v1[14]), "=r"(v1[15])
+      : "r"(a0), "r"(a1)
+      : "memory");
+}
 // Four 8-column loads without the wait; tmem_wait8x4 (which takes the
 // same registers as operands, so their uses cannot move above it) completes
 // them.  Lets the next group's loads overlap this group's arithmetic.
