@@ -513,6 +513,64 @@ def run_sweep(args):
     eng.close()
 
 
+def run_sweep_tc(args):
+    """The tensor-core GEMM (sfk_mul_mat_tc, tcgen05 kind::i8) at the Mixtral
+    expert shapes for n activation rows -- a batch of n tokens' routed pairs
+    of one expert, or n prompt tokens -- and the batched prompt prefill of the
+    full 32-layer Mixtral shape.  GEMM: CUDA events around `iters` calls on the
+    current stream (activation quantization included, its status read-back
+    excluded by timing a whole loop); weights are random bytes in the device
+    layout (the timing does not depend on their values).  One JSON line per
+    case."""
+    import torch
+    from strataflow_b200 import engine as E
+    from strataflow_b200 import lib as L
+    from strataflow_b200 import ops
+    names = {L.TYPE_Q4_K: "Q4_K", L.TYPE_Q6_K: "Q6_K", L.TYPE_Q8_0: "Q8_0"}
+    g = torch.Generator(device="cuda")
+    g.manual_seed(0)
+    iters = 10
+    for t in (L.TYPE_Q4_K, L.TYPE_Q6_K, L.TYPE_Q8_0):
+        for (kern, rows, K) in (("gate", 14336, 4096), ("down", 4096, 14336)):
+            rb = L.load().sfk_dev_row_bytes(t, K)
+            w = torch.randint(0, 255, (rows * rb,), dtype=torch.uint8, device="cuda", generator=g)
+            for n in (16, 64, 128, 512):
+                x = torch.randn(n, K, device="cuda", generator=g)
+                for _ in range(2):
+                    ops.mul_mat_tc(t, w, rows, K, x)
+                torch.cuda.synchronize()
+                e0 = torch.cuda.Event(enable_timing=True)
+                e1 = torch.cuda.Event(enable_timing=True)
+                e0.record()
+                for _ in range(iters):
+                    ops.mul_mat_tc(t, w, rows, K, x)
+                e1.record()
+                e1.synchronize()
+                ms = e0.elapsed_time(e1) / iters
+                print(json.dumps({"sweep": "mul_mat_tc", "kernel": kern, "wtype": names[t], "n": n, "rows": rows,
+                                  "K": K, "us": ms * 1e3, "int8_TOPS": 2.0 * rows * K * n / (ms * 1e-3) / 1e12,
+                                  "weight_GBps": rows * rb / (ms * 1e-3) / 1e9,
+                                  "note": "one matrix per call; includes activation quantization"}), flush=True)
+            del w
+    # the batched prefill of the benchmark's model
+    cfg = E.mixtral_config(n_ctx=PROMPT + 16, n_layer=args.layers)
+    eng = E.Engine.load(cfg, seed=SEED)
+    prompt = np.random.default_rng(SEED).integers(0, cfg.n_vocab, PROMPT).astype(np.int32)
+    eng.prefill(prompt, want_logits=False)
+    times = []
+    for _ in range(3):
+        eng.reset_kv()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        eng.prefill(prompt, want_logits=False)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    print(json.dumps({"sweep": "prefill", "model": f"Mixtral-8x7B shape, {cfg.n_layer} layers", "tokens": PROMPT,
+                      "s": best, "tok_s": PROMPT / best, "runs_s": times,
+                      "timing": "host wall clock around sfk_prefill (synchronous), best of 3"}), flush=True)
+    eng.close()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -530,6 +588,8 @@ def main():
                     help="1t: configs[4], experts sharded over the torchrun ranks")
     ap.add_argument("--sweep", action="store_true",
                     help="operator sweeps (configs[1] mul_mat_id, configs[2] attention), one JSON line per case")
+    ap.add_argument("--sweep-tc", action="store_true",
+                    help="tensor-core GEMM sweep (n = 16..512 rows) and the batched 512-token prefill")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -539,6 +599,9 @@ def main():
         return
     if args.sweep:
         run_sweep(args)
+        return
+    if args.sweep_tc:
+        run_sweep_tc(args)
         return
     if args.model == "1t":
         if args.layers == 32:
