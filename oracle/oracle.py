@@ -41,7 +41,7 @@ class Hparams(C.Structure):
         "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
         ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
             "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_f16", "fp32_mode",
-            "head_dim")]
+            "head_dim", "ep_size", "ep_head_par")]
 
 
 _lib = None
@@ -235,6 +235,8 @@ class ModelConfig:
     kv_f16: bool = False
     fp32_mode: bool = False
     head_dim: int = 0   # 0: n_embd / n_head
+    ep_size: int = 0    # expert parallelism's fp32 order over ep_size ranks (0 / 1: one GPU)
+    ep_head_par: int = 0  # ... with the output projection split by heads
 
     def to_c(self) -> Hparams:
         h = Hparams()

@@ -867,10 +867,23 @@ void sfo_router(const float *w_r, int n_expert, int d, const float *x, int k,
 
 static inline float silu_f32(float x) { return x / (1.0f + sfo_expf(-x)); }
 
+static int moe_ffn_impl(int type_gu, int type_down, const void *gate, const void *up, const void *down,
+                        int n_expert, int d, int F, int b, int k,
+                        const float *x, const float *res, const int32_t *ids, const float *wts,
+                        float *out, float *gu_out, int fp32_mode, int ep_size);
+
 int sfo_moe_ffn(int type_gu, int type_down, const void *gate, const void *up, const void *down,
                 int n_expert, int d, int F, int b, int k,
                 const float *x, const float *res, const int32_t *ids, const float *wts,
                 float *out, float *gu_out, int fp32_mode) {
+    return moe_ffn_impl(type_gu, type_down, gate, up, down, n_expert, d, F, b, k, x, res, ids, wts, out, gu_out,
+                        fp32_mode, 1);
+}
+
+static int moe_ffn_impl(int type_gu, int type_down, const void *gate, const void *up, const void *down,
+                        int n_expert, int d, int F, int b, int k,
+                        const float *x, const float *res, const int32_t *ids, const float *wts,
+                        float *out, float *gu_out, int fp32_mode, int ep_size) {
     const size_t gu_rb = sfo_row_bytes(type_gu, d), dn_rb = sfo_row_bytes(type_down, F);
     float *g = (float *)malloc(sizeof(float) * (size_t)F);
     float *u = (float *)malloc(sizeof(float) * (size_t)F);
@@ -891,6 +904,24 @@ int sfo_moe_ffn(int type_gu, int type_down, const void *gate, const void *up, co
         }
         /* engine.cpp:1974-1986: moe_out = e0 + e1 + ...; then + ffn_inp */
         float *o = out + (size_t)t * d;
+        if (ep_size > 1) {
+            /* expert parallelism: rank r sums its own experts' outputs in slot
+             * order from 0 (rank 0 then adds the residual); the partials are
+             * added in rank order */
+            const int el = n_expert / ep_size;
+            for (int i = 0; i < d; ++i) {
+                float tot = 0.0f;
+                for (int r = 0; r < ep_size; ++r) {
+                    float a = 0.0f;
+                    for (int j = 0; j < k; ++j)
+                        if (ids[t * k + j] / el == r) a = a + yk[(size_t)j * d + i];
+                    if (r == 0 && res) a = a + res[(size_t)t * d + i];
+                    tot = r == 0 ? a : tot + a;
+                }
+                o[i] = tot;
+            }
+            continue;
+        }
         for (int i = 0; i < d; ++i) {
             float acc = yk[i];
             for (int j = 1; j < k; ++j) acc = acc + yk[(size_t)j * d + i];
@@ -1173,8 +1204,24 @@ int32_t sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t pos, 
         dbg_put(s, il, 4, q, Hq * hd);
         sfo_attn_decode(q, Kl, Vl, pos + 1, Hq, Hkv, hd, att);
         dbg_put(s, il, 0, att, Hq * hd);
-        sfo_mul_mat(wo->type, wo->data, d, Hq * hd, att, tmp, fp32);
-        for (int i = 0; i < d; ++i) ffn_inp[i] = tmp[i] + hidden[i];
+        if (hp->ep_size > 1 && hp->ep_head_par) {
+            /* heads split over the ranks: rank r projects its heads' columns
+             * (a matrix of its own), rank 0 adds the residual, the partials
+             * are added in rank order */
+            const int N = hp->ep_size, Kl = Hq * hd / N;
+            const size_t rbf = sfo_row_bytes(wo->type, Hq * hd), rbl = sfo_row_bytes(wo->type, Kl);
+            uint8_t *ws = (uint8_t *)malloc((size_t)d * rbl);
+            for (int r = 0; r < N; ++r) {
+                for (int row = 0; row < d; ++row)
+                    memcpy(ws + (size_t)row * rbl, (const uint8_t *)wo->data + (size_t)row * rbf + (size_t)r * rbl, rbl);
+                sfo_mul_mat(wo->type, ws, d, Kl, att + (size_t)r * Kl, tmp, fp32);
+                for (int i = 0; i < d; ++i) ffn_inp[i] = r == 0 ? tmp[i] + hidden[i] : ffn_inp[i] + tmp[i];
+            }
+            free(ws);
+        } else {
+            sfo_mul_mat(wo->type, wo->data, d, Hq * hd, att, tmp, fp32);
+            for (int i = 0; i < d; ++i) ffn_inp[i] = tmp[i] + hidden[i];
+        }
         sfo_rms_norm(ffn_inp, (const float *)m->t[SFO_T_FFN_NORM][il].data, d, hp->rms_eps, cur);
         int32_t *ids = s->ids + (size_t)il * k;
         float wts[64];
@@ -1185,8 +1232,8 @@ int32_t sfo_forward(const sfo_model *m, sfo_seq *s, int32_t token, int32_t pos, 
         /* --- expert segment: engine.cpp:1956-1989 --- */
         const sfo_tensor *tg = &m->t[SFO_T_FFN_GATE_EXPS][il], *tu = &m->t[SFO_T_FFN_UP_EXPS][il];
         const sfo_tensor *tdn = &m->t[SFO_T_FFN_DOWN_EXPS][il];
-        sfo_moe_ffn(tg->type, tdn->type, tg->data, tu->data, tdn->data, E, d, F, 1, k, cur, ffn_inp, ids, wts,
-                    hidden, NULL, fp32);
+        moe_ffn_impl(tg->type, tdn->type, tg->data, tu->data, tdn->data, E, d, F, 1, k, cur, ffn_inp, ids, wts,
+                     hidden, NULL, fp32, hp->ep_size);
         memcpy(s->hidden + (size_t)il * d, hidden, sizeof(float) * (size_t)d);
     }
 

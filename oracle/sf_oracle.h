@@ -117,6 +117,15 @@ typedef struct sfo_hparams {
     int32_t kv_f16;       /* round stored K/V through f16 (the paged-f16 KV mode) */
     int32_t fp32_mode;    /* diagnostic: dequantize weights, f32 activations */
     int32_t head_dim;     /* 0: n_embd / n_head (engine.cpp:1161); else the stated head width */
+    /* Expert parallelism's fp32 order (the B200 engine over ep_size GPUs; the
+     * reference has no such mode): each rank's expert outputs are summed
+     * over its own experts [r E/N, (r+1) E/N) in slot order, rank 0 adds the
+     * residual, and the ranks' partials are added in rank order; with
+     * ep_head_par the output projection is the same: each rank's dot over its
+     * heads' column slice, residual on rank 0, partials in rank order.
+     * 0 or 1: one GPU. */
+    int32_t ep_size;
+    int32_t ep_head_par;
 } sfo_hparams;
 
 /* tensor ids shared with the CUDA engine's C ABI (include/sfk.h) */
