@@ -95,6 +95,19 @@ typedef struct sfk_hparams {
     /* Attention head width; 0 = n_embd / n_head (the reference's rule,
      * engine.cpp:1161).  Set it when n_head * head_dim != n_embd. */
     int32_t head_dim;
+    /* HBM slots for routed expert bundles (the reference's expert_slots,
+     * Engine::load engine.h:153, engine.cpp:1386-1422).  0 or >= n_layer *
+     * n_expert: every expert resident.  Otherwise the bundles live in pinned
+     * host memory and a bounded pool of this many HBM slots holds the working
+     * set: a layer-stratified LRU (SlotPool, src/tws/weight_store.h:69-266;
+     * SFK_POOL_GLOBAL_LRU=1 selects the single global LRU), refilled by one
+     * host-to-device copy per missing bundle on a copy stream, with the next
+     * layer's predicted experts prefetched (ExpertPredictor,
+     * src/predict/predictor.h; SFK_PREFETCH=0 turns it off).  The expert
+     * kernels read the slots in place, so a pool must hold one step's routed
+     * experts of a layer: at least min(n_expert, max_batch * n_expert_used).
+     * Single-GPU engines only (ep_size <= 1). */
+    int32_t expert_slots;
 } sfk_hparams;
 
 typedef struct sfk_engine sfk_engine;
@@ -269,8 +282,53 @@ typedef struct sfk_stats {
     uint64_t steps;              /* decode steps run */
     uint64_t kernels_per_step;   /* kernel launches per decode step */
     uint64_t active_bytes_per_token; /* weight bytes one b=1 token streams */
+    /* bounded expert tier (zero when every expert is resident): the
+     * reference's CacheStats (weight_store.h) and prefetch counters
+     * (engine.cpp:187-201) */
+    uint64_t pool_slots;         /* HBM expert slots */
+    uint64_t pool_hits;          /* acquires that found the bundle resident */
+    uint64_t pool_misses;        /* acquires that copied the bundle in */
+    uint64_t pool_evictions;     /* bundles displaced from a slot */
+    uint64_t h2d_expert_bytes;   /* bundle bytes copied host -> HBM */
+    uint64_t prefetch_warmed;    /* bundles copied in ahead of their layer */
+    uint64_t prefetch_used;      /* of those, routed when their layer ran */
 } sfk_stats;
 SFK_API sfk_status sfk_get_stats(const sfk_engine *eng, sfk_stats *out);
+
+/* ---- the bounded expert tier's host logic (no GPU needed) ---------------
+ * The slot pool and the predictor the engine drives when expert_slots bounds
+ * the HBM tier, exposed for the host-side tests.  sfk_pool restates
+ * SlotPool (src/tws/weight_store.h:69-266, weight_store.cpp): n_layer == 0
+ * gives the global-LRU pool (the two-argument constructor), otherwise the
+ * layer-stratified one.  Pins (an addition: slots still read by queued
+ * kernels) keep a slot from being chosen as a victim. */
+typedef struct sfk_pool sfk_pool;
+SFK_API sfk_status sfk_pool_create(uint32_t n_slots, uint32_t n_layer, uint32_t n_expert, uint32_t n_expert_used,
+                                   sfk_pool **out);
+SFK_API void sfk_pool_free(sfk_pool *pool);
+/* SlotPool::acquire: the slot of (layer, expert), loading it on a miss
+ * (*miss_out = 1); -1 when there is no slot (n_slots 0, or all victims
+ * pinned). */
+SFK_API int64_t sfk_pool_acquire(sfk_pool *pool, uint32_t layer, uint32_t expert, int32_t *miss_out);
+SFK_API int32_t sfk_pool_resident(const sfk_pool *pool, uint32_t layer, uint32_t expert);
+SFK_API int32_t sfk_pool_stratified(const sfk_pool *pool);
+SFK_API uint32_t sfk_pool_layer_capacity(const sfk_pool *pool, uint32_t layer);
+SFK_API int32_t sfk_pool_has_free_slot_in_layer(const sfk_pool *pool, uint32_t layer);
+SFK_API sfk_status sfk_pool_set_layer_weights(sfk_pool *pool, const uint64_t *weights, uint32_t n_layer);
+SFK_API sfk_status sfk_pool_pin(sfk_pool *pool, uint32_t slot);
+SFK_API sfk_status sfk_pool_unpin_all(sfk_pool *pool);
+/* hits, misses, evictions */
+SFK_API sfk_status sfk_pool_stats(const sfk_pool *pool, uint64_t out[3]);
+/* ExpertPredictor (src/predict/predictor.h:15-43): per-layer activation
+ * counts; predict() returns up to k experts, most frequent first (equal
+ * counts by the lower id) and the count written. */
+typedef struct sfk_predictor sfk_predictor;
+SFK_API sfk_status sfk_predictor_create(uint32_t n_layer, uint32_t n_expert, sfk_predictor **out);
+SFK_API void sfk_predictor_free(sfk_predictor *pred);
+SFK_API sfk_status sfk_predictor_observe(sfk_predictor *pred, uint32_t layer, uint32_t expert);
+SFK_API uint32_t sfk_predictor_predict(sfk_predictor *pred, uint32_t layer, uint32_t k, uint32_t *out);
+SFK_API double sfk_predictor_accuracy(const sfk_predictor *pred);
+SFK_API sfk_status sfk_predictor_layer_activity(const sfk_predictor *pred, uint64_t *out, uint32_t n_layer);
 
 /* ---- operator-level entry points (device pointers, caller's stream) -----
  * `stream` is a cudaStream_t (NULL = legacy default stream). */

@@ -26,9 +26,9 @@ COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler",
 # per-file extra flags: the synthetic generator must round exactly as written
 EXTRA = {"sfk_synth.cu": ["-fmad=false"]}
 SOURCES = ["sfk_kernels.cu", "sfk_mega.cu", "sfk_tc.cu", "sfk_prefill.cu", "sfk_sample.cu", "sfk_synth.cu", "sfk_api.cu", "sfk_noalloc.cu",
-           "sfk_strata.cpp"]
+           "sfk_strata.cpp", "sfk_tier.cpp"]
 HEADERS = ["sfk_device.cuh", "sfk_act.cuh", "sfk_dequant.cuh", "sfk_kernels.cuh", "sfk_route.cuh", "sfk_mega.cuh",
-           "sfk_tc.cuh", "sfk_prefill.cuh", "sfk_sample.cuh"]
+           "sfk_tc.cuh", "sfk_prefill.cuh", "sfk_sample.cuh", "sfk_tier.h"]
 
 
 def nvcc() -> str:

@@ -19,8 +19,10 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <memory>
 #include <mutex>
 #include <new>
+#include <set>
 #include <string>
 #include <vector>
 
@@ -32,6 +34,7 @@
 #include "sfk_prefill.cuh"
 #include "sfk_sample.cuh"
 #include "sfk_tc.cuh"
+#include "sfk_tier.h"
 
 using namespace sfk;
 
@@ -303,11 +306,35 @@ struct sfk_engine {
     float* score = nullptr;     // attention score rows (pf_attn scratch)
     size_t score_bytes = 0;
     uint8_t *act = nullptr, *xqd = nullptr;
+    uint8_t* act_dn = nullptr;  // bounded tier only: the down GEMM's activation slabs
     int *ids = nullptr, *pos_of_pair = nullptr, *rows_tok = nullptr, *rows_self = nullptr, *tile_expert = nullptr;
   } pf;
   // generate loop: the sampler's probabilities [V] and its token
   float* sample_p = nullptr;
   int* sample_tok = nullptr;
+  // bounded expert tier (hp.expert_slots): every bundle gate|up|down in the
+  // device row layout in pinned host memory, a pool of HBM slots holding the
+  // working set, and per layer the slot of each routed expert
+  struct Tier {
+    bool on = false;
+    uint32_t n_slots = 0;
+    int64_t slot_bytes = 0, off_up = 0, off_down = 0;  // one slot: gate at 0, up, down
+    uint8_t* pool = nullptr;   // [n_slots][slot_bytes] HBM
+    uint8_t* host = nullptr;   // [n_layer][n_expert][slot_bytes] pinned
+    int* d_map = nullptr;      // [n_layer][n_expert] slot of each routed expert (device)
+    int* h_map = nullptr;      // pinned mirror
+    Route* h_route = nullptr;  // pinned read-back of one layer's routing
+    int* d_tile = nullptr;     // prefill: the slot of each expert tile of a pass (-1: not in it)
+    int* h_tile = nullptr;     // pinned: tile experts read back, then the pass's tile slots
+    int* h_ids = nullptr;      // pinned: a prefill chunk's routed ids
+    cudaStream_t copy = nullptr;
+    cudaEvent_t copied = nullptr;
+    std::unique_ptr<SlotPool> sp;
+    std::unique_ptr<ExpertPredictor> pred;
+    bool prefetch = true;
+    uint64_t h2d = 0, warmed = 0, used = 0, tokens = 0;
+    std::set<uint64_t> warmed_now;  // (layer, expert) prefetched during this step
+  } tier;
 
   template <typename T>
   sfk_status alloc(T** p, size_t bytes, uint64_t* acct) {
@@ -454,6 +481,13 @@ StreamParams gateup_params(const sfk_engine* e, int l, int b) {
   if (e->ep_size > 1) {
     p.ep_e0 = e->e0;
     p.ep_eloc = e->e_loc;
+  }
+  if (e->tier.on) {  // the routed experts' slots of the bounded pool
+    p.w0 = e->tier.pool;
+    p.w1 = e->tier.pool + e->tier.off_up;
+    p.expert_stride = e->tier.slot_bytes;
+    p.slot_map = e->tier.d_map + (size_t)l * hp.n_expert;
+    p.n_map_slots = (int)e->tier.n_slots;
   }
   if (e->fused_route) {
     p.pro = PRO_ROUTE;  // ffn_norm + quantize + router + top-k in the prologue
@@ -637,6 +671,12 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
         p.res = e->ep_rank == 0 ? e->ffn_inp : nullptr;
       }
       p.y_stride = d;
+      if (e->tier.on) {
+        p.w0 = e->tier.pool + e->tier.off_down;
+        p.expert_stride = e->tier.slot_bytes;
+        p.slot_map = e->tier.d_map + (size_t)l * hp.n_expert;
+        p.n_map_slots = (int)e->tier.n_slots;
+      }
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
       CK(launch_stream(p, grid, st, pdl));
@@ -917,11 +957,188 @@ sfk_status get_graph(sfk_engine* e, int b, bool greedy, cudaGraphExec_t* out) {
   return SFK_OK;
 }
 
+// ---- the bounded expert tier ----------------------------------------------
+// The reference keeps every expert bundle in its .strata file and a bounded
+// SlotPool of host slots that it copies into staging tensors for the expert
+// segment (engine.cpp:2004-2133); its prefetch warms the next layer's
+// predicted experts (engine.cpp:2900-2923).  Here the bundles sit in pinned
+// host memory in the device row layout, the slots are HBM, the expert kernels
+// read the slots in place through a per-layer slot table, and every missing
+// bundle is one host-to-device copy on a copy stream that the expert kernels
+// wait for.  A layer's routing is read back before its experts run (the
+// reference reads its ids back at the same point, engine.cpp:2840-2880).
+
+int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
+
+sfk_status tier_create(sfk_engine* e) {
+  sfk_engine::Tier& T = e->tier;
+  const sfk_hparams& hp = e->hp;
+  const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
+  const int64_t gu = (int64_t)F * dev_row_bytes(hp.type_ffn_gu, d);
+  T.off_up = round256(gu);
+  T.off_down = T.off_up + round256(gu);
+  T.slot_bytes = round256(T.off_down + (int64_t)d * dev_row_bytes(hp.type_ffn_down, F));
+  T.n_slots = (uint32_t)hp.expert_slots;
+  sfk_status s = e->alloc(&T.pool, (size_t)T.n_slots * T.slot_bytes, &e->weight_bytes);
+  if (!s) s = e->alloc(&T.d_map, sizeof(int) * (size_t)hp.n_layer * E, &e->scratch_bytes);
+  if (s) return s;
+  // the expert tiles of a prefill chunk (prefill_alloc's bound)
+  const int C = std::min(512, hp.n_ctx), np = C * k;
+  const int mt = (np + TC_TT - 1) / TC_TT + std::min(E, np);
+  if ((s = e->alloc(&T.d_tile, sizeof(int) * mt, &e->scratch_bytes))) return s;
+  CK(cudaMemset(T.d_map, 0xFF, sizeof(int) * (size_t)hp.n_layer * E));
+  CK(cudaHostAlloc(&T.host, (size_t)hp.n_layer * E * T.slot_bytes, cudaHostAllocDefault));
+  CK(cudaHostAlloc(&T.h_map, sizeof(int) * (size_t)hp.n_layer * E, cudaHostAllocDefault));
+  CK(cudaHostAlloc(&T.h_route, sizeof(Route), cudaHostAllocDefault));
+  CK(cudaHostAlloc(&T.h_tile, sizeof(int) * mt, cudaHostAllocDefault));
+  CK(cudaHostAlloc(&T.h_ids, sizeof(int) * np, cudaHostAllocDefault));
+  std::fill(T.h_map, T.h_map + (size_t)hp.n_layer * E, -1);
+  CK(cudaStreamCreateWithFlags(&T.copy, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&T.copied, cudaEventDisableTiming));
+  // layer-stratified unless SFK_POOL_GLOBAL_LRU=1 (the reference's
+  // STRATAFLOW_ENGINE_GLOBAL_LRU, engine.cpp:1404-1420)
+  const char* g = getenv("SFK_POOL_GLOBAL_LRU");
+  if (g && g[0] == '1')
+    T.sp.reset(new (std::nothrow) SlotPool(T.n_slots));
+  else
+    T.sp.reset(new (std::nothrow) SlotPool(T.n_slots, hp.n_layer, E, k));
+  T.pred.reset(new (std::nothrow) ExpertPredictor(hp.n_layer, E));
+  if (!T.sp || !T.pred) return fail(SFK_ERR_OUT_OF_MEMORY, "host alloc");
+  const char* pf = getenv("SFK_PREFETCH");
+  T.prefetch = !(pf && pf[0] == '0');
+  return SFK_OK;
+}
+
+// Bundle bytes of (layer l, expert x) in the pinned store.
+uint8_t* tier_bundle(sfk_engine* e, int l, int x) {
+  return e->tier.host + ((int64_t)l * e->hp.n_expert + x) * e->tier.slot_bytes;
+}
+
+// The host store changed: no slot holds a current copy any more.
+sfk_status tier_invalidate(sfk_engine* e) {
+  CK(cudaStreamSynchronize(e->tier.copy));
+  CK(cudaStreamSynchronize(e->stream));
+  e->tier.sp->clear();
+  std::fill(e->tier.h_map, e->tier.h_map + (size_t)e->hp.n_layer * e->hp.n_expert, -1);
+  return SFK_OK;
+}
+
+// SlotPool::acquire of (l, x); a miss copies the bundle into its slot on the
+// copy stream.  *slot is SlotPool::NONE when every candidate slot is pinned.
+sfk_status tier_acquire(sfk_engine* e, int l, int x, bool pin, uint32_t* slot) {
+  sfk_engine::Tier& T = e->tier;
+  bool miss = false;
+  *slot = T.sp->acquire((uint32_t)l, (uint32_t)x, &miss);
+  if (*slot == SlotPool::NONE) return SFK_OK;
+  if (pin) T.sp->pin(*slot);
+  if (miss) {
+    CK(cudaMemcpyAsync(T.pool + (int64_t)*slot * T.slot_bytes, tier_bundle(e, l, x), T.slot_bytes,
+                       cudaMemcpyHostToDevice, T.copy));
+    T.h2d += T.slot_bytes;
+  }
+  return SFK_OK;
+}
+
+// The engine's stream waits for every bundle copy issued so far.
+sfk_status tier_fence(sfk_engine* e) {
+  CK(cudaEventRecord(e->tier.copied, e->tier.copy));
+  CK(cudaStreamWaitEvent(e->stream, e->tier.copied, 0));
+  return SFK_OK;
+}
+
+// Layer l's routing (already queued on the stream) read back; its experts
+// acquired in the reference's order (each token's top-k in rank order, a
+// token's duplicates skipped: engine.cpp:2036-2047) after the predictor
+// observed them (engine.cpp:2863-2880); the layer's slot table uploaded.
+sfk_status tier_route_layer(sfk_engine* e, int l, int b) {
+  sfk_engine::Tier& T = e->tier;
+  const int E = e->hp.n_expert, k = e->hp.n_expert_used;
+  CK(cudaMemcpyAsync(T.h_route, e->route, sizeof(Route), cudaMemcpyDeviceToHost, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  // every kernel queued before the read-back has finished: no slot is read
+  T.sp->unpin_all();
+  const Route& r = *T.h_route;
+  if (r.b != b || r.k != k) return fail(SFK_ERR_RUNTIME, "layer %d: routing read back for %d x %d", l, r.b, r.k);
+  for (int i = 0; i < b * k; ++i)
+    if (r.ids[i] < 0 || r.ids[i] >= E) return fail(SFK_ERR_RUNTIME, "layer %d: routed expert %d", l, r.ids[i]);
+  for (int i = 0; i < b * k; ++i) {
+    const uint64_t key = (uint64_t)l << 32 | (uint32_t)r.ids[i];
+    if (T.warmed_now.count(key)) ++T.used;
+    T.pred->observe((uint32_t)l, (uint32_t)r.ids[i]);
+  }
+  int* row = T.h_map + (size_t)l * E;
+  for (int t = 0; t < b; ++t)
+    for (int j = 0; j < k; ++j) {
+      const int x = r.ids[t * k + j];
+      bool dup = false;
+      for (int q = 0; q < j; ++q) dup = dup || r.ids[t * k + q] == x;
+      if (dup) continue;
+      uint32_t slot = 0;
+      sfk_status s = tier_acquire(e, l, x, true, &slot);
+      if (s) return s;
+      if (slot == SlotPool::NONE)
+        return fail(SFK_ERR_RUNTIME, "layer %d: no unpinned slot for expert %d", l, x);
+      row[x] = (int)slot;
+    }
+  CK(cudaMemcpyAsync(T.d_map + (size_t)l * E, row, sizeof(int) * E, cudaMemcpyHostToDevice, e->stream));
+  return tier_fence(e);
+}
+
+// Warm layer l's predicted experts (engine.cpp:2900-2923): no pin, so a
+// later acquire may take the slot back; the copies overlap the kernels
+// already queued.
+sfk_status tier_prefetch(sfk_engine* e, int l) {
+  sfk_engine::Tier& T = e->tier;
+  if (!T.prefetch || l >= e->hp.n_layer) return SFK_OK;
+  for (uint32_t x : T.pred->predict((uint32_t)l, (uint32_t)e->hp.n_expert_used)) {
+    if (T.sp->resident((uint32_t)l, x)) continue;
+    uint32_t slot = 0;
+    sfk_status s = tier_acquire(e, l, (int)x, false, &slot);
+    if (s) return s;
+    if (slot == SlotPool::NONE) continue;
+    T.warmed_now.insert((uint64_t)l << 32 | x);
+    ++T.warmed;
+  }
+  return SFK_OK;
+}
+
+// One decode step with the bounded tier: the launch chain with a host read
+// of each layer's routing between its router and its experts.
+sfk_status run_step_tier(sfk_engine* e, int b, bool greedy) {
+  sfk_engine::Tier& T = e->tier;
+  // spare slots follow the observed per-layer activity, every 4 tokens
+  // (engine.cpp:2511-2523)
+  if (T.sp->stratified() && T.tokens % 4 == 0) T.sp->set_layer_weights(T.pred->layer_activity());
+  T.warmed_now.clear();
+  sfk_status s = launch_one(e, K_EMBED, 0, b, greedy, true);
+  int nk = 1;
+  for (int l = 0; l < e->hp.n_layer && !s; ++l) {
+    for (int c = K_QKV; c <= K_ROUTER && !s; ++c, ++nk) s = launch_one(e, c, l, b, greedy, true);
+    if (!s) s = tier_route_layer(e, l, b);
+    // (the gate/up kernel follows a copy and an event wait: a plain launch)
+    if (!s) s = launch_one(e, K_GATEUP, l, b, greedy, false);
+    if (!s) s = launch_one(e, K_DOWN, l, b, greedy, true);
+    nk += 2;
+    if (!s) s = tier_prefetch(e, l + 1);
+  }
+  if (!s) s = launch_one(e, K_LMHEAD, 0, b, greedy, true);
+  if (s) {
+    cudaStreamSynchronize(e->stream);
+    cudaStreamSynchronize(T.copy);
+    T.sp->unpin_all();
+    return s;
+  }
+  e->kernels_per_step = nk + 1;
+  T.tokens += 1;
+  return SFK_OK;
+}
+
 sfk_status validate_hp(const sfk_hparams* hp) {
   if (!hp) return fail(SFK_ERR_INVALID_ARGUMENT, "null hparams");
   if (hp->n_embd <= 0 || hp->n_head <= 0 || hp->n_head_kv <= 0 || hp->n_layer <= 0 || hp->n_ff <= 0 ||
       hp->n_expert <= 0 || hp->n_expert_used <= 0 || hp->n_vocab <= 0 || hp->n_ctx <= 0)
     return fail(SFK_ERR_INVALID_ARGUMENT, "hparams must be positive");
+  if (hp->expert_slots < 0) return fail(SFK_ERR_INVALID_ARGUMENT, "expert_slots %d", hp->expert_slots);
   if (hp->n_head % hp->n_head_kv || (hp->head_dim <= 0 && hp->n_embd % hp->n_head))
     return fail(SFK_ERR_INVALID_ARGUMENT, "n_head must divide by n_head_kv and n_embd by n_head");
   const int hd = hp->head_dim > 0 ? hp->head_dim : hp->n_embd / hp->n_head;
@@ -974,7 +1191,13 @@ void sfk_engine_free(sfk_engine* e) {
   if (e->stream) cudaStreamSynchronize(e->stream);
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   for (void* p : e->ep_opened) cudaIpcCloseMemHandle(p);
+  if (e->tier.copy) cudaStreamSynchronize(e->tier.copy);
   for (void* p : e->allocs) cudaFree(p);
+  for (void* p : {(void*)e->tier.host, (void*)e->tier.h_map, (void*)e->tier.h_route, (void*)e->tier.h_tile,
+                  (void*)e->tier.h_ids})
+    if (p) cudaFreeHost(p);
+  if (e->tier.copied) cudaEventDestroy(e->tier.copied);
+  if (e->tier.copy) cudaStreamDestroy(e->tier.copy);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_hist) cudaFreeHost(e->h_hist);
   if (e->h_keys) cudaFreeHost(e->h_keys);
@@ -1038,6 +1261,21 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   }
   const int d = hp->n_embd, F = hp->n_ff, E = hp->n_expert, V = hp->n_vocab;
   const int B = hp->max_batch, k = hp->n_expert_used;
+  // a bounded expert tier when expert_slots is below the whole working set
+  // (engine.cpp:1386-1394: 0 = auto, every expert resident)
+  e->tier.on = hp->expert_slots > 0 && (int64_t)hp->expert_slots < (int64_t)hp->n_layer * E;
+  if (e->tier.on && e->ep_size > 1) {
+    sfk_engine_free(e);
+    return fail(SFK_ERR_UNSUPPORTED, "a bounded expert tier (expert_slots %d) needs a single-GPU engine",
+                hp->expert_slots);
+  }
+  if (e->tier.on && hp->expert_slots < std::min(E, B * k)) {
+    sfk_engine_free(e);
+    return fail(SFK_ERR_INVALID_ARGUMENT,
+                "expert_slots %d cannot hold one step's routed experts of a layer (%d): the kernels read the "
+                "slots in place",
+                hp->expert_slots, std::min(E, B * k));
+  }
   // weights (HBM tier)
   TRY(e->alloc(&e->tok_embd, dev_gguf_row_bytes(hp->type_embd, d) * V, &e->weight_bytes));
   TRY(e->alloc(&e->out_norm, sizeof(float) * d, &e->weight_bytes));
@@ -1050,11 +1288,13 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     TRY(e->alloc(&W.attn_norm, sizeof(float) * d, &e->weight_bytes));
     TRY(e->alloc(&W.ffn_norm, sizeof(float) * d, &e->weight_bytes));
     TRY(e->alloc(&W.router, sizeof(float) * d * E, &e->weight_bytes));
+    if (e->tier.on) continue;  // the experts live in the pool's slots
     const int El = e->e_loc;  // this rank's experts
     TRY(e->alloc(&W.gate, dev_row_bytes(hp->type_ffn_gu, d) * F * El, &e->weight_bytes));
     TRY(e->alloc(&W.up, dev_row_bytes(hp->type_ffn_gu, d) * F * El, &e->weight_bytes));
     TRY(e->alloc(&W.down, dev_row_bytes(hp->type_ffn_down, F) * d * El, &e->weight_bytes));
   }
+  if (e->tier.on) TRY(tier_create(e));
   // paged KV: one pool per layer of B * ceil(n_ctx/16) pages [Hkv][16][hd];
   // pages are handed to sequences in a seeded permuted order (a fragmented
   // pool, as a page allocator produces).
@@ -1165,7 +1405,8 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     // experts) are scored a few logits per CTA and exchanged.
     // SFK_ROUTER_KERNEL=1 keeps the separate router kernel.
     const char* rk = getenv("SFK_ROUTER_KERNEL");
-    e->fused_route = !(rk && atoi(rk) == 1);
+    // (a bounded tier reads each layer's routing back before its experts run)
+    e->fused_route = !(rk && atoi(rk) == 1) && !e->tier.on;
     StreamParams gp = gateup_params(e, 0, B);
     int grid = 0;
     if (e->fused_route &&
@@ -1180,7 +1421,7 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     const int gqa = hp->n_head / hp->n_head_kv;
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-    if (pv && atoi(pv) == 1 && coop && e->ep_size == 1 && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
+    if (pv && atoi(pv) == 1 && coop && e->ep_size == 1 && !e->tier.on && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
         (gqa & (gqa - 1)) == 0 &&
         mega_types_supported(hp->type_attn, hp->type_ffn_gu, hp->type_ffn_down, hp->type_output)) {
       const int Hq = hp->n_head, Hkv = hp->n_head_kv;
@@ -1241,7 +1482,31 @@ size_t sfk_tensor_bytes(const sfk_engine* e, int tid, int layer) {
   return (size_t)dev_gguf_row_bytes(tensor_type(e, tid), tensor_cols(e, tid)) * (size_t)tensor_rows(e, tid);
 }
 
+static bool expert_tensor(int tid) {
+  return tid == SFK_T_FFN_GATE_EXPS || tid == SFK_T_FFN_UP_EXPS || tid == SFK_T_FFN_DOWN_EXPS;
+}
+
+// Bounded tier: a stacked expert tensor's rows, re-laid out, into each
+// expert's bundle in the pinned store (gate / up / down part of the slot).
+static sfk_status tier_put_stacked(sfk_engine* e, int tid, int layer, const uint8_t* dev_gguf) {
+  sfk_engine::Tier& T = e->tier;
+  const int type = tensor_type(e, tid), E = e->hp.n_expert;
+  const int64_t cols = tensor_cols(e, tid), per = tensor_rows(e, tid) / E;
+  const int64_t rs = dev_row_bytes(type, cols);
+  const int64_t part = tid == SFK_T_FFN_GATE_EXPS ? 0 : tid == SFK_T_FFN_UP_EXPS ? T.off_up : T.off_down;
+  uint8_t* tmp = nullptr;
+  CK(cudaMallocAsync(&tmp, (size_t)E * per * rs, e->stream));
+  cudaError_t ce = launch_repack(type, dev_gguf, tmp, E * per, (int)cols, e->stream);
+  for (int x = 0; x < E && ce == cudaSuccess; ++x)
+    ce = cudaMemcpyAsync(tier_bundle(e, layer, x) + part, tmp + (int64_t)x * per * rs, per * rs,
+                         cudaMemcpyDeviceToHost, e->stream);
+  cudaFreeAsync(tmp, e->stream);
+  CK(ce);
+  return tier_invalidate(e);
+}
+
 static sfk_status put_gguf_device(sfk_engine* e, int tid, int layer, const uint8_t* dev_gguf) {
+  if (e->tier.on && expert_tensor(tid)) return tier_put_stacked(e, tid, layer, dev_gguf);
   const int type = tensor_type(e, tid);
   const int64_t rows = tensor_rows(e, tid), cols = tensor_cols(e, tid);
   uint8_t* dst = tensor_dst(e, tid, layer);
@@ -1293,6 +1558,21 @@ sfk_status sfk_expert_put(sfk_engine* e, int layer, int expert, const void* bund
   CK(cudaMemcpyAsync(tmp, bundle, n_bytes, cudaMemcpyHostToDevice, e->stream));
   const LayerW& W = e->L[layer];
   const int64_t rs_gu = dev_row_bytes(hp.type_ffn_gu, hp.n_embd), rs_dn = dev_row_bytes(hp.type_ffn_down, hp.n_ff);
+  if (e->tier.on) {  // re-laid out into a device bundle, then into the pinned store
+    sfk_engine::Tier& T = e->tier;
+    uint8_t* slot = nullptr;
+    cudaError_t ce = cudaMallocAsync(&slot, T.slot_bytes, e->stream);
+    if (ce == cudaSuccess) ce = launch_repack(hp.type_ffn_gu, tmp, slot, hp.n_ff, hp.n_embd, e->stream);
+    if (ce == cudaSuccess) ce = launch_repack(hp.type_ffn_gu, tmp + gl, slot + T.off_up, hp.n_ff, hp.n_embd, e->stream);
+    if (ce == cudaSuccess)
+      ce = launch_repack(hp.type_ffn_down, tmp + 2 * gl, slot + T.off_down, hp.n_embd, hp.n_ff, e->stream);
+    if (ce == cudaSuccess)
+      ce = cudaMemcpyAsync(tier_bundle(e, layer, expert), slot, T.slot_bytes, cudaMemcpyDeviceToHost, e->stream);
+    if (slot) cudaFreeAsync(slot, e->stream);
+    cudaFreeAsync(tmp, e->stream);
+    CK(ce);
+    return tier_invalidate(e);
+  }
   CK(launch_repack(hp.type_ffn_gu, tmp, W.gate + (int64_t)expert * hp.n_ff * rs_gu, hp.n_ff, hp.n_embd, e->stream));
   CK(launch_repack(hp.type_ffn_gu, tmp + gl, W.up + (int64_t)expert * hp.n_ff * rs_gu, hp.n_ff, hp.n_embd, e->stream));
   CK(launch_repack(hp.type_ffn_down, tmp + 2 * gl, W.down + (int64_t)expert * hp.n_embd * rs_dn, hp.n_embd, hp.n_ff,
@@ -1308,6 +1588,25 @@ sfk_status sfk_weights_get(sfk_engine* e, int tid, int layer, void* host_out, si
   if (want == 0 || n_bytes != want) return fail(SFK_ERR_INVALID_ARGUMENT, "tensor %d: bad size", tid);
   CK(cudaSetDevice(e->device));
   const uint8_t* src = tensor_dst(e, tid, layer);
+  if (e->tier.on && expert_tensor(tid)) {  // from the pinned store's bundles
+    sfk_engine::Tier& T = e->tier;
+    const int type = tensor_type(e, tid), E = e->hp.n_expert;
+    const int64_t cols = tensor_cols(e, tid), per = tensor_rows(e, tid) / E, rs = dev_row_bytes(type, cols);
+    const int64_t part = tid == SFK_T_FFN_GATE_EXPS ? 0 : tid == SFK_T_FFN_UP_EXPS ? T.off_up : T.off_down;
+    uint8_t *dev = nullptr, *tmp = nullptr;
+    CK(cudaMallocAsync(&dev, (size_t)E * per * rs, e->stream));
+    cudaError_t ce = cudaMallocAsync(&tmp, want, e->stream);
+    for (int x = 0; x < E && ce == cudaSuccess; ++x)
+      ce = cudaMemcpyAsync(dev + (int64_t)x * per * rs, tier_bundle(e, layer, x) + part, per * rs,
+                           cudaMemcpyHostToDevice, e->stream);
+    if (ce == cudaSuccess) ce = launch_unpack(type, dev, tmp, E * per, (int)cols, e->stream);
+    if (ce == cudaSuccess) ce = cudaMemcpyAsync(host_out, tmp, want, cudaMemcpyDeviceToHost, e->stream);
+    cudaFreeAsync(dev, e->stream);
+    if (tmp) cudaFreeAsync(tmp, e->stream);
+    CK(ce);
+    CK(cudaStreamSynchronize(e->stream));
+    return SFK_OK;
+  }
   if (relaid(tid)) {
     uint8_t* tmp = nullptr;
     CK(cudaMallocAsync(&tmp, want, e->stream));
@@ -1376,6 +1675,13 @@ sfk_status sfk_kv_reset(sfk_engine* e) {
 }
 
 static sfk_status run_step(sfk_engine* e, int b, bool greedy) {
+  if (e->tier.on) {
+    sfk_status s = run_step_tier(e, b, greedy);
+    if (s) return s;
+    e->steps += 1;
+    e->last_b = b;
+    return SFK_OK;
+  }
   cudaGraphExec_t g = nullptr;
   sfk_status s = get_graph(e, b, greedy, &g);
   if (s) return s;
@@ -1460,6 +1766,9 @@ sfk_status prefill_alloc(sfk_engine* e) {
       (s = e->alloc(&f.rows_self, sizeof(int) * rows_pad, acct)) ||
       (s = e->alloc(&f.tile_expert, sizeof(int) * mt, acct)))
     return s;
+  // bounded tier: the down GEMM's activations apart from gate/up's, which
+  // every pass over the experts reads again
+  if (e->tier.on && (s = e->alloc(&f.act_dn, tc_act_bytes(rows_pad, F), acct))) return s;
   if (pf_attn_supported(e->hd, e->hq_loc, e->hkv_loc)) {
     // score rows of a whole chunk at the longest context, at most 256 MB
     // (longer contexts run the attention in token sub-batches of whole tiles)
@@ -1478,6 +1787,94 @@ sfk_status prefill_alloc(sfk_engine* e) {
 // sequence `seq`: the reference's per-token layer (engine.cpp:1878-1986) with
 // the matrices as tensor-core GEMMs over all m tokens (the routed experts
 // grouped by expert) and the attention of every token over its own prefix.
+// Bounded tier: the routed gate/up and down GEMMs of a prefill chunk, in
+// passes over as many of the chunk's experts as the pool can hold at once.
+// Each expert tile is computed exactly as in one pass (tiles are
+// independent); a pass's GEMMs see only its own tiles (the others are marked
+// -1), and the next pass may reuse the slots once the stream has drained.
+sfk_status tier_prefill_experts(sfk_engine* e, int l, int m) {
+  const sfk_hparams& hp = e->hp;
+  sfk_engine::Prefill& f = e->pf;
+  sfk_engine::Tier& T = e->tier;
+  cudaStream_t st = e->stream;
+  const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
+  const int act_gu = act_for(hp.type_ffn_gu), act_dn = act_for(hp.type_ffn_down);
+  CK(cudaMemcpyAsync(T.h_tile, f.tile_expert, sizeof(int) * f.mt, cudaMemcpyDeviceToHost, st));
+  CK(cudaMemcpyAsync(T.h_ids, f.ids, sizeof(int) * m * k, cudaMemcpyDeviceToHost, st));
+  CK(cudaStreamSynchronize(st));
+  T.sp->unpin_all();
+  std::vector<int> tile(T.h_tile, T.h_tile + f.mt), order;
+  for (int i = 0; i < m * k; ++i) {
+    if (T.h_ids[i] < 0 || T.h_ids[i] >= E) return fail(SFK_ERR_RUNTIME, "layer %d: routed expert %d", l, T.h_ids[i]);
+    T.pred->observe((uint32_t)l, (uint32_t)T.h_ids[i]);
+  }
+  // the experts in order of their first routed pair (the reference acquires
+  // them token by token)
+  std::vector<char> seen(E, 0);
+  for (int i = 0; i < m * k; ++i)
+    if (!seen[T.h_ids[i]]) {
+      seen[T.h_ids[i]] = 1;
+      order.push_back(T.h_ids[i]);
+    }
+  std::vector<int> slot_of(E, -1);
+  size_t next = 0;
+  while (next < order.size()) {
+    std::fill(slot_of.begin(), slot_of.end(), -1);
+    size_t taken = 0;
+    for (; next < order.size(); ++next, ++taken) {
+      uint32_t slot = 0;
+      sfk_status s = tier_acquire(e, l, order[next], true, &slot);
+      if (s) return s;
+      if (slot == SlotPool::NONE) break;
+      slot_of[order[next]] = (int)slot;
+    }
+    if (taken == 0) return fail(SFK_ERR_RUNTIME, "layer %d: no free expert slot", l);
+    for (int t = 0; t < f.mt; ++t) T.h_tile[t] = tile[t] >= 0 && tile[t] < E ? slot_of[tile[t]] : -1;
+    CK(cudaMemcpyAsync(T.d_tile, T.h_tile, sizeof(int) * f.mt, cudaMemcpyHostToDevice, st));
+    sfk_status s = tier_fence(e);
+    if (s) return s;
+    TcGemmParams g{};
+    g.w = T.pool;
+    g.w2 = T.pool + T.off_up;
+    g.rowstride = dev_row_bytes(hp.type_ffn_gu, d);
+    g.expert_stride = T.slot_bytes;
+    g.rows = F;
+    g.K = d;
+    g.wtype = hp.type_ffn_gu;
+    g.act_type = act_gu;
+    g.xq = f.act;
+    g.ntile = f.mt;
+    g.tile_expert = T.d_tile;
+    g.y = f.h;
+    g.ldy = F;
+    g.epi = TC_EPI_SWIGLU;
+    g.status = e->status;
+    CK(launch_tc_gemm(g, st));
+    CK(launch_tc_quant(act_dn, f.h, F, f.rows_self, f.mt * TC_TT, f.mt * TC_TT, F, f.act_dn, st));
+    g = TcGemmParams{};
+    g.w = T.pool + T.off_down;
+    g.rowstride = dev_row_bytes(hp.type_ffn_down, F);
+    g.expert_stride = T.slot_bytes;
+    g.rows = d;
+    g.K = F;
+    g.wtype = hp.type_ffn_down;
+    g.act_type = act_dn;
+    g.xq = f.act_dn;
+    g.ntile = f.mt;
+    g.tile_expert = T.d_tile;
+    g.y = f.yd;
+    g.ldy = d;
+    g.epi = TC_EPI_STORE;
+    g.status = e->status;
+    CK(launch_tc_gemm(g, st));
+    if (next < order.size()) {  // the next pass may take these slots back
+      CK(cudaStreamSynchronize(st));
+      T.sp->unpin_all();
+    }
+  }
+  return SFK_OK;
+}
+
 sfk_status prefill_layer(sfk_engine* e, int l, int seq, int m, int pos0) {
   const sfk_hparams& hp = e->hp;
   const LayerW& W = e->L[l];
@@ -1559,6 +1956,12 @@ sfk_status prefill_layer(sfk_engine* e, int l, int seq, int m, int pos0) {
   CK(launch_pf_group(f.ids, m * k, k, E, f.mt, f.pos_of_pair, f.rows_tok, f.rows_self, f.tile_expert, e->status, st));
   // gate / up + SwiGLU of every routed pair (engine.cpp:1967-1969)
   CK(launch_tc_quant(act_gu, f.xn, d, f.rows_tok, m, f.mt * TC_TT, d, f.act, st));
+  if (e->tier.on) {
+    sfk_status s = tier_prefill_experts(e, l, m);
+    if (s) return s;
+    CK(launch_pf_combine(f.yd, f.pos_of_pair, f.w, k, m, d, f.ffn, f.x, st));
+    return SFK_OK;
+  }
   g = TcGemmParams{};
   g.w = W.gate;
   g.w2 = W.up;
@@ -1841,6 +2244,14 @@ sfk_status sfk_get_stats(const sfk_engine* e, sfk_stats* out) {
                        (uint64_t)hp.n_expert_used * (2ull * dev_gguf_row_bytes(hp.type_ffn_gu, d) * F +
                                                      (uint64_t)dev_gguf_row_bytes(hp.type_ffn_down, F) * d);
   out->active_bytes_per_token = per_layer * hp.n_layer + (uint64_t)dev_gguf_row_bytes(hp.type_output, d) * hp.n_vocab;
+  const sfk_engine::Tier& T = e->tier;
+  out->pool_slots = T.on ? T.n_slots : 0;
+  out->pool_hits = T.on ? T.sp->stats().hits : 0;
+  out->pool_misses = T.on ? T.sp->stats().misses : 0;
+  out->pool_evictions = T.on ? T.sp->stats().evictions : 0;
+  out->h2d_expert_bytes = T.h2d;
+  out->prefetch_warmed = T.warmed;
+  out->prefetch_used = T.used;
   return SFK_OK;
 }
 
@@ -1848,6 +2259,7 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
   if (!e || !ms_out || n_out < K_NCLASS || iters < 1 || n_seq < 1 || n_seq > e->hp.max_batch)
     return fail(SFK_ERR_INVALID_ARGUMENT, "time_kernels arguments");
   if (e->steps == 0) return fail(SFK_ERR_INVALID_ARGUMENT, "run a decode step first");
+  if (e->tier.on) return fail(SFK_ERR_UNSUPPORTED, "per-kernel timing needs every expert resident");
   CK(cudaSetDevice(e->device));
   cudaEvent_t a = nullptr, z = nullptr;
   CK(cudaEventCreate(&a));

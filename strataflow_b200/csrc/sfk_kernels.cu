@@ -114,6 +114,17 @@ struct TileWalk {
 __device__ __forceinline__ int slot_expert(const StreamParams& p, int si) {
   return p.route ? p.route->slot_expert[si] : 0;
 }
+// Where expert e's matrices sit: e itself, or its slot of the bounded pool
+// (a slot outside the pool reads slot 0 and reports).
+__device__ __forceinline__ int expert_home(const StreamParams& p, int e) {
+  if (!p.slot_map) return e;
+  const int s = p.slot_map[e];
+  if (s < 0 || s >= p.n_map_slots) {
+    atomicExch(p.status, ERR_BAD_ID);
+    return 0;
+  }
+  return s;
+}
 
 template <int WT>
 __device__ __forceinline__ float unit_dot(const uint8_t* wg, const uint8_t* xg, int ng, int lane) {
@@ -505,7 +516,8 @@ __global__ void __launch_bounds__((NW + 1) * 32, 1) stream_kernel(const StreamPa
       const int rbase = r0 + tw.rb * pl.rows_tile;
       const int nrows = min(pl.rows_tile, r1 - rbase);
       mbar_arrive_expect_tx(&full[s], (uint32_t)(nrows * p.nmat * gb));
-      const int64_t eoff = (int64_t)slot_expert(p, tw.si) * p.expert_stride + group_offset(WT, p.K, tw.g);
+      const int64_t eoff =
+          (int64_t)expert_home(p, slot_expert(p, tw.si)) * p.expert_stride + group_offset(WT, p.K, tw.g);
       uint8_t* dst = ring + (int64_t)s * pl.stage_bytes;
       for (int m = 0; m < p.nmat; ++m) {
         const uint8_t* base = (m == 0 ? p.w0 : p.w1) + eoff;
@@ -782,7 +794,7 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
     const int rbase = r0 + rb * R;
     const uint32_t bytes = (uint32_t)(min(R, r1 - rbase) * rs);
     mbar_arrive_expect_tx(&full[s], bytes * NMAT);
-    const int expert = routed ? rt->slot_expert[si] : 0;
+    const int expert = routed ? expert_home(p, rt->slot_expert[si]) : 0;
     const int64_t eoff = (int64_t)expert * p.expert_stride + (int64_t)rbase * rs;
     uint8_t* dst = ring + (int64_t)s * pl.tile_bytes;
     const uint64_t pol = l2_evict_first_policy();

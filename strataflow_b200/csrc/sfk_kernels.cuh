@@ -127,6 +127,11 @@ struct StreamParams {
   // (ep_eloc = 0: all experts are local); routed tiles and the weighted
   // combine skip the others
   int ep_e0, ep_eloc;
+  // bounded expert tier: routed expert e is read from slot slot_map[e] of the
+  // pool (w0 / w1 = the pool's matrices, expert_stride = the slot size);
+  // null: experts are addressed directly
+  const int* slot_map;
+  int n_map_slots;
   Plan2 pl;  // filled by the launcher
 };
 

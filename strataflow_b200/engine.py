@@ -46,6 +46,7 @@ class ModelConfig:
     ep_size: int = 1   # expert-parallel ranks (one engine per GPU)
     ep_rank: int = 0
     head_dim: int = 0  # 0: n_embd / n_head
+    expert_slots: int = 0  # HBM expert slots; 0: every expert resident (Engine::load's expert_slots)
 
     @property
     def hd(self) -> int:
@@ -123,16 +124,19 @@ class Engine:
 
     @classmethod
     def load_strata(cls, path: str, n_ctx: int = 0, max_batch: int = 1, kv_type: int = L.KV_F16,
-                    ep_size: int = 1, ep_rank: int = 0, device: int = 0) -> "Engine":
+                    ep_size: int = 1, ep_rank: int = 0, device: int = 0, expert_slots: int = 0) -> "Engine":
         """Engine::load of a .strata file (engine.cpp:983-1137 with
         load_strata_weights): the model shape from the file's GGUF metadata,
-        every trunk tensor and expert bundle uploaded to the HBM tier.  n_ctx
-        <= 0 takes the file's llama.context_length."""
+        every trunk tensor and expert bundle uploaded to the HBM tier (or,
+        with expert_slots below n_layer * n_expert, to the pinned host store
+        behind a pool of that many HBM slots).  n_ctx <= 0 takes the file's
+        llama.context_length."""
         from .strata import StrataFile
         with StrataFile(path) as f:
             base = L.Hparams()
             base.n_ctx, base.max_batch, base.kv_type, base.ep_size, base.ep_rank = n_ctx, max_batch, kv_type, \
                 ep_size, ep_rank
+            base.expert_slots = expert_slots
             hp = f.hparams(base)
             cfg = ModelConfig(**{n: getattr(hp, n) for n, _ in L.Hparams._fields_})
             eng = cls(cfg, device)

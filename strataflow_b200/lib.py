@@ -33,7 +33,7 @@ class Hparams(C.Structure):
         "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
         ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
             "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_type", "max_batch",
-            "ep_size", "ep_rank", "head_dim")]
+            "ep_size", "ep_rank", "head_dim", "expert_slots")]
 
 
 EP_HANDLE_BYTES = 64  # SFK_EP_HANDLE_BYTES
@@ -42,7 +42,8 @@ EP_HANDLE_BYTES = 64  # SFK_EP_HANDLE_BYTES
 class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "weight_bytes_hbm", "kv_bytes_hbm", "scratch_bytes_hbm", "steps", "kernels_per_step",
-        "active_bytes_per_token")]
+        "active_bytes_per_token", "pool_slots", "pool_hits", "pool_misses", "pool_evictions", "h2d_expert_bytes",
+        "prefetch_warmed", "prefetch_used")]
 
 
 class Sampling(C.Structure):
@@ -54,6 +55,7 @@ class Sampling(C.Structure):
 TOKEN_CB = C.CFUNCTYPE(C.c_int, C.c_int32, C.c_void_p)
 
 P, I32, I64, U64, SZ, F = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_size_t, C.c_float
+U32 = C.c_uint32
 _SIGS = {
     "sfk_last_error": (C.c_char_p, []),
     "sfk_status_str": (C.c_char_p, [I32]),
@@ -100,6 +102,23 @@ _SIGS = {
     "sfk_strata_bundle_bytes": (SZ, [P, I32]),
     "sfk_strata_read_bundle": (I32, [P, I32, I32, P, SZ]),
     "sfk_strata_load": (I32, [P, P]),
+    "sfk_pool_create": (I32, [U32, U32, U32, U32, C.POINTER(P)]),
+    "sfk_pool_free": (None, [P]),
+    "sfk_pool_acquire": (I64, [P, U32, U32, C.POINTER(I32)]),
+    "sfk_pool_resident": (I32, [P, U32, U32]),
+    "sfk_pool_stratified": (I32, [P]),
+    "sfk_pool_layer_capacity": (U32, [P, U32]),
+    "sfk_pool_has_free_slot_in_layer": (I32, [P, U32]),
+    "sfk_pool_set_layer_weights": (I32, [P, P, U32]),
+    "sfk_pool_pin": (I32, [P, U32]),
+    "sfk_pool_unpin_all": (I32, [P]),
+    "sfk_pool_stats": (I32, [P, P]),
+    "sfk_predictor_create": (I32, [U32, U32, C.POINTER(P)]),
+    "sfk_predictor_free": (None, [P]),
+    "sfk_predictor_observe": (I32, [P, U32, U32]),
+    "sfk_predictor_predict": (U32, [P, U32, U32, P]),
+    "sfk_predictor_accuracy": (C.c_double, [P]),
+    "sfk_predictor_layer_activity": (I32, [P, P, U32]),
 }
 
 _lib = None
