@@ -571,6 +571,81 @@ def run_sweep_tc(args):
     eng.close()
 
 
+def run_tier(args):
+    """Decode at the Mixtral shape with a bounded expert tier: `expert_slots`
+    of the 256 expert bundles in HBM, the rest streamed from pinned host
+    memory (one host-to-device copy per missing bundle).  One JSON line: the
+    device-timed decode rate and, over the timed steps, the pool's hits,
+    misses and host-to-device traffic against the measured pinned copy rate."""
+    import torch
+    from strataflow_b200 import engine as E
+
+    torch.cuda.set_device(0)
+    B = args.batch
+    n_ctx = args.prompt + args.warmup + args.steps + 16
+    cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B, n_layer=args.layers, expert_slots=args.expert_slots)
+    t_load = time.perf_counter()
+    eng = E.Engine.load(cfg, seed=SEED)
+    t_load = time.perf_counter() - t_load
+    stream = torch.cuda.ExternalStream(eng.stream, device=torch.device("cuda", 0))
+    prompt = np.random.default_rng(SEED).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
+    torch.cuda.synchronize()
+    t_pf = time.perf_counter()
+    for s_ in range(B):
+        eng.prefill(prompt[s_], seq=s_, want_logits=False)
+    t_pf = time.perf_counter() - t_pf
+    eng.decode_greedy(args.warmup, B, want_tokens=False)
+    s0 = eng.stats()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        ev0.record(stream)
+        eng.decode_greedy(args.steps, B, want_tokens=False)
+        ev1.record(stream)
+        ev1.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    s1 = eng.stats()
+    d = {k: s1[k] - s0[k] for k in ("pool_hits", "pool_misses", "pool_evictions", "h2d_expert_bytes",
+                                    "prefetch_warmed", "prefetch_used")}
+    h2d_gbs = d["h2d_expert_bytes"] / (ms / 1e3) / 1e9
+    eng.close()
+    # the pinned host-to-device copy rate of this box (1 GiB, 5 copies)
+    host = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
+    dev = torch.empty(1 << 30, dtype=torch.uint8, device="cuda")
+    dev.copy_(host, non_blocking=True)
+    torch.cuda.synchronize()
+    c0 = torch.cuda.Event(enable_timing=True)
+    c1 = torch.cuda.Event(enable_timing=True)
+    c0.record()
+    for _ in range(5):
+        dev.copy_(host, non_blocking=True)
+    c1.record()
+    c1.synchronize()
+    pin_gbs = 5 * (1 << 30) / (c0.elapsed_time(c1) / 1e3) / 1e9
+    bundle = 3 * 14336 * (4096 // 256 * 144)
+    line = {
+        "metric": METRIC, "value": B * args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "q4_k/q6_k weights x q8_k int8 dot (dp4a), fp32 accum", "data": "synthetic",
+        "config": {"workload": f"Mixtral-8x7B-shape decode b={B} with a bounded expert tier: "
+                               f"{args.expert_slots} of {cfg.n_layer * 8} expert bundles in HBM",
+                   "model": "mixtral-8x7b-shape (32L d4096 32q/8kv E8 top2 F14336 V32000)",
+                   "global_batch": B, "seq_len": args.prompt, "expert_slots": args.expert_slots,
+                   "pool": "global LRU" if os.environ.get("SFK_POOL_GLOBAL_LRU") == "1" else "layer-stratified LRU",
+                   "prefetch": {"0": "off", "2": "evicting warm"}.get(os.environ.get("SFK_PREFETCH", "1"),
+                                                                       "into free slots")},
+        "clocks": clk.summary(),
+        "tier": {"bundle_bytes": bundle, "hits": d["pool_hits"], "misses": d["pool_misses"],
+                 "evictions": d["pool_evictions"], "hit_rate": d["pool_hits"] / max(1, d["pool_hits"] + d["pool_misses"]),
+                 "misses_per_token": d["pool_misses"] / (B * args.steps), "prefetch_warmed": d["prefetch_warmed"],
+                 "prefetch_used": d["prefetch_used"], "h2d_gbs": h2d_gbs, "pinned_h2d_peak_gbs": pin_gbs,
+                 "h2d_frac": h2d_gbs / pin_gbs},
+        "load_s": t_load, "prefill_s": t_pf,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -590,6 +665,8 @@ def main():
                     help="operator sweeps (configs[1] mul_mat_id, configs[2] attention), one JSON line per case")
     ap.add_argument("--sweep-tc", action="store_true",
                     help="tensor-core GEMM sweep (n = 16..512 rows) and the batched 512-token prefill")
+    ap.add_argument("--expert-slots", type=int, default=0,
+                    help="decode with a bounded expert tier of this many HBM bundle slots (one GPU)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -602,6 +679,9 @@ def main():
         return
     if args.sweep_tc:
         run_sweep_tc(args)
+        return
+    if args.expert_slots > 0:
+        run_tier(args)
         return
     if args.model == "1t":
         if args.layers == 32:

@@ -103,7 +103,8 @@ typedef struct sfk_hparams {
      * SFK_POOL_GLOBAL_LRU=1 selects the single global LRU), refilled by one
      * host-to-device copy per missing bundle on a copy stream, with the next
      * layer's predicted experts prefetched (ExpertPredictor,
-     * src/predict/predictor.h; SFK_PREFETCH=0 turns it off).  The expert
+     * src/predict/predictor.h) into free slots (SFK_PREFETCH=2: evicting
+     * within that layer; SFK_PREFETCH=0: off).  The expert
      * kernels read the slots in place, so a pool must hold one step's routed
      * experts of a layer: at least min(n_expert, max_batch * n_expert_used).
      * Single-GPU engines only (ep_size <= 1). */

@@ -331,7 +331,7 @@ struct sfk_engine {
     cudaEvent_t copied = nullptr;
     std::unique_ptr<SlotPool> sp;
     std::unique_ptr<ExpertPredictor> pred;
-    bool prefetch = true;
+    int prefetch = 1;  // 0 off; 1 only into free slots; 2 may evict within the predicted layer
     uint64_t h2d = 0, warmed = 0, used = 0, tokens = 0;
     std::set<uint64_t> warmed_now;  // (layer, expert) prefetched during this step
   } tier;
@@ -1004,8 +1004,13 @@ sfk_status tier_create(sfk_engine* e) {
     T.sp.reset(new (std::nothrow) SlotPool(T.n_slots, hp.n_layer, E, k));
   T.pred.reset(new (std::nothrow) ExpertPredictor(hp.n_layer, E));
   if (!T.sp || !T.pred) return fail(SFK_ERR_OUT_OF_MEMORY, "host alloc");
+  // prefetch policy (SFK_PREFETCH): 1 (default) installs a predicted bundle
+  // only where that evicts nothing -- the reference's asynchronous install
+  // rule (has_free_slot_in_layer, weight_store.h:94-123); 2 warms like its
+  // synchronous warm_expert (engine.cpp:2135-2196), evicting within the
+  // predicted layer; 0 turns prefetch off
   const char* pf = getenv("SFK_PREFETCH");
-  T.prefetch = !(pf && pf[0] == '0');
+  T.prefetch = pf && (pf[0] == '0' || pf[0] == '2') ? pf[0] - '0' : 1;
   return SFK_OK;
 }
 
@@ -1086,12 +1091,14 @@ sfk_status tier_route_layer(sfk_engine* e, int l, int b) {
 
 // Warm layer l's predicted experts (engine.cpp:2900-2923): no pin, so a
 // later acquire may take the slot back; the copies overlap the kernels
-// already queued.
+// already queued.  By default only into free capacity: a warm that evicts
+// trades a likely hit of the layer's resident set for a guess.
 sfk_status tier_prefetch(sfk_engine* e, int l) {
   sfk_engine::Tier& T = e->tier;
   if (!T.prefetch || l >= e->hp.n_layer) return SFK_OK;
   for (uint32_t x : T.pred->predict((uint32_t)l, (uint32_t)e->hp.n_expert_used)) {
     if (T.sp->resident((uint32_t)l, x)) continue;
+    if (T.prefetch == 1 && !T.sp->has_free_slot_in_layer((uint32_t)l)) break;
     uint32_t slot = 0;
     sfk_status s = tier_acquire(e, l, (int)x, false, &slot);
     if (s) return s;
