@@ -109,6 +109,17 @@ typedef struct sfk_hparams {
      * experts of a layer: at least min(n_expert, max_batch * n_expert_used).
      * Single-GPU engines only (ep_size <= 1). */
     int32_t expert_slots;
+    /* Resident KV window in tokens (the reference's kv_window, KvStore
+     * src/kv/kv_store.h:30-95; engine.cpp:1633-1762).  0 or >= n_ctx: the
+     * whole context's KV stays in HBM.  Otherwise each sequence keeps its most
+     * recent ceil(kv_window / 16) 16-token pages in HBM, written as a ring;
+     * the page a new position would overwrite is first copied to a pinned
+     * host cold store, and every layer's attention reads the cold pages
+     * staged back into one layer's worth of HBM -- lossless: the same keys
+     * and values in the same order as the resident cache.  Positions of a
+     * sequence move forward (a position whose page has gone cold is refused);
+     * at least two pages; single-GPU engines only. */
+    int32_t kv_window;
 } sfk_hparams;
 
 typedef struct sfk_engine sfk_engine;
@@ -293,6 +304,10 @@ typedef struct sfk_stats {
     uint64_t h2d_expert_bytes;   /* bundle bytes copied host -> HBM */
     uint64_t prefetch_warmed;    /* bundles copied in ahead of their layer */
     uint64_t prefetch_used;      /* of those, routed when their layer ran */
+    /* KV window (zero without one) */
+    uint64_t kv_window_pages;    /* HBM pages per sequence */
+    uint64_t kv_pages_evicted;   /* pages moved to the cold store */
+    uint64_t kv_staged_bytes;    /* cold K/V bytes staged back for attention */
 } sfk_stats;
 SFK_API sfk_status sfk_get_stats(const sfk_engine *eng, sfk_stats *out);
 

@@ -240,9 +240,24 @@ struct sfk_engine {
   void* k_pool = nullptr;
   void* v_pool = nullptr;
   int64_t kv_layer_elems = 0;
-  int* page_table = nullptr;
+  int* page_table = nullptr;  // [max_batch][max_pages]
   int max_pages = 0;
-  int n_pages = 0;
+  int n_pages = 0;  // HBM pages per layer
+  // KV window (hp.kv_window): each sequence's last `pages` pages form a ring
+  // of HBM pages; older pages live in a pinned host cold store and are staged
+  // back into one layer's worth of HBM for each layer's attention
+  struct Window {
+    bool on = false;
+    int pages = 0;                              // ring pages per sequence
+    int64_t page_bytes = 0;                     // one page of K (or V) of one layer
+    void *k_stage = nullptr, *v_stage = nullptr;  // [max_batch][max_pages] pages
+    uint8_t *k_cold = nullptr, *v_cold = nullptr; // pinned [n_layer][max_batch][max_pages] pages
+    std::vector<int> cold;                      // per sequence: logical pages 0 .. cold-1 are cold
+    std::vector<int> ring;                      // [max_batch][pages] HBM page of each ring slot
+    uint64_t evicted = 0, staged_bytes = 0;
+  } win;
+  std::vector<int> step_pos;  // host: the position of each sequence in the step being launched
+  std::vector<int> pt0;       // the page table after a reset
   // step buffers
   float *x = nullptr, *ffn_inp = nullptr, *q = nullptr, *attn_out = nullptr, *h = nullptr, *logits = nullptr;
   float *router_logits = nullptr;
@@ -458,6 +473,12 @@ KvView kv_view(const sfk_engine* e, int l) {
   const size_t kv_elem = kv.f16 ? 2 : 4;
   kv.k = static_cast<uint8_t*>(e->k_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
   kv.v = static_cast<uint8_t*>(e->v_pool) + (int64_t)l * e->kv_layer_elems * kv_elem;
+  if (e->win.on) {  // ids from n_pages up: the staged cold pages (page_table: n_pages + seq * max_pages + page)
+    kv.n_hot = e->n_pages;
+    kv.n_pages = e->n_pages + hp.max_batch * e->max_pages;
+    kv.k2 = e->win.k_stage;
+    kv.v2 = e->win.v_stage;
+  }
   return kv;
 }
 
@@ -1109,34 +1130,124 @@ sfk_status tier_prefetch(sfk_engine* e, int l) {
   return SFK_OK;
 }
 
-// One decode step with the bounded tier: the launch chain with a host read
-// of each layer's routing between its router and its experts.
-sfk_status run_step_tier(sfk_engine* e, int b, bool greedy) {
+// ---- the KV window ----------------------------------------------------------
+// KvStore (src/kv/kv_store.h:30-95) with 16-token pages: sequence t's logical
+// page j lives in ring slot j % pages of its HBM pages; before a position
+// whose slot still holds a live older page is written, that page (every
+// layer, K and V) goes to the pinned cold store and its page-table entry to
+// its staged copy (KvStore::evicts, kv_store.h:84: the evicted column is saved
+// before the ring write).  Each layer's attention then reads the cold pages
+// from one layer's worth of staging HBM, refilled before the layer (the
+// reference assembles cold + ring columns per layer, engine.cpp:1660-1749).
+
+// The page table after a reset: every logical page in its first ring slot
+// (or the permuted pool without a window); no page cold.
+sfk_status window_table(sfk_engine* e) {
+  CK(cudaMemcpyAsync(e->page_table, e->pt0.data(), sizeof(int) * e->pt0.size(), cudaMemcpyHostToDevice, e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  std::fill(e->win.cold.begin(), e->win.cold.end(), 0);
+  return SFK_OK;
+}
+
+// Make position `pos` of sequence t writable: its page must not have gone
+// cold, and every older page still in the slot it lands in is evicted.
+sfk_status window_advance(sfk_engine* e, int t, int pos) {
+  sfk_engine::Window& w = e->win;
+  const int j = pos / 16, MP = e->max_pages, L = e->hp.n_layer;
+  if (j < w.cold[t])
+    return fail(SFK_ERR_INVALID_ARGUMENT, "sequence %d: position %d lies in a page that has left the KV window", t,
+                pos);
+  const size_t kv_elem = e->hp.kv_type == SFK_KV_F16 ? 2 : 4;
+  const size_t layer_bytes = (size_t)e->kv_layer_elems * kv_elem;          // HBM pool, one layer
+  const size_t cold_layer = (size_t)e->hp.max_batch * MP * w.page_bytes;    // cold store, one layer
+  while (w.cold[t] + w.pages <= j) {
+    const int q = w.cold[t];
+    const int h = w.ring[(size_t)t * w.pages + q % w.pages];
+    for (int v = 0; v < 2; ++v) {
+      const uint8_t* src = static_cast<const uint8_t*>(v ? e->v_pool : e->k_pool) + (int64_t)h * w.page_bytes;
+      uint8_t* dst = (v ? w.v_cold : w.k_cold) + ((size_t)t * MP + q) * w.page_bytes;
+      if (layer_bytes < (1ull << 31) && cold_layer < (1ull << 31)) {
+        CK(cudaMemcpy2DAsync(dst, cold_layer, src, layer_bytes, w.page_bytes, L, cudaMemcpyDeviceToHost, e->stream));
+      } else {
+        for (int l = 0; l < L; ++l)
+          CK(cudaMemcpyAsync(dst + l * cold_layer, src + l * layer_bytes, w.page_bytes, cudaMemcpyDeviceToHost,
+                             e->stream));
+      }
+    }
+    CK(launch_pt_set(e->page_table, t * MP + q, e->n_pages + t * MP + q, e->stream));
+    w.cold[t] = q + 1;
+    ++w.evicted;
+  }
+  return SFK_OK;
+}
+
+// Layer l's cold pages of sequences [t0, t1) into the staging pages (ids
+// n_pages + t * max_pages + j); *copied tells whether any were.
+sfk_status window_stage(sfk_engine* e, int l, int t0, int t1, bool* copied) {
+  sfk_engine::Window& w = e->win;
+  *copied = false;
+  const int B = e->hp.max_batch, MP = e->max_pages;
+  for (int t = t0; t < t1; ++t) {
+    const int c = w.cold[t];
+    if (c == 0) continue;
+    for (int v = 0; v < 2; ++v) {
+      const uint8_t* src = (v ? w.v_cold : w.k_cold) + ((size_t)l * B + t) * MP * w.page_bytes;
+      uint8_t* dst = static_cast<uint8_t*>(v ? w.v_stage : w.k_stage) + (size_t)t * MP * w.page_bytes;
+      CK(cudaMemcpyAsync(dst, src, (size_t)c * w.page_bytes, cudaMemcpyHostToDevice, e->stream));
+    }
+    w.staged_bytes += 2ull * c * w.page_bytes;
+    *copied = true;
+  }
+  return SFK_OK;
+}
+
+// A decode step as a direct launch chain, for engines whose steps need the
+// host between launches: a bounded expert tier reads each layer's routing
+// back before its experts run; a KV window evicts pages before the step and
+// stages each layer's cold pages before its QKV kernel.
+sfk_status run_step_direct(sfk_engine* e, int b, bool greedy) {
   sfk_engine::Tier& T = e->tier;
-  // spare slots follow the observed per-layer activity, every 4 tokens
-  // (engine.cpp:2511-2523)
-  if (T.sp->stratified() && T.tokens % 4 == 0) T.sp->set_layer_weights(T.pred->layer_activity());
-  T.warmed_now.clear();
-  sfk_status s = launch_one(e, K_EMBED, 0, b, greedy, true);
+  sfk_status s = SFK_OK;
+  if (e->win.on)
+    for (int t = 0; t < b && !s; ++t) s = window_advance(e, t, e->step_pos[t]);
+  if (s) return s;
+  if (T.on) {
+    // spare slots follow the observed per-layer activity, every 4 tokens
+    // (engine.cpp:2511-2523)
+    if (T.sp->stratified() && T.tokens % 4 == 0) T.sp->set_layer_weights(T.pred->layer_activity());
+    T.warmed_now.clear();
+  }
+  s = launch_one(e, K_EMBED, 0, b, greedy, false);
   int nk = 1;
   for (int l = 0; l < e->hp.n_layer && !s; ++l) {
-    for (int c = K_QKV; c <= K_ROUTER && !s; ++c, ++nk) s = launch_one(e, c, l, b, greedy, true);
-    if (!s) s = tier_route_layer(e, l, b);
-    // (the gate/up kernel follows a copy and an event wait: a plain launch)
-    if (!s) s = launch_one(e, K_GATEUP, l, b, greedy, false);
+    bool staged = false;
+    if (e->win.on) s = window_stage(e, l, 0, b, &staged);
+    // (a kernel that follows a copy is a plain launch)
+    if (!s) s = launch_one(e, K_QKV, l, b, greedy, !staged);
+    if (!s) s = launch_one(e, K_ATTN, l, b, greedy, true);
+    if (!s) s = launch_one(e, K_OPROJ, l, b, greedy, true);
+    nk += 3;
+    if (!e->fused_route) {
+      if (!s) s = launch_one(e, K_ROUTER, l, b, greedy, true);
+      ++nk;
+    }
+    if (!s && T.on) s = tier_route_layer(e, l, b);
+    if (!s) s = launch_one(e, K_GATEUP, l, b, greedy, !T.on);
     if (!s) s = launch_one(e, K_DOWN, l, b, greedy, true);
     nk += 2;
-    if (!s) s = tier_prefetch(e, l + 1);
+    if (!s && T.on) s = tier_prefetch(e, l + 1);
   }
   if (!s) s = launch_one(e, K_LMHEAD, 0, b, greedy, true);
   if (s) {
     cudaStreamSynchronize(e->stream);
-    cudaStreamSynchronize(T.copy);
-    T.sp->unpin_all();
+    if (T.on) {
+      cudaStreamSynchronize(T.copy);
+      T.sp->unpin_all();
+    }
     return s;
   }
   e->kernels_per_step = nk + 1;
-  T.tokens += 1;
+  if (T.on) T.tokens += 1;
   return SFK_OK;
 }
 
@@ -1201,7 +1312,7 @@ void sfk_engine_free(sfk_engine* e) {
   if (e->tier.copy) cudaStreamSynchronize(e->tier.copy);
   for (void* p : e->allocs) cudaFree(p);
   for (void* p : {(void*)e->tier.host, (void*)e->tier.h_map, (void*)e->tier.h_route, (void*)e->tier.h_tile,
-                  (void*)e->tier.h_ids})
+                  (void*)e->tier.h_ids, (void*)e->win.k_cold, (void*)e->win.v_cold})
     if (p) cudaFreeHost(p);
   if (e->tier.copied) cudaEventDestroy(e->tier.copied);
   if (e->tier.copy) cudaStreamDestroy(e->tier.copy);
@@ -1306,13 +1417,26 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   // pages are handed to sequences in a seeded permuted order (a fragmented
   // pool, as a page allocator produces).
   e->max_pages = (hp->n_ctx + 15) / 16;
-  e->n_pages = B * e->max_pages;
+  e->win.on = hp->kv_window > 0 && hp->kv_window < hp->n_ctx;
+  if (e->win.on) {
+    e->win.pages = (hp->kv_window + 15) / 16;
+    if (e->win.pages < 2 || e->ep_size > 1) {
+      sfk_engine_free(e);
+      return fail(e->ep_size > 1 ? SFK_ERR_UNSUPPORTED : SFK_ERR_INVALID_ARGUMENT,
+                  "kv_window %d: a window spans at least two 16-token pages, on a single-GPU engine", hp->kv_window);
+    }
+    if (e->win.pages >= e->max_pages) e->win.on = false;  // the window holds the whole context
+  }
+  e->n_pages = B * (e->win.on ? e->win.pages : e->max_pages);
   e->kv_layer_elems = (int64_t)e->n_pages * e->hkv_loc * 16 * e->hd;
   const size_t kv_elem = hp->kv_type == SFK_KV_F16 ? 2 : 4;
   TRY(e->alloc(&e->k_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
   TRY(e->alloc(&e->v_pool, kv_elem * e->kv_layer_elems * hp->n_layer, &e->kv_bytes));
-  TRY(e->alloc(&e->page_table, sizeof(int) * e->n_pages, &e->kv_bytes));
+  TRY(e->alloc(&e->page_table, sizeof(int) * B * e->max_pages, &e->kv_bytes));
   {
+    // HBM pages handed out in a seeded permuted order (a fragmented pool, as
+    // a page allocator produces); with a window, sequence t's ring slot r is
+    // page perm[t * pages + r] and logical page j starts in slot j % pages
     std::vector<int> perm(e->n_pages);
     for (int i = 0; i < e->n_pages; ++i) perm[i] = i;
     uint64_t st = 0x5F3759DFull;
@@ -1321,8 +1445,25 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
       const int j = (int)(st % (uint64_t)(i + 1));
       std::swap(perm[i], perm[j]);
     }
-    CK(cudaMemcpy(e->page_table, perm.data(), sizeof(int) * e->n_pages, cudaMemcpyHostToDevice));
+    e->pt0 = perm;
+    if (e->win.on) {
+      sfk_engine::Window& w = e->win;
+      w.ring = perm;
+      w.cold.assign(B, 0);
+      e->pt0.assign((size_t)B * e->max_pages, 0);
+      for (int t = 0; t < B; ++t)
+        for (int j = 0; j < e->max_pages; ++j)
+          e->pt0[(size_t)t * e->max_pages + j] = w.ring[(size_t)t * w.pages + j % w.pages];
+      w.page_bytes = (int64_t)e->hkv_loc * 16 * e->hd * kv_elem;
+      const size_t stage = (size_t)B * e->max_pages * w.page_bytes;
+      TRY(e->alloc(&w.k_stage, stage, &e->kv_bytes));
+      TRY(e->alloc(&w.v_stage, stage, &e->kv_bytes));
+      CK(cudaHostAlloc(&w.k_cold, stage * hp->n_layer, cudaHostAllocDefault));
+      CK(cudaHostAlloc(&w.v_cold, stage * hp->n_layer, cudaHostAllocDefault));
+    }
+    TRY(window_table(e));
   }
+  e->step_pos.assign(B, 0);
   // step buffers
   e->attn_cluster = attn_cluster_for(e->max_pages * 16);
   e->attn_max_chunk = (e->max_pages + e->attn_cluster - 1) / e->attn_cluster * 16;  // whole pages per CTA
@@ -1428,7 +1569,8 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     const int gqa = hp->n_head / hp->n_head_kv;
     int coop = 0;
     cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device);
-    if (pv && atoi(pv) == 1 && coop && e->ep_size == 1 && !e->tier.on && E <= MEGA_MAXE && gqa <= MEGA_MAXGQA &&
+    if (pv && atoi(pv) == 1 && coop && e->ep_size == 1 && !e->tier.on && !e->win.on && E <= MEGA_MAXE &&
+        gqa <= MEGA_MAXGQA &&
         (gqa & (gqa - 1)) == 0 &&
         mega_types_supported(hp->type_attn, hp->type_ffn_gu, hp->type_ffn_down, hp->type_output)) {
       const int Hq = hp->n_head, Hkv = hp->n_head_kv;
@@ -1678,12 +1820,13 @@ sfk_status sfk_kv_reset(sfk_engine* e) {
   CK(cudaMemsetAsync(e->pos_state, 0, sizeof(int) * e->hp.max_batch, e->stream));
   CK(cudaStreamSynchronize(e->stream));
   std::fill(e->seq_pos.begin(), e->seq_pos.end(), 0);
+  if (e->win.on) return window_table(e);
   return SFK_OK;
 }
 
 static sfk_status run_step(sfk_engine* e, int b, bool greedy) {
-  if (e->tier.on) {
-    sfk_status s = run_step_tier(e, b, greedy);
+  if (e->tier.on || e->win.on) {
+    sfk_status s = run_step_direct(e, b, greedy);
     if (s) return s;
     e->steps += 1;
     e->last_b = b;
@@ -1714,6 +1857,7 @@ sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens
   const int B = e->hp.max_batch;
   memcpy(e->h_tok, tokens, sizeof(int) * n_seq);
   memcpy(e->h_pos, positions, sizeof(int) * n_seq);
+  for (int t = 0; t < n_seq; ++t) e->step_pos[t] = positions[t];
   CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * 2 * B, cudaMemcpyHostToDevice, e->stream));
   sfk_status s = run_step(e, n_seq, false);
   if (s) return s;
@@ -1890,6 +2034,11 @@ sfk_status prefill_layer(sfk_engine* e, int l, int seq, int m, int pos0) {
   const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
   const int mpad = (m + TC_TT - 1) / TC_TT * TC_TT;
   const int act_attn = act_for(hp.type_attn);
+  if (e->win.on) {  // this layer's cold pages of the sequence, for its attention
+    bool staged = false;
+    sfk_status s = window_stage(e, l, seq, seq + 1, &staged);
+    if (s) return s;
+  }
   // attn_norm -> QKV (engine.cpp:1878-1889)
   CK(launch_pf_norm(f.x, W.attn_norm, m, d, hp.rms_eps, f.xn, st));
   CK(launch_tc_quant(act_attn, f.xn, d, nullptr, m, mpad, d, f.act, st));
@@ -2058,8 +2207,17 @@ sfk_status sfk_prefill(sfk_engine* e, int32_t seq, const int32_t* tokens, int32_
   sfk_status s = prefill_alloc(e);
   if (s) return s;
   sfk_engine::Prefill& f = e->pf;
-  for (int c0 = 0; c0 < n; c0 += f.cap) {
-    const int m = std::min(f.cap, n - c0);
+  // with a KV window a chunk spans at most the window's pages, all written
+  // in HBM; the pages before them are evicted first
+  const int cap = e->win.on ? std::min(f.cap, (e->win.pages - 1) * 16) : f.cap;
+  for (int c0 = 0; c0 < n; c0 += cap) {
+    const int m = std::min(cap, n - c0);
+    if (e->win.on) {
+      if ((pos0 + c0) / 16 < e->win.cold[seq])
+        return fail(SFK_ERR_INVALID_ARGUMENT, "sequence %d: position %d lies in a page that has left the KV window",
+                    seq, pos0 + c0);
+      if ((s = window_advance(e, seq, pos0 + c0 + m - 1))) return s;
+    }
     CK(cudaMemcpyAsync(f.tok, tokens + c0, sizeof(int) * m, cudaMemcpyHostToDevice, e->stream));
     CK(launch_pf_embed(e->tok_embd, hp.type_embd, hp.n_embd, hp.n_vocab, f.tok, m, pos0 + c0, f.x, f.pos,
                        e->pos_state + seq, e->status, e->stream));
@@ -2147,6 +2305,7 @@ sfk_status sfk_generate(sfk_engine* e, const int32_t* prompt, int32_t n_prompt, 
     if (cb && cb(tok, user) != 0) break;
     if (i + 1 == limit || e->seq_pos[0] + 1 > hp.n_ctx) break;
     // one decode step on the token (device greedy-loop form: the key holds it)
+    e->step_pos[0] = e->seq_pos[0];
     if ((s = run_step(e, 1, true))) return s;
     if ((s = engine_check(e))) return s;
     e->seq_pos[0] += 1;
@@ -2163,6 +2322,7 @@ sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int3
       return fail(SFK_ERR_INVALID_ARGUMENT, "sequence %d would exceed n_ctx", t);
   CK(cudaSetDevice(e->device));
   for (int i = 0; i < n_steps; ++i) {
+    for (int t = 0; t < n_seq; ++t) e->step_pos[t] = e->seq_pos[t] + i;
     sfk_status s = run_step(e, n_seq, true);
     if (s) return s;
     if (tokens_out) {
@@ -2259,6 +2419,9 @@ sfk_status sfk_get_stats(const sfk_engine* e, sfk_stats* out) {
   out->h2d_expert_bytes = T.h2d;
   out->prefetch_warmed = T.warmed;
   out->prefetch_used = T.used;
+  out->kv_window_pages = e->win.on ? (uint64_t)e->win.pages : 0;
+  out->kv_pages_evicted = e->win.evicted;
+  out->kv_staged_bytes = e->win.staged_bytes;
   return SFK_OK;
 }
 
@@ -2266,7 +2429,8 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
   if (!e || !ms_out || n_out < K_NCLASS || iters < 1 || n_seq < 1 || n_seq > e->hp.max_batch)
     return fail(SFK_ERR_INVALID_ARGUMENT, "time_kernels arguments");
   if (e->steps == 0) return fail(SFK_ERR_INVALID_ARGUMENT, "run a decode step first");
-  if (e->tier.on) return fail(SFK_ERR_UNSUPPORTED, "per-kernel timing needs every expert resident");
+  if (e->tier.on || e->win.on)
+    return fail(SFK_ERR_UNSUPPORTED, "per-kernel timing needs every expert and the whole KV resident");
   CK(cudaSetDevice(e->device));
   cudaEvent_t a = nullptr, z = nullptr;
   CK(cudaEventCreate(&a));

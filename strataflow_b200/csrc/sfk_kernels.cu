@@ -313,7 +313,7 @@ __device__ void epi_qkv(const StreamParams& p, const float* acc, int r0, int r1)
       const int rr = r - nq - (is_k ? 0 : nk);
       const int h = rr / hd, i0 = rr % hd;
       const int page = p.kv.page_table[t * p.kv.max_pages + pos / 16];
-      if (page < 0 || (p.kv.n_pages > 0 && page >= p.kv.n_pages)) {  // never write outside the pool
+      if (!kv_page_writable(p.kv, page)) {  // never write outside the pool
         atomicExch(p.status, ERR_BAD_PAGE);
         continue;
       }
@@ -1230,7 +1230,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attn_kernel(const AttnParams p) {
       return;
     }
     mbar_arrive_expect_tx(bar, (uint32_t)pl.slot_bytes);
-    const uint8_t* src = reinterpret_cast<const uint8_t*>(isv ? p.kv.v : p.kv.k) + pg * page_stride + head_off;
+    const uint8_t* src = kv_page(p.kv, isv, pg, page_stride) + head_off;
     bulk_g2s((isv ? vring : kring) + (int64_t)slot * pl.slot_bytes, src, (uint32_t)pl.slot_bytes, bar);
   };
 

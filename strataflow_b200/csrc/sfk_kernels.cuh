@@ -54,7 +54,24 @@ struct KvView {
   int n_head_kv;
   int head_dim;
   int f16;
+  // KV window: ids from n_hot up name the cold pages staged for this layer
+  // at k2 / v2 (page id - n_hot); n_hot = 0: every id addresses k / v.
+  // Only pages below n_hot are written.
+  void* k2;
+  void* v2;
+  int n_hot;
 };
+
+// Address of page `pg` of K (v = 0) or V (v = 1), `page_bytes` apart.
+__host__ __device__ __forceinline__ const uint8_t* kv_page(const KvView& kv, int v, int pg, int64_t page_bytes) {
+  const bool cold = kv.n_hot > 0 && pg >= kv.n_hot;
+  const void* base = cold ? (v ? kv.v2 : kv.k2) : (v ? kv.v : kv.k);
+  return static_cast<const uint8_t*>(base) + (int64_t)(cold ? pg - kv.n_hot : pg) * page_bytes;
+}
+// A page id that may be written: inside the pool and not a staged cold page.
+__host__ __device__ __forceinline__ bool kv_page_writable(const KvView& kv, int pg) {
+  return pg >= 0 && (kv.n_pages <= 0 || pg < kv.n_pages) && (kv.n_hot <= 0 || pg < kv.n_hot);
+}
 
 // Shared-memory plan of the warp-tile streaming kernel (computed on the host
 // at launch; the kernel reads it from its parameters)

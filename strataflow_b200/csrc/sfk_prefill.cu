@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(256) pf_rope_kv_kernel(const float* qkv, int n
   const int rr = r - nq - (is_k ? 0 : nk);
   const int h = rr / hd, i0 = rr % hd;
   const int page = pt_row[pos / 16];
-  if (page < 0 || (kv.n_pages > 0 && page >= kv.n_pages)) {  // never write outside the pool
+  if (!kv_page_writable(kv, page)) {  // never write outside the pool
     atomicExch(status, ERR_BAD_PAGE);
     return;
   }
@@ -319,7 +319,7 @@ __device__ __forceinline__ void load_vrow(const KT* row, int tx, float (&v)[HD /
 // Stage rows kb*64 .. +63 of the kv head's K (or V) pool into `dst` (row
 // stride `stride` elements); positions past qpos_max read as zero.
 template <int HD, typename KT>
-__device__ __forceinline__ void stage_kv(KT* dst, int stride, const void* pool, const PfAttnParams& p, int kvh, int kb,
+__device__ __forceinline__ void stage_kv(KT* dst, int stride, int isv, const PfAttnParams& p, int kvh, int kb,
                                          int qpos_max) {
   constexpr int VEC = 16 / sizeof(KT);  // elements per 16 bytes
   const int Hkv = p.kv.n_head_kv;
@@ -332,8 +332,9 @@ __device__ __forceinline__ void stage_kv(KT* dst, int stride, const void* pool, 
       if (page < 0 || (p.kv.n_pages > 0 && page >= p.kv.n_pages)) {
         atomicExch(p.status, ERR_BAD_PAGE);
       } else {
-        const int64_t off = ((((int64_t)page * Hkv + kvh) * 16 + (kp & 15)) * HD + c * VEC) * (int64_t)sizeof(KT);
-        v4 = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(pool) + off));
+        const int64_t off = (((int64_t)kvh * 16 + (kp & 15)) * HD + c * VEC) * (int64_t)sizeof(KT);
+        const int64_t page_bytes = (int64_t)Hkv * 16 * HD * (int64_t)sizeof(KT);
+        v4 = __ldg(reinterpret_cast<const uint4*>(kv_page(p.kv, isv, page, page_bytes) + off));
       }
     }
     // padded rows keep 8-byte alignment: two 8-byte stores
@@ -381,7 +382,7 @@ __global__ void __launch_bounds__(256, HD >= 256 ? 1 : 2) pf_attn_kernel(const P
   float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
   for (int kb = 0; kb < nkb; ++kb) {
     __syncthreads();  // the previous block's K is consumed
-    stage_kv<HD>(KVs, KS, p.kv.k, p, kvh, kb, qpos_max);
+    stage_kv<HD>(KVs, KS, 0, p, kvh, kb, qpos_max);
     __syncthreads();
     double s[4][4];
 #pragma unroll
@@ -445,7 +446,7 @@ __global__ void __launch_bounds__(256, HD >= 256 ? 1 : 2) pf_attn_kernel(const P
     for (int i = 0; i < CPT; ++i) o[a][i] = 0.0;
   for (int kb = 0; kb < nkb; ++kb) {
     __syncthreads();  // the previous block's V and P are consumed
-    stage_kv<HD>(KVs, HD, p.kv.v, p, kvh, kb, qpos_max);
+    stage_kv<HD>(KVs, HD, 1, p, kvh, kb, qpos_max);
 #pragma unroll
     for (int a = 0; a < 4; ++a)
 #pragma unroll
@@ -562,6 +563,13 @@ cudaError_t launch_pf_attn(const float* q, const KvView& kv, const int* pt_row, 
     case 513: return launch_pf_attn_t<256, 1>(p, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+__global__ void pt_set_kernel(int* pt, int idx, int id) { pt[idx] = id; }
+
+cudaError_t launch_pt_set(int* page_table, int idx, int id, cudaStream_t st) {
+  pt_set_kernel<<<1, 1, 0, st>>>(page_table, idx, id);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_pf_pt(const int* pt_row, int max_pages, int n, int* pt_out, cudaStream_t st) {

@@ -30,6 +30,9 @@ cudaError_t launch_pf_attn(const float* q, const KvView& kv, const int* pt_row, 
 // pt_out[t][:] = pt_row[:] for t < n (every prompt token reads the
 // sequence's pages).
 cudaError_t launch_pf_pt(const int* pt_row, int max_pages, int n, int* pt_out, cudaStream_t st);
+// page_table[idx] = id, in stream order (the id travels as a kernel argument,
+// so the host may enqueue later changes without waiting for this one)
+cudaError_t launch_pt_set(int* page_table, int idx, int id, cudaStream_t st);
 // ffn_norm + router + softmax + top-k of n tokens: ids / w [n][k], xn [n][d]
 // (the normed rows); xq_scratch [n][qact_bytes(d)] is written and unused.
 cudaError_t launch_pf_route(const float* x, const float* norm_w, const float* w_r, int n, int d, int E, int k,

@@ -47,6 +47,7 @@ class ModelConfig:
     ep_rank: int = 0
     head_dim: int = 0  # 0: n_embd / n_head
     expert_slots: int = 0  # HBM expert slots; 0: every expert resident (Engine::load's expert_slots)
+    kv_window: int = 0     # resident KV tokens per sequence; 0: the whole context (Engine::load's kv_window)
 
     @property
     def hd(self) -> int:

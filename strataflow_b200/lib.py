@@ -33,7 +33,7 @@ class Hparams(C.Structure):
         "n_embd", "n_head", "n_head_kv", "n_layer", "n_ff", "n_expert", "n_expert_used", "n_vocab", "n_ctx")] + [
         ("rms_eps", C.c_float), ("freq_base", C.c_float)] + [(n, C.c_int32) for n in (
             "type_embd", "type_attn", "type_ffn_gu", "type_ffn_down", "type_output", "kv_type", "max_batch",
-            "ep_size", "ep_rank", "head_dim", "expert_slots")]
+            "ep_size", "ep_rank", "head_dim", "expert_slots", "kv_window")]
 
 
 EP_HANDLE_BYTES = 64  # SFK_EP_HANDLE_BYTES
@@ -43,7 +43,7 @@ class Stats(C.Structure):
     _fields_ = [(n, C.c_uint64) for n in (
         "weight_bytes_hbm", "kv_bytes_hbm", "scratch_bytes_hbm", "steps", "kernels_per_step",
         "active_bytes_per_token", "pool_slots", "pool_hits", "pool_misses", "pool_evictions", "h2d_expert_bytes",
-        "prefetch_warmed", "prefetch_used")]
+        "prefetch_warmed", "prefetch_used", "kv_window_pages", "kv_pages_evicted", "kv_staged_bytes")]
 
 
 class Sampling(C.Structure):
