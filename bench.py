@@ -583,7 +583,8 @@ def run_tier(args):
     torch.cuda.set_device(0)
     B = args.batch
     n_ctx = args.prompt + args.warmup + args.steps + 16
-    cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B, n_layer=args.layers, expert_slots=args.expert_slots)
+    cfg = E.mixtral_config(n_ctx=n_ctx, max_batch=B, n_layer=args.layers, expert_slots=args.expert_slots,
+                           kv_window=args.kv_window)
     t_load = time.perf_counter()
     eng = E.Engine.load(cfg, seed=SEED)
     t_load = time.perf_counter() - t_load
@@ -607,8 +608,8 @@ def run_tier(args):
     ms = ev0.elapsed_time(ev1)
     s1 = eng.stats()
     d = {k: s1[k] - s0[k] for k in ("pool_hits", "pool_misses", "pool_evictions", "h2d_expert_bytes",
-                                    "prefetch_warmed", "prefetch_used")}
-    h2d_gbs = d["h2d_expert_bytes"] / (ms / 1e3) / 1e9
+                                    "prefetch_warmed", "prefetch_used", "kv_pages_evicted", "kv_staged_bytes")}
+    h2d_gbs = (d["h2d_expert_bytes"] + d["kv_staged_bytes"]) / (ms / 1e3) / 1e9
     eng.close()
     # the pinned host-to-device copy rate of this box (1 GiB, 5 copies)
     host = torch.empty(1 << 30, dtype=torch.uint8).pin_memory()
@@ -628,19 +629,23 @@ def run_tier(args):
         "metric": METRIC, "value": B * args.steps / (ms / 1e3), "unit": "tok/s", "n_gpus": 1, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "q4_k/q6_k weights x q8_k int8 dot (dp4a), fp32 accum", "data": "synthetic",
-        "config": {"workload": f"Mixtral-8x7B-shape decode b={B} with a bounded expert tier: "
-                               f"{args.expert_slots} of {cfg.n_layer * 8} expert bundles in HBM",
+        "config": {"workload": f"Mixtral-8x7B-shape decode b={B}, {args.prompt}-token prompt"
+                               + (f", bounded expert tier: {args.expert_slots} of {cfg.n_layer * 8} expert bundles "
+                                  "in HBM" if args.expert_slots else "")
+                               + (f", KV window of {args.kv_window} tokens" if args.kv_window else ""),
                    "model": "mixtral-8x7b-shape (32L d4096 32q/8kv E8 top2 F14336 V32000)",
                    "global_batch": B, "seq_len": args.prompt, "expert_slots": args.expert_slots,
                    "pool": "global LRU" if os.environ.get("SFK_POOL_GLOBAL_LRU") == "1" else "layer-stratified LRU",
                    "prefetch": {"0": "off", "2": "evicting warm"}.get(os.environ.get("SFK_PREFETCH", "1"),
                                                                        "into free slots")},
         "clocks": clk.summary(),
-        "tier": {"bundle_bytes": bundle, "hits": d["pool_hits"], "misses": d["pool_misses"],
+        "tier": None if not args.expert_slots else {"bundle_bytes": bundle, "hits": d["pool_hits"], "misses": d["pool_misses"],
                  "evictions": d["pool_evictions"], "hit_rate": d["pool_hits"] / max(1, d["pool_hits"] + d["pool_misses"]),
                  "misses_per_token": d["pool_misses"] / (B * args.steps), "prefetch_warmed": d["prefetch_warmed"],
                  "prefetch_used": d["prefetch_used"], "h2d_gbs": h2d_gbs, "pinned_h2d_peak_gbs": pin_gbs,
                  "h2d_frac": h2d_gbs / pin_gbs},
+        "kv_window": {"tokens": args.kv_window, "pages_evicted": d["kv_pages_evicted"],
+                      "staged_bytes_per_token": d["kv_staged_bytes"] / (B * args.steps)} if args.kv_window else None,
         "load_s": t_load, "prefill_s": t_pf,
     }
     print(json.dumps(line), flush=True)
@@ -667,6 +672,8 @@ def main():
                     help="tensor-core GEMM sweep (n = 16..512 rows) and the batched 512-token prefill")
     ap.add_argument("--expert-slots", type=int, default=0,
                     help="decode with a bounded expert tier of this many HBM bundle slots (one GPU)")
+    ap.add_argument("--kv-window", type=int, default=0,
+                    help="decode with a KV window of this many resident tokens per sequence (one GPU)")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -680,7 +687,7 @@ def main():
     if args.sweep_tc:
         run_sweep_tc(args)
         return
-    if args.expert_slots > 0:
+    if args.expert_slots > 0 or args.kv_window > 0:
         run_tier(args)
         return
     if args.model == "1t":

@@ -250,7 +250,9 @@ struct sfk_engine {
     bool on = false;
     int pages = 0;                              // ring pages per sequence
     int64_t page_bytes = 0;                     // one page of K (or V) of one layer
-    void *k_stage = nullptr, *v_stage = nullptr;  // [max_batch][max_pages] pages
+    void *k_stage[2] = {}, *v_stage[2] = {};     // [max_batch][max_pages] pages; layer l uses l & 1
+    cudaStream_t copy = nullptr;                 // decode steps stage cold pages here, a layer ahead
+    cudaEvent_t start = nullptr, staged[2] = {}, used[2] = {};
     uint8_t *k_cold = nullptr, *v_cold = nullptr; // pinned [n_layer][max_batch][max_pages] pages
     std::vector<int> cold;                      // per sequence: logical pages 0 .. cold-1 are cold
     std::vector<int> ring;                      // [max_batch][pages] HBM page of each ring slot
@@ -476,8 +478,8 @@ KvView kv_view(const sfk_engine* e, int l) {
   if (e->win.on) {  // ids from n_pages up: the staged cold pages (page_table: n_pages + seq * max_pages + page)
     kv.n_hot = e->n_pages;
     kv.n_pages = e->n_pages + hp.max_batch * e->max_pages;
-    kv.k2 = e->win.k_stage;
-    kv.v2 = e->win.v_stage;
+    kv.k2 = e->win.k_stage[l & 1];
+    kv.v2 = e->win.v_stage[l & 1];
   }
   return kv;
 }
@@ -1181,9 +1183,9 @@ sfk_status window_advance(sfk_engine* e, int t, int pos) {
   return SFK_OK;
 }
 
-// Layer l's cold pages of sequences [t0, t1) into the staging pages (ids
-// n_pages + t * max_pages + j); *copied tells whether any were.
-sfk_status window_stage(sfk_engine* e, int l, int t0, int t1, bool* copied) {
+// Layer l's cold pages of sequences [t0, t1) into staging buffer l & 1 (ids
+// n_pages + t * max_pages + j), on stream `st`; *copied tells whether any were.
+sfk_status window_stage(sfk_engine* e, int l, int t0, int t1, cudaStream_t st, bool* copied) {
   sfk_engine::Window& w = e->win;
   *copied = false;
   const int B = e->hp.max_batch, MP = e->max_pages;
@@ -1192,12 +1194,25 @@ sfk_status window_stage(sfk_engine* e, int l, int t0, int t1, bool* copied) {
     if (c == 0) continue;
     for (int v = 0; v < 2; ++v) {
       const uint8_t* src = (v ? w.v_cold : w.k_cold) + ((size_t)l * B + t) * MP * w.page_bytes;
-      uint8_t* dst = static_cast<uint8_t*>(v ? w.v_stage : w.k_stage) + (size_t)t * MP * w.page_bytes;
-      CK(cudaMemcpyAsync(dst, src, (size_t)c * w.page_bytes, cudaMemcpyHostToDevice, e->stream));
+      uint8_t* dst = static_cast<uint8_t*>(v ? w.v_stage[l & 1] : w.k_stage[l & 1]) + (size_t)t * MP * w.page_bytes;
+      CK(cudaMemcpyAsync(dst, src, (size_t)c * w.page_bytes, cudaMemcpyHostToDevice, st));
     }
     w.staged_bytes += 2ull * c * w.page_bytes;
     *copied = true;
   }
+  return SFK_OK;
+}
+
+// Decode steps stage on the window's copy stream, a layer ahead: layer l's
+// copies go into buffer l & 1 once layer l - 2's attention has read it, and
+// layer l's attention waits for them.  The first two layers' copies wait
+// for everything queued before the step (evictions included).
+sfk_status window_stage_async(sfk_engine* e, int l, int b, bool* copied) {
+  sfk_engine::Window& w = e->win;
+  CK(cudaStreamWaitEvent(w.copy, l < 2 ? w.start : w.used[l & 1], 0));
+  sfk_status s = window_stage(e, l, 0, b, w.copy, copied);
+  if (s) return s;
+  if (*copied) CK(cudaEventRecord(w.staged[l & 1], w.copy));
   return SFK_OK;
 }
 
@@ -1217,14 +1232,25 @@ sfk_status run_step_direct(sfk_engine* e, int b, bool greedy) {
     if (T.sp->stratified() && T.tokens % 4 == 0) T.sp->set_layer_weights(T.pred->layer_activity());
     T.warmed_now.clear();
   }
-  s = launch_one(e, K_EMBED, 0, b, greedy, false);
+  const int L = e->hp.n_layer;
+  bool staged[2] = {false, false};
+  if (e->win.on) {
+    if (!s) s = cudaEventRecord(e->win.start, e->stream) == cudaSuccess ? SFK_OK : fail(SFK_ERR_RUNTIME, "event");
+    for (int l = 0; l < std::min(2, L) && !s; ++l) s = window_stage_async(e, l, b, &staged[l]);
+  }
+  if (!s) s = launch_one(e, K_EMBED, 0, b, greedy, false);
   int nk = 1;
-  for (int l = 0; l < e->hp.n_layer && !s; ++l) {
-    bool staged = false;
-    if (e->win.on) s = window_stage(e, l, 0, b, &staged);
-    // (a kernel that follows a copy is a plain launch)
-    if (!s) s = launch_one(e, K_QKV, l, b, greedy, !staged);
-    if (!s) s = launch_one(e, K_ATTN, l, b, greedy, true);
+  for (int l = 0; l < L && !s; ++l) {
+    s = launch_one(e, K_QKV, l, b, greedy, true);
+    const bool wait = e->win.on && staged[l & 1];
+    if (!s && wait && cudaStreamWaitEvent(e->stream, e->win.staged[l & 1], 0) != cudaSuccess)
+      s = fail(SFK_ERR_RUNTIME, "stream wait");
+    // (a kernel that follows an event wait is a plain launch)
+    if (!s) s = launch_one(e, K_ATTN, l, b, greedy, !wait);
+    if (!s && e->win.on && l + 2 < L) {
+      if (cudaEventRecord(e->win.used[l & 1], e->stream) != cudaSuccess) s = fail(SFK_ERR_RUNTIME, "event");
+      if (!s) s = window_stage_async(e, l + 2, b, &staged[l & 1]);
+    }
     if (!s) s = launch_one(e, K_OPROJ, l, b, greedy, true);
     nk += 3;
     if (!e->fused_route) {
@@ -1240,6 +1266,7 @@ sfk_status run_step_direct(sfk_engine* e, int b, bool greedy) {
   if (!s) s = launch_one(e, K_LMHEAD, 0, b, greedy, true);
   if (s) {
     cudaStreamSynchronize(e->stream);
+    if (e->win.on) cudaStreamSynchronize(e->win.copy);
     if (T.on) {
       cudaStreamSynchronize(T.copy);
       T.sp->unpin_all();
@@ -1310,12 +1337,16 @@ void sfk_engine_free(sfk_engine* e) {
   for (auto& kv : e->graphs) cudaGraphExecDestroy(kv.second);
   for (void* p : e->ep_opened) cudaIpcCloseMemHandle(p);
   if (e->tier.copy) cudaStreamSynchronize(e->tier.copy);
+  if (e->win.copy) cudaStreamSynchronize(e->win.copy);
   for (void* p : e->allocs) cudaFree(p);
   for (void* p : {(void*)e->tier.host, (void*)e->tier.h_map, (void*)e->tier.h_route, (void*)e->tier.h_tile,
                   (void*)e->tier.h_ids, (void*)e->win.k_cold, (void*)e->win.v_cold})
     if (p) cudaFreeHost(p);
   if (e->tier.copied) cudaEventDestroy(e->tier.copied);
   if (e->tier.copy) cudaStreamDestroy(e->tier.copy);
+  for (cudaEvent_t ev : {e->win.start, e->win.staged[0], e->win.staged[1], e->win.used[0], e->win.used[1]})
+    if (ev) cudaEventDestroy(ev);
+  if (e->win.copy) cudaStreamDestroy(e->win.copy);
   if (e->h_tok) cudaFreeHost(e->h_tok);
   if (e->h_hist) cudaFreeHost(e->h_hist);
   if (e->h_keys) cudaFreeHost(e->h_keys);
@@ -1456,10 +1487,18 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
           e->pt0[(size_t)t * e->max_pages + j] = w.ring[(size_t)t * w.pages + j % w.pages];
       w.page_bytes = (int64_t)e->hkv_loc * 16 * e->hd * kv_elem;
       const size_t stage = (size_t)B * e->max_pages * w.page_bytes;
-      TRY(e->alloc(&w.k_stage, stage, &e->kv_bytes));
-      TRY(e->alloc(&w.v_stage, stage, &e->kv_bytes));
+      for (int i = 0; i < 2; ++i) {
+        TRY(e->alloc(&w.k_stage[i], stage, &e->kv_bytes));
+        TRY(e->alloc(&w.v_stage[i], stage, &e->kv_bytes));
+      }
       CK(cudaHostAlloc(&w.k_cold, stage * hp->n_layer, cudaHostAllocDefault));
       CK(cudaHostAlloc(&w.v_cold, stage * hp->n_layer, cudaHostAllocDefault));
+      CK(cudaStreamCreateWithFlags(&w.copy, cudaStreamNonBlocking));
+      CK(cudaEventCreateWithFlags(&w.start, cudaEventDisableTiming));
+      for (int i = 0; i < 2; ++i) {
+        CK(cudaEventCreateWithFlags(&w.staged[i], cudaEventDisableTiming));
+        CK(cudaEventCreateWithFlags(&w.used[i], cudaEventDisableTiming));
+      }
     }
     TRY(window_table(e));
   }
@@ -2034,9 +2073,9 @@ sfk_status prefill_layer(sfk_engine* e, int l, int seq, int m, int pos0) {
   const int d = hp.n_embd, F = hp.n_ff, E = hp.n_expert, k = hp.n_expert_used;
   const int mpad = (m + TC_TT - 1) / TC_TT * TC_TT;
   const int act_attn = act_for(hp.type_attn);
-  if (e->win.on) {  // this layer's cold pages of the sequence, for its attention
+  if (e->win.on) {  // this layer's cold pages of the sequence, for its attention (in stream order)
     bool staged = false;
-    sfk_status s = window_stage(e, l, seq, seq + 1, &staged);
+    sfk_status s = window_stage(e, l, seq, seq + 1, st, &staged);
     if (s) return s;
   }
   // attn_norm -> QKV (engine.cpp:1878-1889)

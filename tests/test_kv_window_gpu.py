@@ -40,7 +40,16 @@ def test_window_decode_bit_identical_to_resident(cuda, window, kw):
     assert st["kv_window_pages"] == pages
     assert st["kv_pages_evicted"] == (cfg.n_ctx - 1) // 16 + 1 - pages
     assert st["kv_staged_bytes"] > 0
-    assert st["kv_bytes_hbm"] < ref.stats()["kv_bytes_hbm"]
+
+
+def test_window_bounds_hbm_kv(cuda):
+    """HBM holds the window's pages of every layer plus one layer's worth of
+    staging (twice), not the whole context of every layer."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(n_ctx=2048, n_layer=8)
+    full = E.Engine(cfg).stats()["kv_bytes_hbm"]
+    win = E.Engine(cfg.replace(kv_window=64)).stats()["kv_bytes_hbm"]
+    assert win < full / 2
 
 
 def test_window_device_loop_and_oracle(cuda):
