@@ -267,6 +267,33 @@ SFK_API sfk_status sfk_generate(sfk_engine *eng, const int32_t *prompt, int32_t 
 SFK_API sfk_status sfk_sample_logits(const float *dev_logits, int32_t n_vocab, const sfk_sampling *sampling,
                                      int32_t step, int32_t *token_out, void *stream);
 
+/* ---- per-layer entry points: the reference's segment structure ---------
+ * For a host engine that keeps its own layer loop (engine.cpp:2498-3025 runs
+ * an attention segment and an expert segment per layer, engine.cpp:
+ * 1854-1989).  n_tok sequences 0 .. n_tok-1 of the engine, one token each;
+ * `hidden` is a DEVICE buffer [n_tok][n_embd] f32 read and written in place;
+ * `positions` are host [n_tok].  Each call runs on the engine's stream and
+ * returns after its kernels finished (their device status checked).  The
+ * chain embed -> L x (attn, moe) -> lm_head computes exactly what
+ * sfk_forward_batch computes.  Single-GPU engines (ep_size <= 1). */
+/* token_embd rows of `tokens` (host [n_tok]) into hidden (engine.cpp:2708-2723) */
+SFK_API sfk_status sfk_embed(sfk_engine *eng, const int32_t *tokens, const int32_t *positions, int32_t n_tok,
+                             float *dev_hidden);
+/* attn_norm -> Q/K/V -> RoPE -> KV append at `positions` -> GQA attention ->
+ * O-projection + residual (engine.cpp:1878-1906) */
+SFK_API sfk_status sfk_decode_layer_attn(sfk_engine *eng, int32_t layer, const int32_t *positions, int32_t n_tok,
+                                         float *dev_hidden);
+/* ffn_norm -> router softmax / top-k -> routed gate/up + SwiGLU -> routed down
+ * -> weighted combine + residual (engine.cpp:1909-1986).  dev_ids_out /
+ * dev_w_out (optional, DEVICE [n_tok][n_expert_used]) receive the routing. */
+SFK_API sfk_status sfk_decode_layer_moe(sfk_engine *eng, int32_t layer, int32_t n_tok, float *dev_hidden,
+                                        int32_t *dev_ids_out, float *dev_w_out);
+/* output_norm -> lm_head -> argmax (engine.cpp:2988-3006): dev_logits_out
+ * (optional, DEVICE [n_tok][n_vocab]) and argmax_out (optional, host
+ * [n_tok]). */
+SFK_API sfk_status sfk_lm_head(sfk_engine *eng, const float *dev_hidden, int32_t n_tok, float *dev_logits_out,
+                               int32_t *argmax_out);
+
 /* Routing of the last layer of the last step: ids [n_seq][k] and weights
  * [n_seq][k] (host) -- the router segment's read-back (engine.cpp:2823-2833). */
 SFK_API sfk_status sfk_route_get(sfk_engine *eng, int32_t *ids_out, float *w_out, size_t n);

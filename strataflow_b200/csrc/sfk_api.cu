@@ -14,6 +14,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstddef>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -2403,6 +2404,117 @@ sfk_status sfk_debug_get(sfk_engine* e, int32_t which, float* host_out, size_t n
   CK(cudaSetDevice(e->device));
   CK(cudaMemcpyAsync(host_out, src, n * sizeof(float), cudaMemcpyDeviceToHost, e->stream));
   CK(cudaStreamSynchronize(e->stream));
+  return SFK_OK;
+}
+
+// ---- per-layer entry points ---------------------------------------------------
+static sfk_status layer_call_check(sfk_engine* e, int32_t n_tok, const void* hidden) {
+  if (!e || !hidden) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  if (n_tok < 1 || n_tok > e->hp.max_batch) return fail(SFK_ERR_INVALID_ARGUMENT, "n_tok %d", n_tok);
+  if (e->ep_size > 1) return fail(SFK_ERR_UNSUPPORTED, "per-layer calls run on single-GPU engines");
+  CK(cudaSetDevice(e->device));
+  return SFK_OK;
+}
+
+// tokens / positions into the step's device inputs (and the host mirror the
+// KV window reads)
+static sfk_status layer_positions(sfk_engine* e, const int32_t* positions, int32_t n_tok) {
+  for (int t = 0; t < n_tok; ++t)
+    if (positions[t] < 0 || positions[t] >= e->hp.n_ctx)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "position %d outside [0, n_ctx=%d)", positions[t], e->hp.n_ctx);
+  memcpy(e->h_pos, positions, sizeof(int) * n_tok);
+  for (int t = 0; t < n_tok; ++t) e->step_pos[t] = positions[t];
+  return SFK_OK;
+}
+
+sfk_status sfk_embed(sfk_engine* e, const int32_t* tokens, const int32_t* positions, int32_t n_tok, float* hidden) {
+  sfk_status s = layer_call_check(e, n_tok, hidden);
+  if (s) return s;
+  if (!tokens || !positions) return fail(SFK_ERR_INVALID_ARGUMENT, "null argument");
+  for (int t = 0; t < n_tok; ++t)
+    if (tokens[t] < 0 || tokens[t] >= e->hp.n_vocab)
+      return fail(SFK_ERR_INVALID_ARGUMENT, "token %d outside the vocabulary", tokens[t]);
+  if ((s = layer_positions(e, positions, n_tok))) return s;
+  memcpy(e->h_tok, tokens, sizeof(int) * n_tok);
+  const int B = e->hp.max_batch;
+  CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * 2 * B, cudaMemcpyHostToDevice, e->stream));
+  if ((s = launch_one(e, K_EMBED, 0, n_tok, false, false))) return s;
+  CK(cudaMemcpyAsync(hidden, e->x, sizeof(float) * n_tok * e->hp.n_embd, cudaMemcpyDeviceToDevice, e->stream));
+  return engine_check(e);
+}
+
+sfk_status sfk_decode_layer_attn(sfk_engine* e, int32_t layer, const int32_t* positions, int32_t n_tok,
+                                 float* hidden) {
+  sfk_status s = layer_call_check(e, n_tok, hidden);
+  if (s) return s;
+  if (!positions || layer < 0 || layer >= e->hp.n_layer) return fail(SFK_ERR_INVALID_ARGUMENT, "layer %d", layer);
+  if ((s = layer_positions(e, positions, n_tok))) return s;
+  const int B = e->hp.max_batch, d = e->hp.n_embd;
+  // positions as the embedding kernel leaves them (pos_cur), then the layer
+  CK(cudaMemcpyAsync(e->pos_in, e->h_pos, sizeof(int) * B, cudaMemcpyHostToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->pos_cur, e->pos_in, sizeof(int) * n_tok, cudaMemcpyDeviceToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->x, hidden, sizeof(float) * n_tok * d, cudaMemcpyDeviceToDevice, e->stream));
+  if (e->win.on) {
+    for (int t = 0; t < n_tok && !s; ++t) s = window_advance(e, t, positions[t]);
+    bool staged = false;
+    if (!s) s = window_stage(e, layer, 0, n_tok, e->stream, &staged);
+    if (s) return s;
+  }
+  for (int c = K_QKV; c <= K_OPROJ && !s; ++c) s = launch_one(e, c, layer, n_tok, false, c != K_QKV);
+  if (s) return s;
+  CK(cudaMemcpyAsync(hidden, e->ffn_inp, sizeof(float) * n_tok * d, cudaMemcpyDeviceToDevice, e->stream));
+  if ((s = engine_check(e))) return s;
+  for (int t = 0; t < n_tok; ++t) e->seq_pos[t] = std::max(e->seq_pos[t], positions[t] + 1);
+  e->last_b = n_tok;
+  return SFK_OK;
+}
+
+sfk_status sfk_decode_layer_moe(sfk_engine* e, int32_t layer, int32_t n_tok, float* hidden, int32_t* ids_out,
+                                float* w_out) {
+  sfk_status s = layer_call_check(e, n_tok, hidden);
+  if (s) return s;
+  if (layer < 0 || layer >= e->hp.n_layer) return fail(SFK_ERR_INVALID_ARGUMENT, "layer %d", layer);
+  const int d = e->hp.n_embd, k = e->hp.n_expert_used;
+  CK(cudaMemcpyAsync(e->ffn_inp, hidden, sizeof(float) * n_tok * d, cudaMemcpyDeviceToDevice, e->stream));
+  if (!e->fused_route) s = launch_one(e, K_ROUTER, layer, n_tok, false, false);
+  if (!s && e->tier.on) {
+    e->tier.warmed_now.clear();
+    s = tier_route_layer(e, layer, n_tok);
+  }
+  if (!s) s = launch_one(e, K_GATEUP, layer, n_tok, false, false);
+  if (!s) s = launch_one(e, K_DOWN, layer, n_tok, false, true);
+  if (!s && e->tier.on) s = tier_prefetch(e, layer + 1);
+  if (s) return s;
+  CK(cudaMemcpyAsync(hidden, e->x, sizeof(float) * n_tok * d, cudaMemcpyDeviceToDevice, e->stream));
+  if (ids_out)
+    CK(cudaMemcpyAsync(ids_out, reinterpret_cast<const uint8_t*>(e->route) + offsetof(Route, ids),
+                       sizeof(int) * n_tok * k, cudaMemcpyDeviceToDevice, e->stream));
+  if (w_out)
+    CK(cudaMemcpyAsync(w_out, reinterpret_cast<const uint8_t*>(e->route) + offsetof(Route, w),
+                       sizeof(float) * n_tok * k, cudaMemcpyDeviceToDevice, e->stream));
+  e->last_b = n_tok;
+  return engine_check(e);
+}
+
+sfk_status sfk_lm_head(sfk_engine* e, const float* hidden, int32_t n_tok, float* logits_out, int32_t* argmax_out) {
+  sfk_status s = layer_call_check(e, n_tok, hidden);
+  if (s) return s;
+  const int B = e->hp.max_batch, V = e->hp.n_vocab;
+  CK(cudaMemcpyAsync(e->x, hidden, sizeof(float) * n_tok * e->hp.n_embd, cudaMemcpyDeviceToDevice, e->stream));
+  CK(cudaMemsetAsync(e->argmax_key, 0, sizeof(unsigned long long) * n_tok, e->stream));
+  if ((s = launch_one(e, K_LMHEAD, 0, n_tok, false, false))) return s;
+  if (logits_out)
+    CK(cudaMemcpyAsync(logits_out, e->logits, sizeof(float) * n_tok * V, cudaMemcpyDeviceToDevice, e->stream));
+  CK(cudaMemcpyAsync(e->h_keys, e->argmax_key, sizeof(unsigned long long) * B + sizeof(int), cudaMemcpyDeviceToHost,
+                     e->stream));
+  CK(cudaStreamSynchronize(e->stream));
+  if ((s = status_result(e->status, *e->h_status))) {
+    reset_counters(e);
+    return s;
+  }
+  if (argmax_out)
+    for (int t = 0; t < n_tok; ++t)
+      argmax_out[t] = (int32_t)(0xFFFFFFFFu - (uint32_t)(e->h_keys[t] & 0xFFFFFFFFull));
   return SFK_OK;
 }
 

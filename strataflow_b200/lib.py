@@ -102,6 +102,10 @@ _SIGS = {
     "sfk_strata_bundle_bytes": (SZ, [P, I32]),
     "sfk_strata_read_bundle": (I32, [P, I32, I32, P, SZ]),
     "sfk_strata_load": (I32, [P, P]),
+    "sfk_embed": (I32, [P, P, P, I32, P]),
+    "sfk_decode_layer_attn": (I32, [P, I32, P, I32, P]),
+    "sfk_decode_layer_moe": (I32, [P, I32, I32, P, P, P]),
+    "sfk_lm_head": (I32, [P, P, I32, P, P]),
     "sfk_pool_create": (I32, [U32, U32, U32, U32, C.POINTER(P)]),
     "sfk_pool_free": (None, [P]),
     "sfk_pool_acquire": (I64, [P, U32, U32, C.POINTER(I32)]),
