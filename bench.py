@@ -335,8 +335,10 @@ def ep_rank_bytes(cfg, world: int, B: int) -> tuple[float, bool]:
     split over the ranks.  The heads split, as the engine decides at
     creation, when both head counts divide by the ranks and a rank's query
     columns are whole 256-column blocks (SFK_HEAD_PARALLEL=0 keeps them
-    replicated); the router (F32), the norms and the lm_head stay replicated,
-    and each rank streams its share of the expected routed experts."""
+    replicated); the router (F32) and the norms stay replicated, the device
+    greedy loop scores each rank's slice of the vocabulary (SFK_VOCAB_SHARD=0
+    keeps the lm_head whole), and each rank streams its share of the expected
+    routed experts."""
     d, F, k = cfg.n_embd, cfg.n_ff, cfg.n_expert_used
     hd = cfg.head_dim if cfg.head_dim > 0 else cfg.n_embd // cfg.n_head   # as sfk_engine_create decides it
     q8 = lambda K: K // 32 * 34   # noqa: E731
@@ -345,7 +347,8 @@ def ep_rank_bytes(cfg, world: int, B: int) -> tuple[float, bool]:
              (cfg.n_head // world * hd) % 256 == 0 and os.environ.get("SFK_HEAD_PARALLEL", "1") != "0")
     share = world if split else 1
     attn = ((cfg.n_head + 2 * cfg.n_head_kv) * hd * q8(d) + d * q8(cfg.n_head * hd)) / share
-    trunk = cfg.n_layer * (attn + 4 * d * cfg.n_expert) + cfg.n_vocab * q8(d)
+    vshare = world if world > 1 and os.environ.get("SFK_VOCAB_SHARD", "1") != "0" else 1
+    trunk = cfg.n_layer * (attn + 4 * d * cfg.n_expert) + -(-cfg.n_vocab // vshare) * q8(d)
     experts_rank = cfg.n_layer * B * k / world * (2 * F * q4(d) + d * q4(F))   # expected routed bytes per rank
     return trunk + experts_rank, split
 

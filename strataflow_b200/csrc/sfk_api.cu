@@ -283,6 +283,16 @@ struct sfk_engine {
   unsigned* ep_step = nullptr;
   const float* ep_parts[MAXR] = {};
   unsigned* ep_peer_flags[MAXR] = {};
+  // vocabulary-sharded lm_head (expert parallelism, steps that return no
+  // logits): this rank scores rows [v0, v0 + v_loc) and the argmax keys are
+  // exchanged (ep_argmax_kernel) through the tail of ep_buf
+  bool head_shard = false;  // the engine may shard the head
+  bool shard_now = false;   // the step being captured / launched does
+  int v0 = 0, v_loc = 0;
+  unsigned* ep_head_flags = nullptr;
+  unsigned long long* ep_keys = nullptr;
+  unsigned* ep_peer_head_flags[MAXR] = {};
+  const unsigned long long* ep_peer_keys[MAXR] = {};
   std::vector<void*> ep_opened;  // peer buffers opened through IPC
   bool ep_connected = false;
   int attn_cluster = 8;
@@ -726,9 +736,31 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.y_stride = hp.n_vocab;
       p.argmax_key = e->argmax_key;
       p.store_logits = 1;
+      if (e->shard_now) {  // this rank's vocabulary slice; the keys carry global row ids
+        p.w0 = e->output + (int64_t)e->v0 * p.rowstride;
+        p.rows = e->v_loc;
+        p.y = e->logits + e->v0;
+        p.argmax_base = e->v0;
+      }
       p.status = e->status;
       if ((s = plan_stream(p, e->sm_count, &grid))) return s;
       CK(launch_stream(p, grid, st, pdl));
+      if (e->shard_now) {  // the first maximum over every rank's slice
+        EpHeadParams h{};
+        h.key = e->argmax_key;
+        h.own_keys = e->ep_keys;
+        for (int r = 0; r < e->ep_size; ++r) {
+          h.peer_keys[r] = e->ep_peer_keys[r];
+          h.peer_flags[r] = e->ep_peer_head_flags[r];
+        }
+        h.flags = e->ep_head_flags;
+        h.n_ranks = e->ep_size;
+        h.rank = e->ep_rank;
+        h.b = b;
+        h.ep_step = e->ep_step;
+        h.status = e->status;
+        CK(launch_ep_argmax(h, st, true));
+      }
       return SFK_OK;
     }
     default: return fail(SFK_ERR_INVALID_ARGUMENT, "kernel class %d", c);
@@ -949,7 +981,7 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
     }
   }
   if ((s = launch_one(e, K_LMHEAD, 0, b, greedy, true))) return s;
-  ++nk;
+  nk += e->shard_now ? 2 : 1;  // (+ the argmax exchange)
   e->kernels_per_step = nk;
   return SFK_OK;
 }
@@ -957,7 +989,7 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
 sfk_status get_graph(sfk_engine* e, int b, bool greedy, cudaGraphExec_t* out) {
   if (e->ep_size > 1 && !e->ep_connected)
     return fail(SFK_ERR_INVALID_ARGUMENT, "expert-parallel engine: call sfk_ep_connect before decoding");
-  const int key = b * 2 + (greedy ? 1 : 0);
+  const int key = (b * 2 + (greedy ? 1 : 0)) * 2 + (e->shard_now ? 1 : 0);
   auto it = e->graphs.find(key);
   if (it != e->graphs.end()) {
     *out = it->second;
@@ -1556,11 +1588,25 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
   if (e->ep_size > 1) {
     // exchange buffer: [layer parity][stage][B][d] partial outputs, then MAXR
     // flag words; its own allocation so that its IPC handle exposes nothing else
+    // tail: flag words [MAXR] at +0, head flag words [MAXR] at +128, argmax keys [MAXB] at +256
     const size_t part = sizeof(float) * 4 * (size_t)B * d;
-    TRY(e->alloc(&e->ep_buf, part + 256, sb));
-    e->ep_flags = reinterpret_cast<unsigned*>(reinterpret_cast<uint8_t*>(e->ep_buf) + part);
+    const size_t tail = 256 + sizeof(unsigned long long) * MAXB;
+    TRY(e->alloc(&e->ep_buf, part + tail, sb));
+    uint8_t* tb = reinterpret_cast<uint8_t*>(e->ep_buf) + part;
+    e->ep_flags = reinterpret_cast<unsigned*>(tb);
+    e->ep_head_flags = reinterpret_cast<unsigned*>(tb + 128);
+    e->ep_keys = reinterpret_cast<unsigned long long*>(tb + 256);
+    {
+      // SFK_VOCAB_SHARD=0 keeps the lm_head replicated
+      const char* vs = getenv("SFK_VOCAB_SHARD");
+      const int N = e->ep_size;
+      e->v_loc = (V + N - 1) / N;
+      e->v0 = e->ep_rank * e->v_loc;
+      e->v_loc = std::max(0, std::min(e->v_loc, V - e->v0));
+      e->head_shard = !(vs && vs[0] == '0') && (int64_t)(N - 1) * ((V + N - 1) / N) < V;  // no empty slice
+    }
     TRY(e->alloc(&e->ep_step, sizeof(unsigned), sb));
-    cudaError_t ce = cudaMemset(e->ep_buf, 0, part + 256);
+    cudaError_t ce = cudaMemset(e->ep_buf, 0, part + tail);
     if (ce == cudaSuccess) ce = cudaMemset(e->ep_step, 0, sizeof(unsigned));
     if (ce != cudaSuccess) {
       sfk_engine_free(e);
@@ -1864,7 +1910,11 @@ sfk_status sfk_kv_reset(sfk_engine* e) {
   return SFK_OK;
 }
 
-static sfk_status run_step(sfk_engine* e, int b, bool greedy) {
+// full_logits: the caller reads this step's logits (otherwise an
+// expert-parallel engine scores only its vocabulary slice and exchanges the
+// argmax)
+static sfk_status run_step(sfk_engine* e, int b, bool greedy, bool full_logits) {
+  e->shard_now = e->head_shard && !full_logits;
   if (e->tier.on || e->win.on) {
     sfk_status s = run_step_direct(e, b, greedy);
     if (s) return s;
@@ -1899,7 +1949,7 @@ sfk_status sfk_forward_batch(sfk_engine* e, int32_t n_seq, const int32_t* tokens
   memcpy(e->h_pos, positions, sizeof(int) * n_seq);
   for (int t = 0; t < n_seq; ++t) e->step_pos[t] = positions[t];
   CK(cudaMemcpyAsync(e->tok_in, e->h_tok, sizeof(int) * 2 * B, cudaMemcpyHostToDevice, e->stream));
-  sfk_status s = run_step(e, n_seq, false);
+  sfk_status s = run_step(e, n_seq, false, logits_host != nullptr);
   if (s) return s;
   const size_t n_logits = (size_t)n_seq * e->hp.n_vocab;
   if (logits_host)
@@ -2346,7 +2396,7 @@ sfk_status sfk_generate(sfk_engine* e, const int32_t* prompt, int32_t n_prompt, 
     if (i + 1 == limit || e->seq_pos[0] + 1 > hp.n_ctx) break;
     // one decode step on the token (device greedy-loop form: the key holds it)
     e->step_pos[0] = e->seq_pos[0];
-    if ((s = run_step(e, 1, true))) return s;
+    if ((s = run_step(e, 1, true, true))) return s;
     if ((s = engine_check(e))) return s;
     e->seq_pos[0] += 1;
   }
@@ -2363,7 +2413,7 @@ sfk_status sfk_decode_greedy(sfk_engine* e, int32_t n_seq, int32_t n_steps, int3
   CK(cudaSetDevice(e->device));
   for (int i = 0; i < n_steps; ++i) {
     for (int t = 0; t < n_seq; ++t) e->step_pos[t] = e->seq_pos[t] + i;
-    sfk_status s = run_step(e, n_seq, true);
+    sfk_status s = run_step(e, n_seq, true, false);
     if (s) return s;
     if (tokens_out) {
       // token consumed by this step = previous argmax
@@ -2582,6 +2632,7 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
   if (e->steps == 0) return fail(SFK_ERR_INVALID_ARGUMENT, "run a decode step first");
   if (e->tier.on || e->win.on)
     return fail(SFK_ERR_UNSUPPORTED, "per-kernel timing needs every expert and the whole KV resident");
+  e->shard_now = false;  // the whole lm_head, as the replicated engine runs it
   CK(cudaSetDevice(e->device));
   cudaEvent_t a = nullptr, z = nullptr;
   CK(cudaEventCreate(&a));
@@ -2637,6 +2688,8 @@ sfk_status sfk_ep_connect(sfk_engine* e, const void* handles, int32_t n_ranks) {
     }
     e->ep_parts[r] = reinterpret_cast<const float*>(base);
     e->ep_peer_flags[r] = reinterpret_cast<unsigned*>(base + part);
+    e->ep_peer_head_flags[r] = reinterpret_cast<unsigned*>(base + part + 128);
+    e->ep_peer_keys[r] = reinterpret_cast<const unsigned long long*>(base + part + 256);
   }
   e->ep_connected = true;
   return SFK_OK;

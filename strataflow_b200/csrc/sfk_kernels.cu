@@ -406,7 +406,7 @@ __device__ void epi_lmhead(const StreamParams& p, const float* acc, int r0, int 
     for (int row = tid; row < nr; row += NWS * 32) {
       const float v = acc[row * p.n_pairs + t];
       if (p.store_logits) p.y[(int64_t)t * p.y_stride + r0 + row] = v;
-      if (v > best) { best = v; bi = r0 + row; }
+      if (v > best) { best = v; bi = p.argmax_base + r0 + row; }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1605,6 +1605,46 @@ __global__ void __launch_bounds__(256) ep_combine_kernel(const EpParams p) {
   }
 }
 
+__global__ void __launch_bounds__(32) ep_argmax_kernel(const EpHeadParams p) {
+  pdl_wait();
+  pdl_launch_dependents();
+  const unsigned epoch = *p.ep_step;  // written by this step's embed kernel: one exchange per step
+  const int tid = threadIdx.x;
+  if (tid < p.b) {
+    p.own_keys[tid] = p.key[tid];
+    __threadfence_system();  // the published keys before the flag
+  }
+  __syncthreads();
+  if (tid < p.n_ranks) {
+    __threadfence_system();
+    st_release_sys(p.peer_flags[tid] + p.rank, epoch);
+  }
+  __shared__ int ok;
+  if (tid == 0) {
+    ok = 1;
+    const long long t0 = clock64();
+    for (int r = 0; r < p.n_ranks && ok; ++r) {
+      while (!ep_reached(ld_acquire_sys(p.flags + r), epoch)) {
+        __nanosleep(32);
+        if (clock64() - t0 > (1ll << 31)) {
+          atomicExch(p.status, ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (ok && tid < p.b) {
+    unsigned long long m = 0;
+    for (int r = 0; r < p.n_ranks; ++r) {
+      const unsigned long long k = __ldcv(p.peer_keys[r] + tid);
+      m = k > m ? k : m;
+    }
+    p.key[tid] = m;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Route from caller-supplied ids / weights (operator-level mul_mat_id / moe_ffn)
 // ---------------------------------------------------------------------------
@@ -1774,6 +1814,11 @@ int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_ch
     case 256: return f16 ? attn_active_clusters_t<256, 1>(gqa, cluster, max_chunk) : attn_active_clusters_t<256, 0>(gqa, cluster, max_chunk);
     default: return 0;
   }
+}
+
+cudaError_t launch_ep_argmax(const EpHeadParams& p, cudaStream_t st, bool pdl) {
+  if (p.b < 1 || p.b > 32 || p.n_ranks < 1 || p.n_ranks > MAXR) return cudaErrorInvalidValue;
+  return launch_pdl(ep_argmax_kernel, dim3(1), dim3(32), 0, st, pdl, p);
 }
 
 cudaError_t launch_ep_combine(const EpParams& p, cudaStream_t st, bool pdl) {

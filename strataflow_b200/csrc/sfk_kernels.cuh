@@ -144,6 +144,8 @@ struct StreamParams {
   // (ep_eloc = 0: all experts are local); routed tiles and the weighted
   // combine skip the others
   int ep_e0, ep_eloc;
+  // EPI_LMHEAD: index of row 0 in the argmax keys (a rank's vocabulary slice)
+  int argmax_base;
   // bounded expert tier: routed expert e is read from slot slot_map[e] of the
   // pool (w0 / w1 = the pool's matrices, expert_stride = the slot size);
   // null: experts are addressed directly
@@ -236,6 +238,23 @@ int stream2_occupancy(const StreamParams& p);   // CTAs per SM its plan allows (
 cudaError_t launch_stream(const StreamParams& p, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st, bool pdl);
 cudaError_t launch_ep_combine(const EpParams& p, cudaStream_t st, bool pdl);
+
+// The lm_head's argmax across ranks when each rank scored a slice of the
+// vocabulary: every rank publishes its b keys ((ordered value, ~index) as the
+// lm_head epilogue writes them), raises its flag on every rank (epoch = the
+// step counter), waits for all flags, and takes the maximum key per token --
+// the first maximum of the whole vocabulary on every rank.
+struct EpHeadParams {
+  unsigned long long* key;                     // [b]: this rank's keys in, the global keys out
+  unsigned long long* own_keys;                // this rank's published keys [b] (peers read them)
+  const unsigned long long* peer_keys[MAXR];   // every rank's published keys
+  unsigned* flags;                             // this rank's head flag words [MAXR]
+  unsigned* peer_flags[MAXR];                  // every rank's head flag words
+  int n_ranks, rank, b;
+  const unsigned* ep_step;
+  int* status;
+};
+cudaError_t launch_ep_argmax(const EpHeadParams& p, cudaStream_t st, bool pdl);
 // clusters of `cluster` attention CTAs that fit on the device at once (0 if
 // that cluster size cannot be launched)
 int attn_active_clusters(int head_dim, int f16, int gqa, int cluster, int max_chunk);

@@ -8,7 +8,9 @@ residual, partials added in rank order -- the only arithmetic that differs
 from one GPU): identical greedy tokens, every step's logits within the
 north-star 1e-3 relative L2 / 1e-2 max-abs, the same logits on both ranks
 (bit-identical: the ranks add the same partials in the same order), and the
-device greedy loop continuing with the oracle's tokens.  Skipped on a box
+device greedy loop continuing with the oracle's tokens; steps that return no
+logits (the device loop, host steps without logits) score each rank's slice
+of the vocabulary and exchange the argmax.  Skipped on a box
 with fewer than two GPUs.
 """
 import os
@@ -40,7 +42,16 @@ def _rank(rank, world, port, cfg_kw, seed, prompt, n_gen, q, env=None):
         eng.ep_connect_group()
         toks, logits = eng.generate(prompt, n_gen, host_loop=True)
         dev = eng.decode_greedy(6, 1)[:, 0].tolist()   # device loop continues the sequence
-        q.put((rank, toks, np.stack(logits), dev, None))
+        # host steps that return no logits: each rank scores its vocabulary
+        # slice and the argmax is exchanged
+        eng.reset_kv()
+        for pos, t in enumerate(prompt):
+            am, _ = eng.forward(t, pos, want_logits=False)
+        nl = []
+        for i in range(4):
+            nl.append(int(am))
+            am, _ = eng.forward(am, len(prompt) + i, want_logits=False)
+        q.put((rank, toks, np.stack(logits), dev + [nl], None))
         dist.barrier()
         eng.close()
         dist.destroy_process_group()
@@ -99,4 +110,5 @@ def test_expert_parallel_two_ranks_match_oracle(cuda, cfg_kw, env):
         ok, rel, mx = close(res[0][1][i], ref_logits[i])
         assert ok, (i, rel, mx)
     # the device loop's first token is the argmax of the last host step
-    assert res[0][2] == res[1][2] == ref_toks[n_gen:n_gen + n_dev]
+    assert res[0][2][:-1] == res[1][2][:-1] == ref_toks[n_gen:n_gen + n_dev]
+    assert res[0][2][-1] == res[1][2][-1] == ref_toks[:4]
