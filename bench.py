@@ -288,6 +288,12 @@ def run_ours(args, rank: int, world: int, local_rank: int):
     if rank == 0 and world == 1 and not args.no_cpu:
         eng.close()
         cpu = cpu_baseline_both()
+    # at 4 or more GPUs the same job also runs configs[4] (the ~1T model,
+    # expert-parallel over these ranks) and nests its line
+    ep_line = None
+    if world >= 4 and not args.no_ep:
+        eng.close()
+        ep_line = ep_measure(1, 256, 61, 64, 3, rank, world, local_rank, dist)
 
     if rank == 0:
         line = {
@@ -314,6 +320,8 @@ def run_ours(args, rank: int, world: int, local_rank: int):
             "load_s": t_load, "prefill_s": t_pf, "prefill_tok_s": B * PROMPT / t_pf,
             "prefill": "batched (sfk_prefill: tensor-core GEMMs, one call per sequence)",
         }
+        if ep_line is not None:
+            line["ep_1t"] = ep_line
         print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
@@ -353,14 +361,15 @@ def ep_rank_bytes(cfg, world: int, B: int) -> tuple[float, bool]:
     return trunk + experts_rank, split
 
 
+EP_METRIC = "decode tok/s, ~1T-parameter MoE (61L d7168 E384 top-8) Q4_K experts, expert-parallel"
+
+
 def run_ep(args, rank: int, world: int, local_rank: int):
     """the ~1T-parameter MoE, experts sharded over the torchrun
     ranks (expert parallelism), trunk replicated; one sequence decoded by the
     whole job."""
     import datetime
     import torch
-    from strataflow_b200 import engine as E
-    from strataflow_b200 import lib as L
 
     torch.cuda.set_device(local_rank)
     dist = None
@@ -368,10 +377,25 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         import torch.distributed as dist
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
-    B = args.batch
-    prompt_n = args.prompt
-    metric = "decode tok/s, ~1T-parameter MoE (61L d7168 E384 top-8) Q4_K experts, expert-parallel"
-    cfg = E.trillion_config(n_ctx=prompt_n + args.warmup + args.steps + 16, max_batch=B, n_layer=args.layers,
+    line = ep_measure(args.batch, args.prompt, args.layers, args.steps, args.warmup, rank, world, local_rank, dist)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.destroy_process_group()
+
+
+def ep_measure(B: int, prompt_n: int, n_layer: int, steps: int, warmup: int, rank: int, world: int,
+               local_rank: int, dist) -> dict | None:
+    """Load the ~1T model sharded over the job's ranks, feed a random prompt,
+    time `steps` greedy decode steps (max over ranks) and return rank 0's
+    JSON line (other ranks: None).  Every rank takes the same collective
+    steps, also when the model does not fit."""
+    import torch
+    from strataflow_b200 import engine as E
+    from strataflow_b200 import lib as L
+
+    metric = EP_METRIC
+    cfg = E.trillion_config(n_ctx=prompt_n + warmup + steps + 16, max_batch=B, n_layer=n_layer,
                             ep_size=world, ep_rank=rank)
     t_load = time.perf_counter()
     try:
@@ -384,13 +408,11 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         ok = int(t.item())
     if not ok:
-        if rank == 0:
-            print(json.dumps({"metric": metric, "n_gpus": world, "unavailable":
-                              f"the model does not fit: {world} GPU(s) -> {why if eng is None else 'another rank'}"}),
-                  flush=True)
-        if dist:
-            dist.destroy_process_group()
-        return
+        if eng is not None:
+            eng.close()
+        return {"metric": metric, "n_gpus": world, "unavailable":
+                f"the model does not fit: {world} GPU(s) -> {why if eng is None else 'another rank'}"} \
+            if rank == 0 else None
     t_load = time.perf_counter() - t_load
     if world > 1:
         eng.ep_connect_group()
@@ -401,7 +423,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     for p in range(prompt_n):
         eng.forward_batch(prompt[:, p], np.full(B, p, np.int32), want_logits=False)
     t_pf = time.perf_counter() - t_pf
-    eng.decode_greedy(args.warmup, B, want_tokens=False)
+    eng.decode_greedy(warmup, B, want_tokens=False)
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     if dist:
@@ -409,7 +431,7 @@ def run_ep(args, rank: int, world: int, local_rank: int):
     torch.cuda.synchronize()
     with ClockSampler(local_rank) as clk:
         ev0.record(stream)
-        toks = eng.decode_greedy(args.steps, B, want_tokens=True)
+        toks = eng.decode_greedy(steps, B, want_tokens=True)
         ev1.record(stream)
         ev1.synchronize()
     ms = ev0.elapsed_time(ev1)
@@ -425,14 +447,15 @@ def run_ep(args, rank: int, world: int, local_rank: int):
         s_ = torch.tensor([int(torch.equal(tt, t0))], device="cuda")
         dist.all_reduce(s_, op=dist.ReduceOp.MIN)
         same = int(s_.item())
-    value = B * args.steps / (ms / 1000.0)
+    value = B * steps / (ms / 1000.0)
     st = eng.stats()
     peak, peak_kind = _peaks()
     rank_bytes, heads_split = ep_rank_bytes(cfg, world, B)
+    line = None
     if rank == 0:
         line = {
-            "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "strong",
+            "metric": metric, "value": value, "unit": "tok/s", "n_gpus": world, "steps": steps,
+            "warmup": warmup, "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "q4_k experts / q8_0 trunk x int8 dot (dp4a), fp32 accum",
             "data": "synthetic",
             "config": {"workload": f"~1T-param MoE decode b={B}: {prompt_n}-token random prompt, then greedy decode",
@@ -441,18 +464,16 @@ def run_ep(args, rank: int, world: int, local_rank: int):
                        "parallelism": f"ep{world} (experts sharded, "
                                       f"{'attention heads split' if heads_split else 'trunk replicated'})"},
             "clocks": clk.summary(), "ranks_agree": bool(same),
-            "gpu_launches": st["kernels_per_step"] * args.steps,
-            "step_roofline": {"achieved": rank_bytes * args.steps / (ms / 1000.0) / 1e9, "peak": peak,
-                              "unit": "GB/s per GPU", "frac": rank_bytes * args.steps / (ms / 1000.0) / 1e9 / peak,
+            "gpu_launches": st["kernels_per_step"] * steps,
+            "step_roofline": {"achieved": rank_bytes * steps / (ms / 1000.0) / 1e9, "peak": peak,
+                              "unit": "GB/s per GPU", "frac": rank_bytes * steps / (ms / 1000.0) / 1e9 / peak,
                               "bytes_per_token_per_gpu": rank_bytes, "peak_kind": peak_kind},
             "weight_bytes_per_gpu": st["weight_bytes_hbm"], "load_s": t_load, "prefill_s": t_pf,
         }
-        print(json.dumps(line), flush=True)
     if dist:
         dist.barrier()
     eng.close()
-    if dist:
-        dist.destroy_process_group()
+    return line
 
 
 def run_sweep(args):
@@ -675,6 +696,8 @@ def main():
                     help="tensor-core GEMM sweep (n = 16..512 rows) and the batched 512-token prefill")
     ap.add_argument("--expert-slots", type=int, default=0,
                     help="decode with a bounded expert tier of this many HBM bundle slots (one GPU)")
+    ap.add_argument("--no-ep", action="store_true",
+                    help="at 4+ GPUs, skip the nested expert-parallel ~1T measurement")
     ap.add_argument("--kv-window", type=int, default=0,
                     help="decode with a KV window of this many resident tokens per sequence (one GPU)")
     args = ap.parse_args()
