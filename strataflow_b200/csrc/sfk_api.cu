@@ -547,6 +547,17 @@ StreamParams gateup_params(const sfk_engine* e, int l, int b) {
   return p;
 }
 
+// Kernels whose first weight fill goes out before their wait on the previous
+// kernel (bit 0: output projection, 1: QKV, 2: lm_head); SFK_EARLY_FILL
+// overrides the default.
+int early_fill_mask() {
+  static const int m = [] {
+    const char* v = getenv("SFK_EARLY_FILL");
+    return v ? atoi(v) : 3;
+  }();
+  return m;
+}
+
 // Launch one kernel of the step: class `c` of layer `l` for b sequences.
 sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl) {
   const sfk_hparams& hp = e->hp;
@@ -592,6 +603,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.norm_w = W.attn_norm;
       p.eps = hp.rms_eps;
       p.epi = EPI_QKV;
+      p.early_fill = (early_fill_mask() >> 1) & 1;
       p.y = e->q;
       p.kv = kv_view(e, l);
       p.n_head = e->hq_loc;
@@ -634,6 +646,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.pro = PRO_QUANT;
       p.x = e->attn_out;
       p.epi = EPI_RESID;
+      p.early_fill = early_fill_mask() & 1;
       p.y = e->ffn_inp;
       p.res = e->x;
       p.y_stride = d;
@@ -732,6 +745,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       p.norm_w = e->out_norm;
       p.eps = hp.rms_eps;
       p.epi = EPI_LMHEAD;
+      p.early_fill = (early_fill_mask() >> 2) & 1;
       p.y = e->logits;
       p.y_stride = hp.n_vocab;
       p.argmax_key = e->argmax_key;

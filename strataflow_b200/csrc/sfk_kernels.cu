@@ -833,6 +833,14 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
     for (int i = 0; i < WPRE; ++i)
       if (i < rcols / 128) wpre[i] = *reinterpret_cast<const float4*>(wr + i * 128);
   }
+  // An unrouted matrix's weights do not depend on the previous kernel: with
+  // early_fill its first ring fill goes out before the wait.  The CTAs of a
+  // kernel can be resident long before their predecessor ends (the output
+  // projection's beside the attention's), and the fill then lands in that
+  // time instead of after it.
+  const bool early = p.early_fill && !routed;
+  if (early && lane == 0)
+    for (int k = 0; k < S && warp + k * NWS < n_rb; ++k) issue(warp + k * NWS, k, 1);
   pdl_wait();
   pdl_launch_dependents();
   // inputs written by the previous kernels: the routing (when another kernel
@@ -1001,7 +1009,7 @@ __global__ void __launch_bounds__(NWS * 32, MINB) stream2_kernel(const StreamPar
   // activation loads (copied ahead of them, it would delay them by the time
   // the whole GPU's first fill takes to drain)
   auto first_fill = [&]() {
-    if (!routed && lane == 0)
+    if (!routed && !early && lane == 0)
       for (int k = 0; k < S && warp + k * NWS < n_tiles; ++k) issue(warp + k * NWS, k, 1);
   };
   if (!self_route && pl.xq_smem && p.pro == PRO_QUANT) {

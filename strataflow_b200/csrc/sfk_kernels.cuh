@@ -146,6 +146,9 @@ struct StreamParams {
   int ep_e0, ep_eloc;
   // EPI_LMHEAD: index of row 0 in the argmax keys (a rank's vocabulary slice)
   int argmax_base;
+  // unrouted matrices: issue the first ring fill before waiting on the
+  // previous kernel (the weights do not depend on it)
+  int early_fill;
   // bounded expert tier: routed expert e is read from slot slot_map[e] of the
   // pool (w0 / w1 = the pool's matrices, expert_stride = the slot size);
   // null: experts are addressed directly
