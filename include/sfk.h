@@ -196,6 +196,15 @@ SFK_API sfk_status sfk_strata_read_bundle(const sfk_strata *s, int32_t layer, in
  * V and its heads' columns of the output projection.  The engine must have
  * been created with sfk_strata_hparams' shape. */
 SFK_API sfk_status sfk_strata_load(const sfk_strata *s, sfk_engine *eng);
+/* Pack a GGUF checkpoint into a .strata file: the reference's
+ * pack_gguf_to_strata (src/tws/strata_pack.h:16-46, strata_pack.cpp:251-1108)
+ * without its optional LZ compression.  Weight bytes are copied verbatim;
+ * stacked (blk.N.ffn_*_exps) and per-expert (blk.N.ffn_*.E) expert tensors
+ * become one gate|up|down bundle per (layer, expert); a file mixing the two,
+ * one whose metadata declares experts none of which are found, and fused
+ * gate_up expert tensors are refused.  Tensor types: F32, F16, Q8_0, Q4_K,
+ * Q6_K.  Host-only; a failed pack removes its partial output. */
+SFK_API sfk_status sfk_strata_pack(const char *gguf_path, const char *strata_path);
 
 /* ---- decode: replaces Engine::forward / reset_kv (engine.h:241,245) ----- */
 /* Clear every sequence's KV so the next step starts at position 0. */

@@ -20,6 +20,7 @@
 #include <fcntl.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <array>
 #include <cstdarg>
 #include <cstdint>
@@ -28,6 +29,7 @@
 #include <map>
 #include <new>
 #include <string>
+#include <tuple>
 #include <vector>
 
 #include "sfk.h"
@@ -638,3 +640,441 @@ SFK_API sfk_status sfk_strata_load(const sfk_strata* s, sfk_engine* eng) {
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// The packer: a GGUF checkpoint -> .strata, the reference's
+// pack_gguf_to_strata (src/tws/strata_pack.h:16-46, strata_pack.cpp:251-1108)
+// without its optional LZ compression.  Weight bytes are copied verbatim.
+//   * Expert tensors are recognised by name: stacked blk.N.ffn_{gate,up,down}
+//     _exps.weight (3-D, experts outermost) or legacy per-expert
+//     blk.N.ffn_{gate,up,down}.E.weight; a file mixing the two, or one whose
+//     metadata declares experts none of which are found, is refused.  Fused
+//     gate_up expert tensors are refused (this library's bundles are
+//     gate | up | down).
+//   * Embedded metadata: the source's own header, key/values and tensor
+//     infos verbatim (stacked input), or for legacy input a GGUF prefix built
+//     here with the same key/values and stacked _exps tensor declarations.
+//   * Layout: superblock (v2) | metadata | expert index | trunk block (4 KiB
+//     aligned, every other tensor in source order, no padding) | expert
+//     region (4 KiB aligned, one 4 KiB-aligned gate|up|down blob per (layer,
+//     expert), layer-major) | trunk index (4 KiB aligned).
+// ---------------------------------------------------------------------------
+namespace {
+
+constexpr uint64_t IO_ALIGN = 4096;
+
+uint64_t align_up64(uint64_t v, uint64_t a) { return (v + a - 1) / a * a; }
+
+struct SrcTensor {
+  std::string name;
+  uint32_t nd = 0;
+  int64_t ne[4] = {1, 1, 1, 1};
+  int type = 0;
+  uint64_t off = 0;     // from the start of the source file
+  uint64_t nbytes = 0;
+  int kind = -1;        // expert kind 0 gate, 1 up, 2 down (or -1: trunk)
+  int layer = -1, expert = -1;  // expert tensors; expert >= 0: a legacy per-expert tensor
+  size_t info_begin = 0, info_end = 0;  // its tensor-info bytes in the source prefix
+};
+
+// blk.N.ffn_{gate,up,down}.E.weight -> (layer, kind, expert)
+bool legacy_expert(const std::string& name, int* layer, int* kind, int* expert) {
+  std::string suf;
+  const int l = parse_layer(name, &suf);
+  if (l < 0) return false;
+  static const char* kinds[3] = {"ffn_gate.", "ffn_up.", "ffn_down."};
+  for (int k = 0; k < 3; ++k) {
+    const size_t n = strlen(kinds[k]);
+    if (suf.compare(0, n, kinds[k]) != 0) continue;
+    std::string rest = suf.substr(n);
+    if (rest.size() < 8 || rest.compare(rest.size() - 7, 7, ".weight") != 0) return false;
+    rest = rest.substr(0, rest.size() - 7);
+    if (rest.empty() || rest.size() > 6) return false;
+    int e = 0;
+    for (char c : rest) {
+      if (c < '0' || c > '9') return false;
+      e = e * 10 + (c - '0');
+    }
+    *layer = l;
+    *kind = k;
+    *expert = e;
+    return true;
+  }
+  return false;
+}
+
+int stacked_kind(const std::string& name, int* layer) {
+  std::string suf;
+  const int l = parse_layer(name, &suf);
+  if (l < 0) return -1;
+  *layer = l;
+  if (suf == "ffn_gate_exps.weight") return 0;
+  if (suf == "ffn_up_exps.weight") return 1;
+  if (suf == "ffn_down_exps.weight") return 2;
+  if (suf == "ffn_gate_up_exps.weight") return 3;
+  return -1;
+}
+
+struct Out {
+  int fd = -1;
+  uint64_t pos = 0;
+  bool ok = true;
+  void write(const void* p, uint64_t n) {
+    const uint8_t* b = static_cast<const uint8_t*>(p);
+    while (ok && n > 0) {
+      const ssize_t w = ::write(fd, b, n > (1u << 30) ? (1u << 30) : (size_t)n);
+      if (w <= 0) {
+        ok = false;
+        return;
+      }
+      b += w;
+      n -= (uint64_t)w;
+      pos += (uint64_t)w;
+    }
+  }
+  void pad_to(uint64_t target) {
+    static const uint8_t zeros[4096] = {};
+    while (ok && pos < target) write(zeros, std::min<uint64_t>(sizeof(zeros), target - pos));
+  }
+  void pwrite_at(const void* p, uint64_t n, uint64_t off) {
+    if (ok && ::pwrite(fd, p, (size_t)n, (off_t)off) != (ssize_t)n) ok = false;
+  }
+};
+
+// copy [off, off + n) of `src` to the output
+bool copy_range(int src, uint64_t off, uint64_t n, Out& o, std::vector<uint8_t>& buf) {
+  while (o.ok && n > 0) {
+    const size_t chunk = (size_t)std::min<uint64_t>(n, buf.size());
+    size_t got = 0;
+    while (got < chunk) {
+      const ssize_t r = pread(src, buf.data() + got, chunk - got, (off_t)(off + got));
+      if (r <= 0) return false;
+      got += (size_t)r;
+    }
+    o.write(buf.data(), chunk);
+    off += chunk;
+    n -= chunk;
+  }
+  return o.ok;
+}
+
+void put_str(std::vector<uint8_t>& v, const std::string& s) {
+  const uint64_t n = s.size();
+  v.insert(v.end(), reinterpret_cast<const uint8_t*>(&n), reinterpret_cast<const uint8_t*>(&n) + 8);
+  v.insert(v.end(), s.begin(), s.end());
+}
+template <typename T>
+void put(std::vector<uint8_t>& v, T x) {
+  v.insert(v.end(), reinterpret_cast<const uint8_t*>(&x), reinterpret_cast<const uint8_t*>(&x) + sizeof(T));
+}
+
+sfk_status pack(const char* in_path, const char* out_path) {
+  const int src = open(in_path, O_RDONLY);
+  if (src < 0) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: cannot open", in_path);
+  struct Closer {
+    int fd;
+    ~Closer() { close(fd); }
+  } src_closer{src};
+  const off_t fsz = lseek(src, 0, SEEK_END);
+  if (fsz < 24) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: not a GGUF file (too short)", in_path);
+  const uint64_t file_size = (uint64_t)fsz;
+
+  // the metadata prefix: read more of the file until it parses
+  std::vector<uint8_t> pre;
+  Cursor c{nullptr, 0};
+  std::vector<SrcTensor> tensors;
+  std::map<std::string, KV> kv;
+  std::vector<std::pair<size_t, size_t>> kv_bytes;  // each key/value's bytes in the prefix
+  uint64_t n_tensors = 0, n_kv = 0;
+  uint32_t gguf_ver = 0;
+  for (uint64_t want = std::min<uint64_t>(file_size, 1u << 22);; want = std::min<uint64_t>(file_size, want * 4)) {
+    pre.resize((size_t)want);
+    size_t got = 0;
+    while (got < pre.size()) {
+      const ssize_t r = pread(src, pre.data() + got, pre.size() - got, (off_t)got);
+      if (r <= 0) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: read failed", in_path);
+      got += (size_t)r;
+    }
+    c = Cursor{pre.data(), pre.size()};
+    tensors.clear();
+    kv.clear();
+    kv_bytes.clear();
+    const uint32_t magic = c.get<uint32_t>();
+    gguf_ver = c.get<uint32_t>();
+    n_tensors = c.get<uint64_t>();
+    n_kv = c.get<uint64_t>();
+    if (!c.ok || magic != 0x46554747u || (gguf_ver != 2 && gguf_ver != 3))
+      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: not a GGUF v2/v3 file", in_path);
+    if (n_tensors > (1u << 24) || n_kv > (1u << 24))
+      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: GGUF counts out of range", in_path);
+    for (uint64_t i = 0; i < n_kv && c.ok; ++i) {
+      const size_t b = c.off;
+      std::string key = c.str();
+      KV v;
+      v.type = c.get<uint32_t>();
+      if (!c.ok || !read_value(c, v.type, &v)) {
+        c.ok = false;
+        break;
+      }
+      kv[key] = v;
+      kv_bytes.emplace_back(b, c.off);
+    }
+    for (uint64_t i = 0; i < n_tensors && c.ok; ++i) {
+      SrcTensor t;
+      t.info_begin = c.off;
+      t.name = c.str();
+      t.nd = c.get<uint32_t>();
+      if (!c.ok || t.nd < 1 || t.nd > 4) {
+        if (c.ok) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor %llu has %u dims", in_path,
+                               (unsigned long long)i, t.nd);
+        break;
+      }
+      for (uint32_t d = 0; d < t.nd; ++d) t.ne[d] = (int64_t)c.get<uint64_t>();
+      t.type = (int)c.get<uint32_t>();
+      t.off = c.get<uint64_t>();
+      t.info_end = c.off;
+      tensors.push_back(t);
+    }
+    if (c.ok) break;
+    if (want >= file_size) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: GGUF metadata truncated", in_path);
+  }
+  uint64_t alignment = 32;
+  if (kv.count("general.alignment")) alignment = kv["general.alignment"].u;
+  if (alignment == 0 || (alignment & (alignment - 1)))
+    return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: general.alignment %llu", in_path, (unsigned long long)alignment);
+  const uint64_t data_off = align_up64(c.off, alignment);
+  std::string arch = "llama";
+  if (kv.count("general.architecture") && kv["general.architecture"].type == G_STR)
+    arch = kv["general.architecture"].s;
+  auto key_u = [&](const std::string& k) -> uint64_t {
+    auto it = kv.find(k);
+    return it == kv.end() || it->second.type == G_STR || it->second.type == G_ARR || it->second.type == G_F32 ||
+                   it->second.type == G_F64
+               ? 0
+               : it->second.u;
+  };
+  const uint64_t meta_experts = key_u(arch + ".expert_count");
+
+  // classify
+  int max_layer = -1, n_exp = 0;
+  bool stacked = false, legacy = false;
+  for (SrcTensor& t : tensors) {
+    int64_t blk, bb;
+    if (!type_block(t.type, &blk, &bb))
+      return sfail(SFK_ERR_UNSUPPORTED, "%s: tensor %s has ggml type %d (F32, F16, Q8_0, Q4_K, Q6_K are packed)",
+                   in_path, t.name.c_str(), t.type);
+    bool shape_ok = t.ne[0] > 0 && t.ne[0] % blk == 0;
+    for (int d = 0; d < 4; ++d) shape_ok = shape_ok && t.ne[d] > 0 && t.ne[d] < ((int64_t)1 << 31);
+    if (!shape_ok) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor %s shape", in_path, t.name.c_str());
+    t.nbytes = (uint64_t)(t.ne[0] / blk * bb) * (uint64_t)t.ne[1] * (uint64_t)t.ne[2] * (uint64_t)t.ne[3];
+    if (t.off % alignment || data_off + t.off + t.nbytes > file_size || data_off + t.off < data_off)
+      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor %s lies outside the file", in_path, t.name.c_str());
+    t.off += data_off;
+    int l = -1, k = stacked_kind(t.name, &l), e = -1;
+    if (k == 3)
+      return sfail(SFK_ERR_UNSUPPORTED, "%s: fused gate_up expert tensor %s (bundles here are gate | up | down)",
+                   in_path, t.name.c_str());
+    if (k >= 0) {
+      if (t.ne[2] < 1 || t.nbytes % (uint64_t)t.ne[2])
+        return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: expert tensor %s is not 3-D with the experts outermost",
+                     in_path, t.name.c_str());
+      if (n_exp && n_exp != (int)t.ne[2])
+        return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: expert tensors disagree on the expert count", in_path);
+      n_exp = (int)t.ne[2];
+      stacked = true;
+    } else if (legacy_expert(t.name, &l, &k, &e)) {
+      legacy = true;
+    } else {
+      continue;  // trunk
+    }
+    t.kind = k;
+    t.layer = l;
+    t.expert = e;
+    max_layer = std::max(max_layer, l);
+  }
+  if (stacked && legacy)
+    return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: stacked and per-expert expert tensors mixed", in_path);
+  if (meta_experts > 0 && !stacked && !legacy)
+    return sfail(SFK_ERR_INVALID_ARGUMENT,
+                 "%s: the metadata declares %llu experts but no expert tensor was recognised by name", in_path,
+                 (unsigned long long)meta_experts);
+  const int n_layers = max_layer + 1;
+  // expert tensors per (layer, kind[, expert])
+  std::map<std::tuple<int, int, int>, const SrcTensor*> xt;
+  if (legacy) {
+    n_exp = (int)meta_experts;
+    if (n_exp == 0)
+      for (const SrcTensor& t : tensors)
+        if (t.kind >= 0) n_exp = std::max(n_exp, t.expert + 1);
+  }
+  for (const SrcTensor& t : tensors) {
+    if (t.kind < 0) continue;
+    if (legacy && t.expert >= n_exp)
+      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: %s: expert %d of %d", in_path, t.name.c_str(), t.expert, n_exp);
+    const auto key = std::make_tuple(t.layer, t.kind, legacy ? t.expert : 0);
+    if (xt.count(key)) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: %s appears twice", in_path, t.name.c_str());
+    xt[key] = &t;
+  }
+  for (int l = 0; l < n_layers; ++l)
+    for (int k = 0; k < 3; ++k)
+      for (int e = 0; e < (legacy ? n_exp : 1); ++e)
+        if (!xt.count(std::make_tuple(l, k, e)))
+          return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: layer %d lacks its %s expert tensor%s", in_path, l,
+                       k == 0 ? "gate" : k == 1 ? "up" : "down", legacy ? "s" : "");
+  if (legacy)  // every expert of a (layer, kind) must share a shape and type
+    for (int l = 0; l < n_layers; ++l)
+      for (int k = 0; k < 3; ++k) {
+        const SrcTensor* a = xt[std::make_tuple(l, k, 0)];
+        for (int e = 1; e < n_exp; ++e) {
+          const SrcTensor* b = xt[std::make_tuple(l, k, e)];
+          if (b->type != a->type || b->nbytes != a->nbytes || b->ne[0] != a->ne[0] || b->ne[1] != a->ne[1])
+            return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: %s differs from %s", in_path, b->name.c_str(),
+                         a->name.c_str());
+        }
+      }
+  for (const SrcTensor& t : tensors)
+    if (t.kind < 0 && t.name.size() >= 64)
+      return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: tensor name %s is too long for the trunk index", in_path,
+                   t.name.c_str());
+
+  // embedded metadata
+  std::vector<uint8_t> meta;
+  if (!legacy) {
+    meta.assign(pre.begin(), pre.begin() + (size_t)std::min<uint64_t>(data_off, pre.size()));
+    meta.resize((size_t)data_off, 0);  // the alignment padding (zeros)
+  } else {
+    uint64_t nt = 0;
+    for (const SrcTensor& t : tensors) nt += t.kind < 0 ? 1 : 0;
+    nt += (uint64_t)n_layers * 3;
+    put<uint32_t>(meta, 0x46554747u);
+    put<uint32_t>(meta, 3);
+    put<uint64_t>(meta, nt);
+    put<uint64_t>(meta, n_kv);
+    for (const auto& b : kv_bytes) meta.insert(meta.end(), pre.begin() + b.first, pre.begin() + b.second);
+    uint64_t doff = 0;
+    auto info = [&](const std::string& name, uint32_t nd, const int64_t* ne, int type, uint64_t nbytes) {
+      put_str(meta, name);
+      put<uint32_t>(meta, nd);
+      for (uint32_t d = 0; d < nd; ++d) put<uint64_t>(meta, (uint64_t)ne[d]);
+      put<uint32_t>(meta, (uint32_t)type);
+      put<uint64_t>(meta, doff);
+      doff = align_up64(doff + nbytes, alignment);
+    };
+    for (const SrcTensor& t : tensors)
+      if (t.kind < 0) info(t.name, t.nd, t.ne, t.type, t.nbytes);
+    static const char* sfx[3] = {"ffn_gate_exps.weight", "ffn_up_exps.weight", "ffn_down_exps.weight"};
+    for (int l = 0; l < n_layers; ++l)
+      for (int k : {0, 2, 1}) {  // llama.cpp's per-block order: gate, down, up
+        const SrcTensor* a = xt[std::make_tuple(l, k, 0)];
+        const int64_t ne[3] = {a->ne[0], a->ne[1], n_exp};
+        info("blk." + std::to_string(l) + "." + sfx[k], 3, ne, a->type, a->nbytes * (uint64_t)n_exp);
+      }
+    meta.resize((size_t)align_up64(meta.size(), alignment), 0);
+  }
+
+  Out o;
+  o.fd = open(out_path, O_WRONLY | O_CREAT | O_TRUNC, 0644);
+  if (o.fd < 0) return sfail(SFK_ERR_INVALID_ARGUMENT, "%s: cannot create", out_path);
+  struct Cleanup {
+    Out& o;
+    const char* path;
+    bool keep = false;
+    ~Cleanup() {
+      close(o.fd);
+      if (!keep) unlink(path);
+    }
+  } cleanup{o, out_path};
+  std::vector<uint8_t> buf(64u << 20);
+  const uint8_t zsb[SB_SIZE] = {};
+  o.write(zsb, SB_SIZE);
+  const uint64_t meta_off = o.pos;
+  o.write(meta.data(), meta.size());
+  const uint64_t index_off = o.pos, n_index = (uint64_t)n_layers * (uint64_t)n_exp;
+  std::vector<uint8_t> index((size_t)(n_index * INDEX_ENTRY), 0);
+  o.write(index.data(), index.size());
+  o.pad_to(align_up64(o.pos, IO_ALIGN));
+  const uint64_t trunk_off = o.pos;
+  std::vector<uint8_t> tix;
+  uint64_t n_trunk = 0;
+  for (const SrcTensor& t : tensors) {
+    if (t.kind >= 0) continue;
+    uint8_t e[TRUNK_ENTRY] = {};
+    memcpy(e, t.name.data(), t.name.size());
+    const uint64_t rel = o.pos - trunk_off;
+    memcpy(e + 64, &rel, 8);
+    memcpy(e + 72, &t.nbytes, 8);
+    tix.insert(tix.end(), e, e + TRUNK_ENTRY);
+    ++n_trunk;
+    if (!copy_range(src, t.off, t.nbytes, o, buf))
+      return sfail(SFK_ERR_RUNTIME, "%s: copying %s failed", out_path, t.name.c_str());
+  }
+  const uint64_t trunk_size = o.pos - trunk_off;
+  o.pad_to(align_up64(o.pos, IO_ALIGN));
+  const uint64_t expert_off = o.pos;
+  size_t ii = 0;
+  for (int l = 0; l < n_layers; ++l)
+    for (int e = 0; e < n_exp; ++e, ++ii) {
+      o.pad_to(align_up64(o.pos, IO_ALIGN));
+      const uint64_t blob = o.pos;
+      uint64_t rel[3] = {};
+      for (int k = 0; k < 3; ++k) {
+        rel[k] = o.pos - blob;
+        const SrcTensor* t = xt[std::make_tuple(l, k, legacy ? e : 0)];
+        const uint64_t per = legacy ? t->nbytes : t->nbytes / (uint64_t)n_exp;
+        const uint64_t off = legacy ? t->off : t->off + (uint64_t)e * per;
+        if (!copy_range(src, off, per, o, buf))
+          return sfail(SFK_ERR_RUNTIME, "%s: copying expert (%d, %d) failed", out_path, l, e);
+      }
+      uint8_t* x = index.data() + ii * INDEX_ENTRY;
+      const uint32_t lu = (uint32_t)l, eu = (uint32_t)e;
+      const uint64_t len = o.pos - blob;
+      memcpy(x, &lu, 4);
+      memcpy(x + 4, &eu, 4);
+      memcpy(x + 8, &blob, 8);
+      memcpy(x + 16, &len, 8);
+      memcpy(x + 24, &rel[0], 8);
+      memcpy(x + 32, &rel[1], 8);
+      memcpy(x + 40, &rel[2], 8);
+    }
+  const uint64_t expert_size = o.pos - expert_off;
+  uint64_t tix_off = 0;
+  if (n_trunk) {
+    o.pad_to(align_up64(o.pos, IO_ALIGN));
+    tix_off = o.pos;
+    o.write(tix.data(), tix.size());
+  }
+  o.pwrite_at(index.data(), index.size(), index_off);
+  // superblock (v2): magic, version, flags, eight offsets / sizes, the trunk
+  // index, n_layers, n_experts, alignment, then the CRC of all of it
+  uint8_t sb[SB_SIZE] = {};
+  const uint32_t ver = 2, flags = 1u | 2u | (n_trunk ? 4u : 0u), al = (uint32_t)IO_ALIGN;
+  const uint32_t nl = (uint32_t)n_layers, ne = (uint32_t)n_exp;
+  const uint64_t meta_size = meta.size();
+  memcpy(sb, MAGIC, 8);
+  memcpy(sb + 8, &ver, 4);
+  memcpy(sb + 12, &flags, 4);
+  const uint64_t f8[8] = {meta_off, meta_size, index_off, n_index, trunk_off, trunk_size, expert_off, expert_size};
+  memcpy(sb + 16, f8, sizeof(f8));
+  memcpy(sb + 80, &tix_off, 8);
+  memcpy(sb + 88, &n_trunk, 8);
+  memcpy(sb + 96, &nl, 4);
+  memcpy(sb + 100, &ne, 4);
+  memcpy(sb + 104, &al, 4);
+  const uint32_t crc = crc32_ieee(sb, 108);
+  memcpy(sb + 108, &crc, 4);
+  o.pwrite_at(sb, SB_SIZE, 0);
+  if (!o.ok) return sfail(SFK_ERR_RUNTIME, "%s: write failed", out_path);
+  cleanup.keep = true;
+  return SFK_OK;
+}
+
+}  // namespace
+
+extern "C" SFK_API sfk_status sfk_strata_pack(const char* gguf_path, const char* strata_path) {
+  if (!gguf_path || !strata_path) return sfail(SFK_ERR_INVALID_ARGUMENT, "null path");
+  try {
+    return pack(gguf_path, strata_path);
+  } catch (const std::bad_alloc&) {
+    return sfail(SFK_ERR_OUT_OF_MEMORY, "%s: host allocation failed", gguf_path);
+  }
+}

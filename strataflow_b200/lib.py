@@ -102,6 +102,7 @@ _SIGS = {
     "sfk_strata_bundle_bytes": (SZ, [P, I32]),
     "sfk_strata_read_bundle": (I32, [P, I32, I32, P, SZ]),
     "sfk_strata_load": (I32, [P, P]),
+    "sfk_strata_pack": (I32, [C.c_char_p, C.c_char_p]),
     "sfk_embed": (I32, [P, P, P, I32, P]),
     "sfk_decode_layer_attn": (I32, [P, I32, P, I32, P]),
     "sfk_decode_layer_moe": (I32, [P, I32, I32, P, P, P]),

@@ -75,3 +75,11 @@ class StrataFile:
     def load_into(self, engine) -> None:
         """Upload every trunk tensor and every expert bundle into `engine`."""
         L.check(self._lib.sfk_strata_load(self.h, engine.h))
+
+
+def pack(gguf_path: str, strata_path: str) -> None:
+    """sfk_strata_pack: a GGUF checkpoint into a .strata file (the reference's
+    pack_gguf_to_strata, src/tws/strata_pack.cpp:251, without LZ
+    compression); raises SfkError on a refused or unreadable input."""
+    lib = L.load()
+    L.check(lib.sfk_strata_pack(str(gguf_path).encode(), str(strata_path).encode()))

@@ -150,3 +150,62 @@ def write_strata(path, model, cfg, version: int = 2, compressed_flag: bool = Fal
     return {"trunk": {n: d.tobytes() for n, d in trunk},
             "bundles": {k: b"".join(v) for k, v in bundles.items()},
             "tensors": [(n, t, l, q, ne) for n, t, l, q, ne, _ in tensors]}
+
+
+def write_gguf(path, model, cfg, legacy: bool = False, alignment: int = 32, hide_experts: bool = False,
+               mix: bool = False) -> dict:
+    """A whole GGUF file (metadata + aligned data section) of `model`, the
+    input of the product packer.  legacy: the experts as per-expert 2-D
+    tensors blk.L.ffn_{gate,up,down}.E.weight (the old Mixtral naming);
+    hide_experts: expert tensors renamed so nothing recognises them; mix:
+    layer 0 stacked, the others per-expert.  Returns the source layout:
+    {"data_offset", "meta", "tensors": [(name, type, ne, bytes)]}."""
+    _, tensors = gguf_meta(model, cfg)
+    E = cfg.n_expert
+    kind = {10: "ffn_gate", 11: "ffn_up", 12: "ffn_down"}
+    out = []
+    for name, tid, layer, qtype, ne, data in tensors:
+        per_expert = tid in EXPERT_TIDS and (legacy or (mix and layer > 0))
+        if per_expert:
+            per = data.nbytes // E
+            for e in range(E):
+                out.append((f"blk.{layer}.{kind[tid]}.{e}.weight", qtype, [ne[0], ne[1]],
+                            data.view(np.uint8)[e * per:(e + 1) * per].copy()))
+        else:
+            nm = name.replace("_exps.", "_xps.") if hide_experts and tid in EXPERT_TIDS else name
+            out.append((nm, qtype, list(ne), data))
+    kvs = [
+        _kv("general.architecture", 8, _gstr("llama")),
+        _kv("general.alignment", 4, struct.pack("<I", alignment)),
+        _kv("llama.block_count", 4, struct.pack("<I", cfg.n_layer)),
+        _kv("llama.context_length", 4, struct.pack("<I", cfg.n_ctx)),
+        _kv("llama.embedding_length", 4, struct.pack("<I", cfg.n_embd)),
+        _kv("llama.feed_forward_length", 4, struct.pack("<I", cfg.n_ff)),
+        _kv("llama.attention.head_count", 4, struct.pack("<I", cfg.n_head)),
+        _kv("llama.attention.head_count_kv", 4, struct.pack("<I", cfg.n_head_kv)),
+        _kv("llama.expert_count", 4, struct.pack("<I", cfg.n_expert)),
+        _kv("llama.expert_used_count", 4, struct.pack("<I", cfg.n_expert_used)),
+        _kv("llama.attention.layer_norm_rms_epsilon", 6, struct.pack("<f", cfg.rms_eps)),
+        _kv("llama.rope.freq_base", 6, struct.pack("<f", cfg.freq_base)),
+        _kv("tokenizer.ggml.tokens", 9, struct.pack("<IQ", 8, 3) + _gstr("<s>") + _gstr("</s>") + _gstr("a")),
+    ]
+    meta = b"GGUF" + struct.pack("<IQQ", 3, len(out), len(kvs)) + b"".join(kvs)
+    off = 0
+    offs = []
+    for name, qtype, ne, data in out:
+        dims = list(ne)
+        while len(dims) > 1 and dims[-1] == 1:
+            dims.pop()
+        meta += _gstr(name) + struct.pack("<I", len(dims)) + struct.pack(f"<{len(dims)}Q", *dims)
+        meta += struct.pack("<IQ", qtype, off)
+        offs.append(off)
+        off += (data.nbytes + alignment - 1) // alignment * alignment
+    data_offset = (len(meta) + alignment - 1) // alignment * alignment
+    f = bytearray(meta) + b"\0" * (data_offset - len(meta))
+    for (name, qtype, ne, data), o in zip(out, offs):
+        f += b"\0" * (data_offset + o - len(f))
+        f += data.tobytes()
+    with open(path, "wb") as fh:
+        fh.write(bytes(f))
+    return {"data_offset": data_offset, "meta": bytes(f[:data_offset]),
+            "tensors": [(n, q, ne, d.tobytes()) for n, q, ne, d in out]}
