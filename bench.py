@@ -448,6 +448,27 @@ def ep_measure(B: int, prompt_n: int, n_layer: int, steps: int, warmup: int, ran
         dist.all_reduce(s_, op=dist.ReduceOp.MIN)
         same = int(s_.item())
     value = B * steps / (ms / 1000.0)
+    # the collective the step's peer-memory exchanges stand in for: an NCCL
+    # all-reduce (sum) of the same [b, d] f32 partial, timed alone on this
+    # job's process group (max over ranks), against the step's
+    # 2 x n_layer exchanges
+    nccl_us = None
+    if dist:
+        buf = torch.zeros((B, cfg.n_embd), dtype=torch.float32, device="cuda")
+        for _ in range(20):
+            dist.all_reduce(buf)
+        torch.cuda.synchronize()
+        a0 = torch.cuda.Event(enable_timing=True)
+        a1 = torch.cuda.Event(enable_timing=True)
+        n_ar = 200
+        a0.record()
+        for _ in range(n_ar):
+            dist.all_reduce(buf)
+        a1.record()
+        a1.synchronize()
+        t = torch.tensor([a0.elapsed_time(a1) * 1000.0 / n_ar], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        nccl_us = float(t.item())
     st = eng.stats()
     peak, peak_kind = _peaks()
     rank_bytes, heads_split = ep_rank_bytes(cfg, world, B)
@@ -469,6 +490,10 @@ def ep_measure(B: int, prompt_n: int, n_layer: int, steps: int, warmup: int, ran
                               "unit": "GB/s per GPU", "frac": rank_bytes * steps / (ms / 1000.0) / 1e9 / peak,
                               "bytes_per_token_per_gpu": rank_bytes, "peak_kind": peak_kind},
             "weight_bytes_per_gpu": st["weight_bytes_hbm"], "load_s": t_load, "prefill_s": t_pf,
+            "exchanges": {"per_step": 2 * n_layer, "kind": "peer-memory combine kernel (flags + peer loads)",
+                          "nccl_allreduce_us": nccl_us,
+                          "nccl_allreduce_ms_per_step": None if nccl_us is None else nccl_us * 2 * n_layer / 1e3,
+                          "step_ms": ms / steps},
         }
     if dist:
         dist.barrier()
