@@ -508,7 +508,8 @@ def run_sweep(args):
 
     mul_mat_id: Mixtral-shape experts (E=8, gate/up 14336x4096, down
     4096x14336) in Q4_K / Q6_K / Q8_0 at b in {1, 4, 16} tokens (16 is the
-    engine's largest step; 64 is not run).  Four layers are resident and the
+    engine's largest step), then b in {16, 64} through the expert-grouped
+    tensor-core op (run_sweep_id_tc).  Four layers are resident and the
     launches rotate over them, so every launch streams experts that are not
     in L2.  Bytes = unique routed experts x per-expert matrix bytes; the
     router is a seeded random F32 matrix, so the expected unique count of a
@@ -544,6 +545,7 @@ def run_sweep(args):
                                   "peak_kind": peak_kind, "unique_experts_expected": uniq,
                                   "unique_experts_last_launch": int(np.unique(ids).size)}), flush=True)
         eng.close()
+    run_sweep_id_tc(peak, peak_kind)
     ctxs = (512, 4096, 32768)
     cfg = E.mixtral_config(n_layer=1, n_ctx=max(ctxs) + 16, max_batch=8)
     eng = E.Engine.load(cfg, seed=3)
@@ -560,6 +562,59 @@ def run_sweep(args):
                               "GBps": gbs, "frac": gbs / peak, "peak_kind": peak_kind,
                               "l2_resident": byts < 126e6}), flush=True)
     eng.close()
+
+
+def run_sweep_id_tc(peak, peak_kind):
+    """configs[1]'s mul_mat_id at b in {16, 64} through the expert-grouped
+    tensor-core op (sfk_mul_mat_id_tc): the routed pairs grouped by expert
+    into 64-row tiles, one tcgen05 kind::i8 GEMM over every tile, the rows put
+    back in pair order.  Mixtral expert shapes (E=8, gate 14336x4096 with one
+    activation row per token, down 4096x14336 with one row per pair), top-2
+    ids drawn uniformly without replacement (seeded), weights random bytes in
+    the device layout.  Time = CUDA events around each whole call (grouping,
+    activation quantization, GEMM, ungrouping, and the call's status
+    read-back), mean of `iters` calls after 2 warm-up calls; the 8 experts'
+    matrices (264-499 MB) exceed the 126 MB L2, so every call streams them
+    from HBM.  Bytes = the distinct experts of the call x matrix bytes."""
+    import torch
+    from strataflow_b200 import lib as L
+    from strataflow_b200 import ops
+    names = {L.TYPE_Q4_K: "Q4_K", L.TYPE_Q6_K: "Q6_K", L.TYPE_Q8_0: "Q8_0"}
+    d, F, E, k, iters = 4096, 14336, 8, 2, 10
+    g = torch.Generator(device="cuda")
+    g.manual_seed(1)
+    rng = np.random.default_rng(4)
+    for t in (L.TYPE_Q4_K, L.TYPE_Q6_K, L.TYPE_Q8_0):
+        for (kern, rows, K) in (("gate", F, d), ("down", d, F)):
+            rb = L.load().sfk_dev_row_bytes(t, K)
+            w = torch.randint(0, 255, (E * rows * rb,), dtype=torch.uint8, device="cuda", generator=g)
+            for b in (16, 64):
+                ids_np = np.stack([rng.choice(E, k, replace=False) for _ in range(b)]).astype(np.int32)
+                ids = torch.from_numpy(ids_np).cuda()
+                x = torch.randn((b, K) if kern == "gate" else (b, k, K), device="cuda", generator=g)
+                for _ in range(2):
+                    ops.mul_mat_id_tc(t, w, E, rows, K, x, ids)
+                torch.cuda.synchronize()
+                tot = 0.0
+                for _ in range(iters):
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    ops.mul_mat_id_tc(t, w, E, rows, K, x, ids)
+                    e1.record()
+                    e1.synchronize()
+                    tot += e0.elapsed_time(e1)
+                ms = tot / iters
+                uniq = int(np.unique(ids_np).size)
+                byts = uniq * rows * rb
+                gbs = byts / (ms * 1e-3) / 1e9
+                print(json.dumps({"sweep": "mul_mat_id_tc", "kernel": kern, "wtype": names[t], "b": b, "k": k,
+                                  "us": ms * 1e3, "bytes": byts, "GBps": gbs, "frac": gbs / peak,
+                                  "peak_kind": peak_kind, "unique_experts": uniq,
+                                  "int8_TOPS": 2.0 * b * k * rows * K / (ms * 1e-3) / 1e12,
+                                  "note": "whole call: group + quantize + GEMM + ungroup + status read-back"}),
+                      flush=True)
+            del w
 
 
 def run_sweep_tc(args):

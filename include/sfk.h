@@ -421,6 +421,18 @@ SFK_API sfk_status sfk_mul_mat_id(int ggml_type, const void *dev_w, int32_t n_ex
                           const float *dev_x, int32_t x_per_pair, const int32_t *dev_ids, int32_t b, int32_t k,
                           float *dev_y, void *stream);
 
+/* sfk_mul_mat_id on the tensor cores, for batches whose routed pairs give
+ * the experts many activation rows (b * k in the tens and up): the pairs are
+ * grouped by expert into 64-row tiles, each tile is a tcgen05 kind::i8 GEMM
+ * against its expert's matrix (sfk_mul_mat_tc's arithmetic: exact sub-block
+ * integer dots, fp32 sum over 256-column blocks in block order), and the rows
+ * are put back in pair order.  Same arguments and layout as sfk_mul_mat_id,
+ * any b >= 1 with b * k <= 2^20, n_expert <= 1024; an id outside
+ * [0, n_expert) returns SFK_ERR_RUNTIME.  Synchronizes the stream. */
+SFK_API sfk_status sfk_mul_mat_id_tc(int ggml_type, const void *dev_w, int32_t n_expert, int64_t rows, int64_t K,
+                                     const float *dev_x, int32_t x_per_pair, const int32_t *dev_ids, int32_t b,
+                                     int32_t k, float *dev_y, void *stream);
+
 /* The fused routed-expert FFN of build_expert_segment (engine.cpp:1956-1989):
  * out[t] = res[t] + sum_j w[t][j] * Down_e( silu(Gate_e x[t]) * Up_e x[t] ),
  * e = ids[t][j].  gate/up: [E][F][d], down: [E][d][F] (device layout);

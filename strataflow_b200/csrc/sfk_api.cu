@@ -2775,6 +2775,56 @@ sfk_status sfk_mul_mat_tc(int t, const void* w, int64_t rows, int64_t K, const f
   return check_status_word(sc->status, st);
 }
 
+sfk_status sfk_mul_mat_id_tc(int t, const void* w, int32_t n_expert, int64_t rows, int64_t K, const float* x,
+                             int32_t x_per_pair, const int32_t* ids, int32_t b, int32_t k, float* y, void* stream) {
+  if (!quant_ok(t) || K % 256 || !w || !x || !ids || !y || b < 1 || k < 1 || (int64_t)b * k > (1 << 20) ||
+      n_expert < 1 || n_expert > 1024 || rows < 1 || rows > 65535 * 128)
+    return fail(SFK_ERR_INVALID_ARGUMENT, "mul_mat_id_tc arguments");
+  const int act = act_for(t);
+  const int np = b * k;
+  // every expert's pairs in whole 64-row tiles: at most one partial tile per
+  // routed expert beyond the full ones
+  const int mt = (np + TC_TT - 1) / TC_TT + std::min(n_expert, np);
+  const int rows_pad = mt * TC_TT;
+  auto up = [](size_t v) { return (v + 255) & ~(size_t)255; };
+  const size_t act_b = up(tc_act_bytes(rows_pad, (int)K));
+  const size_t ypad_b = up(sizeof(float) * (size_t)rows_pad * (size_t)rows);
+  const size_t ints_b = up(sizeof(int) * ((size_t)np + 2 * (size_t)rows_pad + (size_t)mt));
+  OpScratch* sc = nullptr;
+  sfk_status s = op_scratch(act_b + ypad_b + ints_b, 1, &sc);
+  if (s) return s;
+  cudaStream_t st = (cudaStream_t)stream;
+  uint8_t* buf = static_cast<uint8_t*>(sc->buf);
+  float* ypad = reinterpret_cast<float*>(buf + act_b);
+  int* pos_of_pair = reinterpret_cast<int*>(buf + act_b + ypad_b);
+  int* rows_tok = pos_of_pair + np;
+  int* rows_self = rows_tok + rows_pad;
+  int* tile_expert = rows_self + rows_pad;
+  // group the pairs by expert; the activation row of pair i is token i / k,
+  // or pair i itself when every pair has its own row
+  CK(launch_pf_group(ids, np, x_per_pair ? 1 : k, n_expert, mt, pos_of_pair, rows_tok, rows_self, tile_expert,
+                     sc->status, st));
+  CK(launch_tc_quant(act, x, K, rows_tok, x_per_pair ? np : b, rows_pad, (int)K, buf, st));
+  TcGemmParams p{};
+  p.w = (const uint8_t*)w;
+  p.rowstride = dev_row_bytes(t, (int)K);
+  p.expert_stride = rows * p.rowstride;
+  p.rows = (int)rows;
+  p.K = (int)K;
+  p.wtype = t;
+  p.act_type = act;
+  p.xq = buf;
+  p.ntile = mt;
+  p.tile_expert = tile_expert;
+  p.y = ypad;
+  p.ldy = rows;
+  p.epi = TC_EPI_STORE;
+  p.status = sc->status;
+  CK(launch_tc_gemm(p, st));
+  CK(launch_pf_ungroup(ypad, pos_of_pair, np, rows, y, st));
+  return check_status_word(sc->status, st);
+}
+
 sfk_status sfk_sample_logits(const float* logits, int32_t V, const sfk_sampling* sp, int32_t step, int32_t* token_out,
                              void* stream) {
   if (!logits || !sp || !token_out || V < 1 || step < 0 || !(sp->temperature > 0.0f))

@@ -237,6 +237,22 @@ __global__ void __launch_bounds__(256) pf_combine_kernel(const float* yd, const 
 
 unsigned blocks_for(int64_t items, int per) { return (unsigned)((items + per - 1) / per); }
 
+__global__ void __launch_bounds__(256) pf_ungroup_kernel(const float4* src, const int* pos_of_pair, int np,
+                                                         int64_t rows4, float4* y) {
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (idx >= (int64_t)np * rows4) return;
+  const int64_t i = idx / rows4, c = idx % rows4;
+  y[idx] = src[(int64_t)pos_of_pair[i] * rows4 + c];
+}
+
+__global__ void __launch_bounds__(256) pf_ungroup1_kernel(const float* src, const int* pos_of_pair, int np,
+                                                          int64_t rows, float* y) {
+  const int64_t idx = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (idx >= (int64_t)np * rows) return;
+  const int64_t i = idx / rows, c = idx % rows;
+  y[idx] = src[(int64_t)pos_of_pair[i] * rows + c];
+}
+
 // ---- causal attention over the paged KV -----------------------------------------
 // The arithmetic of the reference's per-token attention as the CPU oracle and
 // the decode kernel compute it (engine.cpp:1751-1761: ggml_mul_mat(k, q),
@@ -596,6 +612,16 @@ cudaError_t launch_pf_group(const int* ids, int np, int k, int E, int max_tiles,
   if (e != cudaSuccess) return e;
   pf_group_kernel<<<1, PF_GROUP_THREADS, smem, st>>>(ids, np, k, E, max_tiles, pos_of_pair, rows_tok, rows_self,
                                                      tile_expert, status);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_pf_ungroup(const float* src, const int* pos_of_pair, int np, int64_t rows, float* y,
+                              cudaStream_t st) {
+  if (rows % 4 == 0 && ((uintptr_t)src | (uintptr_t)y) % 16 == 0)
+    pf_ungroup_kernel<<<blocks_for((int64_t)np * (rows / 4), 256), 256, 0, st>>>(
+        (const float4*)src, pos_of_pair, np, rows / 4, (float4*)y);
+  else
+    pf_ungroup1_kernel<<<blocks_for((int64_t)np * rows, 256), 256, 0, st>>>(src, pos_of_pair, np, rows, y);
   return cudaGetLastError();
 }
 

@@ -49,5 +49,9 @@ cudaError_t launch_pf_group(const int* ids, int np, int k, int E, int max_tiles,
 // the experts added in slot order (engine.cpp:1973-1986).
 cudaError_t launch_pf_combine(const float* yd, const int* pos_of_pair, const float* w, int k, int n, int d,
                               const float* res, float* x, cudaStream_t st);
+// y[i][c] = src[pos_of_pair[i]][c] for i < np, c < rows: the expert-grouped
+// GEMM rows put back in pair order.
+cudaError_t launch_pf_ungroup(const float* src, const int* pos_of_pair, int np, int64_t rows, float* y,
+                              cudaStream_t st);
 
 }  // namespace sfk

@@ -88,6 +88,7 @@ _SIGS = {
     "sfk_mul_mat": (I32, [C.c_int, P, I64, I64, P, I32, P, P]),
     "sfk_mul_mat_tc": (I32, [C.c_int, P, I64, I64, P, I32, P, P]),
     "sfk_mul_mat_id": (I32, [C.c_int, P, I32, I64, I64, P, I32, P, I32, I32, P, P]),
+    "sfk_mul_mat_id_tc": (I32, [C.c_int, P, I32, I64, I64, P, I32, P, I32, I32, P, P]),
     "sfk_moe_ffn": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
     "sfk_moe_ffn_noalloc": (I32, [C.c_int, C.c_int, P, P, P, I32, I64, I64, P, P, P, P, I32, I32, P, P]),
     "sfk_attn_decode_paged": (I32, [P, P, P, I32, I32, P, I32, P, I32, I32, I32, I32, P, P]),

@@ -83,6 +83,18 @@ def mul_mat_id(qtype: int, w_dev: torch.Tensor, n_expert: int, rows: int, K: int
     return y
 
 
+def mul_mat_id_tc(qtype: int, w_dev: torch.Tensor, n_expert: int, rows: int, K: int, x: torch.Tensor,
+                  ids: torch.Tensor) -> torch.Tensor:
+    """mul_mat_id on the tensor cores (sfk_mul_mat_id_tc), for batches of
+    many routed pairs; the same arguments and result layout as mul_mat_id."""
+    b, k = ids.shape
+    per_pair = 1 if x.dim() == 3 else 0
+    y = torch.empty((b, k, rows), dtype=torch.float32, device=x.device)
+    L.check(L.load().sfk_mul_mat_id_tc(qtype, _ptr(w_dev), n_expert, rows, K, _ptr(x), per_pair, _ptr(ids), b, k,
+                                       _ptr(y), _stream(x)))
+    return y
+
+
 def moe_ffn(type_gu: int, type_down: int, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor, n_expert: int,
             d: int, F: int, x: torch.Tensor, res: torch.Tensor | None, ids: torch.Tensor,
             w: torch.Tensor) -> torch.Tensor:
