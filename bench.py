@@ -562,6 +562,35 @@ def run_sweep(args):
                               "GBps": gbs, "frac": gbs / peak, "peak_kind": peak_kind,
                               "l2_resident": byts < 126e6}), flush=True)
     eng.close()
+    run_sweep_attn_hbm(peak, peak_kind)
+
+
+def run_sweep_attn_hbm(peak, peak_kind):
+    """configs[2]'s short contexts with the KV read from HBM: the same
+    attention kernel timed by sfk_time_kernels, whose 64 launches rotate over
+    the layers, on an engine with enough layers that their KV (layers x b x
+    ctx x 8 kv heads x 128 x 2 (K, V) x 2 B) exceeds the 126 MB L2 -- 64
+    layers at ctx 512 (134 MB at b = 1), 32 layers at ctx 4096 -- so no launch
+    finds its layer's pages in L2.  The FFN is shrunk to 256 columns (the
+    attention does not read it) to keep the engine small; each sequence's
+    context is filled by sfk_prefill and one batched decode step."""
+    from strataflow_b200 import engine as E
+    rng = np.random.default_rng(5)
+    for ctx, n_layer in ((512, 64), (4096, 32)):
+        cfg = E.mixtral_config(n_layer=n_layer, n_ff=256, n_ctx=ctx + 16, max_batch=8)
+        eng = E.Engine.load(cfg, seed=3)
+        for sq in range(8):
+            eng.prefill(rng.integers(0, cfg.n_vocab, ctx - 1), pos0=0, seq=sq, want_logits=False)
+        eng.forward_batch(rng.integers(0, cfg.n_vocab, 8), np.full(8, ctx - 1, np.int32), want_logits=False)
+        for b in (1, 8):
+            kt = eng.time_kernels(b, iters=64)
+            byts = b * ctx * 8 * 128 * 2 * 2
+            gbs = byts / (kt["attention"] * 1e-3) / 1e9
+            print(json.dumps({"sweep": "attention_hbm", "ctx": ctx, "b": b, "us": kt["attention"] * 1e3,
+                              "bytes": byts, "GBps": gbs, "frac": gbs / peak, "peak_kind": peak_kind,
+                              "layers_rotated": n_layer, "working_set_bytes": n_layer * byts,
+                              "l2_resident": n_layer * byts < 126e6}), flush=True)
+        eng.close()
 
 
 def run_sweep_id_tc(peak, peak_kind):
