@@ -452,8 +452,8 @@ SFK_API sfk_status sfk_moe_ffn(int type_gu, int type_down, const void *dev_gate,
  * the library (every GPU that loads the library holds it until exit); a shape
  * whose scratch does not fit (roughly b*k*F*4 + b*k*F*1.2 + b*d*1.2 bytes) is
  * rejected with SFK_ERR_INVALID_ARGUMENT before any work is queued.  The first
- * call on a device looks up the array's device address (cudaGetSymbolAddress);
- * make that first call before any stream capture on that device.  All calls
+ * call on a device looks up the array's device address (cudaGetSymbolAddress)
+ * and keeps it for the later calls on that device.  All calls
  * share the array and it keeps the last call's contents (the call clears what
  * must start at zero): calls whose work overlaps on the GPU (other streams,
  * other threads on the same device) race on it.  The call returns only after
