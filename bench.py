@@ -514,7 +514,9 @@ def run_sweep(args):
     in L2.  Bytes = unique routed experts x per-expert matrix bytes; the
     router is a seeded random F32 matrix, so the expected unique count of a
     uniform top-2 draw, 8 (1 - 0.75^b), is used (the last launch's measured
-    count is printed beside it).
+    count is printed beside it).  Steps of one or two tokens route inside the
+    gate/up kernel (its time includes the routing, router_us is 0); larger
+    steps run the router kernel first (router_us, not in gate/up's time).
 
     attention: 32q/8kv heads, hd 128, f16 KV in 16-token pages handed out in
     a permuted order, contexts {512, 4096, 32768}, b in {1, 8}; one layer, so
@@ -542,6 +544,7 @@ def run_sweep(args):
                 gbs = byts / (kt[kern] * 1e-3) / 1e9
                 print(json.dumps({"sweep": "mul_mat_id", "kernel": kern, "wtype": names[t], "b": b,
                                   "us": kt[kern] * 1e3, "bytes": byts, "GBps": gbs, "frac": gbs / peak,
+                                  "router_us": kt["router"] * 1e3,
                                   "peak_kind": peak_kind, "unique_experts_expected": uniq,
                                   "unique_experts_last_launch": int(np.unique(ids).size)}), flush=True)
         eng.close()

@@ -271,7 +271,10 @@ struct sfk_engine {
   unsigned long long* argmax_key = nullptr;  // [B] keys, then the status word: one read-back
   int *tok_in = nullptr, *pos_in = nullptr, *pos_state = nullptr, *pos_cur = nullptr, *tok_hist = nullptr;
   int* status = nullptr;  // right after argmax_key[B]
-  bool fused_route = false;  // the gate/up kernel routes in its prologue (no router kernel)
+  // the gate/up kernel can route in its prologue (no router kernel); steps of
+  // at most fused_route_max_b tokens do, larger steps run the router kernel
+  bool fused_route = false;
+  int fused_route_max_b = 0;
   // expert parallelism: this rank holds experts [e0, e0 + e_loc)
   int ep_size = 1, ep_rank = 0, e_loc = 0, e0 = 0;
   // head parallelism (with expert parallelism when the heads divide): this
@@ -495,6 +498,13 @@ KvView kv_view(const sfk_engine* e, int l) {
   return kv;
 }
 
+// Whether a step of b tokens routes inside its gate/up kernel.  The fused
+// prologue routes the step's tokens one after another in every CTA: cheapest
+// for one or two tokens, while from four tokens on the router kernel, which
+// routes them in parallel, and a plain gate/up prologue are faster (Mixtral
+// shape, b = 8: 637 vs 605 tok/s; b = 16: 637 vs 495).
+bool route_fused(const sfk_engine* e, int b) { return e->fused_route && b <= e->fused_route_max_b; }
+
 StreamParams gateup_params(const sfk_engine* e, int l, int b) {
   const sfk_hparams& hp = e->hp;
   const int d = hp.n_embd, F = hp.n_ff, k = hp.n_expert_used;
@@ -523,7 +533,7 @@ StreamParams gateup_params(const sfk_engine* e, int l, int b) {
     p.slot_map = e->tier.d_map + (size_t)l * hp.n_expert;
     p.n_map_slots = (int)e->tier.n_slots;
   }
-  if (e->fused_route) {
+  if (route_fused(e, b)) {
     p.pro = PRO_ROUTE;  // ffn_norm + quantize + router + top-k in the prologue
     p.x = e->ffn_inp;
     p.norm_w = W.ffn_norm;
@@ -662,7 +672,7 @@ sfk_status launch_one(sfk_engine* e, int c, int l, int b, bool greedy, bool pdl)
       return SFK_OK;
     }
     case K_ROUTER: {  // ffn_norm + router + top-k (engine.cpp:1909-1924)
-      if (e->fused_route) return SFK_OK;  // done inside the gate/up kernel
+      if (route_fused(e, b)) return SFK_OK;  // done inside the gate/up kernel
       const LayerW& W = e->L[l];
       RouterParams r{};
       r.x = e->ffn_inp;
@@ -981,7 +991,7 @@ sfk_status enqueue_step(sfk_engine* e, int b, bool greedy) {
   ++nk;
   for (int l = 0; l < e->hp.n_layer; ++l) {
     for (int c = K_QKV; c <= K_DOWN; ++c) {
-      if (c == K_ROUTER && e->fused_route) continue;
+      if (c == K_ROUTER && route_fused(e, b)) continue;
       if ((s = launch_one(e, c, l, b, greedy, true))) return s;
       ++nk;
       if (c == K_OPROJ && e->head_par) {  // add the ranks' attention projections
@@ -1300,7 +1310,7 @@ sfk_status run_step_direct(sfk_engine* e, int b, bool greedy) {
     }
     if (!s) s = launch_one(e, K_OPROJ, l, b, greedy, true);
     nk += 3;
-    if (!e->fused_route) {
+    if (!route_fused(e, b)) {
       if (!s) s = launch_one(e, K_ROUTER, l, b, greedy, true);
       ++nk;
     }
@@ -1655,7 +1665,11 @@ sfk_status sfk_engine_create(int device, const sfk_hparams* hp, sfk_engine** out
     const char* rk = getenv("SFK_ROUTER_KERNEL");
     // (a bounded tier reads each layer's routing back before its experts run)
     e->fused_route = !(rk && atoi(rk) == 1) && !e->tier.on;
-    StreamParams gp = gateup_params(e, 0, B);
+    // SFK_FUSED_ROUTE_MAX_B moves the step size up to which routing stays fused
+    e->fused_route_max_b = 2;
+    if (const char* v = getenv("SFK_FUSED_ROUTE_MAX_B")) e->fused_route_max_b = std::max(1, atoi(v));
+    e->fused_route_max_b = std::min(e->fused_route_max_b, B);
+    StreamParams gp = gateup_params(e, 0, e->fused_route_max_b);
     int grid = 0;
     if (e->fused_route &&
         (plan_stream(gp, e->sm_count, &grid) != SFK_OK || stream2_smem_bytes(gp) > SMEM_LIMIT))
@@ -2540,7 +2554,7 @@ sfk_status sfk_decode_layer_moe(sfk_engine* e, int32_t layer, int32_t n_tok, flo
   if (layer < 0 || layer >= e->hp.n_layer) return fail(SFK_ERR_INVALID_ARGUMENT, "layer %d", layer);
   const int d = e->hp.n_embd, k = e->hp.n_expert_used;
   CK(cudaMemcpyAsync(e->ffn_inp, hidden, sizeof(float) * n_tok * d, cudaMemcpyDeviceToDevice, e->stream));
-  if (!e->fused_route) s = launch_one(e, K_ROUTER, layer, n_tok, false, false);
+  if (!route_fused(e, n_tok)) s = launch_one(e, K_ROUTER, layer, n_tok, false, false);
   if (!s && e->tier.on) {
     e->tier.warmed_now.clear();
     s = tier_route_layer(e, layer, n_tok);
@@ -2660,7 +2674,7 @@ sfk_status sfk_time_kernels(sfk_engine* e, int32_t n_seq, int32_t iters, float* 
     CK(cudaEventSynchronize(z));
     float ms = 0.0f;
     CK(cudaEventElapsedTime(&ms, a, z));
-    ms_out[c] = (c == K_ROUTER && e->fused_route) ? 0.0f : ms / iters;  // routing is inside gate/up
+    ms_out[c] = (c == K_ROUTER && route_fused(e, n_seq)) ? 0.0f : ms / iters;  // routing is inside gate/up
   }
   cudaEventDestroy(a);
   cudaEventDestroy(z);
