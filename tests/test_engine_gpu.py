@@ -130,6 +130,35 @@ def test_batched_step_equals_single_sequences(cuda):
     assert toks.shape == (5, 3) and (toks[0] == am_b).all()
 
 
+@pytest.mark.parametrize("kw", [dict(n_layer=2), dict(n_layer=2, type_ffn_gu=12, type_ffn_down=14, type_attn=14)])
+def test_router_kernel_equals_fused_routing(cuda, monkeypatch, kw):
+    """Steps of more than two tokens route with the router kernel; forcing
+    the gate/up kernel's fused routing prologue for them instead
+    (SFK_FUSED_ROUTE_MAX_B) gives the same routing and logits bit for bit."""
+    from strataflow_b200 import engine as E
+    cfg = E.tiny_config(max_batch=4, **kw)
+    rng = np.random.default_rng(7)
+    steps = [(rng.integers(0, cfg.n_vocab, 3), [p, p + 2, p + 5]) for p in range(8)]
+
+    def run():
+        eng = E.Engine.load(cfg, seed=9)
+        eng.reset_kv()
+        out = []
+        for toks, pos in steps:
+            am, lg = eng.forward_batch(toks, pos)
+            ids, w = eng.route(3)
+            out.append((am, lg, ids, w))
+        return out
+
+    kern = run()
+    monkeypatch.setenv("SFK_FUSED_ROUTE_MAX_B", "16")
+    fused = run()
+    for (a0, l0, i0, w0), (a1, l1, i1, w1) in zip(kern, fused):
+        assert np.array_equal(a0, a1) and np.array_equal(i0, i1)
+        assert np.array_equal(w0.view(np.uint32), w1.view(np.uint32))
+        assert np.array_equal(l0.view(np.uint32), l1.view(np.uint32))
+
+
 def test_mixtral_width_two_layer_parity(cuda):
     """Mid-size model: every Mixtral-8x7B width (d 4096, 32q/8kv x 128,
     8 experts top-2, FFN 14336, vocab 32000, RoPE 1e6, Q4_K experts, Q6_K
