@@ -76,6 +76,10 @@ def _head_par(cfg, world, env):
     (dict(n_layer=2, n_expert=160, n_expert_used=2), {}),                    # logits exchanged between CTAs
     (WIDE, {"SFK_HEAD_PARALLEL": "0"}),                                      # trunk replicated
     (WIDE, {}),                                                              # heads split over the ranks
+    # the router kernel (steps of more than two tokens take it), building each
+    # rank's slot lists for its own experts
+    (dict(n_layer=2), {"SFK_ROUTER_KERNEL": "1"}),
+    (dict(n_layer=2, n_expert=72, n_expert_used=4), {"SFK_ROUTER_KERNEL": "1"}),
 ])
 def test_expert_parallel_two_ranks_match_oracle(cuda, cfg_kw, env):
     import torch
